@@ -1,0 +1,207 @@
+/*
+ * libb200moe - B200 (sm_100a) kernels for the quantized MoE and decode-GEMM
+ * path of sglang-restomod, behind a plain C ABI.
+ *
+ * Every entry point takes raw device pointers, element counts and a CUDA
+ * stream (as void*; NULL is the legacy default stream, which breaks graph
+ * capture, so pass the caller's current stream). Nothing here allocates
+ * device memory: outputs and workspaces belong to the caller. Every function
+ * validates its arguments on the host first and returns a status:
+ *   0  B200_OK
+ *   1  B200_ERR_INVALID      bad argument (message in b200_last_error())
+ *   2  B200_ERR_UNSUPPORTED  a valid call this build declines (shape/dtype)
+ *   3  B200_ERR_CUDA         a CUDA runtime error while launching
+ * No function throws, traps on the device, or reads the environment.
+ *
+ * Workspaces: functions taking (workspace, workspace_bytes) need a buffer of
+ * at least the size the matching *_workspace_bytes() function returns, zero
+ * filled before its first use. The kernels return every counter and partial
+ * sum they touch to zero, so one workspace serves any number of calls - but
+ * calls that share a workspace must be ordered (same stream, or joined by
+ * events); two calls running at once on one workspace race.
+ *
+ * Dtype codes: 0 = bf16, 1 = f16, 2 = f32.
+ *
+ * Reference interfaces replaced are cited as path:line inside the
+ * sglang-restomod source tree.
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_OK 0
+#define B200_ERR_INVALID 1
+#define B200_ERR_UNSUPPORTED 2
+#define B200_ERR_CUDA 3
+
+#define B200_DTYPE_BF16 0
+#define B200_DTYPE_F16 1
+#define B200_DTYPE_F32 2
+
+#define B200_QUANT_FP8_BLOCK 0 /* e4m3 weights, fp32 scales per 128x128 block */
+#define B200_QUANT_NVFP4 1     /* e2m1 weights, e4m3 scales per 16 K, fp32 global */
+
+#define B200_GATED_NONE 0  /* plain rows: out[.., N] */
+#define B200_GATED_FUSED 1 /* gate/up bank: out[.., N/2] = silu(gate) * up */
+#define B200_GATED_SPLIT 2 /* gate/up bank: out[.., N] = gate | up (no activation) */
+
+/* ABI version of this header; bumped on any signature change. */
+int b200_abi_version(void);
+
+/* Message of the last non-zero status returned on this thread. */
+const char* b200_last_error(void);
+
+/* SMs of the current device (the stream GEMM's persistent grid is a multiple). */
+int b200_num_sms(void);
+
+/*
+ * Device-side error bits recorded in a workspace (1 = a pipeline wait timed
+ * out, 2 = an expert id >= E reached a GEMM, 4 = a route pointed past the
+ * activation rows). Synchronizes `stream`; clears the bits when reset != 0.
+ */
+int b200_workspace_status(void* workspace, int32_t* bits, int32_t reset, void* stream);
+
+/* ---------------------------------------------------------------- routing */
+
+/*
+ * moe_align_block_size. Replaces upstream sgl_kernel's moe_align_block_size
+ * as pinned by sglang_restomod/moe/align_sm70.py:35-55 (its consumers:
+ * quant/sm70_fp4_moe/decode_gemv.py:226-260, csrc/decode_gemv_qpn2.cu:73-110),
+ * with the stable expert-major order of quant/sm70_fp8_moe/method.py:285.
+ *
+ * topk_ids[numel] (numel = tokens * top_k) -> sorted_token_ids holds route
+ * indices grouped by expert in route order, each expert padded to a multiple
+ * of block_size with the sentinel `numel`; expert_ids[b] is block b's expert
+ * (-1 past the end); num_tokens_post_pad[0] is the padded total. Ids outside
+ * [0, num_experts) are dropped. Needs sorted_capacity >= numel +
+ * min(numel, num_experts) * (block_size - 1) and expert_capacity >=
+ * ceil(sorted_capacity / block_size); every slot of both arrays is written.
+ * num_experts <= 1024.
+ */
+int b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int32_t num_experts,
+                              int32_t block_size, int32_t* sorted_token_ids,
+                              int64_t sorted_capacity, int32_t* expert_ids,
+                              int64_t expert_capacity, int32_t* num_tokens_post_pad,
+                              void* stream);
+
+/* ---------------------------------------------------------------- combine */
+
+/*
+ * moe_sum_reduce: output[t, :] = routed_scaling_factor * sum_k input[t, k, :]
+ * (fp32 sum, stored in the input dtype). Replaces
+ * quant/sm70_fp4_moe/sum_reduce.py:84-123. hidden % 8 == 0; contiguous.
+ */
+int b200_moe_sum_reduce(const void* input, void* output, int64_t tokens, int32_t top_k,
+                        int64_t hidden, int32_t dtype, float routed_scaling_factor, void* stream);
+
+/*
+ * Top-k combine of rows already multiplied by their router weight
+ * (quant/sm70_fp8_moe/method.py:305-309): out[t] = rsf * sum over k with
+ * 0 <= topk_ids[t, k] < num_experts of routed[t * top_k + k] (+ shared[t]).
+ * topk_ids may be NULL (every route counts); shared_out may be NULL.
+ */
+int b200_moe_combine(const void* routed, int32_t routed_dtype, const int32_t* topk_ids,
+                     int32_t num_experts, int64_t tokens, int32_t top_k, int64_t hidden,
+                     float routed_scaling_factor, const void* shared_out, int32_t shared_dtype,
+                     void* out, int32_t out_dtype, void* stream);
+
+/* ---------------------------------------------------------------- prepack */
+
+/*
+ * Block-FP8 weights [experts, n, k] e4m3 (row-major) -> this library's
+ * streamed layout. Replaces the load-time prepare of
+ * quant/sm70_fp8_moe/__init__.py:161-205 (fp8_prepare with
+ * interleave_gated_silu) and quant/sm70_fp8_dense/_method.py:314-329
+ * (_qpn8_prepack). gated != 0 interleaves the two halves of a [2I, K]
+ * gate/up bank. n % 128 == 0, k % 128 == 0 (gated: n % 256 == 0).
+ */
+int64_t b200_fp8_packed_bytes(int64_t experts, int64_t n, int64_t k);
+int b200_fp8_prepack(const uint8_t* w_e4m3, int64_t experts, int64_t n, int64_t k, int32_t gated,
+                     uint8_t* out, void* stream);
+
+/*
+ * NVFP4 ModelOpt checkpoint [experts, n, k/2] uint8 (low nibble = even K) and
+ * [experts, n, k/16] e4m3 group scales -> streamed layout (scales inline).
+ * Replaces prepare_moe_nvfp4 / qpn2.pack_expert
+ * (quant/sm70_fp4_moe/method.py:290-382, qpn2.py:65-110). The fp32 global
+ * scale stays a separate [experts] array.
+ */
+int64_t b200_nvfp4_packed_bytes(int64_t experts, int64_t n, int64_t k);
+int b200_nvfp4_prepack(const uint8_t* w_packed, const uint8_t* scales_e4m3, int64_t experts,
+                       int64_t n, int64_t k, int32_t gated, uint8_t* out, void* stream);
+
+/* ------------------------------------------------------------------ GEMMs */
+
+/* Workspace for b200_linear / b200_moe_gemm; `convert_elems` is the number of
+ * bf16 activation elements the call converts (0 for f16 activations). */
+int64_t b200_gemm_workspace_bytes(int64_t convert_elems);
+
+/*
+ * Dense W8A16 / W4A16 linear, y[m, :] = x[m, :k] . dequant(W)^T.
+ * Replaces apply_sm70_turbomind_fp8_linear (quant/sm70_fp8_dense/_method.py:
+ * 713-784; its QPN8 decode kernel csrc/sm70_fp8_qpn8_decode.cu:60-149) and,
+ * with gated_mode = B200_GATED_FUSED on a gated bank,
+ * apply_sm70_turbomind_fp8_fused_silu_and_mul (_method.py:787-863,
+ * csrc/sm70_fp8_qpn8_decode.cu:156-246).
+ * quant: B200_QUANT_FP8_BLOCK (w_scales = [n/128, k/128] fp32) or
+ * B200_QUANT_NVFP4 (global_scale = one fp32). x: bf16 or f16, rows of k.
+ * 1 <= m <= 64 per weight pass (larger m runs ceil(m/64) passes).
+ */
+int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* workspace,
+                int64_t workspace_bytes, void* stream);
+
+/*
+ * Grouped expert GEMM routed by moe_align_block_size output, with the
+ * semantics of moe_wna16_marlin_gemm (quant/sm70_fp4_moe/method.py:385-564):
+ * route slot p of block b multiplies activation row sorted_token_ids[p] /
+ * top_k by expert expert_ids[b] and writes output row sorted_token_ids[p]
+ * (times topk_weights[route] when mul_topk_weights). a: [a_rows, k];
+ * c: rows of ldc elements. block_size in {8, 16, 32, 64}.
+ * At most expert_capacity blocks are read, so sorted_token_ids must hold
+ * expert_capacity * block_size entries (pass floor(sorted_len / block_size)
+ * when the align output is shorter). topk_weights and c need num_routes rows.
+ */
+int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+                  const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                  int32_t num_experts, int64_t n, int32_t gated_mode,
+                  const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                  int64_t expert_capacity, const int32_t* num_tokens_post_pad,
+                  int32_t block_size, int32_t top_k, int64_t num_routes,
+                  const float* topk_weights, int32_t mul_topk_weights, void* c, int32_t c_dtype,
+                  int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * One fused-MoE layer forward (SM70Fp8MoEMethod.apply,
+ * quant/sm70_fp8_moe/method.py:239-309; the NVFP4 fused_marlin_moe chain of
+ * quant/sm70_fp4_moe/method.py:385-564 + sum_reduce.py:84-123):
+ * align -> gate_up (+SiLU*up) -> down (x router weight) -> combine
+ * (x routed_scaling_factor, + shared_out when given).
+ * x [tokens, hidden] bf16/f16; topk_ids/topk_weights [tokens, top_k];
+ * w13: gated bank [E, 2*inter, hidden]; w2: [E, hidden, inter].
+ * Ids outside [0, E) contribute nothing (expert-parallel drops).
+ */
+int64_t b200_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
+                                       int32_t num_experts, int32_t top_k, int32_t block_size);
+int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
+                           int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                           const float* topk_weights, int32_t top_k, int32_t num_experts,
+                           const uint8_t* w13_packed, const float* w13_scales,
+                           const float* w13_global, const uint8_t* w2_packed,
+                           const float* w2_scales, const float* w2_global, int32_t block_size,
+                           float routed_scaling_factor, const void* shared_out,
+                           int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,531 @@
+// C ABI of libb200moe: host-side validation, workspace carving and launch
+// orchestration. The signatures are declared (with the reference interface
+// each one replaces) in include/b200moe.h.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/b200moe.h"
+#include "internal.h"
+
+namespace b200 {
+
+int device_sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    cached[dev] = sms;
+  }
+  return cached[dev];
+}
+
+}  // namespace b200
+
+namespace {
+
+using namespace b200;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_cuda(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return B200_OK;
+  return fail(B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int64_t kAlign = 256;
+int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Workspace layout: [status int | pad] [counters, kMaxSlots ints] [partials,
+// slots x kWsSlotFloats fp32] [scratch ...]
+constexpr int64_t kStatusBytes = 256;
+constexpr int kMaxSlots = 1024;
+constexpr int64_t kCounterBytes = kMaxSlots * 4;
+
+int max_grid_slots() {
+  int g = stream_gemm_ctas_per_sm(1) * device_sm_count();
+  return g > kMaxSlots ? kMaxSlots : g;
+}
+
+int64_t stream_ws_bytes() {
+  return kStatusBytes + kCounterBytes + (int64_t)max_grid_slots() * kWsSlotFloats * 4;
+}
+
+struct WsView {
+  int* status;
+  int* counters;
+  float* partials;
+  uint8_t* scratch;
+  int64_t scratch_bytes;
+};
+
+bool carve(void* ws, int64_t bytes, WsView& v) {
+  const int64_t fixed = stream_ws_bytes();
+  if (ws == nullptr || bytes < fixed || (reinterpret_cast<uintptr_t>(ws) % kAlign) != 0) return false;
+  uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+  v.status = reinterpret_cast<int*>(base);
+  v.counters = reinterpret_cast<int*>(base + kStatusBytes);
+  v.partials = reinterpret_cast<float*>(base + kStatusBytes + kCounterBytes);
+  v.scratch = base + fixed;
+  v.scratch_bytes = bytes - fixed;
+  return true;
+}
+
+int nt_for_rows(int64_t rows) {
+  if (rows <= 8) return 1;
+  if (rows <= 16) return 2;
+  if (rows <= 32) return 4;
+  return 8;
+}
+
+bool valid_dtype16(int32_t d) { return d == B200_DTYPE_BF16 || d == B200_DTYPE_F16; }
+
+// Converts bf16 activations into the f16 operand the stream GEMM reads.
+int stage_activations(const void* a, int32_t a_dtype, int64_t elems, WsView& ws, int64_t& used,
+                      const __half** out, cudaStream_t stream) {
+  if (a_dtype == B200_DTYPE_F16) {
+    *out = reinterpret_cast<const __half*>(a);
+    return B200_OK;
+  }
+  const int64_t need = align_up(elems * 2);
+  if (used + need > ws.scratch_bytes)
+    return fail(B200_ERR_INVALID, "workspace too small for %lld converted activations",
+                (long long)elems);
+  __half* dst = reinterpret_cast<__half*>(ws.scratch + used);
+  used += need;
+  int rc = check_cuda(launch_bf16_to_f16(a, dst, elems, stream), "bf16->f16 conversion");
+  if (rc) return rc;
+  *out = dst;
+  return B200_OK;
+}
+
+int check_weight_shape(int32_t quant, int64_t n, int64_t k, int32_t gated_mode) {
+  if (quant != B200_QUANT_FP8_BLOCK && quant != B200_QUANT_NVFP4)
+    return fail(B200_ERR_INVALID, "unknown quant %d", quant);
+  if (n <= 0 || k <= 0) return fail(B200_ERR_INVALID, "needs positive N and K, got N=%lld K=%lld",
+                                    (long long)n, (long long)k);
+  // The reference refuses partial quantization groups the same way
+  // (quant/sm70_fp8_moe/__init__.py:48-73).
+  if (k % 128)
+    return fail(B200_ERR_INVALID,
+                "needs K a multiple of the 128-wide quantization group, got K=%lld", (long long)k);
+  if (n % 128)
+    return fail(B200_ERR_INVALID, "needs N a multiple of 128, got N=%lld", (long long)n);
+  if (gated_mode != B200_GATED_NONE && gated_mode != B200_GATED_FUSED &&
+      gated_mode != B200_GATED_SPLIT)
+    return fail(B200_ERR_INVALID, "unknown gated mode %d", gated_mode);
+  if (gated_mode != B200_GATED_NONE && n % 256)
+    return fail(B200_ERR_INVALID, "a gate/up bank needs N a multiple of 256, got N=%lld",
+                (long long)n);
+  if (n > (1ll << 30) || k > (1ll << 30)) return fail(B200_ERR_INVALID, "N or K too large");
+  return B200_OK;
+}
+
+int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsView& ws,
+               cudaStream_t stream) {
+  p.ws = ws.partials;
+  p.ws_cnt = ws.counters;
+  p.status = ws.status;
+  long long grid = (long long)max_grid_slots();
+  if (nt >= 4) grid = (long long)stream_gemm_ctas_per_sm(nt) * device_sm_count();
+  if (grid > max_units) grid = max_units;
+  if (grid < 1) grid = 1;
+  return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream), "stream GEMM launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_abi_version(void) { return 1; }
+
+const char* b200_last_error(void) { return g_last_error.c_str(); }
+
+int b200_num_sms(void) { return device_sm_count(); }
+
+int b200_workspace_status(void* workspace, int32_t* bits, int32_t reset, void* stream) {
+  if (workspace == nullptr || bits == nullptr) return fail(B200_ERR_INVALID, "null argument");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int host = 0;
+  int rc = check_cuda(cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, st),
+                      "status read");
+  if (rc) return rc;
+  rc = check_cuda(cudaStreamSynchronize(st), "status sync");
+  if (rc) return rc;
+  *bits = host;
+  if (reset && host != 0) {
+    rc = check_cuda(cudaMemsetAsync(workspace, 0, sizeof(int), st), "status reset");
+    if (rc) return rc;
+  }
+  return B200_OK;
+}
+
+int b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int32_t num_experts,
+                              int32_t block_size, int32_t* sorted_token_ids,
+                              int64_t sorted_capacity, int32_t* expert_ids,
+                              int64_t expert_capacity, int32_t* num_tokens_post_pad,
+                              void* stream) {
+  if (numel < 0 || numel >= (1ll << 31)) return fail(B200_ERR_INVALID, "bad numel %lld", (long long)numel);
+  if (num_experts <= 0 || num_experts > moe_align_max_experts())
+    return fail(B200_ERR_UNSUPPORTED, "num_experts must be in [1, %d], got %d",
+                moe_align_max_experts(), num_experts);
+  if (block_size <= 0 || block_size > 4096)
+    return fail(B200_ERR_INVALID, "bad block_size %d", block_size);
+  if ((numel > 0 && topk_ids == nullptr) || sorted_token_ids == nullptr || expert_ids == nullptr ||
+      num_tokens_post_pad == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  const int64_t busy = numel < num_experts ? numel : num_experts;
+  const int64_t need = numel + busy * (block_size - 1);
+  if (sorted_capacity < need)
+    return fail(B200_ERR_INVALID, "sorted_token_ids holds %lld slots, needs %lld",
+                (long long)sorted_capacity, (long long)need);
+  if (expert_capacity < (need + block_size - 1) / block_size)
+    return fail(B200_ERR_INVALID, "expert_ids holds %lld blocks, needs %lld",
+                (long long)expert_capacity, (long long)((need + block_size - 1) / block_size));
+  if (sorted_capacity >= (1ll << 31)) return fail(B200_ERR_INVALID, "sorted_capacity too large");
+  return check_cuda(launch_moe_align(topk_ids, numel, num_experts, block_size, sorted_token_ids,
+                                     sorted_capacity, expert_ids, expert_capacity,
+                                     num_tokens_post_pad,
+                                     reinterpret_cast<cudaStream_t>(stream)),
+                    "moe_align launch");
+}
+
+int b200_moe_sum_reduce(const void* input, void* output, int64_t tokens, int32_t top_k,
+                        int64_t hidden, int32_t dtype, float routed_scaling_factor, void* stream) {
+  if (!valid_dtype16(dtype)) return fail(B200_ERR_UNSUPPORTED, "dtype must be bf16 or f16");
+  if (tokens < 0 || top_k <= 0 || hidden <= 0 || hidden % 8)
+    return fail(B200_ERR_INVALID, "bad shape tokens=%lld top_k=%d hidden=%lld (hidden %% 8 == 0)",
+                (long long)tokens, top_k, (long long)hidden);
+  if (tokens == 0) return B200_OK;
+  if (!aligned16(input) || !aligned16(output))
+    return fail(B200_ERR_INVALID, "input and output must be 16-byte aligned");
+  return check_cuda(launch_moe_sum_reduce(input, output, tokens, top_k, hidden,
+                                          dtype == B200_DTYPE_F16, routed_scaling_factor,
+                                          reinterpret_cast<cudaStream_t>(stream)),
+                    "moe_sum_reduce launch");
+}
+
+int b200_moe_combine(const void* routed, int32_t routed_dtype, const int32_t* topk_ids,
+                     int32_t num_experts, int64_t tokens, int32_t top_k, int64_t hidden,
+                     float routed_scaling_factor, const void* shared_out, int32_t shared_dtype,
+                     void* out, int32_t out_dtype, void* stream) {
+  if (!valid_dtype16(routed_dtype) || !valid_dtype16(out_dtype) ||
+      (shared_out != nullptr && !valid_dtype16(shared_dtype)))
+    return fail(B200_ERR_UNSUPPORTED, "dtypes must be bf16 or f16");
+  if (tokens < 0 || top_k <= 0 || hidden <= 0 || hidden % 8)
+    return fail(B200_ERR_INVALID, "bad shape tokens=%lld top_k=%d hidden=%lld",
+                (long long)tokens, top_k, (long long)hidden);
+  if (tokens == 0) return B200_OK;
+  if (!aligned16(routed) || !aligned16(out) || (shared_out && !aligned16(shared_out)))
+    return fail(B200_ERR_INVALID, "buffers must be 16-byte aligned");
+  return check_cuda(launch_moe_combine(routed, routed_dtype == B200_DTYPE_F16, topk_ids,
+                                       num_experts, tokens, top_k, hidden, routed_scaling_factor,
+                                       shared_out, shared_dtype == B200_DTYPE_F16, out,
+                                       out_dtype == B200_DTYPE_F16,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                    "moe_combine launch");
+}
+
+int64_t b200_fp8_packed_bytes(int64_t experts, int64_t n, int64_t k) {
+  if (experts <= 0 || n <= 0 || k <= 0) return -1;
+  return experts * n * k;
+}
+
+int b200_fp8_prepack(const uint8_t* w_e4m3, int64_t experts, int64_t n, int64_t k, int32_t gated,
+                     uint8_t* out, void* stream) {
+  int rc = check_weight_shape(B200_QUANT_FP8_BLOCK, n, k, gated ? B200_GATED_FUSED : B200_GATED_NONE);
+  if (rc) return rc;
+  if (experts <= 0) return fail(B200_ERR_INVALID, "experts must be positive");
+  if (w_e4m3 == nullptr || out == nullptr) return fail(B200_ERR_INVALID, "null pointer argument");
+  if (!aligned16(w_e4m3) || !aligned16(out))
+    return fail(B200_ERR_INVALID, "weights must be 16-byte aligned");
+  return check_cuda(launch_prepack_fp8(w_e4m3, experts, (int)n, (int)k, gated != 0, out,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                    "fp8 prepack launch");
+}
+
+int64_t b200_nvfp4_packed_bytes(int64_t experts, int64_t n, int64_t k) {
+  if (experts <= 0 || n <= 0 || k <= 0 || n % 128 || k % 128) return -1;
+  return experts * (n / 128) * (k / 128) * (int64_t)kFp4UnitBytes;
+}
+
+int b200_nvfp4_prepack(const uint8_t* w_packed, const uint8_t* scales_e4m3, int64_t experts,
+                       int64_t n, int64_t k, int32_t gated, uint8_t* out, void* stream) {
+  int rc = check_weight_shape(B200_QUANT_NVFP4, n, k, gated ? B200_GATED_FUSED : B200_GATED_NONE);
+  if (rc) return rc;
+  if (experts <= 0) return fail(B200_ERR_INVALID, "experts must be positive");
+  if (w_packed == nullptr || scales_e4m3 == nullptr || out == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (!aligned16(w_packed) || !aligned16(out))
+    return fail(B200_ERR_INVALID, "weights must be 16-byte aligned");
+  return check_cuda(launch_prepack_nvfp4(w_packed, scales_e4m3, experts, (int)n, (int)k,
+                                         gated != 0, out, reinterpret_cast<cudaStream_t>(stream)),
+                    "nvfp4 prepack launch");
+}
+
+int64_t b200_gemm_workspace_bytes(int64_t convert_elems) {
+  if (convert_elems < 0) return -1;
+  return stream_ws_bytes() + align_up(convert_elems * 2);
+}
+
+int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* workspace,
+                int64_t workspace_bytes, void* stream) {
+  int rc = check_weight_shape(quant, n, k, gated_mode);
+  if (rc) return rc;
+  if (!valid_dtype16(x_dtype) || !valid_dtype16(y_dtype))
+    return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
+  if (m < 0 || m >= (1ll << 31)) return fail(B200_ERR_INVALID, "bad M %lld", (long long)m);
+  if (m == 0) return B200_OK;
+  if (x == nullptr || w_packed == nullptr || y == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (quant == B200_QUANT_FP8_BLOCK && w_scales == nullptr)
+    return fail(B200_ERR_INVALID, "FP8 weights need their block scales");
+  if (quant == B200_QUANT_NVFP4 && global_scale == nullptr)
+    return fail(B200_ERR_INVALID, "NVFP4 weights need their global scale");
+  if (!aligned16(x) || !aligned16(w_packed))
+    return fail(B200_ERR_INVALID, "x and weights must be 16-byte aligned");
+  WsView ws;
+  if (!carve(workspace, workspace_bytes, ws))
+    return fail(B200_ERR_INVALID, "workspace missing, misaligned or smaller than %lld bytes",
+                (long long)stream_ws_bytes());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int64_t used = 0;
+  const __half* x16 = nullptr;
+  rc = stage_activations(x, x_dtype, m * k, ws, used, &x16, st);
+  if (rc) return rc;
+
+  StreamParams p{};
+  p.wq = w_packed;
+  p.wscale = w_scales;
+  p.gscale = global_scale;
+  p.x = x16;
+  p.ldx = k;
+  p.x_rows = m;
+  p.sorted_ids = nullptr;
+  p.E = 1;
+  p.N = (int)n;
+  p.K = (int)k;
+  p.gated = gated_mode != B200_GATED_NONE;
+  p.fuse_act = gated_mode == B200_GATED_FUSED;
+  p.mul_w = 0;
+  p.out = y;
+  p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
+  p.out_f16 = y_dtype == B200_DTYPE_F16;
+  const int nt = nt_for_rows(m);
+  p.dense_m = (int)m;
+  const long long groups = (m + 8 * nt - 1) / (8 * nt);
+  const long long units = groups * (n / 128) * (k / 128);
+  return run_stream(quant, nt, p, units, ws, st);
+}
+
+int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+                  const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                  int32_t num_experts, int64_t n, int32_t gated_mode,
+                  const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                  int64_t expert_capacity, const int32_t* num_tokens_post_pad,
+                  int32_t block_size, int32_t top_k, int64_t num_routes,
+                  const float* topk_weights, int32_t mul_topk_weights, void* c, int32_t c_dtype,
+                  int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_weight_shape(quant, n, k, gated_mode);
+  if (rc) return rc;
+  if (!valid_dtype16(a_dtype) || !valid_dtype16(c_dtype))
+    return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
+  if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32 or 64, got %d", block_size);
+  if (num_experts <= 0) return fail(B200_ERR_INVALID, "num_experts must be positive");
+  if (top_k <= 0) return fail(B200_ERR_INVALID, "top_k must be positive");
+  if (a_rows < 0 || num_routes < 0 || num_routes >= (1ll << 31) || expert_capacity < 0)
+    return fail(B200_ERR_INVALID, "bad row counts");
+  const int64_t out_cols = gated_mode == B200_GATED_FUSED ? n / 2 : n;
+  if (ldc < out_cols) return fail(B200_ERR_INVALID, "ldc %lld < output width %lld",
+                                  (long long)ldc, (long long)out_cols);
+  if (expert_capacity == 0 || num_routes == 0 || a_rows == 0) return B200_OK;
+  if (a == nullptr || w_packed == nullptr || c == nullptr || sorted_token_ids == nullptr ||
+      expert_ids == nullptr || num_tokens_post_pad == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (mul_topk_weights && topk_weights == nullptr)
+    return fail(B200_ERR_INVALID, "mul_topk_weights needs topk_weights");
+  if (quant == B200_QUANT_FP8_BLOCK && w_scales == nullptr)
+    return fail(B200_ERR_INVALID, "FP8 weights need their block scales");
+  if (quant == B200_QUANT_NVFP4 && global_scale == nullptr)
+    return fail(B200_ERR_INVALID, "NVFP4 weights need their global scale");
+  if (!aligned16(a) || !aligned16(w_packed))
+    return fail(B200_ERR_INVALID, "activations and weights must be 16-byte aligned");
+  WsView ws;
+  if (!carve(workspace, workspace_bytes, ws))
+    return fail(B200_ERR_INVALID, "workspace missing, misaligned or smaller than %lld bytes",
+                (long long)stream_ws_bytes());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int64_t used = 0;
+  const __half* a16 = nullptr;
+  rc = stage_activations(a, a_dtype, a_rows * k, ws, used, &a16, st);
+  if (rc) return rc;
+
+  StreamParams p{};
+  p.wq = w_packed;
+  p.wscale = w_scales;
+  p.gscale = global_scale;
+  p.x = a16;
+  p.ldx = k;
+  p.x_rows = a_rows;
+  p.sorted_ids = sorted_token_ids;
+  p.expert_ids = expert_ids;
+  p.ntpp = num_tokens_post_pad;
+  p.block_m = block_size;
+  p.max_groups = expert_capacity;
+  p.top_k = top_k;
+  p.num_routes = (int)num_routes;
+  p.topk_w = topk_weights;
+  p.E = num_experts;
+  p.N = (int)n;
+  p.K = (int)k;
+  p.gated = gated_mode != B200_GATED_NONE;
+  p.fuse_act = gated_mode == B200_GATED_FUSED;
+  p.mul_w = mul_topk_weights != 0;
+  p.out = c;
+  p.ldo = ldc;
+  p.out_f16 = c_dtype == B200_DTYPE_F16;
+  const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
+  return run_stream(quant, block_size / 8, p, units, ws, st);
+}
+
+int64_t b200_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
+                                       int32_t num_experts, int32_t top_k, int32_t block_size) {
+  if (tokens < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0 || top_k <= 0 || block_size <= 0)
+    return -1;
+  const int64_t numel = tokens * top_k;
+  const int64_t busy = numel < num_experts ? numel : num_experts;
+  const int64_t cap = numel + busy * (block_size - 1);
+  const int64_t blocks = (cap + block_size - 1) / block_size;
+  return stream_ws_bytes() + align_up(tokens * hidden * 2)  // f16 activations
+         + align_up(cap * 4) + align_up(blocks * 4) + align_up(4)  // routing
+         + align_up(numel * inter * 2)                              // gate_up output
+         + align_up(numel * hidden * 2);                            // per-route down output
+}
+
+int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
+                           int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                           const float* topk_weights, int32_t top_k, int32_t num_experts,
+                           const uint8_t* w13_packed, const float* w13_scales,
+                           const float* w13_global, const uint8_t* w2_packed,
+                           const float* w2_scales, const float* w2_global, int32_t block_size,
+                           float routed_scaling_factor, const void* shared_out,
+                           int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  int rc = check_weight_shape(quant, 2 * inter, hidden, B200_GATED_FUSED);
+  if (rc) return rc;
+  rc = check_weight_shape(quant, hidden, inter, B200_GATED_NONE);
+  if (rc) return rc;
+  if (!valid_dtype16(x_dtype) || !valid_dtype16(out_dtype))
+    return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
+  if (tokens < 0 || top_k <= 0 || num_experts <= 0)
+    return fail(B200_ERR_INVALID, "bad tokens/top_k/num_experts");
+  if (tokens == 0) return B200_OK;
+  if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32 or 64, got %d", block_size);
+  if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
+      w2_packed == nullptr || out == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  const int64_t need = b200_moe_layer_workspace_bytes(tokens, hidden, inter, num_experts, top_k,
+                                                      block_size);
+  if (workspace_bytes < need)
+    return fail(B200_ERR_INVALID, "workspace holds %lld bytes, needs %lld",
+                (long long)workspace_bytes, (long long)need);
+  WsView ws;
+  if (!carve(workspace, workspace_bytes, ws))
+    return fail(B200_ERR_INVALID, "workspace missing or misaligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  const int64_t numel = tokens * top_k;
+  const int64_t busy = numel < num_experts ? numel : num_experts;
+  const int64_t cap = numel + busy * (block_size - 1);
+  const int64_t blocks = (cap + block_size - 1) / block_size;
+  int64_t used = 0;
+  const __half* x16 = nullptr;
+  rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
+  if (rc) return rc;
+  if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(cap * 4);
+  int32_t* eids = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(blocks * 4);
+  int32_t* ntpp = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(4);
+  __half* inter_out = reinterpret_cast<__half*>(ws.scratch + used);
+  used += align_up(numel * inter * 2);
+  __half* routed = reinterpret_cast<__half*>(ws.scratch + used);
+  used += align_up(numel * hidden * 2);
+
+  rc = b200_moe_align_block_size(topk_ids, numel, num_experts, block_size, sorted, cap, eids,
+                                 blocks, ntpp, stream);
+  if (rc) return rc;
+
+  StreamParams p{};
+  p.wq = w13_packed;
+  p.wscale = w13_scales;
+  p.gscale = w13_global;
+  p.x = x16;
+  p.ldx = hidden;
+  p.x_rows = tokens;
+  p.sorted_ids = sorted;
+  p.expert_ids = eids;
+  p.ntpp = ntpp;
+  p.block_m = block_size;
+  p.max_groups = cap / block_size;
+  p.top_k = top_k;
+  p.num_routes = (int)numel;
+  p.topk_w = topk_weights;
+  p.E = num_experts;
+  p.N = (int)(2 * inter);
+  p.K = (int)hidden;
+  p.gated = 1;
+  p.fuse_act = 1;
+  p.mul_w = 0;
+  p.out = inter_out;
+  p.ldo = inter;
+  p.out_f16 = 1;
+  const int nt = block_size / 8;
+  rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
+  if (rc) return rc;
+
+  StreamParams q = p;
+  q.wq = w2_packed;
+  q.wscale = w2_scales;
+  q.gscale = w2_global;
+  q.x = inter_out;
+  q.ldx = inter;
+  q.x_rows = numel;
+  q.top_k = 1;
+  q.N = (int)hidden;
+  q.K = (int)inter;
+  q.gated = 0;
+  q.fuse_act = 0;
+  q.mul_w = 1;
+  q.out = routed;
+  q.ldo = hidden;
+  q.out_f16 = 1;
+  rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
+  if (rc) return rc;
+
+  return b200_moe_combine(routed, B200_DTYPE_F16, topk_ids, num_experts, tokens, top_k, hidden,
+                          routed_scaling_factor, shared_out, shared_dtype, out, out_dtype, stream);
+}
+
+}  // extern "C"

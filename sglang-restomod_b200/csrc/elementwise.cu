@@ -1,0 +1,146 @@
+// Bandwidth-bound helpers around the expert GEMMs.
+//
+//   * bf16 -> f16 activation conversion (the stream GEMM's tensor-core
+//     operand is f16, as the reference's activations are; sm70 has no bf16).
+//   * moe_sum_reduce: out[t, :] = scale * sum_k in[t, k, :] in fp32, stored in
+//     the input dtype. Same contract as the reference's Triton replacement
+//     (sglang_restomod/quant/sm70_fp4_moe/sum_reduce.py:84-123).
+//   * moe_combine: the top-k combine of SM70Fp8MoEMethod.apply
+//     (sglang_restomod/quant/sm70_fp8_moe/method.py:305-309) for rows that the
+//     down GEMM already multiplied by their router weight: routes whose
+//     expert id is outside [0, E) (expert-parallel drops, id -1) contribute
+//     nothing, the sum is fp32, then routed_scaling_factor, plus an optional
+//     shared-expert row.
+// All three move 16 bytes per thread per access.
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200 {
+namespace {
+
+__device__ __forceinline__ void load8(const void* base, long long idx, int f16, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(
+      reinterpret_cast<const uint8_t*>(base) + idx * 2);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (f16) {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      v[2 * i] = __low2float(h);
+      v[2 * i + 1] = __high2float(h);
+    } else {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      v[2 * i] = __low2float(h);
+      v[2 * i + 1] = __high2float(h);
+    }
+  }
+}
+
+__device__ __forceinline__ void store8(void* base, long long idx, int f16, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (f16) {
+      __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(base) + idx * 2) =
+      make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+                                   long long n8) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint4 raw = in[i];
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+      __half2 h = __floats2half2_rn(__low2float(b), __high2float(b));
+      o[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// One thread per 8 hidden elements of one token.
+__global__ void sum_reduce_kernel(const void* __restrict__ in, void* __restrict__ out,
+                                  long long tokens, int top_k, long long hidden, int f16,
+                                  float scale, const int* __restrict__ topk_ids, int num_experts,
+                                  const void* __restrict__ shared_out, int shared_f16,
+                                  int out_f16) {
+  const long long h8 = hidden / 8;
+  const long long total = tokens * h8;
+  for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
+       id += (long long)gridDim.x * blockDim.x) {
+    const long long t = id / h8;
+    const long long c = (id - t * h8) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < top_k; ++k) {
+      if (topk_ids != nullptr) {
+        const int e = topk_ids[t * top_k + k];
+        if (e < 0 || e >= num_experts) continue;
+      }
+      float v[8];
+      load8(in, (t * top_k + k) * hidden + c, f16, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= scale;
+    if (shared_out != nullptr) {
+      float v[8];
+      load8(shared_out, t * hidden + c, shared_f16, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+    }
+    store8(out, t * hidden + c, out_f16, acc);
+  }
+}
+
+int grid_for(long long work, int threads) {
+  long long blocks = (work + threads - 1) / threads;
+  const long long cap = (long long)device_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+}  // namespace
+
+cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream) {
+  const long long n8 = n / 8;
+  if (n8 == 0) return cudaSuccess;
+  bf16_to_f16_kernel<<<grid_for(n8, 256), 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,
+                                  long long hidden, int f16, float scale, cudaStream_t stream) {
+  const long long work = tokens * (hidden / 8);
+  if (work == 0) return cudaSuccess;
+  sum_reduce_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
+      in, out, tokens, top_k, hidden, f16, scale, nullptr, 0, nullptr, 0, f16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const void* routed, int routed_f16, const int* topk_ids,
+                               int num_experts, long long tokens, int top_k, long long hidden,
+                               float scale, const void* shared_out, int shared_f16, void* out,
+                               int out_f16, cudaStream_t stream) {
+  const long long work = tokens * (hidden / 8);
+  if (work == 0) return cudaSuccess;
+  sum_reduce_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
+      routed, out, tokens, top_k, hidden, routed_f16, scale, topk_ids, num_experts, shared_out,
+      shared_f16, out_f16);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -1,0 +1,81 @@
+// Internal launch interface shared by the .cu files of libb200moe. Nothing in
+// here crosses the C ABI; include/b200moe.h is the public surface.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200 {
+
+// Weight-streaming GEMM: Y[rows, N] = X[rows, K] * dequant(W[N, K])^T, with
+// rows either a dense batch or route slots grouped by expert (the
+// moe_align_block_size output).
+enum StreamQuant : int { kQuantFp8Block = 0, kQuantNvfp4 = 1 };
+
+struct StreamParams {
+  const uint8_t* wq;     // prepacked weight units (see prepack.cu)
+  const float* wscale;   // FP8: [E][N/128][K/128] fp32 block scales (logical rows)
+  const float* gscale;   // NVFP4: [E] fp32 global scale
+  const __half* x;       // activations, f16, rows of ldx elements
+  long long ldx;
+  long long x_rows;      // number of activation rows (route rows are checked against it)
+  const int* sorted_ids; // nullptr: dense mode
+  const int* expert_ids;
+  const int* ntpp;       // num_tokens_post_padded (device)
+  int block_m;           // route slots per group (moe mode); == 8 * NT
+  long long max_groups;  // moe mode: groups readable from sorted_ids / expert_ids
+  int top_k;             // activation row = route / top_k
+  int num_routes;        // route ids >= num_routes are padding
+  const float* topk_w;   // one weight per route (mul_w)
+  int dense_m;           // dense mode: number of rows
+  int E, N, K;           // N = weight rows (2I for a gated gate/up bank)
+  int gated;             // bank rows interleaved gate/up
+  int fuse_act;          // gated: write silu(gate)*up [.., N/2]; else gate | up halves
+  int mul_w;             // multiply each route's row by topk_w[route]
+  void* out;
+  long long ldo;
+  int out_f16;           // 1: f16 output, 0: bf16
+  float* ws;             // split-pair partial sums, kWsSlotFloats per grid slot, zeroed
+  int* ws_cnt;           // one arrival counter per grid slot, zeroed
+  int* status;           // device error bits
+};
+
+constexpr int kWsSlotFloats = 128 * 64;
+
+// Stream GEMM tiling constants (also used by the host for sizing).
+constexpr int kUnitRows = 128;
+constexpr int kUnitK = 128;
+constexpr uint32_t kFp8UnitBytes = kUnitRows * kUnitK;                       // 16 KiB
+constexpr uint32_t kFp4UnitBytes = kUnitRows * kUnitK / 2 + kUnitRows * 8;   // 9 KiB
+
+cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int grid,
+                               cudaStream_t stream);
+int stream_gemm_ctas_per_sm(int nt);
+
+// moe_align_block_size: stable expert-major counting sort with per-expert
+// padding to block_size.
+cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_experts, int block_size,
+                             int* sorted_ids, long long sorted_cap, int* expert_ids,
+                             long long expert_cap, int* ntpp, cudaStream_t stream);
+int moe_align_max_experts();
+
+// Elementwise / reduction kernels.
+cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);
+cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,
+                                  long long hidden, int f16, float scale, cudaStream_t stream);
+cudaError_t launch_moe_combine(const void* routed, int routed_f16, const int* topk_ids,
+                               int num_experts, long long tokens, int top_k, long long hidden,
+                               float scale, const void* shared_out, int shared_f16, void* out,
+                               int out_f16, cudaStream_t stream);
+
+// Load-time re-layouts.
+cudaError_t launch_prepack_fp8(const uint8_t* w, long long E, int N, int K, int gated,
+                               uint8_t* out, cudaStream_t stream);
+cudaError_t launch_prepack_nvfp4(const uint8_t* w, const uint8_t* scales, long long E, int N,
+                                 int K, int gated, uint8_t* out, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace b200

@@ -1,0 +1,187 @@
+// moe_align_block_size for B200: bucket routes by expert, pad each bucket to
+// block_size, emit the expert of every block.
+//
+// Contract (the one the reference's kernels consume; the align op itself is
+// upstream sgl_kernel, forced onto its CUDA pair by
+// sglang_restomod/moe/align_sm70.py:35-55, and read by
+// quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:73-110 and
+// quant/sm70_fp4_moe/decode_gemv.py:226-260):
+//   * sorted_ids[p] holds a route index (token * top_k + slot) or the
+//     sentinel numel for a padding slot;
+//   * expert_ids[b] is the expert of block b (block b = slots [b*bs, b*bs+bs));
+//   * num_tokens_post_pad[0] = sum over experts of ceil(count / bs) * bs.
+// Order inside an expert is the route index order: the stable expert-major
+// order of SM70Fp8MoEMethod.apply's torch.argsort(flat_ids, stable=True)
+// (quant/sm70_fp8_moe/method.py:285). Route ids outside [0, E) (the -1 that
+// expert parallelism writes for routes owned elsewhere) are dropped. The
+// whole output is written: slots past the padded total hold the sentinel and
+// blocks past it hold expert -1, so the result is bit-reproducible.
+//
+// One CTA of 32 warps; each warp owns a contiguous segment of routes:
+//   1. per-warp per-expert counts (warp match_any aggregates equal ids);
+//   2. per-expert exclusive scan over warps, then a block scan of the padded
+//      counts gives every expert's first slot;
+//   3. each warp re-reads its segment in order and scatters route indices at
+//      offset + (earlier warps' count) + (rank among equal ids so far).
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200 {
+namespace {
+
+constexpr int kWarps = 32;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxExperts = 1024;
+constexpr int kBatch = 8;  // loads in flight per lane
+
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_align_kernel(const int* __restrict__ topk_ids, long long numel, int E, int bs,
+                     int* __restrict__ sorted_ids, long long sorted_cap,
+                     int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                  // [kWarps][E] per-warp counts, then running bases
+  int* off = cnt + kWarps * E;    // [E + 1] first padded slot of each expert
+  int* tot = off + E + 1;         // [E] routes per expert
+  int* wsum = tot + E;            // [kWarps] scan scratch
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  for (int i = tid; i < kWarps * E; i += kThreads) cnt[i] = 0;
+  __syncthreads();
+
+  const long long seg = (numel + kWarps - 1) / kWarps;
+  const long long s0 = (long long)warp * seg;
+  const long long s1 = (s0 + seg < numel) ? s0 + seg : numel;
+
+  // 1. histogram
+  for (long long base = s0; base < s1; base += 32 * kBatch) {
+    int ids[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const long long idx = base + b * 32 + lane;
+      ids[b] = (idx < s1) ? __ldg(topk_ids + idx) : -1;
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int e = ids[b];
+      const bool valid = e >= 0 && e < E;
+      const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+      if (valid && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+    }
+  }
+  __syncthreads();
+
+  // 2a. per-expert exclusive scan over warps
+  for (int e = tid; e < E; e += kThreads) {
+    int run = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+
+  // 2b. exclusive block scan of the padded counts (E <= kThreads)
+  const int pad = (tid < E) ? (tot[tid] + bs - 1) / bs * bs : 0;
+  int x = pad;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int v = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    wsum[lane] = v;
+  }
+  __syncthreads();
+  const int excl = x - pad + (warp > 0 ? wsum[warp - 1] : 0);
+  if (tid < E) off[tid] = excl;
+  if (tid == E - 1) off[E] = excl + pad;
+  __syncthreads();
+
+  const int total = off[E];
+  if (tid == 0) ntpp[0] = total;
+
+  // Block -> expert map; blocks past the total get -1.
+  for (long long b = tid; b < expert_cap; b += kThreads) {
+    const long long slot = b * bs;
+    int v = -1;
+    if (slot < total) {
+      int lo = 0, hi = E - 1;  // last e with off[e] <= slot
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (off[mid] <= slot) lo = mid; else hi = mid - 1;
+      }
+      v = lo;
+    }
+    expert_ids[b] = v;
+  }
+  // Padding slots inside each expert's range, and the tail.
+  for (int e = tid; e < E; e += kThreads) {
+    for (int p = off[e] + tot[e]; p < off[e + 1]; ++p)
+      if (p < sorted_cap) sorted_ids[p] = (int)numel;
+  }
+  for (long long p = total + tid; p < sorted_cap; p += kThreads) sorted_ids[p] = (int)numel;
+
+  // 3. stable scatter
+  for (long long base = s0; base < s1; base += 32 * kBatch) {
+    int ids[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const long long idx = base + b * 32 + lane;
+      ids[b] = (idx < s1) ? __ldg(topk_ids + idx) : -1;
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const long long idx = base + b * 32 + lane;
+      const int e = ids[b];
+      const bool valid = idx < s1 && e >= 0 && e < E;
+      const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+      if (valid) {
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const long long pos = (long long)off[e] + cnt[warp * E + e] + rank;
+        if (pos < sorted_cap) sorted_ids[pos] = (int)idx;
+      }
+      __syncwarp();
+      if (valid && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+}
+
+}  // namespace
+
+int moe_align_max_experts() { return kMaxExperts; }
+
+cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_experts, int block_size,
+                             int* sorted_ids, long long sorted_cap, int* expert_ids,
+                             long long expert_cap, int* ntpp, cudaStream_t stream) {
+  const size_t smem = sizeof(int) * ((size_t)kWarps * num_experts + 2 * num_experts + 1 + kWarps);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const int max_smem = (int)(sizeof(int) * ((size_t)kWarps * kMaxExperts + 2 * kMaxExperts + 1 + kWarps));
+    cudaError_t err = cudaFuncSetAttribute(moe_align_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
+  moe_align_kernel<<<1, kThreads, smem, stream>>>(topk_ids, numel, num_experts, block_size,
+                                                  sorted_ids, sorted_cap, expert_ids, expert_cap,
+                                                  ntpp);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

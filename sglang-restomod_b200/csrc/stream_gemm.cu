@@ -1,0 +1,472 @@
+// Weight-streaming GEMM for the decode regime (few rows per weight tile).
+//
+// Replaces, for B200, the reference's decode kernels:
+//   * FP8 block-scaled dense decode (sglang_restomod/quant/sm70_fp8_dense/csrc/
+//     sm70_fp8_qpn8_decode.cu:60-149, gated variant :156-246);
+//   * the TurboMind block-FP8 expert GEMM used by SM70Fp8MoEMethod.apply
+//     (sglang_restomod/quant/sm70_fp8_moe/method.py:303-304, contract in
+//     quant/sm70_fp8_moe/README.md:23-58);
+//   * the NVFP4 MoE decode GEMVs routed by moe_align_block_size
+//     (sglang_restomod/quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:63-200).
+//
+// Design (B200-first, not a port of any of the above):
+//   * Weights are prepacked at load time into 128-row x 128-K "units" whose
+//     bytes are ordered exactly as the consumer warps read them (prepack.cu).
+//     A unit is one FP8 scale block: 16 KiB of E4M3, or 8 KiB of E2M1 codes
+//     plus 1 KiB of E4M3 group scales.
+//   * A persistent grid splits the flattened (row-group, row-block, K-unit)
+//     space evenly across CTAs (stream-K). Each CTA runs one producer warp
+//     that streams its units with cp.async.bulk (TMA, L2 evict-first) into a
+//     4-stage shared-memory ring tracked by mbarriers, and 8 consumer warps.
+//   * A consumer warp owns 16 weight rows of the unit. It converts its bytes
+//     with the hardware cvt.rn.f16x2.{e4m3x2,e2m1x2} instructions straight
+//     into m16n8k16 A fragments and multiplies them against f16 activation
+//     fragments on the tensor cores (fp32 accumulate). FP8 block scales are
+//     applied once per unit to the accumulators; NVFP4 group scales
+//     (fp16_rne(e4m3 * global), as the reference rounds them) multiply the
+//     fragments.
+//   * The K index inside a unit is permuted consistently on both operands so
+//     that every lane reads 32 contiguous K of its rows and of its activation
+//     row (two 16-byte loads each) - the sum over K is order-free.
+//   * A (row-group, row-block) pair that straddles CTAs is reduced through a
+//     zeroed fp32 workspace slot with an arrival counter; the last arriving
+//     CTA applies the epilogue and leaves slot and counter zeroed again.
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200 {
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 4;
+
+// Two CTAs per SM keep 8 stages (128 KiB) of weights in flight per SM; the
+// 32- and 64-row variants need the registers of a whole SM for themselves.
+template <int NT>
+struct CtasPerSm {
+  static constexpr int value = NT >= 4 ? 1 : 2;
+};
+
+template <int Q>
+struct UnitBytes;
+template <>
+struct UnitBytes<kQuantFp8Block> {
+  static constexpr uint32_t value = kFp8UnitBytes;
+};
+template <>
+struct UnitBytes<kQuantNvfp4> {
+  static constexpr uint32_t value = kFp4UnitBytes;
+};
+
+__device__ __forceinline__ long long cta_containing(long long u, long long U, long long G) {
+  // Largest c with floor(c*U/G) <= u.
+  long long c = ((u + 1) * G + U - 1) / U - 1;
+  return c < G ? c : G - 1;
+}
+
+__device__ __forceinline__ uint32_t f16x2_splat(float v) {
+  __half h = __float2half_rn(v);
+  __half2 h2 = __halves2half2(h, h);
+  return *reinterpret_cast<uint32_t*>(&h2);
+}
+
+template <int NT>
+__device__ __forceinline__ void store_pair(const StreamParams& p, long long gi, int rb, int warp,
+                                           int lane, const float (&acc)[NT][4]) {
+  const int g8 = lane >> 2, cq = lane & 3;
+  const int row_top = warp * 16 + g8;  // local row inside the 128-row block
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {
+      const int tok = nt * 8 + 2 * cq + e2;
+      long long orow;
+      float w = 1.0f;
+      if (p.sorted_ids == nullptr) {
+        orow = gi * (8 * NT) + tok;
+        if (orow >= p.dense_m) continue;
+      } else {
+        const int r = p.sorted_ids[gi * p.block_m + tok];
+        if (r < 0 || r >= p.num_routes) continue;
+        orow = r;
+        if (p.mul_w) w = p.topk_w[r];
+      }
+      const float vt = acc[nt][e2];
+      const float vb = acc[nt][2 + e2];
+      if (p.gated) {
+        const long long col = (long long)rb * 64 + warp * 8 + g8;
+        if (p.fuse_act) {
+          const float v = silu_f32(vt) * vb * w;
+          if (p.out_f16)
+            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col] = __float2half_rn(v);
+          else
+            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col] = __float2bfloat16_rn(v);
+        } else {
+          const long long col_u = col + p.N / 2;
+          if (p.out_f16) {
+            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col] = __float2half_rn(vt * w);
+            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_u] = __float2half_rn(vb * w);
+          } else {
+            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col] =
+                __float2bfloat16_rn(vt * w);
+            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_u] =
+                __float2bfloat16_rn(vb * w);
+          }
+        }
+      } else {
+        const long long col_t = (long long)rb * 128 + row_top;
+        const long long col_b = col_t + 8;
+        if (p.out_f16) {
+          reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_t] = __float2half_rn(vt * w);
+          reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_b] = __float2half_rn(vb * w);
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_t] =
+              __float2bfloat16_rn(vt * w);
+          reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_b] =
+              __float2bfloat16_rn(vb * w);
+        }
+      }
+    }
+  }
+}
+
+template <int Q, int NT>
+__global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_kernel(const StreamParams p) {
+  constexpr uint32_t UB = UnitBytes<Q>::value;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * UB);
+  uint64_t* empty = full + kStages;
+  volatile int* flag = reinterpret_cast<volatile int*>(empty + kStages);
+  volatile int* abort_flag = flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nrb = p.N / kUnitRows;
+  const int kch = p.K / kUnitK;
+  const bool dense = p.sorted_ids == nullptr;
+
+  long long groups;
+  if (dense) {
+    groups = (long long)(p.dense_m + 8 * NT - 1) / (8 * NT);
+  } else {
+    groups = (long long)(p.ntpp[0] / p.block_m);
+    if (groups < 0) groups = 0;
+    if (groups > p.max_groups) groups = p.max_groups;
+  }
+  const long long U = groups * nrb * (long long)kch;
+  const long long G = gridDim.x;
+  const long long u0 = (long long)blockIdx.x * U / G;
+  const long long u1 = ((long long)blockIdx.x + 1) * U / G;
+  if (u0 >= u1) return;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int i = 0;
+      for (long long u = u0; u < u1; ++u) {
+        const long long pair = u / kch;
+        const int kc = (int)(u - pair * kch);
+        const long long gi = pair / nrb;
+        const int rb = (int)(pair - gi * nrb);
+        const int e = dense ? 0 : p.expert_ids[gi];
+        if (e < 0 || e >= p.E) continue;
+        const int s = i % kStages;
+        if (i >= kStages) {
+          if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.status)) break;
+        }
+        mbar_arrive_expect_tx(&full[s], UB);
+        const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + kc) * (long long)UB;
+        bulk_g2s(smem + (size_t)s * UB, src, UB, &full[s], pol);
+        ++i;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  // Every consumer warp walks the same unit sequence and takes the same
+  // branches at pair ends, so the named barriers below always line up. A
+  // timed-out wait raises the CTA abort flag instead of returning.
+  const int g8 = lane >> 2;
+  const int cq = lane & 3;
+  float acc[NT][4];
+  const __half* xrow[NT];
+  long long cur_pair = -1;
+  int i = 0;
+
+  for (long long u = u0; u < u1; ++u) {
+    const long long pair = u / kch;
+    const int kc = (int)(u - pair * kch);
+    const long long gi = pair / nrb;
+    const int rb = (int)(pair - gi * nrb);
+    const int e = dense ? 0 : p.expert_ids[gi];
+    if (e < 0 || e >= p.E) {
+      if (e >= p.E && kc == 0 && rb == 0 && warp == 0 && lane == 0) atomicOr(p.status, kDevBadExpert);
+      continue;
+    }
+
+    if (pair != cur_pair) {
+      cur_pair = pair;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
+        const int n = nt * 8 + g8;
+        const __half* ptr = nullptr;
+        if (dense) {
+          const long long t = gi * (8 * NT) + n;
+          if (t < p.dense_m) ptr = p.x + t * p.ldx;
+        } else {
+          const int r = p.sorted_ids[gi * p.block_m + n];
+          if (r >= 0 && r < p.num_routes) {
+            const long long row = r / p.top_k;
+            if (row < p.x_rows)
+              ptr = p.x + row * p.ldx;
+            else
+              atomicOr(p.status, kDevBadRoute);
+          }
+        }
+        xrow[nt] = ptr;
+      }
+    }
+
+    // Activation fragments: lane (g8, cq) holds K [32cq, 32cq+32) of row
+    // nt*8+g8 of this unit. Small NT preloads all of them before the wait.
+    constexpr bool kPreload = NT <= 1;
+    uint4 bx[kPreload ? NT : 1][4];
+    if constexpr (kPreload) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (xrow[nt] != nullptr) {
+          const __half* src = xrow[nt] + (long long)kc * kUnitK + 32 * cq;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) bx[nt][q] = ldg_u128(src + 8 * q);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) bx[nt][q] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
+    auto load_b = [&](int nt, int q) -> uint4 {
+      if constexpr (kPreload) {
+        return bx[nt][q];
+      } else {
+        if (xrow[nt] == nullptr) return make_uint4(0u, 0u, 0u, 0u);
+        return ldg_u128(xrow[nt] + (long long)kc * kUnitK + 32 * cq + 8 * q);
+      }
+    };
+
+    float s_top = 1.f, s_bot = 1.f;
+    float gs = 1.f;
+    if constexpr (Q == kQuantFp8Block) {
+      const int nsr = p.N / kUnitRows;  // scale rows per expert
+      if (p.gated) {
+        const int half_rows = p.N / 2 / kUnitRows;
+        s_top = __ldg(p.wscale + ((long long)e * nsr + rb / 2) * kch + kc);
+        s_bot = __ldg(p.wscale + ((long long)e * nsr + half_rows + rb / 2) * kch + kc);
+      } else {
+        s_top = __ldg(p.wscale + ((long long)e * nsr + rb) * kch + kc);
+        s_bot = s_top;
+      }
+    } else {
+      gs = __ldg(p.gscale + e);
+    }
+
+    const int s = i % kStages;
+    const uint32_t parity = (uint32_t)((i / kStages) & 1);
+    ++i;
+    bool ok = (*abort_flag == 0);
+    if (ok && !mbar_wait(&full[s], parity, p.status)) {
+      *abort_flag = 1;
+      ok = false;
+    }
+    if (ok) {
+      const uint8_t* stage = smem + (size_t)s * UB;
+      float t[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) t[nt][r] = 0.f;
+
+      if constexpr (Q == kQuantFp8Block) {
+        uint4 wa[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          wa[q] = ld_shared_u128(stage + warp * 2048 + q * 512 + lane * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t top = h ? wa[q].y : wa[q].x;
+            const uint32_t bot = h ? wa[q].w : wa[q].z;
+            uint32_t a[4];
+            a[0] = e4m3x2_to_f16x2((uint16_t)(top & 0xffffu));
+            a[1] = e4m3x2_to_f16x2((uint16_t)(bot & 0xffffu));
+            a[2] = e4m3x2_to_f16x2((uint16_t)(top >> 16));
+            a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4 b = load_b(nt, q);
+              mma_16816(t[nt], a, h ? b.z : b.x, h ? b.w : b.y);
+            }
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[nt][0] = fmaf(s_top, t[nt][0], acc[nt][0]);
+          acc[nt][1] = fmaf(s_top, t[nt][1], acc[nt][1]);
+          acc[nt][2] = fmaf(s_bot, t[nt][2], acc[nt][2]);
+          acc[nt][3] = fmaf(s_bot, t[nt][3], acc[nt][3]);
+        }
+      } else {
+        const uint4 ct = ld_shared_u128(stage + warp * 1024 + lane * 32);
+        const uint4 cb = ld_shared_u128(stage + warp * 1024 + lane * 32 + 16);
+        const uint32_t sc = ld_shared_u32(stage + 8192 + warp * 128 + lane * 4);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // Group scales: fp16_rne(float(e4m3) * global), the single rounding
+        // the reference applies (quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:40-45).
+        const uint32_t st2 = e4m3x2_to_f16x2((uint16_t)(sc & 0xffffu));
+        const uint32_t sb2 = e4m3x2_to_f16x2((uint16_t)(sc >> 16));
+        const __half2 st_h = *reinterpret_cast<const __half2*>(&st2);
+        const __half2 sb_h = *reinterpret_cast<const __half2*>(&sb2);
+        const uint32_t st[2] = {f16x2_splat(__low2float(st_h) * gs),
+                                f16x2_splat(__high2float(st_h) * gs)};
+        const uint32_t sb[2] = {f16x2_splat(__low2float(sb_h) * gs),
+                                f16x2_splat(__high2float(sb_h) * gs)};
+        const uint32_t ctw[4] = {ct.x, ct.y, ct.z, ct.w};
+        const uint32_t cbw[4] = {cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          uint32_t wt[4], wb[4];
+          e2m1x8_to_f16x2x4(ctw[m], wt);
+          e2m1x8_to_f16x2x4(cbw[m], wb);
+          const uint32_t sct = st[m >> 1];
+          const uint32_t scb = sb[m >> 1];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t a[4];
+            a[0] = hmul2_u32(wt[2 * h], sct);
+            a[1] = hmul2_u32(wb[2 * h], scb);
+            a[2] = hmul2_u32(wt[2 * h + 1], sct);
+            a[3] = hmul2_u32(wb[2 * h + 1], scb);
+            // k-step j = 2m + h uses activation words 2j, 2j+1 = uint4 m, half h
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4 b = load_b(nt, m);
+              mma_16816(t[nt], a, h ? b.z : b.x, h ? b.w : b.y);
+            }
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[nt][r] += t[nt][r];
+      }
+    }
+
+    const bool pair_end = (kc == kch - 1) || (u == u1 - 1);
+    if (!pair_end) continue;
+
+    const long long pu0 = pair * kch;
+    const long long pu1 = pu0 + kch;
+    if (pu0 >= u0 && pu1 <= u1) {
+      if (*abort_flag == 0) store_pair<NT>(p, gi, rb, warp, lane, acc);
+      continue;
+    }
+    // Split pair: reduce through the workspace slot of the CTA where it starts.
+    const long long slot = cta_containing(pu0, U, G);
+    float* wsl = p.ws + slot * kWsSlotFloats;
+    const int my_units = (int)((pu1 < u1 ? pu1 : u1) - (pu0 > u0 ? pu0 : u0));
+    const int row_top = warp * 16 + g8;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const int tok = nt * 8 + 2 * cq + e2;
+        atomicAdd(wsl + row_top * 64 + tok, acc[nt][e2]);
+        atomicAdd(wsl + (row_top + 8) * 64 + tok, acc[nt][2 + e2]);
+      }
+    }
+    __threadfence();
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (warp == 0 && lane == 0) {
+      const int old = atomicAdd(p.ws_cnt + slot, my_units);
+      *flag = (old + my_units == kch) ? 1 : 0;
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (*flag != 0) {
+      __threadfence();
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int tok = nt * 8 + 2 * cq + e2;
+          acc[nt][e2] = atomicExch(wsl + row_top * 64 + tok, 0.f);
+          acc[nt][2 + e2] = atomicExch(wsl + (row_top + 8) * 64 + tok, 0.f);
+        }
+      }
+      if (*abort_flag == 0) store_pair<NT>(p, gi, rb, warp, lane, acc);
+      if (warp == 0 && lane == 0) atomicExch(p.ws_cnt + slot, 0);
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+  }
+}
+
+template <int Q, int NT>
+cudaError_t launch_one(const StreamParams& p, int grid, cudaStream_t stream) {
+  constexpr uint32_t UB = UnitBytes<Q>::value;
+  const size_t smem = (size_t)kStages * UB + 2 * kStages * sizeof(uint64_t) + 16;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(stream_gemm_kernel<Q, NT>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
+  stream_gemm_kernel<Q, NT><<<grid, kThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int stream_gemm_ctas_per_sm(int nt) { return nt >= 4 ? CtasPerSm<4>::value : CtasPerSm<1>::value; }
+
+cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int grid,
+                               cudaStream_t stream) {
+  if (quant == kQuantFp8Block) {
+    switch (nt) {
+      case 1: return launch_one<kQuantFp8Block, 1>(p, grid, stream);
+      case 2: return launch_one<kQuantFp8Block, 2>(p, grid, stream);
+      case 4: return launch_one<kQuantFp8Block, 4>(p, grid, stream);
+      case 8: return launch_one<kQuantFp8Block, 8>(p, grid, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (nt) {
+    case 1: return launch_one<kQuantNvfp4, 1>(p, grid, stream);
+    case 2: return launch_one<kQuantNvfp4, 2>(p, grid, stream);
+    case 4: return launch_one<kQuantNvfp4, 4>(p, grid, stream);
+    case 8: return launch_one<kQuantNvfp4, 8>(p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace b200

@@ -1,0 +1,310 @@
+"""Torch-facing wrappers of the libb200moe C ABI.
+
+Every function here takes CUDA tensors, validates what the C ABI cannot see
+(dtype, device, contiguity), and calls the library on the current CUDA stream.
+Outputs are allocated here unless the caller passes them (the reference's
+``Tensor(a!) out`` convention, ``quant/sm70_fp8_moe/shim.cpp:50-56``).
+
+Workspaces are cached per device, sized once and zero-filled; a call that
+needs a larger one grows it, except during CUDA-graph capture, where growing
+would be an allocation inside the capture and raises instead (size them up
+front with :func:`reserve_workspace`, as the reference sizes its decode
+workspace for the largest capture batch, ``decode_gemv.py:170-180``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+_WS_LOCK = threading.Lock()
+_WORKSPACES: dict[int, torch.Tensor] = {}
+
+
+def _vp(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _code(t: torch.Tensor, what: str) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise TypeError(f"{what} must be bf16 or f16, got {t.dtype}") from None
+
+
+def _cuda(t: torch.Tensor, what: str) -> None:
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise ValueError(f"{what} must be a CUDA tensor")
+
+
+def _contig(t: torch.Tensor, what: str) -> None:
+    _cuda(t, what)
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+
+
+def lib():
+    return _lib.load()
+
+
+def num_sms() -> int:
+    return int(lib().b200_num_sms())
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Per-device zero-filled workspace of at least ``nbytes`` bytes."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    with _WS_LOCK:
+        ws = _WORKSPACES.get(index)
+        if ws is not None and ws.numel() >= nbytes:
+            return ws
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                f"b200 workspace needs {nbytes} bytes during CUDA-graph capture; "
+                "call reserve_workspace() before capturing"
+            )
+        size = max(nbytes, 0 if ws is None else ws.numel())
+        ws = torch.zeros(size + 256, dtype=torch.uint8, device=torch.device("cuda", index))
+        # The library wants a 256-byte aligned base.
+        offset = (-ws.data_ptr()) % 256
+        ws = ws[offset : offset + size]
+        _WORKSPACES[index] = ws
+        return ws
+
+
+def reserve_workspace(nbytes: int, device: torch.device | None = None) -> torch.Tensor:
+    return workspace(nbytes, device or torch.device("cuda", torch.cuda.current_device()))
+
+
+def workspace_status(device: torch.device | None = None, reset: bool = True) -> int:
+    """Device error bits recorded by the kernels (0 = none). Synchronizes."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    ws = _WORKSPACES.get(device.index if device.index is not None else torch.cuda.current_device())
+    if ws is None:
+        return 0
+    bits = ctypes.c_int32(0)
+    _lib.check(lib().b200_workspace_status(_vp(ws), ctypes.byref(bits), int(reset), _stream(ws.device)))
+    return int(bits.value)
+
+
+# ----------------------------------------------------------------- routing
+def align_capacity(numel: int, num_experts: int, block_size: int) -> tuple[int, int]:
+    cap = numel + min(numel, num_experts) * (block_size - 1)
+    return cap, (cap + block_size - 1) // block_size
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int, out=None):
+    """(sorted_token_ids, expert_ids, num_tokens_post_pad) for ``topk_ids``."""
+    _contig(topk_ids, "topk_ids")
+    if topk_ids.dtype != torch.int32:
+        raise TypeError(f"topk_ids must be int32, got {topk_ids.dtype}")
+    numel = topk_ids.numel()
+    cap, blocks = align_capacity(numel, num_experts, block_size)
+    if out is None:
+        dev = topk_ids.device
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=dev)
+        expert_ids = torch.empty(blocks, dtype=torch.int32, device=dev)
+        ntpp = torch.empty(1, dtype=torch.int32, device=dev)
+    else:
+        sorted_ids, expert_ids, ntpp = out
+    _lib.check(
+        lib().b200_moe_align_block_size(
+            _vp(topk_ids), numel, num_experts, block_size, _vp(sorted_ids), sorted_ids.numel(),
+            _vp(expert_ids), expert_ids.numel(), _vp(ntpp), _stream(topk_ids.device),
+        )
+    )
+    return sorted_ids, expert_ids, ntpp
+
+
+# ----------------------------------------------------------------- combine
+def moe_sum_reduce(input_tensor: torch.Tensor, output_tensor: torch.Tensor,
+                   routed_scaling_factor: float = 1.0) -> torch.Tensor:
+    """``out[t] = rsf * sum_k in[t, k]`` (``quant/sm70_fp4_moe/sum_reduce.py:84-123``)."""
+    _contig(input_tensor, "input")
+    _contig(output_tensor, "output")
+    if input_tensor.dtype != output_tensor.dtype:
+        raise ValueError(
+            f"moe_sum_reduce dtype mismatch: input {input_tensor.dtype}, output {output_tensor.dtype}"
+        )
+    tokens, top_k, hidden = input_tensor.shape
+    if tuple(output_tensor.shape) != (tokens, hidden):
+        raise ValueError(f"output must be [{tokens}, {hidden}], got {tuple(output_tensor.shape)}")
+    _lib.check(
+        lib().b200_moe_sum_reduce(
+            _vp(input_tensor), _vp(output_tensor), tokens, top_k, hidden,
+            _code(input_tensor, "input"), float(routed_scaling_factor), _stream(input_tensor.device),
+        )
+    )
+    return output_tensor
+
+
+def moe_combine(routed: torch.Tensor, topk_ids: torch.Tensor | None, num_experts: int,
+                routed_scaling_factor: float = 1.0, shared_out: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16):
+    """Sum weighted per-route rows ``routed [T*k, H]`` over valid slots."""
+    _contig(routed, "routed")
+    if topk_ids is None:
+        raise ValueError("topk_ids is required to know top_k")
+    _contig(topk_ids, "topk_ids")
+    tokens, top_k = topk_ids.shape
+    hidden = routed.shape[-1]
+    if out is None:
+        out = torch.empty(tokens, hidden, dtype=out_dtype, device=routed.device)
+    if shared_out is not None:
+        _contig(shared_out, "shared_out")
+    _lib.check(
+        lib().b200_moe_combine(
+            _vp(routed), _code(routed, "routed"), _vp(topk_ids), num_experts, tokens, top_k, hidden,
+            float(routed_scaling_factor), _vp(shared_out),
+            _code(shared_out, "shared_out") if shared_out is not None else 0,
+            _vp(out), _code(out, "out"), _stream(routed.device),
+        )
+    )
+    return out
+
+
+# ----------------------------------------------------------------- prepack
+def fp8_prepack(w: torch.Tensor, gated: bool) -> torch.Tensor:
+    """e4m3 ``[E, N, K]`` (or ``[N, K]``) -> streamed bank ``[E, N*K]`` uint8."""
+    _contig(w, "weight")
+    if w.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"weight must be float8_e4m3fn, got {w.dtype}")
+    w3 = w.unsqueeze(0) if w.dim() == 2 else w
+    e, n, k = (int(d) for d in w3.shape)
+    nbytes = int(lib().b200_fp8_packed_bytes(e, n, k))
+    out = torch.empty(e, nbytes // e, dtype=torch.uint8, device=w.device)
+    _lib.check(lib().b200_fp8_prepack(_vp(w3), e, n, k, int(gated), _vp(out), _stream(w.device)))
+    return out
+
+
+def nvfp4_prepack(w: torch.Tensor, scales: torch.Tensor, gated: bool) -> torch.Tensor:
+    """ModelOpt ``[E, N, K/2]`` uint8 + ``[E, N, K/16]`` e4m3 -> streamed bank."""
+    _contig(w, "weight")
+    _contig(scales, "scales")
+    if w.dtype != torch.uint8:
+        raise TypeError(f"packed NVFP4 weight must be uint8, got {w.dtype}")
+    if scales.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"NVFP4 scales must be float8_e4m3fn, got {scales.dtype}")
+    w3 = w.unsqueeze(0) if w.dim() == 2 else w
+    s3 = scales.unsqueeze(0) if scales.dim() == 2 else scales
+    e, n, half_k = (int(d) for d in w3.shape)
+    k = 2 * half_k
+    if tuple(s3.shape) != (e, n, k // 16):
+        raise ValueError(f"scales must be [{e}, {n}, {k // 16}], got {tuple(s3.shape)}")
+    nbytes = int(lib().b200_nvfp4_packed_bytes(e, n, k))
+    if nbytes < 0:
+        raise ValueError(f"NVFP4 bank needs N and K multiples of 128, got N={n} K={k}")
+    out = torch.empty(e, nbytes // e, dtype=torch.uint8, device=w.device)
+    _lib.check(
+        lib().b200_nvfp4_prepack(_vp(w3), _vp(s3), e, n, k, int(gated), _vp(out), _stream(w.device))
+    )
+    return out
+
+
+# ------------------------------------------------------------------- GEMMs
+def gemm_workspace_bytes(convert_elems: int) -> int:
+    return int(lib().b200_gemm_workspace_bytes(int(convert_elems)))
+
+
+def linear(x: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int,
+           scales: torch.Tensor | None = None, global_scale: torch.Tensor | None = None,
+           gated_mode: int = _lib.GATED_NONE, out: torch.Tensor | None = None,
+           out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Dense ``y = x . dequant(W)^T`` on a prepacked bank (one expert)."""
+    _contig(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    m, k = (int(d) for d in x2.shape)
+    cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
+    if out is None:
+        out = torch.empty(m, cols, dtype=out_dtype or x.dtype, device=x.device)
+    ws = workspace(gemm_workspace_bytes(m * k if x.dtype == torch.bfloat16 else 0), x.device)
+    _lib.check(
+        lib().b200_linear(
+            quant, _vp(x2), _code(x2, "x"), m, k, _vp(packed), _vp(scales), _vp(global_scale), n,
+            gated_mode, _vp(out), _code(out, "out"), _vp(ws), ws.numel(), _stream(x.device),
+        )
+    )
+    return out.reshape(*x.shape[:-1], cols)
+
+
+def moe_gemm(a: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int, num_experts: int,
+             sorted_token_ids: torch.Tensor, expert_ids: torch.Tensor,
+             num_tokens_post_pad: torch.Tensor, block_size: int, top_k: int, num_routes: int,
+             c: torch.Tensor, scales: torch.Tensor | None = None,
+             global_scale: torch.Tensor | None = None, topk_weights: torch.Tensor | None = None,
+             mul_topk_weights: bool = False, gated_mode: int = _lib.GATED_NONE) -> torch.Tensor:
+    """Grouped expert GEMM with ``moe_wna16_marlin_gemm`` routing semantics."""
+    _contig(a, "a")
+    _contig(c, "c")
+    a_rows, k = (int(d) for d in a.reshape(-1, a.shape[-1]).shape)
+    if topk_weights is not None:
+        _contig(topk_weights, "topk_weights")
+        if topk_weights.dtype != torch.float32:
+            topk_weights = topk_weights.float().contiguous()
+    if c.shape[0] < num_routes:
+        raise ValueError(f"c has {c.shape[0]} rows, the routes need {num_routes}")
+    if mul_topk_weights and (topk_weights is None or topk_weights.numel() < num_routes):
+        raise ValueError("mul_topk_weights needs one topk weight per route")
+    groups = min(expert_ids.numel(), sorted_token_ids.numel() // block_size)
+    ws = workspace(gemm_workspace_bytes(a_rows * k if a.dtype == torch.bfloat16 else 0), a.device)
+    _lib.check(
+        lib().b200_moe_gemm(
+            quant, _vp(a), _code(a, "a"), a_rows, k, _vp(packed), _vp(scales), _vp(global_scale),
+            num_experts, n, gated_mode, _vp(sorted_token_ids), _vp(expert_ids), groups,
+            _vp(num_tokens_post_pad), block_size, top_k, num_routes, _vp(topk_weights),
+            int(mul_topk_weights), _vp(c), _code(c, "c"), c.shape[-1], _vp(ws), ws.numel(),
+            _stream(a.device),
+        )
+    )
+    return c
+
+
+def moe_layer_workspace_bytes(tokens: int, hidden: int, inter: int, num_experts: int,
+                              top_k: int, block_size: int) -> int:
+    return int(lib().b200_moe_layer_workspace_bytes(tokens, hidden, inter, num_experts, top_k, block_size))
+
+
+def moe_layer_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, *,
+                      quant: int, num_experts: int, inter: int, w13: torch.Tensor,
+                      w2: torch.Tensor, w13_scales: torch.Tensor | None = None,
+                      w2_scales: torch.Tensor | None = None,
+                      w13_global: torch.Tensor | None = None,
+                      w2_global: torch.Tensor | None = None, block_size: int = 16,
+                      routed_scaling_factor: float = 1.0, shared_out: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """align -> gate_up(+SiLU*up) -> down(x weight) -> combine, one library call."""
+    _contig(x, "x")
+    _contig(topk_ids, "topk_ids")
+    _contig(topk_weights, "topk_weights")
+    if topk_ids.dtype != torch.int32:
+        raise TypeError(f"topk_ids must be int32, got {topk_ids.dtype}")
+    if topk_weights.dtype != torch.float32:
+        raise TypeError(f"topk_weights must be float32, got {topk_weights.dtype}")
+    tokens, hidden = (int(d) for d in x.shape)
+    top_k = int(topk_ids.shape[1])
+    if out is None:
+        out = torch.empty(tokens, hidden, dtype=x.dtype, device=x.device)
+    if shared_out is not None:
+        _contig(shared_out, "shared_out")
+    ws = workspace(
+        moe_layer_workspace_bytes(tokens, hidden, inter, num_experts, top_k, block_size), x.device
+    )
+    _lib.check(
+        lib().b200_moe_layer_forward(
+            quant, _vp(x), _code(x, "x"), tokens, hidden, inter, _vp(topk_ids), _vp(topk_weights),
+            top_k, num_experts, _vp(w13), _vp(w13_scales), _vp(w13_global), _vp(w2),
+            _vp(w2_scales), _vp(w2_global), block_size, float(routed_scaling_factor),
+            _vp(shared_out), _code(shared_out, "shared_out") if shared_out is not None else 0,
+            _vp(out), _code(out, "out"), _vp(ws), ws.numel(), _stream(x.device),
+        )
+    )
+    return out

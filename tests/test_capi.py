@@ -1,0 +1,105 @@
+"""The C ABI library loads, exports every declared symbol, and validates on
+the host (these calls return before touching a GPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from sglang_restomod_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "b200moe.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|int64_t|const char\*)\s+(b200_\w+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in b200moe.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+    assert lib.b200_abi_version() == 1
+
+
+def test_library_has_no_torch_dependency():
+    """The C ABI .so stands alone: no libtorch / libc10 in its dependencies."""
+    import subprocess
+
+    out = subprocess.run(["ldd", str(_lib.library_path())], capture_output=True, text=True).stdout
+    assert "torch" not in out and "c10" not in out
+
+
+def _err(status):
+    assert status != 0
+    return _lib.load().b200_last_error().decode()
+
+
+def test_shape_guards_match_the_reference_messages():
+    lib = _lib.load()
+    # K must cover whole 128-wide quantization groups (sm70_fp8_moe/__init__.py:48-73).
+    st = lib.b200_fp8_prepack(ctypes.c_void_p(16), 1, 256, 100, 0, ctypes.c_void_p(16), None)
+    assert st == _lib.ERR_INVALID
+    assert "needs K a multiple of the 128-wide quantization group" in _err(st)
+    st = lib.b200_fp8_prepack(ctypes.c_void_p(16), 1, 96, 128, 0, ctypes.c_void_p(16), None)
+    assert "needs N a multiple of 128" in _err(st)
+    st = lib.b200_fp8_prepack(ctypes.c_void_p(16), 1, 128, 128, 1, ctypes.c_void_p(16), None)
+    assert "gate/up bank needs N a multiple of 256" in _err(st)
+    st = lib.b200_nvfp4_prepack(None, None, 1, 128, 128, 0, None, None)
+    assert st == _lib.ERR_INVALID and "null pointer" in _err(st)
+
+
+def test_align_validation():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    assert lib.b200_moe_align_block_size(p, 10, 0, 8, p, 100, p, 100, p, None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200_moe_align_block_size(p, 10, 2000, 8, p, 100, p, 100, p, None) == _lib.ERR_UNSUPPORTED
+    st = lib.b200_moe_align_block_size(p, 40, 16, 8, p, 50, p, 100, p, None)
+    # 40 routes over 16 experts: at most 40 + 16 * 7 = 152 padded slots
+    assert st == _lib.ERR_INVALID and "sorted_token_ids holds 50 slots, needs 152" in _err(st)
+    st = lib.b200_moe_align_block_size(p, 40, 16, 8, p, 152, p, 18, p, None)
+    assert st == _lib.ERR_INVALID and "expert_ids holds 18 blocks, needs 19" in _err(st)
+
+
+def test_gemm_validation():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    # unsupported block size
+    st = lib.b200_moe_gemm(0, p, 0, 8, 128, p, p, None, 4, 256, 0, p, p, 4, p, 12, 1, 8, None, 0,
+                           p, 0, 256, p, 1 << 30, None)
+    assert st == _lib.ERR_UNSUPPORTED and "block_size" in _err(st)
+    # fp32 activations are not an input this library takes
+    st = lib.b200_linear(0, p, 2, 1, 128, p, p, None, 128, 0, p, 0, p, 1 << 30, None)
+    assert st == _lib.ERR_UNSUPPORTED
+    # FP8 needs scales, NVFP4 needs its global scale
+    st = lib.b200_linear(0, p, 0, 1, 128, p, None, None, 128, 0, p, 0, p, 1 << 30, None)
+    assert "block scales" in _err(st)
+    st = lib.b200_linear(1, p, 0, 1, 128, p, None, None, 128, 0, p, 0, p, 1 << 30, None)
+    assert "global scale" in _err(st)
+    # a workspace below the fixed size is refused
+    st = lib.b200_linear(0, p, 0, 1, 128, p, p, None, 128, 0, p, 0, p, 16, None)
+    assert st == _lib.ERR_INVALID and "workspace" in _err(st)
+
+
+def test_sizes():
+    lib = _lib.load()
+    assert lib.b200_fp8_packed_bytes(3, 256, 512) == 3 * 256 * 512
+    assert lib.b200_nvfp4_packed_bytes(2, 256, 512) == 2 * 2 * 4 * 9216
+    assert lib.b200_nvfp4_packed_bytes(1, 100, 128) == -1
+    fixed = lib.b200_gemm_workspace_bytes(0)
+    assert fixed > 0 and lib.b200_gemm_workspace_bytes(1000) == fixed + 2048
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setenv(_lib.ENV_LIB, str(tmp_path / "nope.so"))
+    monkeypatch.setattr(_lib, "_LIB", None)
+    with pytest.raises(FileNotFoundError):
+        _lib.load()

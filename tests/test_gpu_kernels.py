@@ -1,0 +1,281 @@
+"""GPU parity: every kernel through the C ABI against the CPU oracle.
+
+moe_align is compared bit-exactly; GEMM / MoE outputs within rtol 2e-2 /
+atol 2e-2 (bf16 activations, fp32 accumulation).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sglang_restomod_b200 import _lib, ops, synth
+from tests.conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _dequant_fp8_bank(q, s, experts=None):
+    ids = range(q.shape[0]) if experts is None else experts
+    return {int(e): oracle.dequant_block_fp8(q[e].cpu(), s[e].cpu()) for e in ids}
+
+
+def _dequant_nvfp4_bank(p, s, gs, experts=None):
+    ids = range(p.shape[0]) if experts is None else experts
+    return {int(e): oracle.dequant_nvfp4(p[e].cpu(), s[e].cpu(), float(gs[e])) for e in ids}
+
+
+def _stack(d, n):
+    first = next(iter(d.values()))
+    out = torch.zeros(n, *first.shape)
+    for e, w in d.items():
+        out[e] = w
+    return out
+
+
+# ------------------------------------------------------------------ align
+ALIGN_CASES = [
+    (0, 4, 8),
+    (1, 4, 8),
+    (128, 16, 64),   # configuration 0: 32 tokens x top-4, block 64
+    (40, 512, 8),    # a decode step of the reference's profile
+    (2560, 512, 16),
+    (10, 1, 8),
+    (81920, 512, 64),  # configuration 2 prefill: 8192 tokens x top-10
+    (4096 * 8, 256, 64),
+    (777, 1024, 5),
+]
+
+
+@pytest.mark.parametrize("numel,experts,bs", ALIGN_CASES)
+@pytest.mark.parametrize("drop", [False, True])
+def test_moe_align_bit_exact(cuda_device, numel, experts, bs, drop):
+    rng = np.random.default_rng(numel + experts + bs)
+    ids = rng.integers(0, experts, size=numel).astype(np.int32)
+    if drop and numel:
+        ids[rng.random(numel) < 0.2] = -1
+    t = torch.from_numpy(ids).to(cuda_device)
+    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(t, bs, experts)
+    want_sorted, want_experts, want_total = oracle.moe_align_block_size(ids, experts, bs)
+    torch.cuda.synchronize()
+    assert int(ntpp.item()) == want_total
+    assert np.array_equal(sorted_ids.cpu().numpy(), want_sorted)
+    assert np.array_equal(expert_ids.cpu().numpy(), want_experts)
+
+
+def test_moe_align_all_one_expert_and_repeat(cuda_device):
+    ids = torch.zeros(1000, dtype=torch.int32, device=cuda_device)
+    a = [x.cpu() for x in ops.moe_align_block_size(ids, 16, 8)]
+    b = [x.cpu() for x in ops.moe_align_block_size(ids, 16, 8)]
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    want_sorted, want_experts, total = oracle.moe_align_block_size(ids.cpu().numpy(), 8, 16)
+    assert int(a[2]) == total == 1008
+    assert np.array_equal(a[0].numpy(), want_sorted)
+
+
+# --------------------------------------------------------------- combine
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_moe_sum_reduce(cuda_device, dtype):
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    x = torch.randn(37, 10, 2048, generator=g, device=cuda_device).to(dtype)
+    out = torch.empty(37, 2048, dtype=dtype, device=cuda_device)
+    ops.moe_sum_reduce(x, out, 2.5)
+    want = oracle.moe_sum_reduce_ref(x.cpu(), 2.5)
+    assert_close(out, want, rtol=1e-2, atol=1e-2, what="sum_reduce")
+
+
+def test_moe_combine_skips_dropped_routes(cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    routed = torch.randn(6 * 4, 256, generator=g, device=cuda_device).half()
+    ids = torch.randint(0, 8, (6, 4), generator=g, device=cuda_device, dtype=torch.int32)
+    ids[0, 1] = -1
+    ids[5, :] = -1
+    shared = torch.randn(6, 256, generator=g, device=cuda_device).bfloat16()
+    out = ops.moe_combine(routed, ids, 8, 1.5, shared_out=shared)
+    r = routed.float().cpu().view(6, 4, 256)
+    mask = (ids.cpu() >= 0).float()[..., None]
+    want = (r * mask).sum(1) * 1.5 + shared.float().cpu()
+    assert_close(out, want, rtol=1e-2, atol=1e-2, what="combine")
+    assert_close(out[5], shared[5], rtol=0, atol=0, what="all-dropped token")
+
+
+# ----------------------------------------------------------- dense linear
+DENSE_SMALL = [(1, 256, 384), (4, 512, 256), (16, 384, 512), (64, 256, 256), (13, 1024, 640),
+               (100, 256, 384)]
+
+
+@pytest.mark.parametrize("m,k,n", DENSE_SMALL)
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16])
+def test_fp8_linear_small(cuda_device, m, k, n, x_dtype):
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=m + k + n)
+    x = synth.activations(m, k, cuda_device, seed=5, dtype=x_dtype)
+    packed = ops.fp8_prepack(q[0], gated=False)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0])
+    want = oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu())
+    assert_close(y, want, what=f"fp8 linear m={m} k={k} n={n}")
+    assert ops.workspace_status() == 0
+
+
+@pytest.mark.parametrize("m", [1, 8, 33])
+def test_fp8_linear_gated_fused(cuda_device, m):
+    inter, k = 256, 512
+    q, s = synth.fp8_bank(1, 2 * inter, k, cuda_device, seed=9)
+    x = synth.activations(m, k, cuda_device, seed=6)
+    packed = ops.fp8_prepack(q[0], gated=True)
+    y = ops.linear(x, packed, 2 * inter, quant=_lib.QUANT_FP8_BLOCK, scales=s[0],
+                   gated_mode=_lib.GATED_FUSED)
+    want = oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu(), gated=True)
+    assert_close(y, want, what="fused gate/up")
+    ysplit = ops.linear(x, packed, 2 * inter, quant=_lib.QUANT_FP8_BLOCK, scales=s[0],
+                        gated_mode=_lib.GATED_SPLIT)
+    assert_close(ysplit, oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu()), what="split gate/up")
+
+
+@pytest.mark.parametrize("k,n", [(5120, 25600), (25600, 5120)])
+@pytest.mark.parametrize("m", [1, 4, 16, 64])
+def test_fp8_linear_config1(cuda_device, k, n, m):
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=1)
+    x = synth.activations(m, k, cuda_device, seed=2)
+    packed = ops.fp8_prepack(q[0], gated=False)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0])
+    # Check a fixed sample of 1024 output columns against the oracle.
+    cols = torch.randperm(n, generator=torch.Generator().manual_seed(0))[:1024].sort().values
+    w = oracle.dequant_block_fp8(q[0].cpu(), s[0].cpu())[cols]
+    want = x.cpu().float() @ w.T
+    assert_close(y.cpu()[:, cols], want, what=f"config1 m={m} k={k} n={n}")
+
+
+def test_fp8_linear_lm_head_sampled(cuda_device):
+    k, n, m = 5120, 152064, 4
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=3)
+    x = synth.activations(m, k, cuda_device, seed=4)
+    packed = ops.fp8_prepack(q[0], gated=False)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0])
+    blocks = torch.tensor([0, 7, 600, 1187])  # first, middle, last 128-row blocks
+    rows = (blocks[:, None] * 128 + torch.arange(128)).flatten()
+    qs = q[0][rows.to(cuda_device)].cpu()
+    ss = s[0][blocks.to(cuda_device)].cpu()
+    want = x.cpu().float() @ oracle.dequant_block_fp8(qs, ss).T
+    assert_close(y.cpu()[:, rows], want, what="lm_head")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 256, 256), (8, 512, 384), (16, 1024, 256), (64, 256, 512)])
+def test_nvfp4_linear(cuda_device, m, k, n):
+    p, s, gs = synth.nvfp4_bank(1, n, k, cuda_device, seed=m + n)
+    x = synth.activations(m, k, cuda_device, seed=7)
+    packed = ops.nvfp4_prepack(p[0], s[0], gated=False)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_NVFP4, global_scale=gs[:1])
+    want = oracle.nvfp4_linear_ref(x.cpu(), p[0].cpu(), s[0].cpu(), float(gs[0]))
+    assert_close(y, want, what=f"nvfp4 linear m={m}")
+
+
+def test_linear_cuda_graph_replay(cuda_device):
+    """Capture once, replay with new inputs (graph-safe: no host sync, no allocation)."""
+    m, k, n = 4, 512, 768
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=12)
+    packed = ops.fp8_prepack(q[0], gated=False)
+    x = synth.activations(m, k, cuda_device, seed=1)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_device)
+    ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0], out=y)  # warm-up sizes the workspace
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0], out=y)
+    for seed in (2, 3):
+        x.copy_(synth.activations(m, k, cuda_device, seed=seed))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert_close(y, oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu()), what=f"replay {seed}")
+
+
+# ----------------------------------------------------------- grouped GEMM
+@pytest.mark.parametrize("quant", [_lib.QUANT_FP8_BLOCK, _lib.QUANT_NVFP4])
+@pytest.mark.parametrize("block", [8, 16, 32, 64])
+@pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED, _lib.GATED_SPLIT])
+def test_moe_gemm(cuda_device, quant, block, gated_mode):
+    experts, tokens, top_k, k = 6, 19, 3, 256
+    n = 512
+    ids, weights = synth.route(tokens, experts, top_k, cuda_device, seed=block)
+    ids[0, 0] = -1  # an expert-parallel drop
+    x = synth.activations(tokens, k, cuda_device, seed=8)
+    gated = gated_mode != _lib.GATED_NONE
+    if quant == _lib.QUANT_FP8_BLOCK:
+        q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=2)
+        packed, scales, gs = ops.fp8_prepack(q, gated), s, None
+        dense = _stack(_dequant_fp8_bank(q, s), experts)
+    else:
+        p, s8, gs = synth.nvfp4_bank(experts, n, k, cuda_device, seed=2)
+        packed, scales = ops.nvfp4_prepack(p, s8, gated), None
+        dense = _stack(_dequant_nvfp4_bank(p, s8, gs), experts)
+    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, block, experts)
+    routes = tokens * top_k
+    cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
+    c = torch.zeros(routes, cols, dtype=torch.bfloat16, device=cuda_device)
+    mul = gated_mode == _lib.GATED_NONE
+    ops.moe_gemm(x, packed, n, quant=quant, num_experts=experts, sorted_token_ids=sorted_ids,
+                 expert_ids=expert_ids, num_tokens_post_pad=ntpp, block_size=block, top_k=top_k,
+                 num_routes=routes, c=c, scales=scales, global_scale=gs, topk_weights=weights,
+                 mul_topk_weights=mul, gated_mode=gated_mode)
+    want, written = oracle.moe_gemm_ref(
+        x.cpu(), dense, sorted_ids.cpu().numpy(), expert_ids.cpu().numpy(), int(ntpp.item()),
+        block, top_k, routes, weights.cpu(), mul, 1 if gated_mode == _lib.GATED_FUSED else 0,
+    )
+    assert not bool(written[0])  # the dropped route is never computed
+    assert_close(c.cpu()[written], want[written], what=f"moe_gemm q={quant} bs={block} g={gated_mode}")
+    assert ops.workspace_status() == 0
+
+
+# ------------------------------------------------------------ MoE layer
+def _layer_inputs(shape, tokens, quant, device, seed=0):
+    ids, weights = synth.route(tokens, shape.experts, shape.top_k, device, seed=seed + 1)
+    x = synth.activations(tokens, shape.hidden, device, seed=seed)
+    if quant == _lib.QUANT_FP8_BLOCK:
+        q13, s13 = synth.fp8_bank(shape.experts, 2 * shape.inter, shape.hidden, device, seed=10)
+        q2, s2 = synth.fp8_bank(shape.experts, shape.hidden, shape.inter, device, seed=11)
+        bank = dict(w13=ops.fp8_prepack(q13, True), w2=ops.fp8_prepack(q2, False),
+                    w13_scales=s13, w2_scales=s2)
+        deq = lambda es: (_dequant_fp8_bank(q13, s13, es), _dequant_fp8_bank(q2, s2, es))  # noqa: E731
+    else:
+        p13, s13, g13 = synth.nvfp4_bank(shape.experts, 2 * shape.inter, shape.hidden, device, seed=10)
+        p2, s2, g2 = synth.nvfp4_bank(shape.experts, shape.hidden, shape.inter, device, seed=11)
+        bank = dict(w13=ops.nvfp4_prepack(p13, s13, True), w2=ops.nvfp4_prepack(p2, s2, False),
+                    w13_global=g13, w2_global=g2)
+        deq = lambda es: (_dequant_nvfp4_bank(p13, s13, g13, es), _dequant_nvfp4_bank(p2, s2, g2, es))  # noqa: E731
+    return x, ids, weights, bank, deq
+
+
+def _check_layer(shape, tokens, quant, device, block, sample_tokens=None, rsf=1.0):
+    x, ids, weights, bank, deq = _layer_inputs(shape, tokens, quant, device)
+    out = ops.moe_layer_forward(x, ids, weights, quant=quant, num_experts=shape.experts,
+                                inter=shape.inter, block_size=block, routed_scaling_factor=rsf,
+                                **bank)
+    torch.cuda.synchronize()
+    assert ops.workspace_status() == 0
+    sel = torch.arange(tokens) if sample_tokens is None else sample_tokens
+    ids_c = ids.cpu()[sel]
+    experts = torch.unique(ids_c[ids_c >= 0]).tolist()
+    d13, d2 = deq(experts)
+    # Only the touched experts are dequantized; renumber them compactly.
+    remap = torch.full((shape.experts,), -1, dtype=torch.int32)
+    remap[experts] = torch.arange(len(experts), dtype=torch.int32)
+    ids_m = torch.where(ids_c >= 0, remap[ids_c.clamp(min=0).long()], -1)
+    w13 = torch.stack([d13[e] for e in experts])
+    w2 = torch.stack([d2[e] for e in experts])
+    want = oracle.moe_layer_ref(x.cpu()[sel], ids_m, weights.cpu()[sel], w13, w2,
+                                routed_scaling_factor=rsf)
+    assert_close(out.cpu()[sel], want, what=f"layer q={quant} T={tokens}")
+
+
+@pytest.mark.parametrize("quant", [_lib.QUANT_FP8_BLOCK, _lib.QUANT_NVFP4])
+def test_layer_config0(cuda_device, quant):
+    _check_layer(synth.CONFIG0, 32, quant, cuda_device, block=64 if quant == 0 else 16, rsf=1.0)
+
+
+@pytest.mark.parametrize("quant", [_lib.QUANT_FP8_BLOCK, _lib.QUANT_NVFP4])
+@pytest.mark.parametrize("tokens", [1, 8, 64, 256])
+def test_layer_config2_decode(cuda_device, quant, tokens):
+    sample = None if tokens <= 8 else torch.tensor([0, tokens // 3, tokens - 1])
+    _check_layer(synth.CONFIG2, tokens, quant, cuda_device, block=16, sample_tokens=sample, rsf=2.0)
