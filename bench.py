@@ -1,0 +1,579 @@
+"""Benchmark of the B200 quantized-MoE path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME]
+
+Default workload ("config4-decode"): the expert-parallel block-FP8 MoE layer
+of the benchmark definition - H=7168, I=2048, 256 routed experts, top-8, one
+shared expert (I=2048), 128 tokens per rank - on N GPUs of one node, one
+process per GPU (torchrun), experts split E/N per rank, tokens dispatched
+and combined with NCCL all-to-all. Per-rank work is fixed as N grows
+(weak scaling); ``value`` is the tokens of all ranks divided by the slowest
+rank's device time. Other workloads (``--workload``) are the single-GPU
+configurations: config2-T<t> / config3-T<t> (E=512 FP8 / NVFP4 MoE layer)
+and config1-<K>x<N>-M<m> (dense FP8 GEMV).
+
+Inputs are seeded synthetic tensors (no dataset): activations N(0,1),
+router logits N(0,1) -> softmax -> top-k -> renormalised, weights N(0,0.02)
+quantized to block FP8 (or NVFP4). Weights read per step exceed the 126 MB
+L2 in every default workload, so no L2 flush is inserted.
+
+``--impl reference`` times the reference's CPU torch arithmetic (the
+oracle port of sglang-restomod's dequantize-then-matmul MoE path) on the
+host cores, rank 0 only, on a bounded sample of tokens per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "sglang-restomod_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer & GEMV tokens/s per B200 + % HBM/tensor roofline; EP 1/2/4/8 tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        d = json.loads(path.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+        0x2: "applications_clocks_setting",
+    }
+
+    def __init__(self, device_index: int, period: float = 0.05):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # noqa: BLE001 - clocks are reported, not required
+            self._nvml = None
+            self.error = str(exc)
+        self.period = period
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((mhz, int(reasons)))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = statistics.median(s[0] for s in self.samples)
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = [name for bit, name in self.REASONS.items() if bits & bit]
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local_rank
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- workloads
+def parse_workload(name: str):
+    from sglang_restomod_b200 import synth
+
+    if name in ("config4-decode", "config4-prefill"):
+        return dict(kind="ep", shape=synth.CONFIG4, tokens=128 if name.endswith("decode") else 4096,
+                    quant=0)
+    if name.startswith("config2-T") or name.startswith("config3-T"):
+        return dict(kind="moe", shape=synth.CONFIG2, tokens=int(name.split("-T")[1]),
+                    quant=0 if name.startswith("config2") else 1)
+    if name.startswith("config0"):
+        return dict(kind="moe", shape=synth.CONFIG0, tokens=32, quant=0)
+    if name.startswith("config1-"):
+        kn, m = name[len("config1-"):].split("-M")
+        k, n = (int(v) for v in kn.split("x"))
+        return dict(kind="dense", k=k, n=n, m=int(m))
+    raise SystemExit(f"unknown workload {name}")
+
+
+class MoEWorkload:
+    """One MoE layer forward per step on this rank's tokens."""
+
+    def __init__(self, spec, rank, world, device):
+        import torch
+
+        from sglang_restomod_b200 import synth
+        from sglang_restomod_b200.ep import ExpertParallelMoE
+        from sglang_restomod_b200.layer import QuantMoELayer
+
+        shape = spec["shape"]
+        self.shape = shape
+        self.tokens = spec["tokens"]
+        self.quant = spec["quant"]
+        self.world = world
+        e_local = shape.experts // world
+        self.layer = QuantMoELayer.synthetic(shape, self.quant, device,
+                                             first_expert=rank * e_local, num_experts=e_local)
+        self.model = ExpertParallelMoE(self.layer, shape.experts, rank, world)
+        # Each rank's tokens are its own seeded batch.
+        self.x = synth.activations(self.tokens, shape.hidden, device, seed=100 + rank)
+        self.ids, self.w = synth.route(self.tokens, shape.experts, shape.top_k, device, seed=200 + rank)
+        self.out = torch.empty_like(self.x)
+        # pinned host copies for the end-to-end leg
+        self.h_x = self.x.cpu().pin_memory()
+        self.h_ids = self.ids.cpu().pin_memory()
+        self.h_w = self.w.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.h_x).pin_memory()
+        self.d_x = torch.empty_like(self.x)
+        self.d_ids = torch.empty_like(self.ids)
+        self.d_w = torch.empty_like(self.w)
+
+    def step(self):
+        self.model.forward(self.x, self.ids, self.w, out=self.out)
+
+    def step_e2e(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        self.d_ids.copy_(self.h_ids, non_blocking=True)
+        self.d_w.copy_(self.h_w, non_blocking=True)
+        self.model.forward(self.d_x, self.d_ids, self.d_w, out=self.out)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        h2d = self.h_x.numel() * 2 + self.h_ids.numel() * 4 + self.h_w.numel() * 4
+        return h2d, self.h_out.numel() * 2
+
+    def launches_per_step(self):
+        # local layer (+ shared); under EP one more combine of returned rows
+        return self.layer.launches_per_forward() + (1 if self.world > 1 else 0)
+
+    def algorithmic(self):
+        """(bytes, flops) of one step on this rank (realized routing)."""
+        import torch
+
+        layer = self.layer
+        shape = self.shape
+        ids = self.ids.reshape(-1).long()
+        if self.world > 1:
+            # experts this rank owns that any rank's routing touches is not
+            # known locally; count the local experts (all are touched at
+            # these token counts) - checked by the routing stats below.
+            touched = layer.num_experts
+        else:
+            touched = int(torch.unique(ids).numel())
+        wbytes = touched * layer.weight_bytes_per_expert()
+        if layer.shared is not None:
+            wbytes += 3 * shape.hidden * shape.shared_inter
+        act = self.tokens * shape.hidden * 2 * 2
+        routes = self.tokens * shape.top_k
+        flops = 2 * routes * 3 * shape.hidden * shape.inter
+        if layer.shared is not None:
+            flops += 2 * self.tokens * 3 * shape.hidden * shape.shared_inter
+        return wbytes + act, flops, touched
+
+    def dominant(self):
+        """Closure timing the gate/up expert GEMM alone (the largest kernel)."""
+        import torch
+
+        from sglang_restomod_b200 import _lib, ops
+        from sglang_restomod_b200.layer import block_size_for
+
+        layer = self.layer
+        if self.world == 1:
+            ids, x = self.ids, self.x
+        else:
+            if self.model.last_recv is None:
+                return None
+            x, ids, _ = self.model.last_recv
+        bs = block_size_for(ids.numel(), layer.num_experts)
+        sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, bs, layer.num_experts)
+        x16 = x.half()
+        routes = ids.numel()
+        c = torch.empty(routes, layer.inter, dtype=torch.float16, device=self.x.device)
+
+        def run():
+            ops.moe_gemm(x16, layer.w13, 2 * layer.inter, quant=layer.quant,
+                         num_experts=layer.num_experts, sorted_token_ids=sorted_ids,
+                         expert_ids=expert_ids, num_tokens_post_pad=ntpp, block_size=bs,
+                         top_k=ids.shape[1], num_routes=routes, c=c, scales=layer.w13_scales,
+                         global_scale=layer.w13_global, gated_mode=_lib.GATED_FUSED)
+
+        touched = int(torch.unique(ids).numel())
+        if layer.quant == 0:
+            per_expert = 2 * layer.inter * layer.hidden + (2 * layer.inter // 128) * (layer.hidden // 128) * 4
+        else:
+            per_expert = 2 * layer.inter * layer.hidden // 2 + 2 * layer.inter * layer.hidden // 16
+        nbytes = touched * per_expert + x.shape[0] * layer.hidden * 2 + routes * layer.inter * 2
+        return run, nbytes, "stream_gemm_kernel (gate/up, gated SiLU epilogue)"
+
+
+class DenseWorkload:
+    def __init__(self, spec, device):
+        import torch
+
+        from sglang_restomod_b200 import ops, synth
+
+        self.k, self.n, self.m = spec["k"], spec["n"], spec["m"]
+        self.tokens = self.m
+        q, s = synth.fp8_bank(1, self.n, self.k, device, seed=1)
+        self.packed = ops.fp8_prepack(q[0], gated=False)
+        self.scales = s[0]
+        del q
+        self.x = synth.activations(self.m, self.k, device, seed=2)
+        self.out = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=device)
+        self.h_x = self.x.cpu().pin_memory()
+        self.h_out = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
+        self.d_x = torch.empty_like(self.x)
+
+    def _run(self, x):
+        from sglang_restomod_b200 import _lib, ops
+
+        ops.linear(x, self.packed, self.n, quant=_lib.QUANT_FP8_BLOCK, scales=self.scales, out=self.out)
+
+    def step(self):
+        self._run(self.x)
+
+    def step_e2e(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        self._run(self.d_x)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        return self.h_x.numel() * 2, self.h_out.numel() * 2
+
+    def launches_per_step(self):
+        return 2
+
+    def algorithmic(self):
+        wbytes = self.n * self.k + (self.n // 128) * (self.k // 128) * 4
+        return wbytes + self.m * (self.k + self.n) * 2, 2 * self.m * self.n * self.k, 1
+
+    def dominant(self):
+        return self.step, self.algorithmic()[0], "stream_gemm_kernel (dense)"
+
+
+# -------------------------------------------------------------- CPU legs
+def cpu_sample_tokens_per_s(workload_name: str, spec, sample_tokens: int, repeats: int,
+                            threads: int):
+    """Time the oracle (the reference's CPU torch arithmetic) on a token sample."""
+    import torch
+
+    import oracle
+    from sglang_restomod_b200 import quant as _q  # noqa: F401
+    from sglang_restomod_b200.quant.quantize import quantize_block_fp8, quantize_nvfp4
+
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    if spec["kind"] == "dense":
+        k, n = spec["k"], spec["n"]
+        m = min(spec["m"], sample_tokens)
+        rows = min(n, 4096)  # a slice of the weight; scaled to the full N below
+        w = torch.randn(rows, k, generator=gen) * 0.02
+        q, s = quantize_block_fp8(w)
+        x = torch.randn(m, k, generator=gen).bfloat16()
+        times = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            oracle.fp8_linear_ref(x, q, s)
+            times.append(time.perf_counter() - t0)
+        t = statistics.median(times) * (n / rows)
+        return m / t, f"{m} rows x K={k} through a {rows}-row slice of W, scaled to N={n}"
+
+    shape = spec["shape"]
+    h, i, e_all, top_k = shape.hidden, shape.inter, shape.experts, shape.top_k
+    x = torch.randn(sample_tokens, h, generator=gen).bfloat16()
+    probs = torch.softmax(torch.randn(sample_tokens, e_all, generator=gen), dim=-1)
+    wts, ids = torch.topk(probs, top_k, dim=-1)
+    wts = wts / wts.sum(-1, keepdim=True)
+    experts = torch.unique(ids).tolist()
+    remap = torch.full((e_all,), -1, dtype=torch.int64)
+    remap[experts] = torch.arange(len(experts))
+    ids_m = remap[ids]
+    # checkpoint-format weights of the touched experts (dequantized inside the timed step)
+    bank13, bank2 = [], []
+    for _ in experts:
+        w13 = torch.randn(2 * i, h, generator=gen) * 0.02
+        w2 = torch.randn(h, i, generator=gen) * 0.02
+        if spec["quant"] == 0:
+            bank13.append(quantize_block_fp8(w13))
+            bank2.append(quantize_block_fp8(w2))
+        else:
+            p13, s13, g13 = quantize_nvfp4(w13)
+            p2, s2, g2 = quantize_nvfp4(w2)
+            bank13.append((p13, s13, float(g13)))
+            bank2.append((p2, s2, float(g2)))
+
+    def deq(item):
+        if spec["quant"] == 0:
+            return oracle.dequant_block_fp8(*item)
+        return oracle.dequant_nvfp4(*item)
+
+    def fetch(e):  # dequantized inside the timed step, one expert at a time
+        return deq(bank13[e]), deq(bank2[e])
+
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.moe_layer_ref(x, ids_m.to(torch.int32), wts, fetch, len(experts))
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return sample_tokens / t, (
+        f"{sample_tokens} tokens x top-{top_k} ({len(experts)} experts dequantized and applied)"
+        f" per step, oracle port of the reference's CPU dequantize-then-matmul path"
+    )
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU torch path on host cores, rank 0 only.
+
+    One step is one token of the workload through the oracle port (its
+    experts dequantized and applied); W untimed steps, then min(K, 10) timed
+    steps so the run stays within minutes.
+    """
+    if rank != 0:
+        return
+    spec = parse_workload(args.workload)
+    threads = os.cpu_count() or 1
+    cpu_sample_tokens_per_s(args.workload, spec, 1, 1, threads)  # warm-up
+    timed = max(1, min(args.steps, 10))
+    value, desc = cpu_sample_tokens_per_s(args.workload, spec, 1, timed, threads)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": timed, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (dequantized weights) x bf16", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": args.workload},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- main
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config4-decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        reference_arm(args, rank, world_env)
+        return 0
+
+    import torch
+
+    rank, world, local_rank = dist_setup()
+    device = torch.device("cuda", torch.cuda.current_device())
+    spec = parse_workload(args.workload)
+    if spec["kind"] == "dense":
+        wl = DenseWorkload(spec, device)
+    elif spec["kind"] in ("ep", "moe"):
+        wl = MoEWorkload(spec, rank, world, device)
+    torch.cuda.synchronize()
+
+    from sglang_restomod_b200 import ops
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        wl.step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    sampler.stop()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+
+    # end-to-end: pinned host inputs in, result out, every step
+    for _ in range(3):
+        wl.step_e2e()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        wl.step_e2e()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(start.elapsed_time(end), world)
+
+    # dominant kernel alone, CUDA events on its launch stream
+    dom = wl.dominant()
+    roofline = None
+    hbm_gbs, bf16_tflops, peak_kind = measured_peaks()
+    if dom is not None:
+        run, dom_bytes, dom_name = dom
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        reps = max(args.steps, 20)
+        start.record(stream)
+        for _ in range(reps):
+            run()
+        end.record(stream)
+        torch.cuda.synchronize()
+        dom_ms = start.elapsed_time(end) / reps
+        achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic.json"
+        if tfile.is_file():
+            traffic = json.loads(tfile.read_text()).get(args.workload)
+        roofline = {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": hbm_gbs,
+                    "unit": "GB/s", "frac": achieved / hbm_gbs, "traffic": traffic,
+                    "peak_source": peak_kind, "algorithmic_bytes": dom_bytes,
+                    "launch_us": dom_ms * 1e3}
+
+    status = ops.workspace_status()
+    if status != 0:
+        raise SystemExit(f"kernels reported device error bits {status}")
+
+    alg_bytes, alg_flops, touched = wl.algorithmic()
+    total_tokens = wl.tokens * world
+    value = total_tokens / (elapsed_ms * 1e-3 / args.steps)
+    e2e_value = total_tokens / (e2e_ms * 1e-3 / args.steps)
+    step_s = elapsed_ms * 1e-3 / args.steps
+    h2d, d2h = wl.io_bytes()
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sample = 4 if spec["kind"] != "dense" else 1
+        cpu_value, desc = cpu_sample_tokens_per_s(args.workload, spec, sample, 3, threads)
+        cpu_baseline = {"value": cpu_value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                        "sample": desc}
+
+    if rank == 0:
+        config = {"workload": args.workload, "l2": "weights read per step exceed the 126 MB L2; no flush"}
+        if spec["kind"] != "dense":
+            s = spec["shape"]
+            config.update({"hidden": s.hidden, "inter": s.inter, "experts": s.experts,
+                           "top_k": s.top_k, "shared_inter": s.shared_inter,
+                           "tokens_per_rank": wl.tokens,
+                           "quant": "block-fp8" if spec["quant"] == 0 else "nvfp4",
+                           "parallelism": f"ep{world}", "experts_touched_per_rank": touched})
+        else:
+            config.update({"K": spec["k"], "N": spec["n"], "M": spec["m"], "quant": "block-fp8"})
+        config["layer_hbm_frac"] = (alg_bytes / step_s / 1e9) / hbm_gbs
+        config["layer_algorithmic_bytes"] = alg_bytes
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3*f16->f32" if spec.get("quant", 0) == 0 else "e2m1*f16->f32",
+            "data": "synthetic", "config": config, "roofline": roofline,
+            "cpu_baseline": cpu_baseline,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "clocks": sampler.summary(),
+            "gpu_launches": wl.launches_per_step() * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

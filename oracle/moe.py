@@ -34,23 +34,33 @@ def moe_layer_ref(
     to ``inter_dtype``, the activation dtype the intermediate is stored in),
     times ``W2^T``, times the router weight, summed over slots; then the
     routed scaling factor (``method.py:307-308``) and the shared expert.
-    Vectorised per expert so it doubles as the CPU baseline.
+    Vectorised per expert so it doubles as the CPU baseline. ``w13`` may be
+    a callable ``e -> (w13_e, w2_e)`` with ``w2`` then the expert count.
     """
     tokens, top_k = topk_ids.shape
-    num_experts = w13.shape[0]
+    # w13 / w2 are stacked banks, or w13 is a callable e -> (w13[e], w2[e])
+    # that dequantizes one expert on demand (bounded memory for big banks).
+    fetch = w13 if callable(w13) else (lambda e: (w13[e], w2[e]))
+    num_experts = int(w2) if callable(w13) else w13.shape[0]
+    hidden_out = None if callable(w13) else w2.shape[1]
     ids = topk_ids.reshape(-1).long()
     wts = topk_weights.reshape(-1).float()
     tok = torch.arange(tokens).repeat_interleave(top_k)
     valid = (ids >= 0) & (ids < num_experts)
-    out = torch.zeros(tokens, w2.shape[1], dtype=torch.float32)
+    out = None if hidden_out is None else torch.zeros(tokens, hidden_out, dtype=torch.float32)
     xf = x.float()
     for e in torch.unique(ids[valid]).tolist():
         sel = torch.nonzero(valid & (ids == e)).flatten()
-        h = _silu_mul(xf[tok[sel]] @ w13[e].T)
+        we13, we2 = fetch(e)
+        h = _silu_mul(xf[tok[sel]] @ we13.T)
         if inter_dtype is not None:
             h = h.to(inter_dtype).float()
-        y = (h @ w2[e].T) * wts[sel, None]
+        y = (h @ we2.T) * wts[sel, None]
+        if out is None:
+            out = torch.zeros(tokens, y.shape[1], dtype=torch.float32)
         out.index_add_(0, tok[sel], y)
+    if out is None:
+        out = torch.zeros(tokens, x.shape[1], dtype=torch.float32)
     out = out * routed_scaling_factor
     if shared_out is not None:
         out = out + shared_out.float()

@@ -186,8 +186,9 @@ int b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int32_t nu
                 moe_align_max_experts(), num_experts);
   if (block_size <= 0 || block_size > 4096)
     return fail(B200_ERR_INVALID, "bad block_size %d", block_size);
-  if ((numel > 0 && topk_ids == nullptr) || sorted_token_ids == nullptr || expert_ids == nullptr ||
-      num_tokens_post_pad == nullptr)
+  // Zero-length arrays may be null (an empty torch tensor has no storage).
+  if ((numel > 0 && topk_ids == nullptr) || (sorted_capacity > 0 && sorted_token_ids == nullptr) ||
+      (expert_capacity > 0 && expert_ids == nullptr) || num_tokens_post_pad == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
   const int64_t busy = numel < num_experts ? numel : num_experts;
   const int64_t need = numel + busy * (block_size - 1);

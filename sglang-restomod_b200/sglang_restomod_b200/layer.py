@@ -1,0 +1,134 @@
+"""A quantized fused-MoE layer (routed experts + optional shared expert).
+
+This is the object the method classes and the benchmark drive: it holds the
+prepacked banks and runs one forward through the C ABI
+(``b200_moe_layer_forward`` plus the shared expert's two dense calls).
+Semantics follow ``SM70Fp8MoEMethod.apply``
+(``sglang_restomod/quant/sm70_fp8_moe/method.py:239-309``): stable
+expert-major routing, gated SiLU*up, router-weighted down projection,
+top-k sum, ``routed_scaling_factor``; routes whose local id is -1 (expert
+parallelism) contribute nothing.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops, synth
+
+
+def block_size_for(routes: int, experts: int) -> int:
+    """Route slots per expert group for the streaming kernel.
+
+    A group re-reads its expert's weights, so the block should hold the
+    usual per-expert route count; larger blocks waste tensor-core rows,
+    which the decode regime can afford (it is HBM-bound).
+    """
+    avg = routes / max(experts, 1)
+    for bs in (8, 16, 32):
+        if 2.5 * avg <= bs:
+            return bs
+    return 64
+
+
+@dataclass
+class SharedExpert:
+    """Always-on expert (weight 1): gate/up bank [2I, H] + down [H, I]."""
+
+    quant: int
+    inter: int
+    w13: torch.Tensor
+    w2: torch.Tensor
+    w13_scales: torch.Tensor | None = None
+    w2_scales: torch.Tensor | None = None
+    w13_global: torch.Tensor | None = None
+    w2_global: torch.Tensor | None = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = ops.linear(x, self.w13, 2 * self.inter, quant=self.quant, scales=self.w13_scales,
+                       global_scale=self.w13_global, gated_mode=_lib.GATED_FUSED,
+                       out_dtype=torch.float16)
+        return ops.linear(h, self.w2, x.shape[-1], quant=self.quant, scales=self.w2_scales,
+                          global_scale=self.w2_global, out_dtype=x.dtype)
+
+    launches_per_forward = 3  # bf16->f16 conversion, gate/up(+SiLU), down
+
+
+@dataclass
+class QuantMoELayer:
+    quant: int
+    hidden: int
+    inter: int
+    num_experts: int  # experts held by this layer (local experts under EP)
+    top_k: int
+    w13: torch.Tensor
+    w2: torch.Tensor
+    w13_scales: torch.Tensor | None = None
+    w2_scales: torch.Tensor | None = None
+    w13_global: torch.Tensor | None = None
+    w2_global: torch.Tensor | None = None
+    shared: SharedExpert | None = None
+    routed_scaling_factor: float = 1.0
+    block_size: int | None = None
+
+    def forward(self, x, topk_ids, topk_weights, out=None, shared_out=None, block_size=None,
+                use_shared=True):
+        tokens, top_k = topk_ids.shape
+        if use_shared and shared_out is None and self.shared is not None:
+            shared_out = self.shared.forward(x)
+        bs = block_size or self.block_size or block_size_for(tokens * top_k, self.num_experts)
+        return ops.moe_layer_forward(
+            x, topk_ids, topk_weights, quant=self.quant, num_experts=self.num_experts,
+            inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
+            w2_scales=self.w2_scales, w13_global=self.w13_global, w2_global=self.w2_global,
+            block_size=bs, routed_scaling_factor=self.routed_scaling_factor,
+            shared_out=shared_out, out=out,
+        )
+
+    # launches of one forward: bf16->f16, align, gate/up, down, combine (+ shared)
+    def launches_per_forward(self, x_dtype=torch.bfloat16) -> int:
+        n = 4 + (1 if x_dtype == torch.bfloat16 else 0)
+        return n + (SharedExpert.launches_per_forward if self.shared is not None else 0)
+
+    def weight_bytes_per_expert(self) -> int:
+        if self.quant == _lib.QUANT_FP8_BLOCK:
+            return 3 * self.hidden * self.inter + 3 * (self.hidden // 128) * (self.inter // 128) * 4
+        return 3 * self.hidden * self.inter // 2 + 3 * self.hidden * self.inter // 16
+
+    @classmethod
+    def synthetic(cls, shape: synth.MoEShape, quant: int, device, first_expert: int = 0,
+                  num_experts: int | None = None, seed: int = 10) -> "QuantMoELayer":
+        """Random-init layer of ``shape`` holding experts [first, first + num)."""
+        e = shape.experts if num_experts is None else num_experts
+        h, i = shape.hidden, shape.inter
+        if quant == _lib.QUANT_FP8_BLOCK:
+            q13, s13 = synth.fp8_bank(e, 2 * i, h, device, seed, first_expert)
+            w13 = ops.fp8_prepack(q13, True)
+            del q13
+            q2, s2 = synth.fp8_bank(e, h, i, device, seed + 1, first_expert)
+            w2 = ops.fp8_prepack(q2, False)
+            del q2
+            kw = dict(w13_scales=s13, w2_scales=s2)
+        else:
+            p13, s13, g13 = synth.nvfp4_bank(e, 2 * i, h, device, seed, first_expert)
+            w13 = ops.nvfp4_prepack(p13, s13, True)
+            del p13, s13
+            p2, s2, g2 = synth.nvfp4_bank(e, h, i, device, seed + 1, first_expert)
+            w2 = ops.nvfp4_prepack(p2, s2, False)
+            del p2, s2
+            kw = dict(w13_global=g13, w2_global=g2)
+        shared = None
+        if shape.shared_inter:
+            si = shape.shared_inter
+            # The shared expert stays block-FP8 in both checkpoints
+            # (its dense path is the FP8 linear).
+            q13, s13 = synth.fp8_bank(1, 2 * si, h, device, seed + 2, 0)
+            q2, s2 = synth.fp8_bank(1, h, si, device, seed + 3, 0)
+            shared = SharedExpert(
+                quant=_lib.QUANT_FP8_BLOCK, inter=si, w13=ops.fp8_prepack(q13[0], True),
+                w2=ops.fp8_prepack(q2[0], False), w13_scales=s13[0], w2_scales=s2[0],
+            )
+        return cls(quant=quant, hidden=h, inter=i, num_experts=e, top_k=shape.top_k, w13=w13,
+                   w2=w2, shared=shared, **kw)

@@ -58,24 +58,31 @@ def route(tokens: int, experts: int, top_k: int, device, seed: int = 1):
     return ids.to(torch.int32).contiguous(), w.float().contiguous()
 
 
-def fp8_bank(experts: int, n: int, k: int, device, seed: int):
-    """(e4m3 [E, N, K], fp32 scales [E, N/128, K/128])."""
-    g = _gen(device, seed)
+def _expert_gen(device, seed: int, expert: int) -> torch.Generator:
+    # One generator per global expert: a rank holding experts [a, b) builds
+    # exactly the experts a single GPU would, whatever the world size.
+    return _gen(device, seed * 1_000_003 + expert)
+
+
+def fp8_bank(experts: int, n: int, k: int, device, seed: int, first_expert: int = 0):
+    """(e4m3 [E, N, K], fp32 scales [E, N/128, K/128]) for global experts
+    [first_expert, first_expert + experts)."""
     q = torch.empty(experts, n, k, dtype=torch.float8_e4m3fn, device=device)
     s = torch.empty(experts, n // 128, k // 128, dtype=torch.float32, device=device)
     for e in range(experts):
+        g = _expert_gen(device, seed, first_expert + e)
         w = torch.randn(n, k, generator=g, device=device) * WEIGHT_STD
         q[e], s[e] = quantize_block_fp8(w)
     return q, s
 
 
-def nvfp4_bank(experts: int, n: int, k: int, device, seed: int):
+def nvfp4_bank(experts: int, n: int, k: int, device, seed: int, first_expert: int = 0):
     """(packed uint8 [E, N, K/2], e4m3 [E, N, K/16], fp32 global [E])."""
-    g = _gen(device, seed)
     p = torch.empty(experts, n, k // 2, dtype=torch.uint8, device=device)
     s = torch.empty(experts, n, k // 16, dtype=torch.float8_e4m3fn, device=device)
     gs = torch.empty(experts, dtype=torch.float32, device=device)
     for e in range(experts):
+        g = _expert_gen(device, seed, first_expert + e)
         w = torch.randn(n, k, generator=g, device=device) * WEIGHT_STD
         p[e], s[e], gs[e] = quantize_nvfp4(w)
     return p, s, gs
