@@ -440,6 +440,7 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4-decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph replay at N=1")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -467,6 +468,25 @@ def main() -> int:
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
+    # One process per GPU replays the step as a CUDA graph, as a serving
+    # engine does at decode; under expert parallelism the all-to-all split
+    # sizes are read on the host every step, so that path runs eagerly.
+    use_graph = world == 1 and not args.eager
+    step_fn, e2e_fn = wl.step, wl.step_e2e
+    if use_graph:
+        for _ in range(2):
+            wl.step_e2e()
+        torch.cuda.synchronize()
+        g_step = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step):
+            wl.step()
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e):
+            wl.step_e2e()
+        step_fn, e2e_fn = g_step.replay, g_e2e.replay
+        for _ in range(args.warmup):
+            step_fn()
+        torch.cuda.synchronize()
 
     sampler = ClockSampler(device.index)
     sampler.start()
@@ -476,7 +496,7 @@ def main() -> int:
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for _ in range(args.steps):
-        wl.step()
+        step_fn()
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -485,13 +505,13 @@ def main() -> int:
 
     # end-to-end: pinned host inputs in, result out, every step
     for _ in range(3):
-        wl.step_e2e()
+        e2e_fn()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start.record(stream)
     for _ in range(args.steps):
-        wl.step_e2e()
+        e2e_fn()
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -506,6 +526,13 @@ def main() -> int:
         for _ in range(3):
             run()
         torch.cuda.synchronize()
+        if use_graph:
+            g_dom = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_dom):
+                run()
+            run = g_dom.replay
+            run()
+            torch.cuda.synchronize()
         reps = max(args.steps, 20)
         start.record(stream)
         for _ in range(reps):
@@ -565,6 +592,7 @@ def main() -> int:
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "clocks": sampler.summary(),
+            "cuda_graph": use_graph,
             "gpu_launches": wl.launches_per_step() * args.steps,
         }
         print(json.dumps(line), flush=True)

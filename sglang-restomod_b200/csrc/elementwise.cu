@@ -54,6 +54,7 @@ __device__ __forceinline__ void store8(void* base, long long idx, int f16, const
 
 __global__ void bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
                                    long long n8) {
+  griddep_wait();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
        i += (long long)gridDim.x * blockDim.x) {
     const uint4 raw = in[i];
@@ -67,6 +68,7 @@ __global__ void bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restri
     }
     out[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  griddep_launch_dependents();
 }
 
 // One thread per 8 hidden elements of one token.
@@ -75,6 +77,7 @@ __global__ void sum_reduce_kernel(const void* __restrict__ in, void* __restrict_
                                   float scale, const int* __restrict__ topk_ids, int num_experts,
                                   const void* __restrict__ shared_out, int shared_f16,
                                   int out_f16) {
+  griddep_wait();
   const long long h8 = hidden / 8;
   const long long total = tokens * h8;
   for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
@@ -102,6 +105,7 @@ __global__ void sum_reduce_kernel(const void* __restrict__ in, void* __restrict_
     }
     store8(out, t * hidden + c, out_f16, acc);
   }
+  griddep_launch_dependents();
 }
 
 int grid_for(long long work, int threads) {
@@ -117,18 +121,17 @@ int grid_for(long long work, int threads) {
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream) {
   const long long n8 = n / 8;
   if (n8 == 0) return cudaSuccess;
-  bf16_to_f16_kernel<<<grid_for(n8, 256), 256, 0, stream>>>(
-      reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n8);
-  return cudaGetLastError();
+  return launch_pdl(bf16_to_f16_kernel, dim3(grid_for(n8, 256)), dim3(256), 0, stream,
+                    reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n8);
 }
 
 cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,
                                   long long hidden, int f16, float scale, cudaStream_t stream) {
   const long long work = tokens * (hidden / 8);
   if (work == 0) return cudaSuccess;
-  sum_reduce_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
-      in, out, tokens, top_k, hidden, f16, scale, nullptr, 0, nullptr, 0, f16);
-  return cudaGetLastError();
+  return launch_pdl(sum_reduce_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream, in, out,
+                    tokens, top_k, hidden, f16, scale, static_cast<const int*>(nullptr), 0,
+                    static_cast<const void*>(nullptr), 0, f16);
 }
 
 cudaError_t launch_moe_combine(const void* routed, int routed_f16, const int* topk_ids,
@@ -137,10 +140,9 @@ cudaError_t launch_moe_combine(const void* routed, int routed_f16, const int* to
                                int out_f16, cudaStream_t stream) {
   const long long work = tokens * (hidden / 8);
   if (work == 0) return cudaSuccess;
-  sum_reduce_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
-      routed, out, tokens, top_k, hidden, routed_f16, scale, topk_ids, num_experts, shared_out,
-      shared_f16, out_f16);
-  return cudaGetLastError();
+  return launch_pdl(sum_reduce_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream, routed,
+                    out, tokens, top_k, hidden, routed_f16, scale, topk_ids, num_experts,
+                    shared_out, shared_f16, out_f16);
 }
 
 }  // namespace b200

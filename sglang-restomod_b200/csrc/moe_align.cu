@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   for (int i = tid; i < kWarps * E; i += kThreads) cnt[i] = 0;
+  griddep_wait();  // topk_ids may come from the previous kernel
+  if (tid == 0) griddep_launch_dependents();
   __syncthreads();
 
   const long long seg = (numel + kWarps - 1) / kWarps;
@@ -178,10 +180,8 @@ cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_exper
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
-  moe_align_kernel<<<1, kThreads, smem, stream>>>(topk_ids, numel, num_experts, block_size,
-                                                  sorted_ids, sorted_cap, expert_ids, expert_cap,
-                                                  ntpp);
-  return cudaGetLastError();
+  return launch_pdl(moe_align_kernel, dim3(1), dim3(kThreads), smem, stream, topk_ids, numel,
+                    num_experts, block_size, sorted_ids, sorted_cap, expert_ids, expert_cap, ntpp);
 }
 
 }  // namespace b200

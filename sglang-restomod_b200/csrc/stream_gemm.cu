@@ -15,22 +15,28 @@
 //     A unit is one FP8 scale block: 16 KiB of E4M3, or 8 KiB of E2M1 codes
 //     plus 1 KiB of E4M3 group scales.
 //   * A persistent grid splits the flattened (row-group, row-block, K-unit)
-//     space evenly across CTAs (stream-K). Each CTA runs one producer warp
-//     that streams its units with cp.async.bulk (TMA, L2 evict-first) into a
-//     4-stage shared-memory ring tracked by mbarriers, and 8 consumer warps.
+//     space evenly across CTAs (stream-K). Each CTA runs one producer warp and
+//     8 consumer warps over a 4-stage shared-memory ring tracked by mbarriers.
+//     For every unit the producer issues one cp.async.bulk (TMA) of the weight
+//     unit (L2 evict-first) and, per activation row of the group, two 128-byte
+//     bulk copies of the row's 128-K slice into a padded tile (row stride
+//     304 B, second half at +160 B: bank-conflict-free for the consumers'
+//     16-byte reads).
 //   * A consumer warp owns 16 weight rows of the unit. It converts its bytes
 //     with the hardware cvt.rn.f16x2.{e4m3x2,e2m1x2} instructions straight
 //     into m16n8k16 A fragments and multiplies them against f16 activation
-//     fragments on the tensor cores (fp32 accumulate). FP8 block scales are
+//     fragments read from the tile (fp32 accumulate). FP8 block scales are
 //     applied once per unit to the accumulators; NVFP4 group scales
 //     (fp16_rne(e4m3 * global), as the reference rounds them) multiply the
 //     fragments.
 //   * The K index inside a unit is permuted consistently on both operands so
 //     that every lane reads 32 contiguous K of its rows and of its activation
-//     row (two 16-byte loads each) - the sum over K is order-free.
+//     row - the sum over K is order-free.
 //   * A (row-group, row-block) pair that straddles CTAs is reduced through a
 //     zeroed fp32 workspace slot with an arrival counter; the last arriving
 //     CTA applies the epilogue and leaves slot and counter zeroed again.
+//   * Launched with programmatic dependent launch: the prologue overlaps the
+//     previous kernel, every thread waits on it before reading its outputs.
 #include "common.cuh"
 #include "internal.h"
 
@@ -40,12 +46,12 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = 4;
+constexpr int kRowStride = 304;  // bytes per activation row in the tile
+constexpr int kHalf1 = 160;      // offset of the row's second 128 bytes
 
-// Two CTAs per SM keep 8 stages (128 KiB) of weights in flight per SM; the
-// 32- and 64-row variants need the registers of a whole SM for themselves.
 template <int NT>
 struct CtasPerSm {
-  static constexpr int value = NT >= 4 ? 1 : 2;
+  static constexpr int value = NT >= 8 ? 1 : 2;
 };
 
 template <int Q>
@@ -59,6 +65,16 @@ struct UnitBytes<kQuantNvfp4> {
   static constexpr uint32_t value = kFp4UnitBytes;
 };
 
+template <int Q, int NT>
+struct Layout {
+  static constexpr uint32_t kW = UnitBytes<Q>::value;
+  static constexpr uint32_t kX = 8 * NT * kRowStride;
+  static constexpr uint32_t kStage = (kW + kX + 127) / 128 * 128;
+  static constexpr size_t kSmem = (size_t)kStages * kStage + 2 * kStages * sizeof(uint64_t) + 16;
+};
+
+__device__ __forceinline__ int chunk_pos(int j) { return j * 16 + (j >= 8 ? kHalf1 - 128 : 0); }
+
 __device__ __forceinline__ long long cta_containing(long long u, long long U, long long G) {
   // Largest c with floor(c*U/G) <= u.
   long long c = ((u + 1) * G + U - 1) / U - 1;
@@ -69,6 +85,21 @@ __device__ __forceinline__ uint32_t f16x2_splat(float v) {
   __half h = __float2half_rn(v);
   __half2 h2 = __halves2half2(h, h);
   return *reinterpret_cast<uint32_t*>(&h2);
+}
+
+// Activation row of slot `slot` of group `gi`, or nullptr for a padding slot.
+template <int NT>
+__device__ __forceinline__ const __half* slot_row(const StreamParams& p, long long gi, int slot,
+                                                  bool dense) {
+  if (dense) {
+    const long long t = gi * (8 * NT) + slot;
+    return t < p.dense_m ? p.x + t * p.ldx : nullptr;
+  }
+  const int r = p.sorted_ids[gi * p.block_m + slot];
+  if (r < 0 || r >= p.num_routes) return nullptr;
+  const long long row = r / p.top_k;
+  if (row >= p.x_rows) return nullptr;
+  return p.x + row * p.ldx;
 }
 
 template <int NT>
@@ -94,48 +125,44 @@ __device__ __forceinline__ void store_pair(const StreamParams& p, long long gi, 
       }
       const float vt = acc[nt][e2];
       const float vb = acc[nt][2 + e2];
+      long long c0, c1 = -1;
+      float v0, v1 = 0.f;
       if (p.gated) {
-        const long long col = (long long)rb * 64 + warp * 8 + g8;
+        c0 = (long long)rb * 64 + warp * 8 + g8;
         if (p.fuse_act) {
-          const float v = silu_f32(vt) * vb * w;
-          if (p.out_f16)
-            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col] = __float2half_rn(v);
-          else
-            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col] = __float2bfloat16_rn(v);
+          v0 = silu_f32(vt) * vb * w;
         } else {
-          const long long col_u = col + p.N / 2;
-          if (p.out_f16) {
-            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col] = __float2half_rn(vt * w);
-            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_u] = __float2half_rn(vb * w);
-          } else {
-            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col] =
-                __float2bfloat16_rn(vt * w);
-            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_u] =
-                __float2bfloat16_rn(vb * w);
-          }
+          v0 = vt * w;
+          c1 = c0 + p.N / 2;
+          v1 = vb * w;
         }
       } else {
-        const long long col_t = (long long)rb * 128 + row_top;
-        const long long col_b = col_t + 8;
-        if (p.out_f16) {
-          reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_t] = __float2half_rn(vt * w);
-          reinterpret_cast<__half*>(p.out)[orow * p.ldo + col_b] = __float2half_rn(vb * w);
-        } else {
-          reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_t] =
-              __float2bfloat16_rn(vt * w);
-          reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col_b] =
-              __float2bfloat16_rn(vb * w);
-        }
+        c0 = (long long)rb * 128 + row_top;
+        c1 = c0 + 8;
+        v0 = vt * w;
+        v1 = vb * w;
+      }
+      if (p.out_f16) {
+        __half* o = reinterpret_cast<__half*>(p.out) + orow * p.ldo;
+        o[c0] = __float2half_rn(v0);
+        if (c1 >= 0) o[c1] = __float2half_rn(v1);
+      } else {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + orow * p.ldo;
+        o[c0] = __float2bfloat16_rn(v0);
+        if (c1 >= 0) o[c1] = __float2bfloat16_rn(v1);
       }
     }
   }
 }
 
 template <int Q, int NT>
-__global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_kernel(const StreamParams p) {
-  constexpr uint32_t UB = UnitBytes<Q>::value;
+__global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
+    stream_gemm_kernel(const StreamParams p) {
+  using L = Layout<Q, NT>;
+  constexpr uint32_t UB = L::kW;
+  constexpr int kRows = 8 * NT;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * UB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * L::kStage);
   uint64_t* empty = full + kStages;
   volatile int* flag = reinterpret_cast<volatile int*>(empty + kStages);
   volatile int* abort_flag = flag + 1;
@@ -146,9 +173,22 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
   const int kch = p.K / kUnitK;
   const bool dense = p.sorted_ids == nullptr;
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Routing, activations and the workspace come from earlier kernels.
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+
   long long groups;
   if (dense) {
-    groups = (long long)(p.dense_m + 8 * NT - 1) / (8 * NT);
+    groups = (long long)(p.dense_m + kRows - 1) / kRows;
   } else {
     groups = (long long)(p.ntpp[0] / p.block_m);
     if (groups < 0) groups = 0;
@@ -160,37 +200,58 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
   const long long u1 = ((long long)blockIdx.x + 1) * U / G;
   if (u0 >= u1) return;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      int i = 0;
-      for (long long u = u0; u < u1; ++u) {
-        const long long pair = u / kch;
-        const int kc = (int)(u - pair * kch);
-        const long long gi = pair / nrb;
-        const int rb = (int)(pair - gi * nrb);
-        const int e = dense ? 0 : p.expert_ids[gi];
-        if (e < 0 || e >= p.E) continue;
-        const int s = i % kStages;
-        if (i >= kStages) {
-          if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.status)) break;
+    constexpr int kPerLane = (kRows + 31) / 32;
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_x = l2_policy_evict_last();
+    const __half* rows[kPerLane];
+    uint32_t row_bytes = 0;
+    long long cur_pair = -1;
+    int i = 0;
+    for (long long u = u0; u < u1; ++u) {
+      const long long pair = u / kch;
+      const int kc = (int)(u - pair * kch);
+      const long long gi = pair / nrb;
+      const int rb = (int)(pair - gi * nrb);
+      const int e = dense ? 0 : p.expert_ids[gi];
+      if (e < 0 || e >= p.E) continue;
+      if (pair != cur_pair) {
+        cur_pair = pair;
+        int count = 0;
+#pragma unroll
+        for (int r = 0; r < kPerLane; ++r) {
+          const int slot = lane + 32 * r;
+          rows[r] = slot < kRows ? slot_row<NT>(p, gi, slot, dense) : nullptr;
+          count += __popc(__ballot_sync(0xffffffffu, rows[r] != nullptr));
         }
-        mbar_arrive_expect_tx(&full[s], UB);
-        const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + kc) * (long long)UB;
-        bulk_g2s(smem + (size_t)s * UB, src, UB, &full[s], pol);
-        ++i;
+        row_bytes = (uint32_t)count * 256u;
       }
+      const int s = i % kStages;
+      if (i >= kStages) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.status) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
+      uint8_t* stage = smem + (size_t)s * L::kStage;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], UB + row_bytes);
+        const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + kc) * (long long)UB;
+        bulk_g2s(stage, src, UB, &full[s], pol_w);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int r = 0; r < kPerLane; ++r) {
+        if (rows[r] != nullptr) {
+          const int slot = lane + 32 * r;
+          const __half* src = rows[r] + (long long)kc * kUnitK;
+          uint8_t* dst = stage + UB + slot * kRowStride;
+          bulk_g2s(dst, src, 128, &full[s], pol_x);
+          bulk_g2s(dst + kHalf1, src + 64, 128, &full[s], pol_x);
+        }
+      }
+      ++i;
     }
     return;
   }
@@ -202,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
   const int g8 = lane >> 2;
   const int cq = lane & 3;
   float acc[NT][4];
-  const __half* xrow[NT];
+  bool valid[NT];
   long long cur_pair = -1;
   int i = 0;
 
@@ -223,50 +284,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
-        const int n = nt * 8 + g8;
-        const __half* ptr = nullptr;
-        if (dense) {
-          const long long t = gi * (8 * NT) + n;
-          if (t < p.dense_m) ptr = p.x + t * p.ldx;
-        } else {
-          const int r = p.sorted_ids[gi * p.block_m + n];
-          if (r >= 0 && r < p.num_routes) {
-            const long long row = r / p.top_k;
-            if (row < p.x_rows)
-              ptr = p.x + row * p.ldx;
-            else
-              atomicOr(p.status, kDevBadRoute);
-          }
-        }
-        xrow[nt] = ptr;
+        valid[nt] = slot_row<NT>(p, gi, nt * 8 + g8, dense) != nullptr;
       }
     }
-
-    // Activation fragments: lane (g8, cq) holds K [32cq, 32cq+32) of row
-    // nt*8+g8 of this unit. Small NT preloads all of them before the wait.
-    constexpr bool kPreload = NT <= 1;
-    uint4 bx[kPreload ? NT : 1][4];
-    if constexpr (kPreload) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        if (xrow[nt] != nullptr) {
-          const __half* src = xrow[nt] + (long long)kc * kUnitK + 32 * cq;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) bx[nt][q] = ldg_u128(src + 8 * q);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) bx[nt][q] = make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
-    }
-    auto load_b = [&](int nt, int q) -> uint4 {
-      if constexpr (kPreload) {
-        return bx[nt][q];
-      } else {
-        if (xrow[nt] == nullptr) return make_uint4(0u, 0u, 0u, 0u);
-        return ldg_u128(xrow[nt] + (long long)kc * kUnitK + 32 * cq + 8 * q);
-      }
-    };
 
     float s_top = 1.f, s_bot = 1.f;
     float gs = 1.f;
@@ -293,7 +313,12 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
       ok = false;
     }
     if (ok) {
-      const uint8_t* stage = smem + (size_t)s * UB;
+      const uint8_t* stage = smem + (size_t)s * L::kStage;
+      const uint8_t* xt = stage + UB + g8 * kRowStride;
+      auto load_b = [&](int nt, int q) -> uint4 {
+        if (!valid[nt]) return make_uint4(0u, 0u, 0u, 0u);
+        return ld_shared_u128(xt + nt * 8 * kRowStride + chunk_pos(4 * cq + q));
+      };
       float t[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -305,10 +330,23 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           wa[q] = ld_shared_u128(stage + warp * 2048 + q * 512 + lane * 16);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        uint4 bpre[NT <= 1 ? 4 : 1];
+        if constexpr (NT <= 1) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) bpre[q] = load_b(0, q);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
+          uint4 b[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if constexpr (NT <= 1)
+              b[nt] = bpre[q];
+            else
+              b[nt] = load_b(nt, q);
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t top = h ? wa[q].y : wa[q].x;
@@ -319,11 +357,13 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
             a[2] = e4m3x2_to_f16x2((uint16_t)(top >> 16));
             a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const uint4 b = load_b(nt, q);
-              mma_16816(t[nt], a, h ? b.z : b.x, h ? b.w : b.y);
-            }
+            for (int nt = 0; nt < NT; ++nt)
+              mma_16816(t[nt], a, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
           }
+        }
+        if constexpr (NT > 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -336,8 +376,13 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
         const uint4 ct = ld_shared_u128(stage + warp * 1024 + lane * 32);
         const uint4 cb = ld_shared_u128(stage + warp * 1024 + lane * 32 + 16);
         const uint32_t sc = ld_shared_u32(stage + 8192 + warp * 128 + lane * 4);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        uint4 bpre[NT <= 1 ? 4 : 1];
+        if constexpr (NT <= 1) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) bpre[q] = load_b(0, q);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
         // Group scales: fp16_rne(float(e4m3) * global), the single rounding
         // the reference applies (quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:40-45).
         const uint32_t st2 = e4m3x2_to_f16x2((uint16_t)(sc & 0xffffu));
@@ -357,6 +402,14 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
           e2m1x8_to_f16x2x4(cbw[m], wb);
           const uint32_t sct = st[m >> 1];
           const uint32_t scb = sb[m >> 1];
+          uint4 b[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if constexpr (NT <= 1)
+              b[nt] = bpre[m];
+            else
+              b[nt] = load_b(nt, m);
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t a[4];
@@ -364,13 +417,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
             a[1] = hmul2_u32(wb[2 * h], scb);
             a[2] = hmul2_u32(wt[2 * h + 1], sct);
             a[3] = hmul2_u32(wb[2 * h + 1], scb);
-            // k-step j = 2m + h uses activation words 2j, 2j+1 = uint4 m, half h
+            // k-step j = 2m + h uses activation chunk m, half h
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const uint4 b = load_b(nt, m);
-              mma_16816(t[nt], a, h ? b.z : b.x, h ? b.w : b.y);
-            }
+            for (int nt = 0; nt < NT; ++nt)
+              mma_16816(t[nt], a, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
           }
+        }
+        if constexpr (NT > 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -429,8 +484,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value) stream_gemm_ke
 
 template <int Q, int NT>
 cudaError_t launch_one(const StreamParams& p, int grid, cudaStream_t stream) {
-  constexpr uint32_t UB = UnitBytes<Q>::value;
-  const size_t smem = (size_t)kStages * UB + 2 * kStages * sizeof(uint64_t) + 16;
+  const size_t smem = Layout<Q, NT>::kSmem;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -441,13 +495,12 @@ cudaError_t launch_one(const StreamParams& p, int grid, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
-  stream_gemm_kernel<Q, NT><<<grid, kThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(stream_gemm_kernel<Q, NT>, dim3(grid), dim3(kThreads), smem, stream, p);
 }
 
 }  // namespace
 
-int stream_gemm_ctas_per_sm(int nt) { return nt >= 4 ? CtasPerSm<4>::value : CtasPerSm<1>::value; }
+int stream_gemm_ctas_per_sm(int nt) { return nt >= 8 ? CtasPerSm<8>::value : CtasPerSm<1>::value; }
 
 cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int grid,
                                cudaStream_t stream) {
