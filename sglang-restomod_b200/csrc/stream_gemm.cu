@@ -207,17 +207,32 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     const uint64_t pol_x = l2_policy_evict_last();
     const __half* rows[kPerLane];
     uint32_t row_bytes = 0;
-    long long cur_pair = -1;
+    // (group, row block, K unit) of u0; advanced by counters, not divisions.
+    long long pair = u0 / kch;
+    int kc = (int)(u0 - pair * kch);
+    long long gi = pair / nrb;
+    int rb = (int)(pair - gi * nrb);
+    bool new_pair = true;
+    int e = 0;
     int i = 0;
     for (long long u = u0; u < u1; ++u) {
-      const long long pair = u / kch;
-      const int kc = (int)(u - pair * kch);
-      const long long gi = pair / nrb;
-      const int rb = (int)(pair - gi * nrb);
-      const int e = dense ? 0 : p.expert_ids[gi];
-      if (e < 0 || e >= p.E) continue;
-      if (pair != cur_pair) {
-        cur_pair = pair;
+      if (u != u0) {
+        if (++kc == kch) {
+          kc = 0;
+          new_pair = true;
+          if (++rb == nrb) {
+            rb = 0;
+            ++gi;
+          }
+        }
+      }
+      if (new_pair) e = dense ? 0 : p.expert_ids[gi];
+      if (e < 0 || e >= p.E) {
+        new_pair = false;
+        continue;
+      }
+      if (new_pair) {
+        new_pair = false;
         int count = 0;
 #pragma unroll
         for (int r = 0; r < kPerLane; ++r) {
@@ -264,22 +279,35 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   const int cq = lane & 3;
   float acc[NT][4];
   bool valid[NT];
-  long long cur_pair = -1;
+  long long pair = u0 / kch;
+  int kc = (int)(u0 - pair * kch);
+  long long gi = pair / nrb;
+  int rb = (int)(pair - gi * nrb);
+  bool new_pair = true;
+  int e = 0;
   int i = 0;
 
   for (long long u = u0; u < u1; ++u) {
-    const long long pair = u / kch;
-    const int kc = (int)(u - pair * kch);
-    const long long gi = pair / nrb;
-    const int rb = (int)(pair - gi * nrb);
-    const int e = dense ? 0 : p.expert_ids[gi];
+    if (u != u0) {
+      if (++kc == kch) {
+        kc = 0;
+        new_pair = true;
+        ++pair;
+        if (++rb == nrb) {
+          rb = 0;
+          ++gi;
+        }
+      }
+    }
+    if (new_pair) e = dense ? 0 : p.expert_ids[gi];
     if (e < 0 || e >= p.E) {
-      if (e >= p.E && kc == 0 && rb == 0 && warp == 0 && lane == 0) atomicOr(p.status, kDevBadExpert);
+      if (new_pair && e >= p.E && rb == 0 && warp == 0 && lane == 0) atomicOr(p.status, kDevBadExpert);
+      new_pair = false;
       continue;
     }
 
-    if (pair != cur_pair) {
-      cur_pair = pair;
+    if (new_pair) {
+      new_pair = false;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -319,11 +347,14 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         if (!valid[nt]) return make_uint4(0u, 0u, 0u, 0u);
         return ld_shared_u128(xt + nt * 8 * kRowStride + chunk_pos(4 * cq + q));
       };
-      float t[NT][4];
+      // NT == 1 keeps two accumulators (even / odd K-steps) so the MMA
+      // chain is half as long; wider tiles already interleave NT chains.
+      constexpr int kChains = NT == 1 ? 2 : 1;
+      float t[NT * kChains][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+      for (int c = 0; c < NT * kChains; ++c)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) t[nt][r] = 0.f;
+        for (int r = 0; r < 4; ++r) t[c][r] = 0.f;
 
       if constexpr (Q == kQuantFp8Block) {
         uint4 wa[4];
@@ -358,12 +389,17 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
             a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-              mma_16816(t[nt], a, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
+              mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                        h ? b[nt].w : b[nt].y);
           }
         }
         if constexpr (NT > 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if constexpr (kChains == 2) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) t[0][r] += t[1][r];
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -420,12 +456,17 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
             // k-step j = 2m + h uses activation chunk m, half h
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-              mma_16816(t[nt], a, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
+              mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                        h ? b[nt].w : b[nt].y);
           }
         }
         if constexpr (NT > 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if constexpr (kChains == 2) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) t[0][r] += t[1][r];
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
