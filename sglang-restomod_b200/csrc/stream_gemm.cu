@@ -45,7 +45,8 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 4;
+constexpr int kSmemPerSm = 233472;  // 228 KiB of shared memory per SM
+constexpr int kSmemReserved = 1024; // per CTA, kept by the system
 constexpr int kRowStride = 304;  // bytes per activation row in the tile
 constexpr int kHalf1 = 160;      // offset of the row's second 128 bytes
 
@@ -65,12 +66,19 @@ struct UnitBytes<kQuantNvfp4> {
   static constexpr uint32_t value = kFp4UnitBytes;
 };
 
+// Stage = one weight unit + its activation tile. As many stages as fit when
+// CtasPerSm<NT> CTAs share an SM (capped at 8): 6 for FP8 with 8 rows, 5 with
+// 16, 4 with 32, 8 for the smaller NVFP4 units.
 template <int Q, int NT>
 struct Layout {
   static constexpr uint32_t kW = UnitBytes<Q>::value;
   static constexpr uint32_t kX = 8 * NT * kRowStride;
   static constexpr uint32_t kStage = (kW + kX + 127) / 128 * 128;
-  static constexpr size_t kSmem = (size_t)kStages * kStage + 2 * kStages * sizeof(uint64_t) + 16;
+  static constexpr int kBudget = kSmemPerSm / CtasPerSm<NT>::value - kSmemReserved - 128;
+  static constexpr int kFit = kBudget / (int)kStage;
+  static constexpr int kS = kFit > 8 ? 8 : kFit;
+  static constexpr size_t kSmem = (size_t)kS * kStage + 2 * kS * sizeof(uint64_t) + 16;
+  static_assert(kS >= 2, "stage does not fit");
 };
 
 __device__ __forceinline__ int chunk_pos(int j) { return j * 16 + (j >= 8 ? kHalf1 - 128 : 0); }
@@ -162,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   constexpr uint32_t UB = L::kW;
   constexpr int kRows = 8 * NT;
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kStages = L::kS;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * L::kStage);
   uint64_t* empty = full + kStages;
   volatile int* flag = reinterpret_cast<volatile int*>(empty + kStages);
@@ -182,8 +191,11 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     fence_mbar_init();
   }
   __syncthreads();
-  // Routing, activations and the workspace come from earlier kernels.
-  griddep_wait();
+  // Routing, activations and the workspace come from earlier kernels: every
+  // thread waits for them before its first global read of such data. Only the
+  // dense producer runs ahead, prefetching static weights into L2.
+  const bool early_producer = dense && warp == kConsumerWarps;
+  if (!early_producer) griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
 
   long long groups;
@@ -198,10 +210,24 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   const long long G = gridDim.x;
   const long long u0 = (long long)blockIdx.x * U / G;
   const long long u1 = ((long long)blockIdx.x + 1) * U / G;
-  if (u0 >= u1) return;
+  if (u0 >= u1) {
+    if (early_producer) griddep_wait();
+    return;
+  }
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
+    if (early_producer) {
+      // Dense units of one CTA are contiguous in memory: pull the first ones
+      // into L2 while the previous kernel finishes.
+      if (lane == 0) {
+        const long long pre = (u1 - u0) < 2 * kStages ? (u1 - u0) : 2 * kStages;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wq + u0 * (long long)UB),
+                     "r"((uint32_t)(pre * UB))
+                     : "memory");
+      }
+      griddep_wait();
+    }
     constexpr int kPerLane = (kRows + 31) / 32;
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
@@ -361,10 +387,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           wa[q] = ld_shared_u128(stage + warp * 2048 + q * 512 + lane * 16);
-        uint4 bpre[NT <= 1 ? 4 : 1];
-        if constexpr (NT <= 1) {
+        // Small tiles copy their activation fragments out and release the
+        // stage at once; wider tiles read them during the MMA loop.
+        constexpr bool kPre = NT <= 2;
+        uint4 bpre[kPre ? NT : 1][4];
+        if constexpr (kPre) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) bpre[q] = load_b(0, q);
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -373,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
           uint4 b[NT];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (NT <= 1)
-              b[nt] = bpre[q];
+            if constexpr (kPre)
+              b[nt] = bpre[nt][q];
             else
               b[nt] = load_b(nt, q);
           }
@@ -393,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
                         h ? b[nt].w : b[nt].y);
           }
         }
-        if constexpr (NT > 1) {
+        if constexpr (!kPre) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -412,10 +443,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         const uint4 ct = ld_shared_u128(stage + warp * 1024 + lane * 32);
         const uint4 cb = ld_shared_u128(stage + warp * 1024 + lane * 32 + 16);
         const uint32_t sc = ld_shared_u32(stage + 8192 + warp * 128 + lane * 4);
-        uint4 bpre[NT <= 1 ? 4 : 1];
-        if constexpr (NT <= 1) {
+        // Small tiles copy their activation fragments out and release the
+        // stage at once; wider tiles read them during the MMA loop.
+        constexpr bool kPre = NT <= 2;
+        uint4 bpre[kPre ? NT : 1][4];
+        if constexpr (kPre) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) bpre[q] = load_b(0, q);
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -441,8 +477,8 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
           uint4 b[NT];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (NT <= 1)
-              b[nt] = bpre[m];
+            if constexpr (kPre)
+              b[nt] = bpre[nt][m];
             else
               b[nt] = load_b(nt, m);
           }
@@ -460,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
                         h ? b[nt].w : b[nt].y);
           }
         }
-        if constexpr (NT > 1) {
+        if constexpr (!kPre) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
         }
