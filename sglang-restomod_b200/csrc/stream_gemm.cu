@@ -45,6 +45,19 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
+// Tuning knobs (compile-time). The defaults are the best of a same-box A/B:
+// more stages, register preloading of 16-row activation tiles, and an L2
+// prefetch ahead of the PDL wait each measured slower.
+#ifndef B200_STREAM_MAX_STAGES
+#define B200_STREAM_MAX_STAGES 4
+#endif
+#ifndef B200_STREAM_PRELOAD_NT
+#define B200_STREAM_PRELOAD_NT 1
+#endif
+#ifndef B200_STREAM_DENSE_PREFETCH
+#define B200_STREAM_DENSE_PREFETCH 0
+#endif
+
 constexpr int kSmemPerSm = 233472;  // 228 KiB of shared memory per SM
 constexpr int kSmemReserved = 1024; // per CTA, kept by the system
 constexpr int kRowStride = 304;  // bytes per activation row in the tile
@@ -66,9 +79,8 @@ struct UnitBytes<kQuantNvfp4> {
   static constexpr uint32_t value = kFp4UnitBytes;
 };
 
-// Stage = one weight unit + its activation tile. As many stages as fit when
-// CtasPerSm<NT> CTAs share an SM (capped at 8): 6 for FP8 with 8 rows, 5 with
-// 16, 4 with 32, 8 for the smaller NVFP4 units.
+// Stage = one weight unit + its activation tile; as many stages as fit when
+// CtasPerSm<NT> CTAs share an SM, capped at B200_STREAM_MAX_STAGES.
 template <int Q, int NT>
 struct Layout {
   static constexpr uint32_t kW = UnitBytes<Q>::value;
@@ -76,7 +88,7 @@ struct Layout {
   static constexpr uint32_t kStage = (kW + kX + 127) / 128 * 128;
   static constexpr int kBudget = kSmemPerSm / CtasPerSm<NT>::value - kSmemReserved - 128;
   static constexpr int kFit = kBudget / (int)kStage;
-  static constexpr int kS = kFit > 8 ? 8 : kFit;
+  static constexpr int kS = kFit > B200_STREAM_MAX_STAGES ? B200_STREAM_MAX_STAGES : kFit;
   static constexpr size_t kSmem = (size_t)kS * kStage + 2 * kS * sizeof(uint64_t) + 16;
   static_assert(kS >= 2, "stage does not fit");
 };
@@ -194,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   // Routing, activations and the workspace come from earlier kernels: every
   // thread waits for them before its first global read of such data. Only the
   // dense producer runs ahead, prefetching static weights into L2.
-  const bool early_producer = dense && warp == kConsumerWarps;
+  const bool early_producer = B200_STREAM_DENSE_PREFETCH && dense && warp == kConsumerWarps;
   if (!early_producer) griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
 
@@ -389,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
           wa[q] = ld_shared_u128(stage + warp * 2048 + q * 512 + lane * 16);
         // Small tiles copy their activation fragments out and release the
         // stage at once; wider tiles read them during the MMA loop.
-        constexpr bool kPre = NT <= 2;
+        constexpr bool kPre = NT <= B200_STREAM_PRELOAD_NT;
         uint4 bpre[kPre ? NT : 1][4];
         if constexpr (kPre) {
 #pragma unroll
@@ -445,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         const uint32_t sc = ld_shared_u32(stage + 8192 + warp * 128 + lane * 4);
         // Small tiles copy their activation fragments out and release the
         // stage at once; wider tiles read them during the MMA loop.
-        constexpr bool kPre = NT <= 2;
+        constexpr bool kPre = NT <= B200_STREAM_PRELOAD_NT;
         uint4 bpre[kPre ? NT : 1][4];
         if constexpr (kPre) {
 #pragma unroll
