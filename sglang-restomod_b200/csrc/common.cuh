@@ -112,6 +112,20 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), tracked by an
+// mbarrier through cp_async_arrive_noinc below.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+// The barrier's expected count must include this arrival (noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // ---------------------------------------- programmatic dependent launch
 // A kernel launched with programmatic stream serialization may start while
 // the previous kernel in the stream is still running. It must execute

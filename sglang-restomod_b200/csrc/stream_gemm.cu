@@ -18,10 +18,10 @@
 //     space evenly across CTAs (stream-K). Each CTA runs one producer warp and
 //     8 consumer warps over a 4-stage shared-memory ring tracked by mbarriers.
 //     For every unit the producer issues one cp.async.bulk (TMA) of the weight
-//     unit (L2 evict-first) and, per activation row of the group, two 128-byte
-//     bulk copies of the row's 128-K slice into a padded tile (row stride
+//     unit (L2 evict-first), and its 32 lanes copy the group's activation rows
+//     (128-K slices) with 16-byte cp.async into a padded tile (row stride
 //     304 B, second half at +160 B: bank-conflict-free for the consumers'
-//     16-byte reads).
+//     16-byte reads). Both kinds of copy complete on the stage's mbarrier.
 //   * A consumer warp owns 16 weight rows of the unit. It converts its bytes
 //     with the hardware cvt.rn.f16x2.{e4m3x2,e2m1x2} instructions straight
 //     into m16n8k16 A fragments and multiplies them against f16 activation
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + 32);  // TMA expect_tx arrive + one cp.async arrive per lane
       mbar_init(&empty[s], kConsumerWarps);
     }
     *abort_flag = 0;
@@ -240,11 +240,18 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       }
       griddep_wait();
     }
-    constexpr int kPerLane = (kRows + 31) / 32;
+    // Activation rows go through per-lane 16-byte cp.async copies, which
+    // signal the stage barrier when they land (one arrival per lane); many
+    // small bulk copies would bottleneck the TMA engine. With kRows <= 32,
+    // kLanesPerRow lanes share a tile row, each copying kChunks 16-byte
+    // chunks of its 256 bytes; with 64 rows every lane owns two rows.
+    constexpr int kRowsPerLane = kRows > 32 ? kRows / 32 : 1;
+    constexpr int kLanesPerRow = kRows >= 32 ? 1 : 32 / kRows;
+    constexpr int kChunks = 16 / kLanesPerRow;
+    const int my_row0 = kRows >= 32 ? lane : lane / kLanesPerRow;
+    const int my_chunk0 = kRows >= 32 ? 0 : (lane % kLanesPerRow) * kChunks;
     const uint64_t pol_w = l2_policy_evict_first();
-    const uint64_t pol_x = l2_policy_evict_last();
-    const __half* rows[kPerLane];
-    uint32_t row_bytes = 0;
+    const __half* rows[kRowsPerLane];
     // (group, row block, K unit) of u0; advanced by counters, not divisions.
     long long pair = u0 / kch;
     int kc = (int)(u0 - pair * kch);
@@ -271,14 +278,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       }
       if (new_pair) {
         new_pair = false;
-        int count = 0;
 #pragma unroll
-        for (int r = 0; r < kPerLane; ++r) {
-          const int slot = lane + 32 * r;
-          rows[r] = slot < kRows ? slot_row<NT>(p, gi, slot, dense) : nullptr;
-          count += __popc(__ballot_sync(0xffffffffu, rows[r] != nullptr));
-        }
-        row_bytes = (uint32_t)count * 256u;
+        for (int r = 0; r < kRowsPerLane; ++r)
+          rows[r] = slot_row<NT>(p, gi, my_row0 + 32 * r, dense);
       }
       const int s = i % kStages;
       if (i >= kStages) {
@@ -289,21 +291,20 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       }
       uint8_t* stage = smem + (size_t)s * L::kStage;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], UB + row_bytes);
+        mbar_arrive_expect_tx(&full[s], UB);
         const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + kc) * (long long)UB;
         bulk_g2s(stage, src, UB, &full[s], pol_w);
       }
-      __syncwarp();
 #pragma unroll
-      for (int r = 0; r < kPerLane; ++r) {
+      for (int r = 0; r < kRowsPerLane; ++r) {
         if (rows[r] != nullptr) {
-          const int slot = lane + 32 * r;
-          const __half* src = rows[r] + (long long)kc * kUnitK;
-          uint8_t* dst = stage + UB + slot * kRowStride;
-          bulk_g2s(dst, src, 128, &full[s], pol_x);
-          bulk_g2s(dst + kHalf1, src + 64, 128, &full[s], pol_x);
+          const __half* src = rows[r] + (long long)kc * kUnitK + my_chunk0 * 8;
+          uint8_t* dst = stage + UB + (my_row0 + 32 * r) * kRowStride;
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) cp_async_16(dst + chunk_pos(my_chunk0 + c), src + c * 8);
         }
       }
+      cp_async_arrive_noinc(&full[s]);
       ++i;
     }
     return;
