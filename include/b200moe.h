@@ -159,6 +159,25 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
                 int64_t workspace_bytes, void* stream);
 
 /*
+ * b200_linear for callers that cannot allocate device memory (an engine that
+ * reserved all of it for its own pool before loading this library, a binding
+ * with no access to the device allocator). No counterpart in the reference:
+ * this entry point exists only for such callers. Same arguments and result
+ * as b200_linear, without the workspace: it uses a 16 MiB array compiled
+ * into the library (held on every device that loads it, until exit), which
+ * covers the fixed workspace on a 148-SM B200 plus up to about 3.5 M bf16
+ * activation elements (M*K) to convert; larger bf16 calls are refused with
+ * B200_ERR_INVALID (f16 activations need no conversion room). The array is
+ * shared: calls on one device must not overlap on the GPU. The first call
+ * on each device looks up the array's address (cudaGetSymbolAddress); make
+ * it before any stream capture. Calls no cudaMalloc / cudaFree.
+ */
+int64_t b200_linear_noalloc_scratch_bytes(void);
+int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                        const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                        int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* stream);
+
+/*
  * Grouped expert GEMM routed by moe_align_block_size output, with the
  * semantics of moe_wna16_marlin_gemm (quant/sm70_fp4_moe/method.py:385-564):
  * route slot p of block b multiplies activation row sorted_token_ids[p] /

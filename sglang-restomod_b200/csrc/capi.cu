@@ -150,6 +150,11 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
 
 }  // namespace
 
+int b200::set_last_error(int code, const char* message) {
+  g_last_error = message;
+  return code;
+}
+
 extern "C" {
 
 int b200_abi_version(void) { return 1; }

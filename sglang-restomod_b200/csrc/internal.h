@@ -78,4 +78,7 @@ cudaError_t launch_prepack_nvfp4(const uint8_t* w, const uint8_t* scales, long l
 
 int device_sm_count();
 
+// Records `message` as this thread's b200_last_error() and returns `code`.
+int set_last_error(int code, const char* message);
+
 }  // namespace b200

@@ -72,6 +72,12 @@ SIGNATURES = {
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
          c_int32, c_void_p, c_int32, c_void_p, c_int64, c_void_p],
     ),
+    "b200_linear_noalloc_scratch_bytes": (c_int64, []),
+    "b200_linear_noalloc": (
+        c_int32,
+        [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
+         c_int32, c_void_p, c_int32, c_void_p],
+    ),
     "b200_moe_gemm": (
         c_int32,
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int32,
