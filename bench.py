@@ -494,10 +494,12 @@ def main() -> int:
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("bench_timed")
     start.record(stream)
     for _ in range(args.steps):
         step_fn()
     end.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     sampler.stop()
@@ -543,7 +545,7 @@ def main() -> int:
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
         traffic = None
         tfile = ROOT / "profiles" / "traffic.json"
-        if tfile.is_file():
+        if tfile.is_file() and world == 1:
             traffic = json.loads(tfile.read_text()).get(args.workload)
         roofline = {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": hbm_gbs,
                     "unit": "GB/s", "frac": achieved / hbm_gbs, "traffic": traffic,
