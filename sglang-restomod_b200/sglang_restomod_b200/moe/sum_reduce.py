@@ -1,0 +1,44 @@
+"""``moe_sum_reduce`` on the B200 kernel.
+
+Same contract as the reference's Triton replacement for the op missing from
+``sgl_kernel`` (``sglang_restomod/quant/sm70_fp4_moe/sum_reduce.py:84-123``):
+``output[t] = routed_scaling_factor * sum_k input[t, k]`` in fp32, stored in
+the input dtype. Non-contiguous tensors are refused rather than silently
+taking another path.
+"""
+
+from __future__ import annotations
+
+import logging
+import sys
+
+logger = logging.getLogger(__name__)
+
+
+def moe_sum_reduce(input_tensor, output_tensor, routed_scaling_factor=1.0):
+    from .. import ops
+
+    return ops.moe_sum_reduce(input_tensor, output_tensor, float(routed_scaling_factor))
+
+
+def install() -> bool:
+    """Bind the replacement wherever the installed sgl_kernel lacks the op,
+    including modules that imported the name before this ran."""
+    try:
+        import sgl_kernel
+        import sgl_kernel.moe as sgl_moe
+    except ImportError:
+        return False
+    original = getattr(sgl_moe, "moe_sum_reduce", None)
+    sgl_kernel.moe_sum_reduce = moe_sum_reduce
+    sgl_moe.moe_sum_reduce = moe_sum_reduce
+    if original is not None:
+        for module in list(sys.modules.values()):
+            if module is None:
+                continue
+            try:
+                if getattr(module, "moe_sum_reduce", None) is original:
+                    setattr(module, "moe_sum_reduce", moe_sum_reduce)
+            except Exception:  # noqa: BLE001 - partially imported modules
+                continue
+    return True

@@ -1,0 +1,138 @@
+"""Host-side logic of the plugin surface, without a GPU (the reference's CPU
+test strategy: registry, attestation, mode switches, shape guards)."""
+
+from __future__ import annotations
+
+import json
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from sglang_restomod_b200 import attest, plugins
+from tests.conftest import load_golden
+
+
+@pytest.fixture(autouse=True)
+def _fresh_attest():
+    attest.reset()
+    yield
+    attest.reset()
+
+
+def test_selection_parses_dedups_and_refuses_unknown():
+    env = {plugins.ENV_COMPONENTS: " fp8_moe, fp8_dense,fp8_moe ,, "}
+    assert plugins.selection(env) == ["fp8_moe", "fp8_dense"]
+    assert plugins.selection({}) == []
+    with pytest.raises(ValueError, match="unknown component"):
+        plugins.selection({plugins.ENV_COMPONENTS: "fp8_moe,bogus"})
+    with pytest.raises(ValueError, match="not part of the B200 MoE/GEMV path"):
+        plugins.selection({plugins.ENV_COMPONENTS: "attention_v100"})
+
+
+def test_load_enabled_records_every_outcome(tmp_path, monkeypatch):
+    # On a machine without a B200 each selected component registers but is inactive.
+    monkeypatch.setenv(attest.ENV_ATTEST, str(tmp_path / "attest.json"))
+    names = ["fp8_moe", "fp4_moe", "fp8_dense", "moe_align_sm70", "fp8_dense_quant", "fp4_dense"]
+    loaded = plugins.load_enabled({plugins.ENV_COMPONENTS: ",".join(names)})
+    assert loaded == names
+    snap = json.loads((tmp_path / "attest.json").read_text())
+    assert snap["selected"] == names
+    assert sorted(snap["inactive"]) == sorted(names)
+    assert snap["failed"] == [] and snap["missing"] == []
+    assert "inactive" in snap["components"]["fp8_moe"]["detail"]
+
+
+def test_forced_mode_on_a_non_b200_host_is_a_recorded_failure(monkeypatch):
+    monkeypatch.setenv("SGLANG_B200_FP8_MOE", "on")
+    loaded = plugins.load_enabled({plugins.ENV_COMPONENTS: "fp8_moe,fp8_dense"})
+    snap = attest.snapshot()
+    assert "fp8_moe" in snap["failed"] and "fp8_moe" not in loaded
+    assert "requires a B200" in snap["components"]["fp8_moe"]["detail"]
+    assert "fp8_dense" in loaded  # one failure does not take the others down
+
+
+def test_unknown_mode_value_raises(monkeypatch):
+    from sglang_restomod_b200._common import mode
+
+    monkeypatch.setenv("SGLANG_B200_FP8_MOE", "maybe")
+    with pytest.raises(ValueError, match="auto, on or off"):
+        mode("SGLANG_B200_FP8_MOE")
+    monkeypatch.setenv("SGLANG_B200_FP8_MOE", "OFF")
+    assert mode("SGLANG_B200_FP8_MOE") == "off"
+
+
+def test_attest_inactive_keeps_reason_after_record():
+    attest.inactive("x", "why not")
+    attest.record("x", True)
+    snap = attest.snapshot()
+    assert snap["components"]["x"]["detail"] == "registered, inactive: why not"
+    assert snap["inactive"] == ["x"] and snap["loaded"] == ["x"]
+
+
+def _cfg(**kw):
+    base = dict(activation="silu", is_gated=True, swiglu_limit=None, gemm1_clamp_limit=None,
+                gemm1_alpha=None, gemm1_beta=None, apply_router_weight_on_input=False,
+                no_combine=False, wide_output_scale=1.0, gate_up_input_scale=1.0)
+    base.update(kw)
+    return SimpleNamespace(**base)
+
+
+def test_fp8_moe_method_refuses_what_the_epilogue_cannot_do():
+    from sglang_restomod_b200.quant.fp8_moe.method import B200Fp8MoEMethod
+
+    check = B200Fp8MoEMethod._unsupported_reason
+    assert check(_cfg()) is None
+    assert "activation" in check(_cfg(activation="gelu"))
+    assert check(_cfg(swiglu_limit=7.0)) == "clamped SwiGLU"
+    assert check(_cfg(gemm1_alpha=1.7)) == "SwiGLU alpha/beta"
+    assert "router weight" in check(_cfg(no_combine=True))
+    assert check(_cfg(wide_output_scale=2.0)) == "FP8 range scaling"
+
+
+def test_shape_guards():
+    from sglang_restomod_b200.quant.fp4_moe.method import check_expert_shape
+    from sglang_restomod_b200.quant.fp8_dense import _check_dense_weight_shape
+    from sglang_restomod_b200.quant.fp8_moe import _check_gemm_shape
+
+    with pytest.raises(RuntimeError, match="needs K a multiple of the 128-wide quantization group"):
+        _check_gemm_shape(100, 256)
+    with pytest.raises(RuntimeError, match="needs N a multiple of 256"):
+        _check_gemm_shape(128, 384, gated=True)
+    _check_gemm_shape(128, 384)
+    with pytest.raises(RuntimeError, match="multiples of 128"):
+        check_expert_shape(320, 2560)  # the reference's TP4 shard: not a 128-row multiple
+    with pytest.raises(RuntimeError, match="positive"):
+        _check_dense_weight_shape(0, 128)
+
+
+def test_regroup_unsupported_block_sizes():
+    from sglang_restomod_b200.quant.fp4_moe.method import _regroup
+
+    sentinel = 99
+    # block 48: two blocks (experts 3, 5) holding 2 and 1 real routes
+    sorted_ids = torch.full((96,), sentinel, dtype=torch.int32)
+    sorted_ids[0], sorted_ids[1], sorted_ids[48] = 4, 7, 2
+    expert_ids = torch.tensor([3, 5], dtype=torch.int32)
+    ntpp = torch.tensor([96], dtype=torch.int32)
+    s2, e2, n2, block = _regroup(sorted_ids, expert_ids, ntpp, 48, sentinel)
+    assert block == 64 and e2.tolist() == [3, 5] and int(n2) == 128
+    assert s2[:2].tolist() == [4, 7] and int(s2[64]) == 2 and int((s2 != sentinel).sum()) == 3
+    # block 128 splits into two 64-slot blocks of the same expert
+    sorted_ids = torch.full((128,), sentinel, dtype=torch.int32)
+    sorted_ids[0], sorted_ids[100] = 1, 0
+    s3, e3, n3, block = _regroup(sorted_ids, torch.tensor([6], dtype=torch.int32),
+                                 torch.tensor([128], dtype=torch.int32), 128, sentinel)
+    assert block == 64 and e3.tolist() == [6, 6] and int(n3) == 128
+    assert int(s3[0]) == 1 and int(s3[100]) == 0
+
+
+def test_lm_head_quantizer_matches_reference_golden():
+    from sglang_restomod_b200.quant.fp8_lm_head import _quantize
+
+    g = load_golden("fp8_quant.npz")
+    head = torch.from_numpy(np.ascontiguousarray(g["head"])).view(torch.float16).reshape(256, 256)
+    q, s = _quantize(head)
+    assert np.array_equal(q.view(torch.uint8).numpy().reshape(-1), g["head_q"].reshape(-1))
+    assert np.array_equal(s.numpy(), g["head_s"])
