@@ -28,15 +28,23 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layer import QuantMoELayer, block_size_for
+from .layer import QuantMoELayer, block_size_for  # noqa: F401
 
 
 class ExpertParallelMoE:
-    def __init__(self, local: QuantMoELayer, num_experts: int, rank: int, world: int,
-                 group=None):
+    """``local`` holds this rank's ``num_experts / world`` experts.
+
+    ``local_fn(rows, local_ids[R,1], weights[R,1]) -> weighted rows`` and
+    ``combine_fn(routed[T*k,H], topk_ids, shared) -> out`` default to the
+    library (the local layer and its combine kernel); tests substitute CPU
+    implementations to check the exchange itself over gloo.
+    """
+
+    def __init__(self, local: QuantMoELayer | None, num_experts: int, rank: int, world: int,
+                 group=None, local_fn=None, combine_fn=None, shared_fn=None):
         if num_experts % world:
             raise ValueError(f"{num_experts} experts do not split over {world} ranks")
-        if local.num_experts != num_experts // world:
+        if local is not None and local.num_experts != num_experts // world:
             raise ValueError("local layer must hold num_experts / world experts")
         self.local = local
         self.num_experts = num_experts
@@ -45,6 +53,29 @@ class ExpertParallelMoE:
         self.group = group
         self.experts_per_rank = num_experts // world
         self.last_recv = None  # (rows, local ids, weights) of the last forward
+        self._local_fn = local_fn
+        self._combine_fn = combine_fn
+        self._shared_fn = shared_fn
+
+    def _run_local(self, rows, ids1, w1):
+        if self._local_fn is not None:
+            return self._local_fn(rows, ids1, w1)
+        bs = self.local.block_size or block_size_for(rows.shape[0], self.local.num_experts)
+        return self.local.forward(rows, ids1, w1, block_size=bs, use_shared=False)
+
+    def _combine(self, routed, topk_ids, shared, out):
+        if self._combine_fn is not None:
+            return self._combine_fn(routed, topk_ids, shared)
+        # every route was computed by its owner: no id is dropped here
+        return ops.moe_combine(routed, topk_ids.clamp(min=0), self.num_experts, 1.0,
+                               shared_out=shared, out=out, out_dtype=routed.dtype)
+
+    def _shared(self, x):
+        if self._shared_fn is not None:
+            return self._shared_fn(x)
+        if self.local is not None and self.local.shared is not None:
+            return self.local.shared.forward(x)
+        return None
 
     def dispatch_plan(self, topk_ids: torch.Tensor):
         """(order, send_counts): routes sorted stably by destination rank."""
@@ -55,16 +86,15 @@ class ExpertParallelMoE:
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-        local = self.local
-        shared = local.shared.forward(x) if local.shared is not None else None
-        if self.world == 1:
-            return local.forward(x, topk_ids, topk_weights, out=out, shared_out=shared)
+        shared = self._shared(x)
+        if self.world == 1 and self._local_fn is None:
+            return self.local.forward(x, topk_ids, topk_weights, out=out, shared_out=shared)
 
         tokens, top_k = topk_ids.shape
         order, dest, send_counts = self.dispatch_plan(topk_ids)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        counts = torch.stack([send_counts, recv_counts]).cpu()
+        counts = torch.stack([send_counts, recv_counts]).to("cpu")
         send_split = counts[0].tolist()
         recv_split = counts[1].tolist()
         n_recv = int(sum(recv_split))
@@ -82,15 +112,12 @@ class ExpertParallelMoE:
         if n_recv:
             ids1 = recv_meta[:, :1].contiguous()
             w1 = recv_meta[:, 1:].contiguous().view(torch.float32)
-            bs = local.block_size or block_size_for(n_recv, local.num_experts)
-            done = local.forward(recv_rows, ids1, w1, block_size=bs, use_shared=False)
+            done = self._run_local(recv_rows, ids1, w1).contiguous()
             self.last_recv = (recv_rows, ids1, w1)
         else:
             done = recv_rows
-        back = torch.empty(tokens * top_k, x.shape[1], dtype=x.dtype, device=x.device)
+        back = torch.empty(tokens * top_k, x.shape[1], dtype=done.dtype, device=x.device)
         dist.all_to_all_single(back, done, send_split, recv_split, group=self.group)
         routed = torch.empty_like(back)
         routed.index_copy_(0, order, back)
-        ids_all_valid = topk_ids.clamp(min=0)  # every route was computed by its owner
-        return ops.moe_combine(routed, ids_all_valid, self.num_experts, 1.0, shared_out=shared,
-                               out=out, out_dtype=x.dtype)
+        return self._combine(routed, topk_ids, shared, out)
