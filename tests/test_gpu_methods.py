@@ -78,8 +78,8 @@ def test_fp8_moe_offsets_api(cuda_device):
     experts, n, k, per = 4, 256, 128, 3
     q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=50)
     prepared = fp8_moe.prepare_experts(q, s)
-    x = synth.activations(experts * per + 2, k, cuda_device, seed=51, dtype=torch.float16)
     counts = [per, per + 2, 0, per]
+    x = synth.activations(sum(counts), k, cuda_device, seed=51, dtype=torch.float16)
     offsets = torch.tensor([0, *torch.tensor(counts).cumsum(0).tolist()], dtype=torch.int32,
                            device=cuda_device)
     out = torch.empty(x.shape[0], n // 2, dtype=torch.float16, device=cuda_device)
