@@ -148,6 +148,22 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
   return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream), "stream GEMM launch");
 }
 
+int run_tc(int block, bool x_f16, StreamParams& p, long long max_items, WsView& ws,
+           cudaStream_t stream) {
+  p.ws = ws.partials;
+  p.ws_cnt = ws.counters;
+  p.status = ws.status;
+  long long grid = device_sm_count();
+  if (grid > max_items) grid = max_items;
+  if (grid < 1) grid = 1;
+  return check_cuda(launch_tc_gemm(block, x_f16, p, (int)grid, stream), "tcgen05 GEMM launch");
+}
+
+// Dense rows above this use the tcgen05 GEMM (FP8 weights).
+constexpr int64_t kTcDenseMinRows = 33;
+
+int tc_block_for_rows(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
+
 }  // namespace
 
 int b200::set_last_error(int code, const char* message) {
@@ -312,6 +328,29 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     return fail(B200_ERR_INVALID, "workspace missing, misaligned or smaller than %lld bytes",
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (quant == B200_QUANT_FP8_BLOCK && m >= kTcDenseMinRows) {
+    // Prefill-sized batch: tcgen05 tensor cores, activations read as given.
+    StreamParams p{};
+    const int block = tc_block_for_rows(m);
+    p.wq = w_packed;
+    p.wscale = w_scales;
+    p.x = reinterpret_cast<const __half*>(x);
+    p.ldx = k;
+    p.x_rows = m;
+    p.sorted_ids = nullptr;
+    p.dense_m = (int)m;
+    p.block_m = block;
+    p.E = 1;
+    p.N = (int)n;
+    p.K = (int)k;
+    p.gated = gated_mode != B200_GATED_NONE;
+    p.fuse_act = gated_mode == B200_GATED_FUSED;
+    p.out = y;
+    p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
+    p.out_f16 = y_dtype == B200_DTYPE_F16;
+    const long long items = ((m + block - 1) / block) * (n / 128);
+    return run_tc(block, x_dtype == B200_DTYPE_F16, p, items, ws, st);
+  }
   int64_t used = 0;
   const __half* x16 = nullptr;
   rc = stage_activations(x, x_dtype, m * k, ws, used, &x16, st);
@@ -353,8 +392,10 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   if (rc) return rc;
   if (!valid_dtype16(a_dtype) || !valid_dtype16(c_dtype))
     return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
-  if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
-    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32 or 64, got %d", block_size);
+  const bool tc = quant == B200_QUANT_FP8_BLOCK && tc_gemm_supported(block_size);
+  if (!tc && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+    return fail(B200_ERR_UNSUPPORTED,
+                "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
   if (num_experts <= 0) return fail(B200_ERR_INVALID, "num_experts must be positive");
   if (top_k <= 0) return fail(B200_ERR_INVALID, "top_k must be positive");
   if (a_rows < 0 || num_routes < 0 || num_routes >= (1ll << 31) || expert_capacity < 0)
@@ -380,9 +421,11 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int64_t used = 0;
-  const __half* a16 = nullptr;
-  rc = stage_activations(a, a_dtype, a_rows * k, ws, used, &a16, st);
-  if (rc) return rc;
+  const __half* a16 = reinterpret_cast<const __half*>(a);
+  if (!tc) {
+    rc = stage_activations(a, a_dtype, a_rows * k, ws, used, &a16, st);
+    if (rc) return rc;
+  }
 
   StreamParams p{};
   p.wq = w_packed;
@@ -408,6 +451,7 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.out = c;
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
+  if (tc) return run_tc(block_size, a_dtype == B200_DTYPE_F16, p, (long long)expert_capacity * (n / 128), ws, st);
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
 }
@@ -444,8 +488,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   if (tokens < 0 || top_k <= 0 || num_experts <= 0)
     return fail(B200_ERR_INVALID, "bad tokens/top_k/num_experts");
   if (tokens == 0) return B200_OK;
-  if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
-    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32 or 64, got %d", block_size);
+  const bool tc = quant == B200_QUANT_FP8_BLOCK && tc_gemm_supported(block_size);
+  if (!tc && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+    return fail(B200_ERR_UNSUPPORTED,
+                "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
   if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
       w2_packed == nullptr || out == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
@@ -464,10 +510,12 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   const int64_t cap = numel + busy * (block_size - 1);
   const int64_t blocks = (cap + block_size - 1) / block_size;
   int64_t used = 0;
-  const __half* x16 = nullptr;
-  rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
-  if (rc) return rc;
-  if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+  const __half* x16 = reinterpret_cast<const __half*>(x);
+  if (!tc) {
+    rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
+    if (rc) return rc;
+  }
+  if (tc || x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
   int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(cap * 4);
   int32_t* eids = reinterpret_cast<int32_t*>(ws.scratch + used);
@@ -508,7 +556,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   p.ldo = inter;
   p.out_f16 = 1;
   const int nt = block_size / 8;
-  rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
+  if (tc)
+    rc = run_tc(block_size, x_dtype == B200_DTYPE_F16, p, blocks * (2 * inter / 128), ws, st);
+  else
+    rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
 
   StreamParams q = p;
@@ -527,7 +578,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   q.out = routed;
   q.ldo = hidden;
   q.out_f16 = 1;
-  rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
+  if (tc)
+    rc = run_tc(block_size, true, q, blocks * (hidden / 128), ws, st);
+  else
+    rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;
 
   return b200_moe_combine(routed, B200_DTYPE_F16, topk_ids, num_experts, tokens, top_k, hidden,

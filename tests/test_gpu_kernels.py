@@ -279,3 +279,60 @@ def test_layer_config0(cuda_device, quant):
 def test_layer_config2_decode(cuda_device, quant, tokens):
     sample = None if tokens <= 8 else torch.tensor([0, tokens // 3, tokens - 1])
     _check_layer(synth.CONFIG2, tokens, quant, cuda_device, block=16, sample_tokens=sample, rsf=2.0)
+
+
+# ------------------------------------------------- tcgen05 (prefill) path
+@pytest.mark.parametrize("block", [64, 128, 256])
+@pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED, _lib.GATED_SPLIT])
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16])
+def test_moe_gemm_tcgen05(cuda_device, block, gated_mode, x_dtype):
+    """FP8 expert GEMM on the tensor-core path: many routes per expert."""
+    experts, tokens, top_k, k, n = 5, 150, 3, 384, 512
+    ids, weights = synth.route(tokens, experts, top_k, cuda_device, seed=block + gated_mode)
+    ids[3, 1] = -1
+    x = synth.activations(tokens, k, cuda_device, seed=9, dtype=x_dtype)
+    q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=3)
+    packed = ops.fp8_prepack(q, gated_mode != _lib.GATED_NONE)
+    dense = _stack(_dequant_fp8_bank(q, s), experts)
+    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, block, experts)
+    routes = tokens * top_k
+    cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
+    c = torch.zeros(routes, cols, dtype=x_dtype, device=cuda_device)
+    mul = gated_mode == _lib.GATED_NONE
+    ops.moe_gemm(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, num_experts=experts,
+                 sorted_token_ids=sorted_ids, expert_ids=expert_ids, num_tokens_post_pad=ntpp,
+                 block_size=block, top_k=top_k, num_routes=routes, c=c, scales=s,
+                 topk_weights=weights, mul_topk_weights=mul, gated_mode=gated_mode)
+    want, written = oracle.moe_gemm_ref(
+        x.cpu(), dense, sorted_ids.cpu().numpy(), expert_ids.cpu().numpy(), int(ntpp.item()),
+        block, top_k, routes, weights.cpu(), mul, 1 if gated_mode == _lib.GATED_FUSED else 0,
+    )
+    assert_close(c.cpu()[written], want[written], what=f"tc moe_gemm bs={block} g={gated_mode}")
+    assert ops.workspace_status() == 0
+
+
+@pytest.mark.parametrize("m", [33, 64, 130, 300])
+@pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED])
+def test_fp8_linear_tcgen05(cuda_device, m, gated_mode):
+    k, n = 768, 1024
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=m)
+    x = synth.activations(m, k, cuda_device, seed=4)
+    packed = ops.fp8_prepack(q[0], gated=gated_mode != _lib.GATED_NONE)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0], gated_mode=gated_mode)
+    want = oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu(), gated=gated_mode == _lib.GATED_FUSED)
+    assert_close(y, want, what=f"tc linear m={m} g={gated_mode}")
+
+
+@pytest.mark.parametrize("tokens,block", [(8192, 256), (2048, 64)])
+def test_layer_config2_prefill(cuda_device, tokens, block):
+    sample = torch.tensor([0, 1, tokens // 2, tokens - 1])
+    _check_layer(synth.CONFIG2, tokens, _lib.QUANT_FP8_BLOCK, cuda_device, block=block,
+                 sample_tokens=sample, rsf=1.0)
+
+
+def test_layer_config4_prefill_sampled(cuda_device):
+    """Expert-parallel layer shape (H=7168, I=2048, 256 experts, top-8) at 4096
+    tokens on one GPU; four tokens checked against the oracle."""
+    sample = torch.tensor([0, 1000, 4095])
+    _check_layer(synth.CONFIG4, 4096, _lib.QUANT_FP8_BLOCK, cuda_device, block=256,
+                 sample_tokens=sample, rsf=1.0)
