@@ -186,7 +186,7 @@ int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m
  * (times topk_weights[route] when mul_topk_weights). a: [a_rows, k];
  * c: rows of ldc elements. block_size in {8, 16, 32, 64}; FP8 also takes
  * 128 and 256, and FP8 blocks of 64 and more run on the tcgen05 tensor-core
- * GEMM (activations read as given, bf16 or f16).
+ * GEMM (f16 operands; bf16 activations are converted in the workspace).
  * At most expert_capacity blocks are read, so sorted_token_ids must hold
  * expert_capacity * block_size entries (pass floor(sorted_len / block_size)
  * when the align output is shorter). topk_weights and c need num_routes rows.

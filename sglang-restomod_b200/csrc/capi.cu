@@ -148,15 +148,14 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
   return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream), "stream GEMM launch");
 }
 
-int run_tc(int block, bool x_f16, StreamParams& p, long long max_items, WsView& ws,
-           cudaStream_t stream) {
+int run_tc(int block, StreamParams& p, long long max_items, WsView& ws, cudaStream_t stream) {
   p.ws = ws.partials;
   p.ws_cnt = ws.counters;
   p.status = ws.status;
   long long grid = device_sm_count();
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
-  return check_cuda(launch_tc_gemm(block, x_f16, p, (int)grid, stream), "tcgen05 GEMM launch");
+  return check_cuda(launch_tc_gemm(block, p, (int)grid, stream), "tcgen05 GEMM launch");
 }
 
 // Dense rows above this use the tcgen05 GEMM (FP8 weights).
@@ -329,12 +328,16 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (quant == B200_QUANT_FP8_BLOCK && m >= kTcDenseMinRows) {
-    // Prefill-sized batch: tcgen05 tensor cores, activations read as given.
+    // Prefill-sized batch: tcgen05 tensor cores.
+    int64_t used_tc = 0;
+    const __half* xh = nullptr;
+    rc = stage_activations(x, x_dtype, m * k, ws, used_tc, &xh, st);
+    if (rc) return rc;
     StreamParams p{};
     const int block = tc_block_for_rows(m);
     p.wq = w_packed;
     p.wscale = w_scales;
-    p.x = reinterpret_cast<const __half*>(x);
+    p.x = xh;
     p.ldx = k;
     p.x_rows = m;
     p.sorted_ids = nullptr;
@@ -349,7 +352,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
     p.out_f16 = y_dtype == B200_DTYPE_F16;
     const long long items = ((m + block - 1) / block) * (n / 128);
-    return run_tc(block, x_dtype == B200_DTYPE_F16, p, items, ws, st);
+    return run_tc(block, p, items, ws, st);
   }
   int64_t used = 0;
   const __half* x16 = nullptr;
@@ -421,11 +424,9 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int64_t used = 0;
-  const __half* a16 = reinterpret_cast<const __half*>(a);
-  if (!tc) {
-    rc = stage_activations(a, a_dtype, a_rows * k, ws, used, &a16, st);
-    if (rc) return rc;
-  }
+  const __half* a16 = nullptr;
+  rc = stage_activations(a, a_dtype, a_rows * k, ws, used, &a16, st);
+  if (rc) return rc;
 
   StreamParams p{};
   p.wq = w_packed;
@@ -451,7 +452,7 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.out = c;
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
-  if (tc) return run_tc(block_size, a_dtype == B200_DTYPE_F16, p, (long long)expert_capacity * (n / 128), ws, st);
+  if (tc) return run_tc(block_size, p, (long long)expert_capacity * (n / 128), ws, st);
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
 }
@@ -510,12 +511,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   const int64_t cap = numel + busy * (block_size - 1);
   const int64_t blocks = (cap + block_size - 1) / block_size;
   int64_t used = 0;
-  const __half* x16 = reinterpret_cast<const __half*>(x);
-  if (!tc) {
-    rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
-    if (rc) return rc;
-  }
-  if (tc || x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+  const __half* x16 = nullptr;
+  rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
+  if (rc) return rc;
+  if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
   int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(cap * 4);
   int32_t* eids = reinterpret_cast<int32_t*>(ws.scratch + used);
@@ -557,7 +556,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   p.out_f16 = 1;
   const int nt = block_size / 8;
   if (tc)
-    rc = run_tc(block_size, x_dtype == B200_DTYPE_F16, p, blocks * (2 * inter / 128), ws, st);
+    rc = run_tc(block_size, p, blocks * (2 * inter / 128), ws, st);
   else
     rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
@@ -579,7 +578,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
-    rc = run_tc(block_size, true, q, blocks * (hidden / 128), ws, st);
+    rc = run_tc(block_size, q, blocks * (hidden / 128), ws, st);
   else
     rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;

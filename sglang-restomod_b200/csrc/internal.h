@@ -54,11 +54,10 @@ cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int gri
                                cudaStream_t stream);
 int stream_gemm_ctas_per_sm(int nt);
 
-// tcgen05 grouped GEMM (FP8 weights; bf16 or f16 activations read directly):
-// groups of `block` in {64, 128, 256} rows, p.block_m == block.
+// tcgen05 grouped GEMM (FP8 weights, f16 activations): groups of `block` in
+// {64, 128, 256} rows, p.block_m == block.
 bool tc_gemm_supported(int block);
-cudaError_t launch_tc_gemm(int block, bool x_f16, const StreamParams& p, int grid,
-                           cudaStream_t stream);
+cudaError_t launch_tc_gemm(int block, const StreamParams& p, int grid, cudaStream_t stream);
 
 // moe_align_block_size: stable expert-major counting sort with per-expert
 // padding to block_size.

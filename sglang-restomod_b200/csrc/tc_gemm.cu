@@ -14,10 +14,9 @@
 // stages alternate:
 //   * all 256 threads dequantize the step's 16 KiB FP8 unit (the streamed
 //     layout of prepack.cu, read straight from global, one step ahead in
-//     registers) to bf16(e4m3 * block scale) - the oracle's own dequant
-//     rounding - and store it as the A operand in the K-major 128-byte
-//     swizzled layout;
-//   * they copy the group's activation rows (bf16, gathered through
+//     registers) to f16(e4m3 * block scale) and store it as the A operand in
+//     the K-major 128-byte swizzled layout;
+//   * they copy the group's activation rows (f16, gathered through
 //     sorted_token_ids) into the B operand with 16-byte cp.async, same layout;
 //   * after a proxy fence and a CTA barrier, one thread issues eight
 //     tcgen05.mma (M=128, N=BN, K=16, fp32 accumulate in tensor memory) and
@@ -403,13 +402,14 @@ cudaError_t launch_tc(const StreamParams& p, int grid, cudaStream_t stream) {
 
 bool tc_gemm_supported(int block) { return block == 64 || block == 128 || block == 256; }
 
-// `x_f16`: activations (and the dequantized weights) are f16, else bf16.
-cudaError_t launch_tc_gemm(int block, bool x_f16, const StreamParams& p, int grid,
-                           cudaStream_t stream) {
+// Operands are f16: the weights dequantized as f16(e4m3 * scale), whose
+// rounding (2^-11) keeps long-K sums as close to the exact dequantized
+// product as the decode path; bf16 activations are converted by the caller.
+cudaError_t launch_tc_gemm(int block, const StreamParams& p, int grid, cudaStream_t stream) {
   switch (block) {
-    case 64: return x_f16 ? launch_tc<64, true>(p, grid, stream) : launch_tc<64, false>(p, grid, stream);
-    case 128: return x_f16 ? launch_tc<128, true>(p, grid, stream) : launch_tc<128, false>(p, grid, stream);
-    case 256: return x_f16 ? launch_tc<256, true>(p, grid, stream) : launch_tc<256, false>(p, grid, stream);
+    case 64: return launch_tc<64, true>(p, grid, stream);
+    case 128: return launch_tc<128, true>(p, grid, stream);
+    case 256: return launch_tc<256, true>(p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
