@@ -51,11 +51,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int64_t kAlign = 256;
 int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-// Workspace layout: [status int | pad] [counters, kMaxSlots ints] [partials,
-// slots x kWsSlotFloats fp32] [scratch ...]
+// Workspace layout: [status int | pad] [counters, kMaxSlots ints] [tcgen05
+// GEMM plan] [partials, slots x kWsSlotFloats fp32] [scratch ...]
 constexpr int64_t kStatusBytes = 256;
 constexpr int kMaxSlots = 1024;
 constexpr int64_t kCounterBytes = kMaxSlots * 4;
+constexpr int kTcPlanCap = 32768;  // route-slot groups the tcgen05 path plans for
+int64_t plan_region_bytes() { return align_up(tc_plan_bytes(kTcPlanCap)); }
 
 int max_grid_slots() {
   int g = stream_gemm_ctas_per_sm(1) * device_sm_count();
@@ -63,12 +65,14 @@ int max_grid_slots() {
 }
 
 int64_t stream_ws_bytes() {
-  return kStatusBytes + kCounterBytes + (int64_t)max_grid_slots() * kWsSlotFloats * 4;
+  return kStatusBytes + kCounterBytes + plan_region_bytes() +
+         (int64_t)max_grid_slots() * kWsSlotFloats * 4;
 }
 
 struct WsView {
   int* status;
   int* counters;
+  void* plan;
   float* partials;
   uint8_t* scratch;
   int64_t scratch_bytes;
@@ -80,7 +84,8 @@ bool carve(void* ws, int64_t bytes, WsView& v) {
   uint8_t* base = reinterpret_cast<uint8_t*>(ws);
   v.status = reinterpret_cast<int*>(base);
   v.counters = reinterpret_cast<int*>(base + kStatusBytes);
-  v.partials = reinterpret_cast<float*>(base + kStatusBytes + kCounterBytes);
+  v.plan = base + kStatusBytes + kCounterBytes;
+  v.partials = reinterpret_cast<float*>(base + kStatusBytes + kCounterBytes + plan_region_bytes());
   v.scratch = base + fixed;
   v.scratch_bytes = bytes - fixed;
   return true;
@@ -148,20 +153,28 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
   return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream), "stream GEMM launch");
 }
 
-int run_tc(int block, StreamParams& p, long long max_items, WsView& ws, cudaStream_t stream) {
+// tcgen05 GEMM; in moe mode the plan is built first unless `planned` (the
+// layer's second GEMM reuses the first one's plan).
+int run_tc(StreamParams& p, WsView& ws, bool planned, cudaStream_t stream) {
   p.ws = ws.partials;
   p.ws_cnt = ws.counters;
   p.status = ws.status;
-  long long grid = device_sm_count();
-  if (grid > max_items) grid = max_items;
-  if (grid < 1) grid = 1;
-  return check_cuda(launch_tc_gemm(block, p, (int)grid, stream), "tcgen05 GEMM launch");
+  if (p.sorted_ids != nullptr && !planned) {
+    int rc = check_cuda(launch_tc_plan(p, ws.plan, kTcPlanCap, stream), "tcgen05 plan launch");
+    if (rc) return rc;
+  }
+  return check_cuda(launch_tc_gemm(p, ws.plan, device_sm_count(), stream), "tcgen05 GEMM launch");
 }
 
 // Dense rows above this use the tcgen05 GEMM (FP8 weights).
 constexpr int64_t kTcDenseMinRows = 33;
 
-int tc_block_for_rows(int64_t m) { return m <= 64 ? 64 : (m <= 128 ? 128 : 256); }
+// Moe calls take the tcgen05 GEMM for FP8 blocks of 64 and more (the
+// prefill regime) when every group fits the plan.
+bool use_tc_moe(int32_t quant, int32_t block_size, int64_t groups) {
+  return quant == B200_QUANT_FP8_BLOCK && block_size >= 64 && tc_gemm_supported(block_size) &&
+         groups <= kTcPlanCap;
+}
 
 }  // namespace
 
@@ -334,7 +347,6 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     rc = stage_activations(x, x_dtype, m * k, ws, used_tc, &xh, st);
     if (rc) return rc;
     StreamParams p{};
-    const int block = tc_block_for_rows(m);
     p.wq = w_packed;
     p.wscale = w_scales;
     p.x = xh;
@@ -342,7 +354,6 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.x_rows = m;
     p.sorted_ids = nullptr;
     p.dense_m = (int)m;
-    p.block_m = block;
     p.E = 1;
     p.N = (int)n;
     p.K = (int)k;
@@ -351,8 +362,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.out = y;
     p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
     p.out_f16 = y_dtype == B200_DTYPE_F16;
-    const long long items = ((m + block - 1) / block) * (n / 128);
-    return run_tc(block, p, items, ws, st);
+    return run_tc(p, ws, false, st);
   }
   int64_t used = 0;
   const __half* x16 = nullptr;
@@ -395,11 +405,12 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   if (rc) return rc;
   if (!valid_dtype16(a_dtype) || !valid_dtype16(c_dtype))
     return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
-  const bool tc = quant == B200_QUANT_FP8_BLOCK && tc_gemm_supported(block_size);
+  const bool tc = use_tc_moe(quant, block_size, expert_capacity);
   if (!tc && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED,
                 "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
-  if (num_experts <= 0) return fail(B200_ERR_INVALID, "num_experts must be positive");
+  if (num_experts <= 0 || num_experts >= (1 << 23))
+    return fail(B200_ERR_INVALID, "num_experts must be in [1, 2^23)");
   if (top_k <= 0) return fail(B200_ERR_INVALID, "top_k must be positive");
   if (a_rows < 0 || num_routes < 0 || num_routes >= (1ll << 31) || expert_capacity < 0)
     return fail(B200_ERR_INVALID, "bad row counts");
@@ -452,7 +463,7 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.out = c;
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
-  if (tc) return run_tc(block_size, p, (long long)expert_capacity * (n / 128), ws, st);
+  if (tc) return run_tc(p, ws, false, st);
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
 }
@@ -489,8 +500,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   if (tokens < 0 || top_k <= 0 || num_experts <= 0)
     return fail(B200_ERR_INVALID, "bad tokens/top_k/num_experts");
   if (tokens == 0) return B200_OK;
-  const bool tc = quant == B200_QUANT_FP8_BLOCK && tc_gemm_supported(block_size);
-  if (!tc && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+  if (num_experts >= (1 << 23)) return fail(B200_ERR_INVALID, "num_experts must be below 2^23");
+  const bool tc_block = quant == B200_QUANT_FP8_BLOCK && block_size >= 64 &&
+                        tc_gemm_supported(block_size);
+  if (!tc_block && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED,
                 "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
   if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
@@ -510,6 +523,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   const int64_t busy = numel < num_experts ? numel : num_experts;
   const int64_t cap = numel + busy * (block_size - 1);
   const int64_t blocks = (cap + block_size - 1) / block_size;
+  const bool tc = use_tc_moe(quant, block_size, blocks);
   int64_t used = 0;
   const __half* x16 = nullptr;
   rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
@@ -556,7 +570,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   p.out_f16 = 1;
   const int nt = block_size / 8;
   if (tc)
-    rc = run_tc(block_size, p, blocks * (2 * inter / 128), ws, st);
+    rc = run_tc(p, ws, false, st);
   else
     rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
@@ -578,7 +592,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
-    rc = run_tc(block_size, q, blocks * (hidden / 128), ws, st);
+    rc = run_tc(q, ws, true, st);
   else
     rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;

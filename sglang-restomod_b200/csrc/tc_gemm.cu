@@ -7,33 +7,84 @@
 // (quant/sm70_fp8_dense/_method.py:713-784).
 //
 // Shape: D[128 weight rows, N tokens] = W_e[128 rows, K] . X[N tokens, K]^T
-// ("swap AB": the weight row block is the MMA's M = 128; the expert's token
-// group is N = 64..256, a multiple of 16, so short groups waste little).
+// ("swap AB": the weight row block is the MMA's M = 128; the tokens are
+// N <= 256). An item is one 128-row weight block of one expert against up to
+// 256 of that expert's route slots: a small pre-kernel (tc_plan_kernel) merges
+// runs of consecutive moe_align blocks of the same expert into items, so an
+// expert's weights are dequantized once per 256 routes, and the item's N is
+// trimmed to its last valid route (rounded up to 16).
 //
-// Per CTA (persistent, one per SM) and per 128-K step, two shared-memory
-// stages alternate:
-//   * all 256 threads dequantize the step's 16 KiB FP8 unit (the streamed
-//     layout of prepack.cu, read straight from global, one step ahead in
-//     registers) to f16(e4m3 * block scale) and store it as the A operand in
-//     the K-major 128-byte swizzled layout;
-//   * they copy the group's activation rows (f16, gathered through
-//     sorted_token_ids) into the B operand with 16-byte cp.async, same layout;
-//   * after a proxy fence and a CTA barrier, one thread issues eight
-//     tcgen05.mma (M=128, N=BN, K=16, fp32 accumulate in tensor memory) and
-//     commits them to the stage's mbarrier; the next step's loads overlap.
-// The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32*(w%4).., half of the columns) and applies SiLU*up (gate/up rows are
-// 8 lanes apart in a gated bank), the router weight, and the store.
-// Waits on MMA completion are bounded; a timeout records an error bit and the
-// CTA still frees its tensor memory before returning.
+// One persistent CTA per SM, 16 warps with fixed roles, coupled only through
+// mbarrier rings (every wait bounded, no named barriers):
+//   warp 0       TMA: 16 KiB FP8 weight units (prepack.cu's streamed layout,
+//                one 128x128 block each) into a 4-deep raw ring, each with
+//                its two f16 scale multipliers;
+//   warp 1       MMA: one thread issues tcgen05.mma (M=128, N<=256, K=16,
+//                f16 x f16 -> f32 in tensor memory), four per 64-K substep,
+//                and commits stage releases and accumulator-ready barriers;
+//   warps 2-3    B: gather the item's activation rows (through
+//                sorted_token_ids) with 16-byte cp.async into a 4-deep ring
+//                of [256 rows][64 K] 128-byte-swizzled tiles; each stage's
+//                full barrier completes as the copies land (cp.async
+//                mbarrier arrive), so four stages are in flight;
+//   warps 4-7    dequant: raw FP8 unit -> two [128 rows][64 K] f16 A tiles,
+//                f16(e4m3) * m, one hmul2 per two values;
+//   warps 8-15   epilogue: tcgen05.ld of a double-buffered accumulator (two
+//                256-column TMEM buffers), 2^E, SiLU*up, router weight and
+//                store, overlapping the next item's main loop; warps 8-11
+//                drain buffer 0 (even items), warps 12-15 buffer 1.
+// The producer and the gather warps load each item's plan entry and route
+// ids one item ahead, so no role waits on global memory at an item boundary.
+//
+// Block scales. A 128x128 block's scale s is split as s = m * 2^E with one
+// power of two E per (expert, 128-row scale block) - the exponent of the
+// largest scale of that row - and m = f16(s * 2^-E) in (0, 2). The weights are
+// dequantized as f16(e4m3 * m) (f16 rounding; values below 2^-24 of the row's
+// largest block scale flush) and the accumulator is multiplied by 2^E exactly.
 #include "common.cuh"
 #include "internal.h"
 
 namespace b200 {
 namespace {
 
-constexpr int kTcThreads = 256;
-constexpr uint32_t kABytes = 128 * 128 * 2;  // bf16 [128 rows][128 K], two 64-K atoms
+constexpr int kNMax = 256;
+// 16 warps: four per SM sub-partition, so each thread may hold 128 registers.
+constexpr int kTcWarps = 16;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
+constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
+constexpr int kLoadPasses = kNMax / (kLoadThreads / 2);  // rows per gather thread
+constexpr int kRawStages = 4;
+constexpr int kAStages = 2;
+constexpr int kBStages = 4;
+constexpr uint32_t kRawBytes = kFp8UnitBytes;  // 16 KiB
+constexpr uint32_t kATile = 128 * 128;          // [128 rows][64 K] f16
+constexpr uint32_t kBTile = kNMax * 128;        // [256 rows][64 K] f16
+constexpr uint32_t kOffRaw = 0;
+constexpr uint32_t kOffA = kOffRaw + kRawStages * kRawBytes;
+constexpr uint32_t kOffB = kOffA + kAStages * kATile;
+constexpr uint32_t kOffCtl = kOffB + kBStages * kBTile;
+constexpr int kInfoSlots = 8;
+constexpr uint32_t kTmemCols = 2 * kNMax;
+constexpr size_t kTcSmem = kOffCtl + 512 + 1024;  // control block + base alignment slack
+
+struct Ctl {
+  uint64_t raw_full[kRawStages];
+  uint64_t raw_empty[kRawStages];
+  uint64_t a_full[kAStages];
+  uint64_t a_empty[kAStages];
+  uint64_t b_full[kBStages];
+  uint64_t b_empty[kBStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t done;
+  uint2 raw_mult[kRawStages];  // f16x2 multipliers (top rows, bottom rows) per raw unit
+  int info[kInfoSlots];        // (item << 9) | N of the item's MMAs, atomicMax-combined
+  uint32_t tmem;
+  int abort;
+};
+static_assert(sizeof(Ctl) <= 512, "control block");
+static_assert(kTcSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO),
@@ -47,11 +98,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
-template <bool F16>
-__host__ __device__ constexpr uint32_t instr_desc(int n) {
-  // f32 accumulate, A/B = bf16 (1) or f16 (0), both K-major, M = 128.
-  return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+__device__ __forceinline__ uint32_t instr_desc_f16(int n) {
+  // f32 accumulate, A/B f16, both K-major, M = 128, N = n.
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -64,8 +113,8 @@ __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n"
       "  .reg .pred p;\n"
@@ -74,6 +123,21 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t 
       "}\n" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
+}
+
+// One lane of the (fully active) warp; the others get false.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n"
+      "  .reg .b32 rx;\n"
+      "  .reg .pred px;\n"
+      "  elect.sync rx|px, %1;\n"
+      "  @px mov.s32 %0, 1;\n"
+      "}\n"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -95,58 +159,147 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void st_shared_u128(void* p, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // Byte offset of 16-byte chunk (row, c16) of a [rows][64 x 16-bit] K-major
-// 128B-swizzled atom.
+// 128B-swizzled tile.
 __device__ __forceinline__ uint32_t sw128_off(int row, int c16) {
   return (uint32_t)row * 128u + (uint32_t)((c16 ^ (row & 7)) << 4);
 }
 
-template <bool F16>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if constexpr (F16) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  } else {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+// 8 E4M3 bytes -> 8 f16 values times the f16x2 multiplier m2.
+__device__ __forceinline__ uint4 dequant8(uint32_t lo, uint32_t hi, uint32_t m2) {
+  uint4 o;
+  o.x = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(lo & 0xffffu)), m2);
+  o.y = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(lo >> 16)), m2);
+  o.z = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(hi & 0xffffu)), m2);
+  o.w = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(hi >> 16)), m2);
+  return o;
+}
+
+// Bounded wait that also gives up once another role of the CTA has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0u) {
+      if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (status) atomicOr(status, kDevWaitTimeout);
+        *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+        return false;
+      }
+    }
   }
 }
 
-// 8 E4M3 bytes (one 64-bit half of a 16-byte chunk) -> 8 16-bit values * s.
-template <bool F16>
-__device__ __forceinline__ uint4 dequant8(uint32_t lo, uint32_t hi, float s) {
-  const uint32_t w[2] = {lo, hi};
-  uint32_t o[4];
+__device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const uint32_t a = e4m3x2_to_f16x2((uint16_t)(w[i] & 0xffffu));
-    const uint32_t b = e4m3x2_to_f16x2((uint16_t)(w[i] >> 16));
-    const __half2 ha = *reinterpret_cast<const __half2*>(&a);
-    const __half2 hb = *reinterpret_cast<const __half2*>(&b);
-    o[2 * i] = pack2<F16>(__low2float(ha) * s, __high2float(ha) * s);
-    o[2 * i + 1] = pack2<F16>(__low2float(hb) * s, __high2float(hb) * s);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
 }
 
-template <int BN, bool F16>
-struct TcLayout {
-  static constexpr uint32_t kB = BN * 256u;  // [BN rows][128 K] 16-bit, two atoms
-  static constexpr uint32_t kStage = kABytes + kB;
-  static constexpr size_t kSmem = 2 * (size_t)kStage + 1024 /*align*/ + 64;
-  static constexpr int kRowsPerThread = BN * 16 / kTcThreads;  // B chunks per thread per step
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;          // power of two >= 32
+// Binary exponent of a scale row's largest |scale|, clamped so that both 2^E
+// and 2^-E are normal floats.
+__device__ __forceinline__ int max_exponent(float mx) {
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127;
+  return e < -126 ? -126 : (e > 126 ? 126 : e);
+}
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+__device__ __forceinline__ uint32_t mult_f16x2(float s, int e) {
+  const uint16_t b = __half_as_ushort(__float2half_rn(s * pow2f(-e)));
+  return (uint32_t)b | ((uint32_t)b << 16);
+}
+
+__device__ __forceinline__ float ldg_or0(const float* p, int k, int kch) {
+  return k < kch ? __ldg(p + k) : 0.f;
+}
+
+// One item of the CTA's walk, decoded identically by every role.
+struct Item {
+  int e;            // expert (0 for dense)
+  int rb;           // 128-row weight block
+  long long slot0;  // first route slot (moe) or first activation row (dense)
+  int rows;         // route slots / rows covered (<= 256)
 };
 
-template <int BN, bool F16>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const StreamParams p) {
-  using L = TcLayout<BN, F16>;
+__device__ __forceinline__ int2 plan_entry(const StreamParams& p, const int2* plan, long long g,
+                                           int nrb) {
+  if (p.sorted_ids == nullptr) return make_int2(0, 0);
+  return __ldg(plan + g / nrb);
+}
+
+__device__ __forceinline__ Item make_item(const StreamParams& p, int2 pe, long long g, int nrb) {
+  Item it;
+  const long long sb = g / nrb;
+  it.rb = (int)(g - sb * nrb);
+  if (p.sorted_ids == nullptr) {
+    it.e = 0;
+    it.slot0 = sb * kNMax;
+    const long long left = (long long)p.dense_m - it.slot0;
+    it.rows = left < kNMax ? (int)left : kNMax;
+  } else {
+    it.e = pe.y >> 8;
+    it.slot0 = (long long)pe.x * p.block_m;
+    it.rows = (pe.y & 0xff) * p.block_m;
+  }
+  return it;
+}
+
+// Scale rows of an item's weight block: the gate row for the top 8 rows of
+// every 16 and the up row for the bottom 8 in a gated bank.
+__device__ __forceinline__ void scale_rows(const StreamParams& p, const Item& it, int kch,
+                                           const float*& top, const float*& bot) {
+  const int nsr = p.N / 128;
+  if (p.gated) {
+    top = p.wscale + ((long long)it.e * nsr + it.rb / 2) * kch;
+    bot = p.wscale + ((long long)it.e * nsr + p.N / 2 / 128 + it.rb / 2) * kch;
+  } else {
+    top = p.wscale + ((long long)it.e * nsr + it.rb) * kch;
+    bot = top;
+  }
+}
+
+// Route id of slot n of the item (-1 past the item), loaded without use.
+__device__ __forceinline__ int slot_id(const StreamParams& p, const Item& it, int n) {
+  if (n >= it.rows) return -1;
+  if (p.sorted_ids == nullptr) return (int)(it.slot0 + n);
+  return __ldg(p.sorted_ids + it.slot0 + n);
+}
+
+// Slot id -> activation row, or -1 for padding / an out-of-range route.
+__device__ __forceinline__ long long id_row(const StreamParams& p, int id) {
+  if (p.sorted_ids == nullptr) return id;
+  if (id < 0 || id >= p.num_routes) return -1;
+  const long long row = id / p.top_k;
+  if (row >= p.x_rows) {
+    if (p.status) atomicOr(p.status, kDevBadRoute);
+    return -1;
+  }
+  return row;
+}
+
+template <typename T>
+__device__ __forceinline__ T pick8(const T (&v)[8], int g) {
+  T r = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) r = g == i ? v[i] : r;
+  return r;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
+                   const int* __restrict__ plan_count) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 2 * L::kStage);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(mma_bar + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_bar + 3);
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem + kOffCtl);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -156,262 +309,515 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const StreamPara
   const bool dense = p.sorted_ids == nullptr;
 
   if (tid == 0) {
-    mbar_init(&mma_bar[0], 1);
-    mbar_init(&mma_bar[1], 1);
-    *abort_flag = 0;
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(&ctl->raw_full[s], 1);
+      mbar_init(&ctl->raw_empty[s], 4);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&ctl->a_full[s], 4);
+      mbar_init(&ctl->a_empty[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&ctl->b_full[s], kLoadThreads);
+      mbar_init(&ctl->b_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ctl->acc_full[s], 1);
+      mbar_init(&ctl->acc_empty[s], 4);
+    }
+    mbar_init(&ctl->done, 1);
+    for (int i = 0; i < kInfoSlots; ++i) ctl->info[i] = 0;
+    ctl->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == kWarpTma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32((const void*)tmem_slot)),
-                 "r"(L::kTmemCols)
+                     smem_u32(&ctl->tmem)),
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&ctl->tmem);
 
   griddep_wait();
   if (tid == 0) griddep_launch_dependents();
 
-  long long groups;
+  long long items;
   if (dense) {
-    groups = (long long)(p.dense_m + BN - 1) / BN;
+    items = (long long)((p.dense_m + kNMax - 1) / kNMax) * nrb;
   } else {
-    groups = (long long)(p.ntpp[0] / p.block_m);
-    if (groups < 0) groups = 0;
-    if (groups > p.max_groups) groups = p.max_groups;
+    items = (long long)__ldg(plan_count) * nrb;
   }
-  const long long items = groups * nrb;
-  constexpr uint32_t kIdesc = instr_desc<F16>(BN);
-  uint32_t phase[2] = {0u, 0u};
-  int issued[2] = {0, 0};  // MMA batches committed to each stage barrier, not yet waited
+  // This CTA's items: g = blockIdx.x + j * gridDim.x, j < my_items.
+  const long long my_items =
+      items > (long long)blockIdx.x ? (items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const long long g0 = blockIdx.x, gs = gridDim.x;
 
-  for (long long item = blockIdx.x; item < items; item += gridDim.x) {
-    const long long gi = item / nrb;
-    const int rb = (int)(item - gi * nrb);
-    const int e = dense ? 0 : p.expert_ids[gi];
-    if (e < 0 || e >= p.E) continue;
-
-    // Activation rows this thread copies: chunk c = tid + 256*i of the
-    // [BN rows][16 chunks] step tile -> row c/16, chunk c%16.
-    const uint16_t* xrow[L::kRowsPerThread];
-#pragma unroll
-    for (int i = 0; i < L::kRowsPerThread; ++i) {
-      const int n = (tid + kTcThreads * i) >> 4;
-      const uint16_t* ptr = nullptr;
-      if (dense) {
-        const long long t = gi * BN + n;
-        if (t < p.dense_m) ptr = reinterpret_cast<const uint16_t*>(p.x) + t * p.ldx;
-      } else {
-        const int r = p.sorted_ids[gi * p.block_m + n];
-        if (r >= 0 && r < p.num_routes) {
-          const long long row = r / p.top_k;
-          if (row < p.x_rows) ptr = reinterpret_cast<const uint16_t*>(p.x) + row * p.ldx;
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ producer
+    const uint64_t policy = l2_policy_evict_first();
+    long long u = 0;  // units issued by this CTA
+    bool ok = true;
+    int2 pe_next = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
+    for (long long j = 0; j < my_items && ok; ++j) {
+      const Item it = make_item(p, pe_next, g0 + j * gs, nrb);
+      if (j + 1 < my_items) pe_next = plan_entry(p, plan, g0 + (j + 1) * gs, nrb);
+      const float* stop;
+      const float* sbot;
+      scale_rows(p, it, kch, stop, sbot);
+      // Lane l holds the scales of units 32c + l (window c); the row maxima
+      // give the item's exponents. Runs right after the previous item's last
+      // unit was issued, while the raw ring is full.
+      float ct = ldg_or0(stop, lane, kch), cb = ldg_or0(sbot, lane, kch);
+      float mt = fabsf(ct), mb = fabsf(cb);
+      for (int k = 32 + lane; k < kch; k += 32) {
+        mt = fmaxf(mt, fabsf(__ldg(stop + k)));
+        mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+      }
+      const int et = max_exponent(warp_max(mt));
+      const int eb = max_exponent(warp_max(mb));
+      float nt = ldg_or0(stop, 32 + lane, kch), nb = ldg_or0(sbot, 32 + lane, kch);
+      const uint8_t* wunit = p.wq + ((long long)it.e * nrb + it.rb) * (long long)kch * kRawBytes;
+      for (int kc = 0; kc < kch; ++kc, ++u) {
+        if (kc > 0 && (kc & 31) == 0) {
+          ct = nt;
+          cb = nb;
+          nt = ldg_or0(stop, kc + 32 + lane, kch);
+          nb = ldg_or0(sbot, kc + 32 + lane, kch);
+        }
+        const float vt = __shfl_sync(0xffffffffu, ct, kc & 31);
+        const float vb = __shfl_sync(0xffffffffu, cb, kc & 31);
+        const int s = (int)(u % kRawStages);
+        const uint32_t ph = (uint32_t)((u / kRawStages) & 1);
+        int good = 1;
+        if (lane == 0) {
+          good = wait_bar(&ctl->raw_empty[s], ph ^ 1u, ctl, p.status) ? 1 : 0;
+          if (good) {
+            ctl->raw_mult[s] = make_uint2(mult_f16x2(vt, et), mult_f16x2(vb, eb));
+            mbar_arrive_expect_tx(&ctl->raw_full[s], kRawBytes);
+            bulk_g2s(smem + kOffRaw + s * kRawBytes, wunit + (long long)kc * kRawBytes, kRawBytes,
+                     &ctl->raw_full[s], policy);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, good, 0)) {
+          ok = false;
+          break;
         }
       }
-      xrow[i] = ptr;
     }
-
-    // Weight scales of this row block (logical scale rows; gate/up banks
-    // take the gate scale for the top rows and the up scale for the bottom).
-    const int nsr = p.N / 128;
-    const float* srow_top;
-    const float* srow_bot;
-    if (p.gated) {
-      srow_top = p.wscale + ((long long)e * nsr + rb / 2) * kch;
-      srow_bot = p.wscale + ((long long)e * nsr + p.N / 2 / 128 + rb / 2) * kch;
-    } else {
-      srow_top = p.wscale + ((long long)e * nsr + rb) * kch;
-      srow_bot = srow_top;
+    // Copies still in flight land before the CTA exits (only after an abort).
+    if (lane == 0 && !ok) {
+      for (long long v = u > kRawStages ? u - kRawStages : 0; v < u; ++v)
+        mbar_wait(&ctl->raw_full[v % kRawStages], (uint32_t)((v / kRawStages) & 1), nullptr);
     }
-    const uint8_t* wunit = p.wq + ((long long)e * nrb + rb) * (long long)kch * kFp8UnitBytes;
-
-    // Weight bytes for the next step, one step ahead in registers: chunk
-    // j = tid + 256*i of the 16 KiB unit.
-    uint4 wreg[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      wreg[i] = __ldg(reinterpret_cast<const uint4*>(wunit) + tid + kTcThreads * i);
-
-    for (int kc = 0; kc < kch; ++kc) {
-      const int s = kc & 1;
-      uint8_t* stA = smem + s * L::kStage;
-      uint8_t* stB = stA + kABytes;
-      // Stage s was last read by the MMAs committed two steps ago.
-      if (issued[s]) {
-        bool ok = (*abort_flag == 0) && mbar_wait(&mma_bar[s], phase[s], p.status);
-        phase[s] ^= 1u;
-        issued[s] = 0;
-        if (!ok) *abort_flag = 1;
-      }
+  } else if (warp == kWarpMma) {
+    // ----------------------------------------------------------------- MMA
+    // The whole warp walks the pipeline (uniform control flow keeps the
+    // descriptors in uniform registers); one elected lane issues the MMAs and
+    // commits. Stage descriptors differ only in the start-address field, so
+    // they are precomputed once and advanced by 2 (32 bytes) per K=16 MMA.
+    const uint32_t dhi = (uint32_t)(smem_desc_sw128(0) >> 32);
+    const uint32_t a_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffA));
+    const uint32_t b_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffB));
+    long long t = 0;  // 64-K substeps consumed
+    bool ok = true;
+    for (long long j = 0; j < my_items && ok; ++j) {
+      const int buf = (int)(j & 1);
+      ok = __all_sync(0xffffffffu, wait_bar(&ctl->acc_empty[buf], (uint32_t)(((j >> 1) & 1) ^ 1),
+                                            ctl, p.status));
+      if (!ok) break;
       tc_fence_after();
-      // B: activation rows of this step.
-#pragma unroll
-      for (int i = 0; i < L::kRowsPerThread; ++i) {
-        if (xrow[i] != nullptr) {
-          const int c = tid + kTcThreads * i;
-          const int n = c >> 4, j = c & 15;
-          cp_async_16(stB + (j >> 3) * (BN * 128) + sw128_off(n, j & 7),
-                      xrow[i] + (long long)kc * 128 + j * 8);
-        }
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      // A: dequantize this step's unit from registers, then fetch the next.
-      const float st = __ldg(srow_top + kc);
-      const float sb = __ldg(srow_bot + kc);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int jch = tid + kTcThreads * i;   // 16-byte chunk of the streamed unit
-        const int wp = jch >> 7, q = (jch >> 5) & 3, ln = jch & 31;
-        const int r0 = 16 * wp + (ln >> 2), r1 = r0 + 8;
-        const int k0 = 32 * (ln & 3) + 8 * q;  // K of the chunk's 8 values
-        const int atom = k0 >> 6, c16 = (k0 & 63) >> 3;
-        *reinterpret_cast<uint4*>(stA + atom * 16384 + sw128_off(r0, c16)) =
-            dequant8<F16>(wreg[i].x, wreg[i].y, st);
-        *reinterpret_cast<uint4*>(stA + atom * 16384 + sw128_off(r1, c16)) =
-            dequant8<F16>(wreg[i].z, wreg[i].w, sb);
-      }
-      if (kc + 1 < kch) {
-        const uint4* nxt = reinterpret_cast<const uint4*>(wunit + (long long)(kc + 1) * kFp8UnitBytes);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) wreg[i] = __ldg(nxt + tid + kTcThreads * i);
-      }
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      fence_proxy_async();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0 && *abort_flag == 0) {
+      const uint32_t dcol = tmem + (uint32_t)(buf * kNMax);
+      uint32_t idesc = 0;
+      for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
+        const int sa = (int)(t % kAStages), sb = (int)(t % kBStages);
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(&ctl->a_full[sa], (uint32_t)((t / kAStages) & 1), ctl, p.status) &&
+                            wait_bar(&ctl->b_full[sb], (uint32_t)((t / kBStages) & 1), ctl,
+                                     p.status));
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(stA), b0 = smem_u32(stB);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (uint32_t)(kk & 3) * 32u;
-          const uint64_t da = smem_desc_sw128(a0 + (kk >> 2) * 16384u + off);
-          const uint64_t db = smem_desc_sw128(b0 + (kk >> 2) * (uint32_t)(BN * 128) + off);
-          mma_bf16(tmem, da, db, kIdesc, (kc > 0 || kk > 0) ? 1u : 0u);
+        if (ts == 0) {
+          const int v = *reinterpret_cast<volatile int*>(&ctl->info[j % kInfoSlots]);
+          int n = (v >> 9) == (int)(j & 0x3fffff) ? (v & 511) : kNMax;
+          n = n < 16 ? 16 : (n > kNMax ? kNMax : n);
+          idesc = instr_desc_f16(n);
         }
-        mma_commit(&mma_bar[s]);
+        const uint32_t alo = a_lo0 + (uint32_t)sa * (kATile >> 4);
+        const uint32_t blo = b_lo0 + (uint32_t)sb * (kBTile >> 4);
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(dcol, ((uint64_t)dhi << 32) | (alo + 2u * kk),
+                    ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc, (ts > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&ctl->a_empty[sa]);
+          mma_commit(&ctl->b_empty[sb]);
+        }
+        __syncwarp();
       }
-      issued[s] = 1;
+      if (ok && elect_one()) mma_commit(&ctl->acc_full[buf]);
+      __syncwarp();
     }
-
-    // Wait for this item's last MMAs, then read the accumulator.
+    // Every issued MMA has completed before tensor memory is released.
+    if (elect_one()) {
+      mma_commit(&ctl->done);
+      mbar_wait(&ctl->done, 0u, nullptr);
+    }
+    __syncwarp();
+  } else if (warp < kWarpDeq) {
+    // -------------------------------------------------------- B (activations)
+    const int ltid = tid - kWarpLoad * 32;  // 0..kLoadThreads-1
+    const int rsub = ltid >> 1;             // row within a pass of kLoadThreads/2 rows
+    const int cpar = ltid & 1;              // chunk parity
+    long long t = 0;
+    bool ok = true;
+    // Item j's route ids (ids_a), item j+1's plan entry (pe_b): one item ahead.
+    int2 pe_a = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
+    int ids_a[kLoadPasses];
     {
-      const int s = (kch - 1) & 1;
-      bool ok = (*abort_flag == 0) && mbar_wait(&mma_bar[s], phase[s], p.status);
-      phase[s] ^= 1u;
-      issued[s] = 0;
-      if (!ok) *abort_flag = 1;
-      // The other stage's batch (if any) completed before this one.
-      const int o = s ^ 1;
-      if (issued[o]) {
-        ok = (*abort_flag == 0) && mbar_wait(&mma_bar[o], phase[o], p.status);
-        phase[o] ^= 1u;
-        issued[o] = 0;
-        if (!ok) *abort_flag = 1;
-      }
+      const Item it0 = make_item(p, pe_a, g0, nrb);
+#pragma unroll
+      for (int q = 0; q < kLoadPasses; ++q)
+        ids_a[q] = my_items > 0 ? slot_id(p, it0, q * (kLoadThreads / 2) + rsub) : -1;
     }
-    tc_fence_after();
-    if (*abort_flag == 0) {
-      const int quarter = warp & 3;
-      const int m = quarter * 32 + lane;  // accumulator lane = local weight row
-      const int col0 = (warp >> 2) * (BN / 2);
-      for (int cc = 0; cc < BN / 2; cc += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + cc), v);
-        float up[16];
-        if (p.gated) {
+    int2 pe_b = my_items > 1 ? plan_entry(p, plan, g0 + gs, nrb) : make_int2(0, 0);
+    for (long long j = 0; j < my_items && ok; ++j) {
+      const uint16_t* rowp[kLoadPasses];
+      int nmax = 0;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) up[i] = __shfl_down_sync(0xffffffffu, v[i], 8);
-        }
-        const bool top = (m & 15) < 8;
+      for (int q = 0; q < kLoadPasses; ++q) {
+        const long long row = id_row(p, ids_a[q]);
+        rowp[q] = row >= 0 ? reinterpret_cast<const uint16_t*>(p.x) + row * p.ldx : nullptr;
+        if (row >= 0) nmax = q * (kLoadThreads / 2) + rsub + 1;
+      }
+      nmax = (int)__reduce_max_sync(0xffffffffu, (unsigned)nmax);
+      if (lane == 0)
+        atomicMax(&ctl->info[j % kInfoSlots], (int)(((j & 0x3fffff) << 9) | ((nmax + 15) & ~15)));
+      // Prefetch the next item's route ids and the one after's plan entry.
+      int2 pe_c = make_int2(0, 0);
+      if (j + 1 < my_items) {
+        const Item itn = make_item(p, pe_b, g0 + (j + 1) * gs, nrb);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int n = col0 + cc + i;
-          long long orow;
-          float w = 1.f;
-          if (dense) {
-            orow = gi * BN + n;
-            if (orow >= p.dense_m) continue;
-          } else {
-            const int r = p.sorted_ids[gi * p.block_m + n];
-            if (r < 0 || r >= p.num_routes) continue;
-            orow = r;
-            if (p.mul_w) w = p.topk_w[r];
-          }
-          long long col;
-          float val;
-          if (p.gated) {
-            const long long j = (long long)rb * 64 + (m >> 4) * 8 + (m & 7);
-            if (p.fuse_act) {
-              if (!top) continue;
-              col = j;
-              val = silu_f32(v[i]) * up[i] * w;
-            } else {
-              col = top ? j : j + p.N / 2;
-              val = v[i] * w;
+        for (int q = 0; q < kLoadPasses; ++q)
+          ids_a[q] = slot_id(p, itn, q * (kLoadThreads / 2) + rsub);
+        if (j + 2 < my_items) pe_c = plan_entry(p, plan, g0 + (j + 2) * gs, nrb);
+      }
+      for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
+        const int sb = (int)(t % kBStages);
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(&ctl->b_empty[sb], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl,
+                                 p.status));
+        if (!ok) break;
+        uint8_t* B = smem + kOffB + sb * kBTile;
+        const long long kofs = (long long)(ts >> 1) * 128 + (ts & 1) * 64;
+#pragma unroll
+        for (int q = 0; q < kLoadPasses; ++q) {
+          if (rowp[q] != nullptr) {
+            const int n = q * (kLoadThreads / 2) + rsub;
+#pragma unroll
+            for (int c2 = 0; c2 < 4; ++c2) {
+              const int c = 2 * c2 + cpar;
+              cp_async_16(B + sw128_off(n, c), rowp[q] + kofs + c * 8);
             }
-          } else {
-            col = (long long)rb * 128 + m;
-            val = v[i] * w;
           }
-          if (p.out_f16)
-            reinterpret_cast<__half*>(p.out)[orow * p.ldo + col] = __float2half_rn(val);
-          else
-            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + col] = __float2bfloat16_rn(val);
         }
+        cp_async_arrive_noinc(&ctl->b_full[sb]);
+      }
+      pe_b = pe_c;
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp < kWarpEpi) {
+    // ------------------------------------------------------------- dequant
+    const int dtid = tid - kWarpDeq * 32;  // 0..127
+    long long u = 0, t = 0;
+    bool ok = true;
+    for (long long j = 0; j < my_items && ok; ++j) {
+      for (int kc = 0; kc < kch && ok; ++kc, ++u) {
+        const int s = (int)(u % kRawStages);
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(&ctl->raw_full[s], (uint32_t)((u / kRawStages) & 1), ctl, p.status));
+        if (!ok) break;
+        const uint2 m2 = make_uint2(reinterpret_cast<volatile uint2*>(&ctl->raw_mult[s])->x,
+                                    reinterpret_cast<volatile uint2*>(&ctl->raw_mult[s])->y);
+        const uint8_t* raw = smem + kOffRaw + s * kRawBytes;
+        for (int h = 0; h < 2; ++h, ++t) {
+          const int sa = (int)(t % kAStages);
+          ok = __all_sync(0xffffffffu,
+                          wait_bar(&ctl->a_empty[sa], (uint32_t)(((t / kAStages) & 1) ^ 1), ctl,
+                                   p.status));
+          if (!ok) break;
+          uint8_t* A = smem + kOffA + sa * kATile;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // Chunk c of this K half. The streamed unit's 16-byte chunk
+            // wp*128 + q*32 + ln holds 8 K values (K = 32*(ln&3) + 8q + 0..7)
+            // of row r0 = 16wp + ln/4 and 8 of row r0 + 8.
+            const int c = dtid + 128 * i;
+            const int ln = (c & 1) | (h << 1) | (((c >> 1) & 7) << 2);
+            const int q = (c >> 4) & 3;
+            const int wp = c >> 6;
+            const uint4 w = ld_shared_u128(raw + (wp * 128 + q * 32 + ln) * 16);
+            const int r0 = 16 * wp + (ln >> 2);
+            const int c16 = 4 * (ln & 1) + q;
+            st_shared_u128(A + sw128_off(r0, c16), dequant8(w.x, w.y, m2.x));
+            st_shared_u128(A + sw128_off(r0 + 8, c16), dequant8(w.z, w.w, m2.y));
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->a_full[sa]);
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&ctl->raw_empty[s]);
       }
     }
-    // Every thread's accumulator reads finish before the next item's MMAs.
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Warps 10-13 take the even items (TMEM buffer 0), warps 14-17 the odd
+    // ones (buffer 1): each group has two items' main-loop time for one.
+    const int quarter = warp & 3;  // tensor-memory lanes 32*quarter..+31
+    const int eg = (warp - kWarpEpi) >> 2;
+    const int m = quarter * 32 + lane;  // weight row within the block
+    const bool top = (m & 15) < 8;
+    const bool fused = p.gated && p.fuse_act;
+    const bool lane_stores = !fused || top;
+    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(eg * kNMax);
+    for (long long j = eg; j < my_items; j += 2) {
+      const long long g = g0 + j * gs;
+      const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb);
+      const float* stop;
+      const float* sbot;
+      scale_rows(p, it, kch, stop, sbot);
+      float mt = 0.f, mb = 0.f;
+      for (int k = lane; k < kch; k += 32) {
+        mt = fmaxf(mt, fabsf(__ldg(stop + k)));
+        mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+      }
+      const int et = max_exponent(warp_max(mt));
+      const int eb = max_exponent(warp_max(mb));
+      const float fself = pow2f(top ? et : eb);  // this lane's row
+      long long mycol;
+      if (p.gated) {
+        const long long jj = (long long)it.rb * 64 + (m >> 4) * 8 + (m & 7);
+        mycol = top ? jj : jj + p.N / 2;
+      } else {
+        mycol = (long long)it.rb * 128 + m;
+      }
+      // Output row and router weight of column 32g + lane.
+      int orow[8];
+      float wr[8];
+#pragma unroll
+      for (int gg = 0; gg < 8; ++gg) {
+        const int id = slot_id(p, it, gg * 32 + lane);
+        orow[gg] = -1;
+        wr[gg] = 1.f;
+        if (dense) {
+          orow[gg] = id;
+        } else if (id >= 0 && id < p.num_routes && id / p.top_k < p.x_rows) {
+          orow[gg] = id;
+          if (p.mul_w) wr[gg] = __ldg(p.topk_w + id);
+        }
+      }
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl,
+                                            p.status)))
+        break;
+      tc_fence_after();
+      const int ngroups = (it.rows + 31) >> 5;
+      for (int gg = 0; gg < ngroups; ++gg) {
+        const int og = pick8(orow, gg);
+        const float wg = pick8(wr, gg);
+        const unsigned vmask = __ballot_sync(0xffffffffu, og >= 0);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (((vmask >> (16 * hh)) & 0xffffu) == 0u) continue;
+          float v[16];
+          tmem_ld16(tbase + (uint32_t)(gg * 32 + hh * 16), v);
+          // Column metadata first (independent shuffles), then branch-free
+          // math and predicated stores.
+          int orw[16];
+          float wv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            orw[i] = __shfl_sync(0xffffffffu, og, hh * 16 + i);
+            wv[i] = __shfl_sync(0xffffffffu, wg, hh * 16 + i);
+          }
+          // Each lane scales its own row; a gated top lane then takes the
+          // (scaled) up value of the row 8 lanes below.
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] *= fself;
+          if (fused) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float up = __shfl_down_sync(0xffffffffu, v[i], 8);
+              v[i] = silu_f32(v[i]) * up;
+            }
+          }
+          if (p.out_f16) {
+            __half* o = reinterpret_cast<__half*>(p.out);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (lane_stores && orw[i] >= 0)
+                o[(long long)orw[i] * p.ldo + mycol] = __float2half_rn(v[i] * wv[i]);
+          } else {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (lane_stores && orw[i] >= 0)
+                o[(long long)orw[i] * p.ldo + mycol] = __float2bfloat16_rn(v[i] * wv[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[eg]);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kWarpTma) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(L::kTmemCols)
+                 "r"(kTmemCols)
                  : "memory");
   }
 }
 
-template <int BN, bool F16>
-cudaError_t launch_tc(const StreamParams& p, int grid, cudaStream_t stream) {
-  using L = TcLayout<BN, F16>;
+// ------------------------------------------------------------------ plan
+// Block-wide inclusive max / exclusive sum (blockDim.x == 1024).
+__device__ __forceinline__ int block_incl_max(int v, int* sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v = max(v, x);
+  }
+  if (lane == 31) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    int x = sh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x = max(x, y);
+    }
+    sh[lane] = x;
+  }
+  __syncthreads();
+  if (w > 0) v = max(v, sh[w - 1]);
+  __syncthreads();
+  return v;
+}
+
+__device__ __forceinline__ int block_excl_sum(int v, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int s = sh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    sh[lane] = s;
+  }
+  __syncthreads();
+  total = sh[31];
+  const int excl = x - v + (w > 0 ? sh[w - 1] : 0);
+  __syncthreads();
+  return excl;
+}
+
+// Items of the grouped GEMM: every run of consecutive moe_align blocks with
+// the same (valid) expert, cut into pieces of at most nb_max blocks.
+// plan[i] = {first block, expert << 8 | blocks}; *count = number of items.
+__global__ void __launch_bounds__(1024) tc_plan_kernel(const int* __restrict__ expert_ids,
+                                                       const int* __restrict__ ntpp, int block_m,
+                                                       long long max_groups, int E, int nb_max,
+                                                       int2* __restrict__ plan,
+                                                       int* __restrict__ count, int cap) {
+  __shared__ int sh[32];
+  __shared__ int carry_sh;
+  griddep_wait();
+  long long groups = ntpp[0] / block_m;
+  if (groups < 0) groups = 0;
+  if (groups > max_groups) groups = max_groups;
+  if (groups > cap) groups = cap;
+  int carry = -1, total = 0;
+  for (long long b0 = 0; b0 < groups; b0 += blockDim.x) {
+    const int b = (int)(b0 + threadIdx.x);
+    const bool in = b < groups;
+    const int e = in ? expert_ids[b] : -1;
+    const bool valid = in && e >= 0 && e < E;
+    const int pe = (in && b > 0) ? expert_ids[b - 1] : -1;
+    const bool run_start = valid && (b == 0 || pe != e);
+    int rs = block_incl_max(run_start ? b : -1, sh);
+    rs = max(rs, carry);
+    const bool item = valid && ((b - rs) % nb_max) == 0;
+    int nb = 0;
+    if (item) {
+      nb = 1;
+      for (int k = 1; k < nb_max; ++k) {
+        if (b + k >= groups || expert_ids[b + k] != e) break;
+        ++nb;
+      }
+    }
+    int tile_total = 0;
+    const int idx = total + block_excl_sum(item ? 1 : 0, sh, tile_total);
+    if (item && idx < cap) plan[idx] = make_int2(b, (e << 8) | nb);
+    total += tile_total;
+    // The last thread's run start carries into the next tile.
+    if (threadIdx.x == blockDim.x - 1) carry_sh = rs;
+    __syncthreads();
+    carry = carry_sh;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = total < cap ? total : cap;
+  griddep_launch_dependents();
+}
+
+}  // namespace
+
+int64_t tc_plan_bytes(int cap) { return 256 + (int64_t)cap * (int64_t)sizeof(int2); }
+
+bool tc_gemm_supported(int block) {
+  return block >= 16 && block <= kNMax && kNMax % block == 0 && block % 16 == 0;
+}
+
+cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream) {
+  int* count = reinterpret_cast<int*>(plan_buf);
+  int2* plan = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(plan_buf) + 256);
+  return launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, stream, p.expert_ids, p.ntpp,
+                    p.block_m, p.max_groups, p.E, kNMax / p.block_m, plan, count, cap);
+}
+
+// Operands are f16: the weights dequantized as f16(e4m3 * m) with the scale's
+// power of two applied to the fp32 accumulator; bf16 activations are
+// converted by the caller. `plan_buf` holds launch_tc_plan's output (moe mode).
+cudaError_t launch_tc_gemm(const StreamParams& p, const void* plan_buf, int grid,
+                           cudaStream_t stream) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<BN, F16>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)L::kSmem);
+    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
-  return launch_pdl(tc_gemm_kernel<BN, F16>, dim3(grid), dim3(kTcThreads), L::kSmem, stream, p);
-}
-
-}  // namespace
-
-bool tc_gemm_supported(int block) { return block == 64 || block == 128 || block == 256; }
-
-// Operands are f16: the weights dequantized as f16(e4m3 * scale), whose
-// rounding (2^-11) keeps long-K sums as close to the exact dequantized
-// product as the decode path; bf16 activations are converted by the caller.
-cudaError_t launch_tc_gemm(int block, const StreamParams& p, int grid, cudaStream_t stream) {
-  switch (block) {
-    case 64: return launch_tc<64, true>(p, grid, stream);
-    case 128: return launch_tc<128, true>(p, grid, stream);
-    case 256: return launch_tc<256, true>(p, grid, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  const int* count = reinterpret_cast<const int*>(plan_buf);
+  const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
+  return launch_pdl(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan, count);
 }
 
 }  // namespace b200

@@ -311,6 +311,64 @@ def test_moe_gemm_tcgen05(cuda_device, block, gated_mode, x_dtype):
     assert ops.workspace_status() == 0
 
 
+@pytest.mark.parametrize("block", [64, 256])
+@pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED])
+def test_moe_gemm_tcgen05_long_runs(cuda_device, block, gated_mode):
+    """Skewed routing: experts with thousands of routes (many 256-slot items
+    per expert, runs cut mid-expert), more than 1024 groups (the plan's tile
+    carry), an idle expert and dropped routes."""
+    experts, tokens, top_k, k, n = 9, 20000, 4, 256, 256
+    g = torch.Generator(device="cpu").manual_seed(11 + block)
+    # Experts 0-2 take most routes, expert 5 none.
+    p = torch.tensor([0.3, 0.25, 0.2, 0.05, 0.05, 0.0, 0.05, 0.05, 0.05])
+    ids = torch.multinomial(p.expand(tokens, -1), top_k, replacement=False, generator=g)
+    ids = ids.to(torch.int32)
+    ids[::97, 2] = -1
+    weights = torch.rand(tokens, top_k, generator=g)
+    ids, weights = ids.to(cuda_device), weights.to(cuda_device)
+    x = synth.activations(tokens, k, cuda_device, seed=21)
+    q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=5)
+    packed = ops.fp8_prepack(q, gated_mode != _lib.GATED_NONE)
+    dense = _stack(_dequant_fp8_bank(q, s), experts)
+    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, block, experts)
+    assert int(ntpp.item()) // block > 1024 or block == 256
+    routes = tokens * top_k
+    cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
+    c = torch.zeros(routes, cols, dtype=torch.bfloat16, device=cuda_device)
+    mul = gated_mode == _lib.GATED_NONE
+    ops.moe_gemm(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, num_experts=experts,
+                 sorted_token_ids=sorted_ids, expert_ids=expert_ids, num_tokens_post_pad=ntpp,
+                 block_size=block, top_k=top_k, num_routes=routes, c=c, scales=s,
+                 topk_weights=weights, mul_topk_weights=mul, gated_mode=gated_mode)
+    want, written = oracle.moe_gemm_ref(
+        x.cpu(), dense, sorted_ids.cpu().numpy(), expert_ids.cpu().numpy(), int(ntpp.item()),
+        block, top_k, routes, weights.cpu(), mul, 1 if gated_mode == _lib.GATED_FUSED else 0,
+    )
+    assert int(written.sum()) == int((ids >= 0).sum())
+    assert_close(c.cpu()[written], want[written], what=f"tc long runs bs={block} g={gated_mode}")
+    assert ops.workspace_status() == 0
+
+
+def test_fp8_linear_tcgen05_scale_spread(cuda_device):
+    """Block scales spread over 2^-20..2^12 along K, and an all-zero row
+    block: the per-row power of two keeps the f16 operands in range."""
+    m, k, n = 96, 1024, 512
+    q, s = synth.fp8_bank(1, n, k, cuda_device, seed=17)
+    s = s.clone()
+    spread = torch.tensor([2.0 ** -20, 1.0, 2.0 ** 12, 2.0 ** -6, 0.5, 2.0 ** 7, 1.0, 2.0 ** -12],
+                          device=cuda_device)
+    s[0] = s[0] * spread[None, :]
+    s[0, 2] = 0.0
+    x = synth.activations(m, k, cuda_device, seed=8)
+    packed = ops.fp8_prepack(q[0], gated=False)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, scales=s[0])
+    want = oracle.fp8_linear_ref(x.cpu(), q[0].cpu(), s[0].cpu(), gated=False)
+    assert torch.isfinite(y.float()).all()
+    # The 2^12 block dominates every output: compare at the outputs' scale.
+    scale = float(want.abs().mean())
+    assert_close(y.float().cpu() / scale, want / scale, what="tc linear scale spread")
+
+
 @pytest.mark.parametrize("m", [33, 64, 130, 300])
 @pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED])
 def test_fp8_linear_tcgen05(cuda_device, m, gated_mode):
