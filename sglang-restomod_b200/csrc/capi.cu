@@ -173,7 +173,7 @@ constexpr int64_t kTcDenseMinRows = 33;
 // prefill regime) when every group fits the plan.
 bool use_tc_moe(int32_t quant, int32_t block_size, int64_t groups) {
   return quant == B200_QUANT_FP8_BLOCK && block_size >= 64 && tc_gemm_supported(block_size) &&
-         groups <= kTcPlanCap;
+         groups * tc_plan_slots_per_group(block_size) <= kTcPlanCap;
 }
 
 }  // namespace

@@ -58,7 +58,8 @@ int stream_gemm_ctas_per_sm(int nt);
 // launch_tc_plan (items = runs of same-expert groups, up to 256 route slots
 // each) into a buffer of tc_plan_bytes(cap); groups beyond `cap` are not
 // planned, so callers pick the stream GEMM when max_groups > cap.
-bool tc_gemm_supported(int block);  // block_m a multiple of 16 dividing 256
+bool tc_gemm_supported(int block);  // block_m in {16, 32, 64, 128, 256}
+int tc_plan_slots_per_group(int block);  // plan entries a moe_align group may need
 int64_t tc_plan_bytes(int cap);
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream);
 cudaError_t launch_tc_gemm(const StreamParams& p, const void* plan_buf, int grid,

@@ -8,82 +8,88 @@
 //
 // Shape: D[128 weight rows, N tokens] = W_e[128 rows, K] . X[N tokens, K]^T
 // ("swap AB": the weight row block is the MMA's M = 128; the tokens are
-// N <= 256). An item is one 128-row weight block of one expert against up to
-// 256 of that expert's route slots: a small pre-kernel (tc_plan_kernel) merges
+// N <= 192). An item is one 128-row weight block of one expert against up to
+// 192 of that expert's route slots: a small pre-kernel (tc_plan_kernel) merges
 // runs of consecutive moe_align blocks of the same expert into items, so an
-// expert's weights are dequantized once per 256 routes, and the item's N is
+// expert's weights are dequantized once per 192 routes, and the item's N is
 // trimmed to its last valid route (rounded up to 16).
 //
+// The A operand (dequantized weights) lives in tensor memory; shared memory
+// carries the raw FP8 units and the activation tiles, both written by TMA.
 // One persistent CTA per SM, 16 warps with fixed roles, coupled only through
 // mbarrier rings (every wait bounded, no named barriers):
-//   warp 0       TMA: 16 KiB FP8 weight units (prepack.cu's streamed layout,
-//                one 128x128 block each) into a 4-deep raw ring, each with
-//                its two f16 scale multipliers;
-//   warp 1       MMA: one thread issues tcgen05.mma (M=128, N<=256, K=16,
-//                f16 x f16 -> f32 in tensor memory), four per 64-K substep,
-//                and commits stage releases and accumulator-ready barriers;
-//   warps 2-3    B: gather the item's activation rows (through
+//   warp 0       weights: per 16 KiB FP8 unit (one 128x128 block of
+//                prepack.cu's streamed layout) its two f16 scale multipliers
+//                and a 2-D TMA copy (128-byte swizzle) into a 4-deep raw ring;
+//   warp 1       MMA: one elected lane issues tcgen05.mma (M=128, N<=192,
+//                K=16, A from tensor memory, B from shared memory, f16 x f16
+//                -> f32), four per 64-K stage, and commits stage releases and
+//                accumulator-ready barriers;
+//   warps 2-3    activations: gather the item's rows (through
 //                sorted_token_ids) with 16-byte cp.async into a 4-deep ring
-//                of [256 rows][64 K] 128-byte-swizzled tiles; each stage's
-//                full barrier completes as the copies land (cp.async
-//                mbarrier arrive), so four stages are in flight;
-//   warps 4-7    dequant: raw FP8 unit -> two [128 rows][64 K] f16 A tiles,
-//                f16(e4m3) * m, one hmul2 per two values;
+//                of [192 rows][64 K] 128-byte-swizzled tiles; the stage's full
+//                barrier completes as the copies land (the TMA gather4 path
+//                measured about 60 cycles per four-row copy, slower than this);
+//   warps 4-7    dequant: lane = weight row; each reads its row's FP8 bytes
+//                from the swizzled raw unit (conflict-free 8-byte reads),
+//                f16(e4m3) * m with one hmul2 per two values, and writes the
+//                stage's 64 K values into tensor memory (tcgen05.st);
 //   warps 8-15   epilogue: tcgen05.ld of a double-buffered accumulator (two
-//                256-column TMEM buffers), 2^E, SiLU*up, router weight and
-//                store, overlapping the next item's main loop; warps 8-11
-//                drain buffer 0 (even items), warps 12-15 buffer 1.
-// The producer and the gather warps load each item's plan entry and route
-// ids one item ahead, so no role waits on global memory at an item boundary.
+//                192-column buffers), 2^E, SiLU*up, router weight and store,
+//                overlapping the next item's main loop; warps 8-11 drain
+//                buffer 0 (even items), warps 12-15 buffer 1.
+// Tensor memory: columns [0, 384) accumulators, [384, 512) four A stages.
 //
 // Block scales. A 128x128 block's scale s is split as s = m * 2^E with one
 // power of two E per (expert, 128-row scale block) - the exponent of the
 // largest scale of that row - and m = f16(s * 2^-E) in (0, 2). The weights are
 // dequantized as f16(e4m3 * m) (f16 rounding; values below 2^-24 of the row's
 // largest block scale flush) and the accumulator is multiplied by 2^E exactly.
+#include <cuda.h>  // CUtensorMap and its encoding enums (types only)
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace b200 {
 namespace {
 
-constexpr int kNMax = 256;
+constexpr int kNMax = 192;  // route slots (MMA N) per item
 // 16 warps: four per SM sub-partition, so each thread may hold 128 registers.
 constexpr int kTcWarps = 16;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
+constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
 constexpr int kLoadPasses = kNMax / (kLoadThreads / 2);  // rows per gather thread
-constexpr int kRawStages = 4;
-constexpr int kAStages = 2;
-constexpr int kBStages = 4;
-constexpr uint32_t kRawBytes = kFp8UnitBytes;  // 16 KiB
-constexpr uint32_t kATile = 128 * 128;          // [128 rows][64 K] f16
-constexpr uint32_t kBTile = kNMax * 128;        // [256 rows][64 K] f16
-constexpr uint32_t kOffRaw = 0;
-constexpr uint32_t kOffA = kOffRaw + kRawStages * kRawBytes;
-constexpr uint32_t kOffB = kOffA + kAStages * kATile;
-constexpr uint32_t kOffCtl = kOffB + kBStages * kBTile;
+constexpr int kStages = 4;                               // 64-K stages (A in TMEM, B in smem)
+constexpr int kRawStages = 4;                            // 16 KiB FP8 units
+constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
+constexpr uint32_t kBTile = kNMax * 128;                 // [192 rows][64 K] f16
+constexpr uint32_t kOffB = 0;
+constexpr uint32_t kOffRaw = kOffB + kStages * kBTile;
+constexpr uint32_t kOffCtl = kOffRaw + kRawStages * kUnitBytes;
 constexpr int kInfoSlots = 8;
-constexpr uint32_t kTmemCols = 2 * kNMax;
-constexpr size_t kTcSmem = kOffCtl + 512 + 1024;  // control block + base alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = kNMax;                     // per accumulator buffer
+constexpr uint32_t kACol0 = 2 * kAccCols;                // first A-stage column
+constexpr uint32_t kAStageCols = 32;                     // 64 K f16 = 32 columns
+constexpr size_t kTcSmem = kOffCtl + 1024 + 1024;        // control block + base alignment slack
+static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "tensor memory");
+static_assert(kBTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
 
 struct Ctl {
-  uint64_t raw_full[kRawStages];
-  uint64_t raw_empty[kRawStages];
-  uint64_t a_full[kAStages];
-  uint64_t a_empty[kAStages];
-  uint64_t b_full[kBStages];
-  uint64_t b_empty[kBStages];
+  uint64_t full[kStages];   // 4 dequant warps + the gather threads
+  uint64_t empty[kStages];  // MMA commit
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
+  uint64_t raw_full[kRawStages];   // expect_tx + the unit's bytes
+  uint64_t raw_empty[kRawStages];  // 4 dequant warps
   uint64_t done;
-  uint2 raw_mult[kRawStages];  // f16x2 multipliers (top rows, bottom rows) per raw unit
-  int info[kInfoSlots];        // (item << 9) | N of the item's MMAs, atomicMax-combined
+  uint2 raw_mult[kRawStages];      // f16x2 multipliers: top 8 rows of every 16, bottom 8
+  int info[kInfoSlots];  // (item << 9) | N of the item's MMAs, atomicMax-combined
   uint32_t tmem;
   int abort;
 };
-static_assert(sizeof(Ctl) <= 512, "control block");
+static_assert(sizeof(Ctl) <= 1024, "control block");
 static_assert(kTcSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
@@ -109,19 +115,17 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                        uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] . B[smem descriptor]^T
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
+                                       uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n"
       "  .reg .pred p;\n"
       "  setp.ne.b32 p, %4, 0;\n"
-      "  tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n"
+      "  tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n"
       "}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 
@@ -159,10 +163,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void st_shared_u128(void* p, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
+// Lane i of the warp writes v[0..31] to lane (taddr.lane + i), columns
+// taddr.col .. +31; returns once the stores have completed.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Byte offset of 16-byte chunk (row, c16) of a [rows][64 x 16-bit] K-major
@@ -171,14 +184,14 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int c16) {
   return (uint32_t)row * 128u + (uint32_t)((c16 ^ (row & 7)) << 4);
 }
 
-// 8 E4M3 bytes -> 8 f16 values times the f16x2 multiplier m2.
-__device__ __forceinline__ uint4 dequant8(uint32_t lo, uint32_t hi, uint32_t m2) {
-  uint4 o;
-  o.x = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(lo & 0xffffu)), m2);
-  o.y = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(lo >> 16)), m2);
-  o.z = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(hi & 0xffffu)), m2);
-  o.w = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(hi >> 16)), m2);
-  return o;
+// 2-D tiled TMA load of one box at (x, y); completion as transaction bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // Bounded wait that also gives up once another role of the CTA has aborted.
@@ -196,6 +209,11 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ct
       }
     }
   }
+}
+
+// The same wait, taken by every lane of the warp, with one shared outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, ctl, status));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -226,7 +244,7 @@ struct Item {
   int e;            // expert (0 for dense)
   int rb;           // 128-row weight block
   long long slot0;  // first route slot (moe) or first activation row (dense)
-  int rows;         // route slots / rows covered (<= 256)
+  int rows;         // route slots / rows covered (<= kNMax)
 };
 
 __device__ __forceinline__ int2 plan_entry(const StreamParams& p, const int2* plan, long long g,
@@ -245,9 +263,9 @@ __device__ __forceinline__ Item make_item(const StreamParams& p, int2 pe, long l
     const long long left = (long long)p.dense_m - it.slot0;
     it.rows = left < kNMax ? (int)left : kNMax;
   } else {
-    it.e = pe.y >> 8;
-    it.slot0 = (long long)pe.x * p.block_m;
-    it.rows = (pe.y & 0xff) * p.block_m;
+    it.e = pe.y >> 9;
+    it.slot0 = pe.x;
+    it.rows = pe.y & 511;
   }
   return it;
 }
@@ -285,17 +303,17 @@ __device__ __forceinline__ long long id_row(const StreamParams& p, int id) {
   return row;
 }
 
-template <typename T>
-__device__ __forceinline__ T pick8(const T (&v)[8], int g) {
+template <typename T, int M>
+__device__ __forceinline__ T pick(const T (&v)[M], int g) {
   T r = v[0];
 #pragma unroll
-  for (int i = 1; i < 8; ++i) r = g == i ? v[i] : r;
+  for (int i = 1; i < M; ++i) r = g == i ? v[i] : r;
   return r;
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
-                   const int* __restrict__ plan_count) {
+                   const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -309,28 +327,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool dense = p.sorted_ids == nullptr;
 
   if (tid == 0) {
-    for (int s = 0; s < kRawStages; ++s) {
-      mbar_init(&ctl->raw_full[s], 1);
-      mbar_init(&ctl->raw_empty[s], 4);
-    }
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&ctl->a_full[s], 4);
-      mbar_init(&ctl->a_empty[s], 1);
-    }
-    for (int s = 0; s < kBStages; ++s) {
-      mbar_init(&ctl->b_full[s], kLoadThreads);
-      mbar_init(&ctl->b_empty[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full[s], 4 + kLoadThreads);
+      mbar_init(&ctl->empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&ctl->acc_full[s], 1);
       mbar_init(&ctl->acc_empty[s], 4);
+    }
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(&ctl->raw_full[s], 1);
+      mbar_init(&ctl->raw_empty[s], 4);
     }
     mbar_init(&ctl->done, 1);
     for (int i = 0; i < kInfoSlots; ++i) ctl->info[i] = 0;
     ctl->abort = 0;
     fence_mbar_init();
   }
-  if (warp == kWarpTma) {
+  if (warp == kWarpMeta) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&ctl->tmem)),
                  "r"(kTmemCols)
@@ -356,9 +370,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       items > (long long)blockIdx.x ? (items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const long long g0 = blockIdx.x, gs = gridDim.x;
 
-  if (warp == kWarpTma) {
-    // ------------------------------------------------------------ producer
-    const uint64_t policy = l2_policy_evict_first();
+  if (warp == kWarpMeta) {
+    // ------------------------------------------------------------- weights
     long long u = 0;  // units issued by this CTA
     bool ok = true;
     int2 pe_next = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
@@ -380,7 +393,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int et = max_exponent(warp_max(mt));
       const int eb = max_exponent(warp_max(mb));
       float nt = ldg_or0(stop, 32 + lane, kch), nb = ldg_or0(sbot, 32 + lane, kch);
-      const uint8_t* wunit = p.wq + ((long long)it.e * nrb + it.rb) * (long long)kch * kRawBytes;
+      // The unit's rows of 128 bytes in the weight tensor map.
+      const int row0 = (int)(((long long)it.e * nrb + it.rb) * kch * (kUnitBytes / 128));
       for (int kc = 0; kc < kch; ++kc, ++u) {
         if (kc > 0 && (kc & 31) == 0) {
           ct = nt;
@@ -397,9 +411,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           good = wait_bar(&ctl->raw_empty[s], ph ^ 1u, ctl, p.status) ? 1 : 0;
           if (good) {
             ctl->raw_mult[s] = make_uint2(mult_f16x2(vt, et), mult_f16x2(vb, eb));
-            mbar_arrive_expect_tx(&ctl->raw_full[s], kRawBytes);
-            bulk_g2s(smem + kOffRaw + s * kRawBytes, wunit + (long long)kc * kRawBytes, kRawBytes,
-                     &ctl->raw_full[s], policy);
+            mbar_arrive_expect_tx(&ctl->raw_full[s], kUnitBytes);
+            tma_load_2d(smem + kOffRaw + s * kUnitBytes, &tmap_w, 0,
+                        row0 + kc * (int)(kUnitBytes / 128), &ctl->raw_full[s]);
           }
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) {
@@ -416,28 +430,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == kWarpMma) {
     // ----------------------------------------------------------------- MMA
     // The whole warp walks the pipeline (uniform control flow keeps the
-    // descriptors in uniform registers); one elected lane issues the MMAs and
-    // commits. Stage descriptors differ only in the start-address field, so
-    // they are precomputed once and advanced by 2 (32 bytes) per K=16 MMA.
+    // operands in uniform registers); one elected lane issues the MMAs and
+    // commits. A stage's B descriptor differs from stage 0's only in the
+    // start-address field, advanced by 2 (32 bytes) per K=16 MMA.
     const uint32_t dhi = (uint32_t)(smem_desc_sw128(0) >> 32);
-    const uint32_t a_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffA));
     const uint32_t b_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffB));
-    long long t = 0;  // 64-K substeps consumed
+    long long t = 0;  // 64-K stages consumed
     bool ok = true;
     for (long long j = 0; j < my_items && ok; ++j) {
       const int buf = (int)(j & 1);
-      ok = __all_sync(0xffffffffu, wait_bar(&ctl->acc_empty[buf], (uint32_t)(((j >> 1) & 1) ^ 1),
-                                            ctl, p.status));
+      ok = warp_wait(&ctl->acc_empty[buf], (uint32_t)(((j >> 1) & 1) ^ 1), ctl, p.status);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t dcol = tmem + (uint32_t)(buf * kNMax);
+      const uint32_t dcol = tmem + (uint32_t)buf * kAccCols;
       uint32_t idesc = 0;
       for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
-        const int sa = (int)(t % kAStages), sb = (int)(t % kBStages);
-        ok = __all_sync(0xffffffffu,
-                        wait_bar(&ctl->a_full[sa], (uint32_t)((t / kAStages) & 1), ctl, p.status) &&
-                            wait_bar(&ctl->b_full[sb], (uint32_t)((t / kBStages) & 1), ctl,
-                                     p.status));
+        const int s = (int)(t % kStages);
+        ok = warp_wait(&ctl->full[s], (uint32_t)((t / kStages) & 1), ctl, p.status);
         if (!ok) break;
         tc_fence_after();
         if (ts == 0) {
@@ -446,15 +455,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           n = n < 16 ? 16 : (n > kNMax ? kNMax : n);
           idesc = instr_desc_f16(n);
         }
-        const uint32_t alo = a_lo0 + (uint32_t)sa * (kATile >> 4);
-        const uint32_t blo = b_lo0 + (uint32_t)sb * (kBTile >> 4);
+        const uint32_t acol = tmem + kACol0 + (uint32_t)s * kAStageCols;
+        const uint32_t blo = b_lo0 + (uint32_t)s * (kBTile >> 4);
         if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_f16(dcol, ((uint64_t)dhi << 32) | (alo + 2u * kk),
-                    ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc, (ts > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&ctl->a_empty[sa]);
-          mma_commit(&ctl->b_empty[sb]);
+            mma_ts(dcol, acol + 8u * kk, ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc,
+                   (ts > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&ctl->empty[s]);
         }
         __syncwarp();
       }
@@ -468,7 +476,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else if (warp < kWarpDeq) {
-    // -------------------------------------------------------- B (activations)
+    // ---------------------------------------------------- B (activations)
     const int ltid = tid - kWarpLoad * 32;  // 0..kLoadThreads-1
     const int rsub = ltid >> 1;             // row within a pass of kLoadThreads/2 rows
     const int cpar = ltid & 1;              // chunk parity
@@ -506,12 +514,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (j + 2 < my_items) pe_c = plan_entry(p, plan, g0 + (j + 2) * gs, nrb);
       }
       for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
-        const int sb = (int)(t % kBStages);
-        ok = __all_sync(0xffffffffu,
-                        wait_bar(&ctl->b_empty[sb], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl,
-                                 p.status));
+        const int s = (int)(t % kStages);
+        ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
         if (!ok) break;
-        uint8_t* B = smem + kOffB + sb * kBTile;
+        uint8_t* B = smem + kOffB + s * kBTile;
         const long long kofs = (long long)(ts >> 1) * 128 + (ts & 1) * 64;
 #pragma unroll
         for (int q = 0; q < kLoadPasses; ++q) {
@@ -524,58 +530,71 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
         }
-        cp_async_arrive_noinc(&ctl->b_full[sb]);
+        cp_async_arrive_noinc(&ctl->full[s]);
       }
       pe_b = pe_c;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------- dequant
-    const int dtid = tid - kWarpDeq * 32;  // 0..127
-    long long u = 0, t = 0;
+    // Lane = weight row m of this warp's tensor-memory quarter. In the
+    // streamed unit, row m's 8 K values K = 32*kg4 + 8q + 0..7 are bytes
+    // hf*8 .. +7 of 16-byte chunk wp*128 + q*32 + 4*(m&7) + kg4 (wp = m/16,
+    // hf = (m/8)&1), i.e. unit byte wp*2048 + q*512 + (m&7)*64 + kg4*16 + hf*8.
+    // The TMA copy stores the unit as 128 rows of 128 bytes with 16-byte chunk
+    // c of row r at chunk c ^ (r & 7). A 64-K stage h takes kg4 = 2h + kg.
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;
+    const int hf = (m >> 3) & 1;
+    const int r8 = m & 7;
+    const int rbase = (m >> 4) * 16 + (r8 >> 1);  // 128-byte row of q = 0
+    const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
+    const long long units = my_items * kch;
+    long long t = 0;
     bool ok = true;
-    for (long long j = 0; j < my_items && ok; ++j) {
-      for (int kc = 0; kc < kch && ok; ++kc, ++u) {
-        const int s = (int)(u % kRawStages);
-        ok = __all_sync(0xffffffffu,
-                        wait_bar(&ctl->raw_full[s], (uint32_t)((u / kRawStages) & 1), ctl, p.status));
-        if (!ok) break;
-        const uint2 m2 = make_uint2(reinterpret_cast<volatile uint2*>(&ctl->raw_mult[s])->x,
-                                    reinterpret_cast<volatile uint2*>(&ctl->raw_mult[s])->y);
-        const uint8_t* raw = smem + kOffRaw + s * kRawBytes;
-        for (int h = 0; h < 2; ++h, ++t) {
-          const int sa = (int)(t % kAStages);
-          ok = __all_sync(0xffffffffu,
-                          wait_bar(&ctl->a_empty[sa], (uint32_t)(((t / kAStages) & 1) ^ 1), ctl,
-                                   p.status));
-          if (!ok) break;
-          uint8_t* A = smem + kOffA + sa * kATile;
+    for (long long u = 0; u < units && ok; ++u) {
+      const int rs = (int)(u % kRawStages);
+      ok = warp_wait(&ctl->raw_full[rs], (uint32_t)((u / kRawStages) & 1), ctl, p.status);
+      if (!ok) break;
+      const volatile uint32_t* mm = reinterpret_cast<volatile uint32_t*>(&ctl->raw_mult[rs]);
+      const uint32_t m2 = hf ? mm[1] : mm[0];
+      const uint8_t* raw = smem + kOffRaw + rs * kUnitBytes;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            // Chunk c of this K half. The streamed unit's 16-byte chunk
-            // wp*128 + q*32 + ln holds 8 K values (K = 32*(ln&3) + 8q + 0..7)
-            // of row r0 = 16wp + ln/4 and 8 of row r0 + 8.
-            const int c = dtid + 128 * i;
-            const int ln = (c & 1) | (h << 1) | (((c >> 1) & 7) << 2);
-            const int q = (c >> 4) & 3;
-            const int wp = c >> 6;
-            const uint4 w = ld_shared_u128(raw + (wp * 128 + q * 32 + ln) * 16);
-            const int r0 = 16 * wp + (ln >> 2);
-            const int c16 = 4 * (ln & 1) + q;
-            st_shared_u128(A + sw128_off(r0, c16), dequant8(w.x, w.y, m2.x));
-            st_shared_u128(A + sw128_off(r0 + 8, c16), dequant8(w.z, w.w, m2.y));
-          }
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->a_full[sa]);
+      for (int h = 0; h < 2; ++h) {
+        uint2 r[8];  // [kg][q]
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int kg4 = 2 * h + (i >> 2), q = i & 3;
+          const int row = rbase + 4 * q;
+          const int chunk = (((r8 & 1) * 4 + kg4) ^ row) & 7;
+          r[i] = *reinterpret_cast<const uint2*>(raw + row * 128 + chunk * 16 + hf * 8);
         }
+        const int s = (int)(t % kStages);
+        ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t* o = v + 16 * (i >> 2) + 4 * (i & 3);
+          o[0] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x & 0xffffu)), m2);
+          o[1] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x >> 16)), m2);
+          o[2] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y & 0xffffu)), m2);
+          o[3] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y >> 16)), m2);
+        }
+        tmem_st32(tmem + tlane + kACol0 + (uint32_t)s * kAStageCols, v);
+        tc_fence_before();
         __syncwarp();
-        if (ok && lane == 0) mbar_arrive(&ctl->raw_empty[s]);
+        if (lane == 0) mbar_arrive(&ctl->full[s]);
+        ++t;
       }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->raw_empty[rs]);
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warps 10-13 take the even items (TMEM buffer 0), warps 14-17 the odd
+    // Warps 8-11 take the even items (TMEM buffer 0), warps 12-15 the odd
     // ones (buffer 1): each group has two items' main-loop time for one.
     const int quarter = warp & 3;  // tensor-memory lanes 32*quarter..+31
     const int eg = (warp - kWarpEpi) >> 2;
@@ -583,7 +602,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool top = (m & 15) < 8;
     const bool fused = p.gated && p.fuse_act;
     const bool lane_stores = !fused || top;
-    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(eg * kNMax);
+    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)eg * kAccCols;
+    constexpr int kGroups = kNMax / 32;
     for (long long j = eg; j < my_items; j += 2) {
       const long long g = g0 + j * gs;
       const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb);
@@ -606,10 +626,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mycol = (long long)it.rb * 128 + m;
       }
       // Output row and router weight of column 32g + lane.
-      int orow[8];
-      float wr[8];
+      int orow[kGroups];
+      float wr[kGroups];
 #pragma unroll
-      for (int gg = 0; gg < 8; ++gg) {
+      for (int gg = 0; gg < kGroups; ++gg) {
         const int id = slot_id(p, it, gg * 32 + lane);
         orow[gg] = -1;
         wr[gg] = 1.f;
@@ -620,14 +640,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (p.mul_w) wr[gg] = __ldg(p.topk_w + id);
         }
       }
-      if (!__all_sync(0xffffffffu, wait_bar(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl,
-                                            p.status)))
-        break;
+      if (!warp_wait(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl, p.status)) break;
       tc_fence_after();
       const int ngroups = (it.rows + 31) >> 5;
       for (int gg = 0; gg < ngroups; ++gg) {
-        const int og = pick8(orow, gg);
-        const float wg = pick8(wr, gg);
+        const int og = pick(orow, gg);
+        const float wg = pick(wr, gg);
         const unsigned vmask = __ballot_sync(0xffffffffu, og >= 0);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -677,7 +695,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpTma) {
+  if (warp == kWarpMeta) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
@@ -737,13 +755,15 @@ __device__ __forceinline__ int block_excl_sum(int v, int* sh, int& total) {
   return excl;
 }
 
-// Items of the grouped GEMM: every run of consecutive moe_align blocks with
-// the same (valid) expert, cut into pieces of at most nb_max blocks.
-// plan[i] = {first block, expert << 8 | blocks}; *count = number of items.
+// Items of the grouped GEMM. The route slots are cut into virtual blocks of
+// `vblock` (the moe_align block, or half of it when the block exceeds kNMax);
+// every run of consecutive virtual blocks of the same (valid) expert is cut
+// into items of at most nb_max of them.
+// plan[i] = {first slot, expert << 9 | slots}; *count = number of items.
 __global__ void __launch_bounds__(1024) tc_plan_kernel(const int* __restrict__ expert_ids,
                                                        const int* __restrict__ ntpp, int block_m,
-                                                       long long max_groups, int E, int nb_max,
-                                                       int2* __restrict__ plan,
+                                                       int vblock, long long max_groups, int E,
+                                                       int nb_max, int2* __restrict__ plan,
                                                        int* __restrict__ count, int cap) {
   __shared__ int sh[32];
   __shared__ int carry_sh;
@@ -751,29 +771,31 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int* __restrict__ e
   long long groups = ntpp[0] / block_m;
   if (groups < 0) groups = 0;
   if (groups > max_groups) groups = max_groups;
-  if (groups > cap) groups = cap;
+  const int vpb = block_m / vblock;
+  long long vgroups = groups * vpb;
+  if (vgroups > cap) vgroups = cap;
   int carry = -1, total = 0;
-  for (long long b0 = 0; b0 < groups; b0 += blockDim.x) {
-    const int b = (int)(b0 + threadIdx.x);
-    const bool in = b < groups;
-    const int e = in ? expert_ids[b] : -1;
+  for (long long v0 = 0; v0 < vgroups; v0 += blockDim.x) {
+    const int v = (int)(v0 + threadIdx.x);
+    const bool in = v < vgroups;
+    const int e = in ? expert_ids[v / vpb] : -1;
     const bool valid = in && e >= 0 && e < E;
-    const int pe = (in && b > 0) ? expert_ids[b - 1] : -1;
-    const bool run_start = valid && (b == 0 || pe != e);
-    int rs = block_incl_max(run_start ? b : -1, sh);
+    const int pe = (in && v > 0) ? expert_ids[(v - 1) / vpb] : -1;
+    const bool run_start = valid && (v == 0 || pe != e);
+    int rs = block_incl_max(run_start ? v : -1, sh);
     rs = max(rs, carry);
-    const bool item = valid && ((b - rs) % nb_max) == 0;
+    const bool item = valid && ((v - rs) % nb_max) == 0;
     int nb = 0;
     if (item) {
       nb = 1;
       for (int k = 1; k < nb_max; ++k) {
-        if (b + k >= groups || expert_ids[b + k] != e) break;
+        if (v + k >= vgroups || expert_ids[(v + k) / vpb] != e) break;
         ++nb;
       }
     }
     int tile_total = 0;
     const int idx = total + block_excl_sum(item ? 1 : 0, sh, tile_total);
-    if (item && idx < cap) plan[idx] = make_int2(b, (e << 8) | nb);
+    if (item && idx < cap) plan[idx] = make_int2(v * vblock, (e << 9) | (nb * vblock));
     total += tile_total;
     // The last thread's run start carries into the next tile.
     if (threadIdx.x == blockDim.x - 1) carry_sh = rs;
@@ -790,15 +812,59 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int* __restrict__ e
 int64_t tc_plan_bytes(int cap) { return 256 + (int64_t)cap * (int64_t)sizeof(int2); }
 
 bool tc_gemm_supported(int block) {
-  return block >= 16 && block <= kNMax && kNMax % block == 0 && block % 16 == 0;
+  return block == 16 || block == 32 || block == 64 || block == 128 || block == 256;
 }
+
+int tc_plan_slots_per_group(int block) { return block > kNMax ? 2 : 1; }
 
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream) {
   int* count = reinterpret_cast<int*>(plan_buf);
   int2* plan = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(plan_buf) + 256);
+  const int vblock = p.block_m > kNMax ? p.block_m / 2 : p.block_m;
   return launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, stream, p.expert_ids, p.ntpp,
-                    p.block_m, p.max_groups, p.E, kNMax / p.block_m, plan, count, cap);
+                    p.block_m, vblock, p.max_groups, p.E, kNMax / vblock, plan, count, cap);
 }
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D map over `rows` rows of `row_bytes` (stride `stride` bytes), box
+// `box_x` elements x `box_y` rows, 128-byte swizzle.
+bool make_map(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base,
+              unsigned long long row_elems, unsigned long long rows, unsigned long long stride,
+              unsigned box_x, unsigned box_y, CUtensorMapL2promotion promo) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {row_elems, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t box[2] = {box_x, box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
 
 // Operands are f16: the weights dequantized as f16(e4m3 * m) with the scale's
 // power of two applied to the fp32 accumulator; bf16 activations are
@@ -815,9 +881,20 @@ cudaError_t launch_tc_gemm(const StreamParams& p, const void* plan_buf, int grid
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
+  // Weights: every 16 KiB unit is 128 rows of 128 bytes.
+  const long long experts = p.sorted_ids == nullptr ? 1 : p.E;
+  const unsigned long long wrows =
+      (unsigned long long)experts * (p.N / 128) * (p.K / 128) * (kUnitBytes / 128);
+  if (wrows >= (1ull << 31))
+    return cudaErrorInvalidValue;
+  CUtensorMap tmap_w;
+  if (!make_map(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.wq, 128, wrows, 128, 128, 128,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+    return cudaErrorInvalidValue;
   const int* count = reinterpret_cast<const int*>(plan_buf);
   const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
-  return launch_pdl(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan, count);
+  return launch_pdl(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan, count,
+                    tmap_w);
 }
 
 }  // namespace b200
