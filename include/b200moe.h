@@ -151,8 +151,8 @@ int64_t b200_gemm_workspace_bytes(int64_t convert_elems);
  * csrc/sm70_fp8_qpn8_decode.cu:156-246).
  * quant: B200_QUANT_FP8_BLOCK (w_scales = [n/128, k/128] fp32) or
  * B200_QUANT_NVFP4 (global_scale = one fp32). x: bf16 or f16, rows of k.
- * FP8 with m > 32 runs on the tcgen05 tensor-core GEMM (row groups of
- * 64/128/256); smaller m streams the weights once (decode GEMV).
+ * m > 32 runs on the tcgen05 tensor-core GEMM (row groups of up to 192);
+ * smaller m streams the weights once (decode GEMV).
  */
 int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
                 const uint8_t* w_packed, const float* w_scales, const float* global_scale,
@@ -184,9 +184,10 @@ int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m
  * route slot p of block b multiplies activation row sorted_token_ids[p] /
  * top_k by expert expert_ids[b] and writes output row sorted_token_ids[p]
  * (times topk_weights[route] when mul_topk_weights). a: [a_rows, k];
- * c: rows of ldc elements. block_size in {8, 16, 32, 64}; FP8 also takes
- * 128 and 256, and FP8 blocks of 64 and more run on the tcgen05 tensor-core
- * GEMM (f16 operands; bf16 activations are converted in the workspace).
+ * c: rows of ldc elements. block_size in {8, 16, 32, 64, 128, 256}; blocks
+ * of 64 and more run on the tcgen05 tensor-core GEMM (f16 operands; bf16
+ * activations are converted in the workspace), smaller blocks on the
+ * weight-streaming GEMM.
  * At most expert_capacity blocks are read, so sorted_token_ids must hold
  * expert_capacity * block_size entries (pass floor(sorted_len / block_size)
  * when the align output is shorter). topk_weights and c need num_routes rows.

@@ -155,7 +155,7 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
 
 // tcgen05 GEMM; in moe mode the plan is built first unless `planned` (the
 // layer's second GEMM reuses the first one's plan).
-int run_tc(StreamParams& p, WsView& ws, bool planned, cudaStream_t stream) {
+int run_tc(int32_t quant, StreamParams& p, WsView& ws, bool planned, cudaStream_t stream) {
   p.ws = ws.partials;
   p.ws_cnt = ws.counters;
   p.status = ws.status;
@@ -163,16 +163,19 @@ int run_tc(StreamParams& p, WsView& ws, bool planned, cudaStream_t stream) {
     int rc = check_cuda(launch_tc_plan(p, ws.plan, kTcPlanCap, stream), "tcgen05 plan launch");
     if (rc) return rc;
   }
-  return check_cuda(launch_tc_gemm(p, ws.plan, device_sm_count(), stream), "tcgen05 GEMM launch");
+  return check_cuda(launch_tc_gemm(quant == B200_QUANT_NVFP4 ? kQuantNvfp4 : kQuantFp8Block, p,
+                                   ws.plan, device_sm_count(), stream),
+                    "tcgen05 GEMM launch");
 }
 
-// Dense rows above this use the tcgen05 GEMM (FP8 weights).
+// Dense rows above this use the tcgen05 GEMM.
 constexpr int64_t kTcDenseMinRows = 33;
 
-// Moe calls take the tcgen05 GEMM for FP8 blocks of 64 and more (the
-// prefill regime) when every group fits the plan.
+// Moe calls take the tcgen05 GEMM for blocks of 64 and more (the prefill
+// regime) when every group fits the plan.
 bool use_tc_moe(int32_t quant, int32_t block_size, int64_t groups) {
-  return quant == B200_QUANT_FP8_BLOCK && block_size >= 64 && tc_gemm_supported(block_size) &&
+  return (quant == B200_QUANT_FP8_BLOCK || quant == B200_QUANT_NVFP4) && block_size >= 64 &&
+         tc_gemm_supported(block_size) &&
          groups * tc_plan_slots_per_group(block_size) <= kTcPlanCap;
 }
 
@@ -340,7 +343,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     return fail(B200_ERR_INVALID, "workspace missing, misaligned or smaller than %lld bytes",
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (quant == B200_QUANT_FP8_BLOCK && m >= kTcDenseMinRows) {
+  if (m >= kTcDenseMinRows) {
     // Prefill-sized batch: tcgen05 tensor cores.
     int64_t used_tc = 0;
     const __half* xh = nullptr;
@@ -349,6 +352,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     StreamParams p{};
     p.wq = w_packed;
     p.wscale = w_scales;
+    p.gscale = global_scale;
     p.x = xh;
     p.ldx = k;
     p.x_rows = m;
@@ -362,7 +366,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.out = y;
     p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
     p.out_f16 = y_dtype == B200_DTYPE_F16;
-    return run_tc(p, ws, false, st);
+    return run_tc(quant, p, ws, false, st);
   }
   int64_t used = 0;
   const __half* x16 = nullptr;
@@ -408,7 +412,7 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   const bool tc = use_tc_moe(quant, block_size, expert_capacity);
   if (!tc && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED,
-                "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
+                "block_size must be 8, 16, 32, 64, 128 or 256, got %d", block_size);
   if (num_experts <= 0 || num_experts >= (1 << 23))
     return fail(B200_ERR_INVALID, "num_experts must be in [1, 2^23)");
   if (top_k <= 0) return fail(B200_ERR_INVALID, "top_k must be positive");
@@ -463,7 +467,7 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.out = c;
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
-  if (tc) return run_tc(p, ws, false, st);
+  if (tc) return run_tc(quant, p, ws, false, st);
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
 }
@@ -501,11 +505,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
     return fail(B200_ERR_INVALID, "bad tokens/top_k/num_experts");
   if (tokens == 0) return B200_OK;
   if (num_experts >= (1 << 23)) return fail(B200_ERR_INVALID, "num_experts must be below 2^23");
-  const bool tc_block = quant == B200_QUANT_FP8_BLOCK && block_size >= 64 &&
-                        tc_gemm_supported(block_size);
+  const bool tc_block = block_size >= 64 && tc_gemm_supported(block_size);
   if (!tc_block && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED,
-                "block_size must be 8, 16, 32 or 64 (FP8 also 128 or 256), got %d", block_size);
+                "block_size must be 8, 16, 32, 64, 128 or 256, got %d", block_size);
   if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
       w2_packed == nullptr || out == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
@@ -570,7 +573,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   p.out_f16 = 1;
   const int nt = block_size / 8;
   if (tc)
-    rc = run_tc(p, ws, false, st);
+    rc = run_tc(quant, p, ws, false, st);
   else
     rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
@@ -592,7 +595,7 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
-    rc = run_tc(q, ws, true, st);
+    rc = run_tc(quant, q, ws, true, st);
   else
     rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;

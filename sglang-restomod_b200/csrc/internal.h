@@ -54,7 +54,7 @@ cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int gri
                                cudaStream_t stream);
 int stream_gemm_ctas_per_sm(int nt);
 
-// tcgen05 grouped GEMM (FP8 weights, f16 activations). Moe mode first runs
+// tcgen05 grouped GEMM (FP8 or NVFP4 weights, f16 activations). Moe mode first runs
 // launch_tc_plan (items = runs of same-expert groups, up to 256 route slots
 // each) into a buffer of tc_plan_bytes(cap); groups beyond `cap` are not
 // planned, so callers pick the stream GEMM when max_groups > cap.
@@ -62,7 +62,7 @@ bool tc_gemm_supported(int block);  // block_m in {16, 32, 64, 128, 256}
 int tc_plan_slots_per_group(int block);  // plan entries a moe_align group may need
 int64_t tc_plan_bytes(int cap);
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream);
-cudaError_t launch_tc_gemm(const StreamParams& p, const void* plan_buf, int grid,
+cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
                            cudaStream_t stream);
 
 // moe_align_block_size: stable expert-major counting sort with per-expert

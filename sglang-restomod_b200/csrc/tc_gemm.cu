@@ -303,6 +303,11 @@ __device__ __forceinline__ long long id_row(const StreamParams& p, int id) {
   return row;
 }
 
+__device__ __forceinline__ uint32_t f16x2_splat(float v) {
+  const uint16_t b = __half_as_ushort(__float2half_rn(v));
+  return (uint32_t)b | ((uint32_t)b << 16);
+}
+
 template <typename T, int M>
 __device__ __forceinline__ T pick(const T (&v)[M], int g) {
   T r = v[0];
@@ -311,6 +316,9 @@ __device__ __forceinline__ T pick(const T (&v)[M], int g) {
   return r;
 }
 
+// kFp4: NVFP4 units (9 KiB: codes, then per-16-K E4M3 scales; weights
+// e2m1 * fp16_rne(e4m3 * global)), else block-FP8 units (16 KiB).
+template <bool kFp4>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
                    const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w) {
@@ -378,25 +386,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (long long j = 0; j < my_items && ok; ++j) {
       const Item it = make_item(p, pe_next, g0 + j * gs, nrb);
       if (j + 1 < my_items) pe_next = plan_entry(p, plan, g0 + (j + 1) * gs, nrb);
-      const float* stop;
-      const float* sbot;
-      scale_rows(p, it, kch, stop, sbot);
-      // Lane l holds the scales of units 32c + l (window c); the row maxima
-      // give the item's exponents. Runs right after the previous item's last
-      // unit was issued, while the raw ring is full.
-      float ct = ldg_or0(stop, lane, kch), cb = ldg_or0(sbot, lane, kch);
-      float mt = fabsf(ct), mb = fabsf(cb);
-      for (int k = 32 + lane; k < kch; k += 32) {
-        mt = fmaxf(mt, fabsf(__ldg(stop + k)));
-        mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+      const float* stop = nullptr;
+      const float* sbot = nullptr;
+      int et = 0, eb = 0;
+      float ct = 0.f, cb = 0.f, nt = 0.f, nb = 0.f, gsc = 0.f;
+      if constexpr (kFp4) {
+        gsc = __ldg(p.gscale + it.e);
+      } else {
+        scale_rows(p, it, kch, stop, sbot);
+        // Lane l holds the scales of units 32c + l (window c); the row maxima
+        // give the item's exponents. Runs right after the previous item's
+        // last unit was issued, while the raw ring is full.
+        ct = ldg_or0(stop, lane, kch);
+        cb = ldg_or0(sbot, lane, kch);
+        float mt = fabsf(ct), mb = fabsf(cb);
+        for (int k = 32 + lane; k < kch; k += 32) {
+          mt = fmaxf(mt, fabsf(__ldg(stop + k)));
+          mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+        }
+        et = max_exponent(warp_max(mt));
+        eb = max_exponent(warp_max(mb));
+        nt = ldg_or0(stop, 32 + lane, kch);
+        nb = ldg_or0(sbot, 32 + lane, kch);
       }
-      const int et = max_exponent(warp_max(mt));
-      const int eb = max_exponent(warp_max(mb));
-      float nt = ldg_or0(stop, 32 + lane, kch), nb = ldg_or0(sbot, 32 + lane, kch);
       // The unit's rows of 128 bytes in the weight tensor map.
-      const int row0 = (int)(((long long)it.e * nrb + it.rb) * kch * (kUnitBytes / 128));
+      constexpr int kUnitRows = (kFp4 ? kFp4UnitBytes : kFp8UnitBytes) / 128;
+      const int row0 = (int)(((long long)it.e * nrb + it.rb) * kch * kUnitRows);
       for (int kc = 0; kc < kch; ++kc, ++u) {
-        if (kc > 0 && (kc & 31) == 0) {
+        if (!kFp4 && kc > 0 && (kc & 31) == 0) {
           ct = nt;
           cb = nb;
           nt = ldg_or0(stop, kc + 32 + lane, kch);
@@ -410,10 +427,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
           good = wait_bar(&ctl->raw_empty[s], ph ^ 1u, ctl, p.status) ? 1 : 0;
           if (good) {
-            ctl->raw_mult[s] = make_uint2(mult_f16x2(vt, et), mult_f16x2(vb, eb));
-            mbar_arrive_expect_tx(&ctl->raw_full[s], kUnitBytes);
-            tma_load_2d(smem + kOffRaw + s * kUnitBytes, &tmap_w, 0,
-                        row0 + kc * (int)(kUnitBytes / 128), &ctl->raw_full[s]);
+            if constexpr (kFp4)
+              ctl->raw_mult[s] = make_uint2(__float_as_uint(gsc), 0u);
+            else
+              ctl->raw_mult[s] = make_uint2(mult_f16x2(vt, et), mult_f16x2(vb, eb));
+            mbar_arrive_expect_tx(&ctl->raw_full[s], (uint32_t)(kUnitRows * 128));
+            tma_load_2d(smem + kOffRaw + s * kUnitBytes, &tmap_w, 0, row0 + kc * kUnitRows,
+                        &ctl->raw_full[s]);
           }
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) {
@@ -557,30 +577,71 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       ok = warp_wait(&ctl->raw_full[rs], (uint32_t)((u / kRawStages) & 1), ctl, p.status);
       if (!ok) break;
       const volatile uint32_t* mm = reinterpret_cast<volatile uint32_t*>(&ctl->raw_mult[rs]);
-      const uint32_t m2 = hf ? mm[1] : mm[0];
+      const uint32_t m2 = hf ? mm[1] : mm[0];  // FP8: this row's multiplier
+      const float gsc = __uint_as_float(mm[0]);  // NVFP4: the expert's global scale
       const uint8_t* raw = smem + kOffRaw + rs * kUnitBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint2 r[8];  // [kg][q]
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int kg4 = 2 * h + (i >> 2), q = i & 3;
-          const int row = rbase + 4 * q;
-          const int chunk = (((r8 & 1) * 4 + kg4) ^ row) & 7;
-          r[i] = *reinterpret_cast<const uint2*>(raw + row * 128 + chunk * 16 + hf * 8);
-        }
-        const int s = (int)(t % kStages);
-        ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
-        if (!ok) break;
-        tc_fence_after();
         uint32_t v[32];
+        int s = 0;
+        if constexpr (kFp4) {
+          // NVFP4: row m's codes for K 32c .. +31 are bytes hf*16 .. +15 of
+          // the 32-byte lane record (w = m/16, lane 4*(m&7) + c), i.e. 128-byte
+          // row 8w + (m&7), chunk 2c + hf; its two group scales are bytes
+          // 2hf, 2hf+1 of the record's 4 scale bytes, in row 64 + w at byte
+          // 16*(m&7) + 4c. Stage h takes c = 2h, 2h + 1.
+          const int wr = m >> 4, g = m & 7;
+          const int row = 8 * wr + g;
+          uint4 code[2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t* o = v + 16 * (i >> 2) + 4 * (i & 3);
-          o[0] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x & 0xffffu)), m2);
-          o[1] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x >> 16)), m2);
-          o[2] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y & 0xffffu)), m2);
-          o[3] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y >> 16)), m2);
+          for (int cc = 0; cc < 2; ++cc) {
+            const int chunk = ((2 * (2 * h + cc) + hf) ^ g) & 7;
+            code[cc] = *reinterpret_cast<const uint4*>(raw + row * 128 + chunk * 16);
+          }
+          const uint2 sc = *reinterpret_cast<const uint2*>(
+              raw + (64 + wr) * 128 + ((g ^ wr) & 7) * 16 + 8 * h);
+          s = (int)(t % kStages);
+          ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            // Scale bytes of record c: top g0, top g1, bottom g0, bottom g1.
+            const uint32_t sw = cc ? sc.y : sc.x;
+            const uint32_t sp = e4m3x2_to_f16x2((uint16_t)(hf ? (sw >> 16) : (sw & 0xffffu)));
+            const __half2 sh = *reinterpret_cast<const __half2*>(&sp);
+            const uint32_t s0 = f16x2_splat(__low2float(sh) * gsc);
+            const uint32_t s1 = f16x2_splat(__high2float(sh) * gsc);
+            const uint32_t cw[4] = {code[cc].x, code[cc].y, code[cc].z, code[cc].w};
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+              uint32_t f[4];
+              e2m1x8_to_f16x2x4(cw[wd], f);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[16 * cc + 4 * wd + i] = hmul2_u32(f[i], wd < 2 ? s0 : s1);
+            }
+          }
+        } else {
+          uint2 r[8];  // [kg][q]
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int kg4 = 2 * h + (i >> 2), q = i & 3;
+            const int row = rbase + 4 * q;
+            const int chunk = (((r8 & 1) * 4 + kg4) ^ row) & 7;
+            r[i] = *reinterpret_cast<const uint2*>(raw + row * 128 + chunk * 16 + hf * 8);
+          }
+          s = (int)(t % kStages);
+          ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint32_t* o = v + 16 * (i >> 2) + 4 * (i & 3);
+            o[0] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x & 0xffffu)), m2);
+            o[1] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].x >> 16)), m2);
+            o[2] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y & 0xffffu)), m2);
+            o[3] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y >> 16)), m2);
+          }
         }
         tmem_st32(tmem + tlane + kACol0 + (uint32_t)s * kAStageCols, v);
         tc_fence_before();
@@ -607,17 +668,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (long long j = eg; j < my_items; j += 2) {
       const long long g = g0 + j * gs;
       const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb);
-      const float* stop;
-      const float* sbot;
-      scale_rows(p, it, kch, stop, sbot);
-      float mt = 0.f, mb = 0.f;
-      for (int k = lane; k < kch; k += 32) {
-        mt = fmaxf(mt, fabsf(__ldg(stop + k)));
-        mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+      float fself = 1.f;  // this lane's row: 2^E (FP8), 1 (NVFP4)
+      if constexpr (!kFp4) {
+        const float* stop;
+        const float* sbot;
+        scale_rows(p, it, kch, stop, sbot);
+        float mt = 0.f, mb = 0.f;
+        for (int k = lane; k < kch; k += 32) {
+          mt = fmaxf(mt, fabsf(__ldg(stop + k)));
+          mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
+        }
+        const int et = max_exponent(warp_max(mt));
+        const int eb = max_exponent(warp_max(mb));
+        fself = pow2f(top ? et : eb);
       }
-      const int et = max_exponent(warp_max(mt));
-      const int eb = max_exponent(warp_max(mb));
-      const float fself = pow2f(top ? et : eb);  // this lane's row
       long long mycol;
       if (p.gated) {
         const long long jj = (long long)it.rb * 64 + (m >> 4) * 8 + (m & 7);
@@ -866,35 +930,44 @@ bool make_map(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const 
 
 }  // namespace
 
-// Operands are f16: the weights dequantized as f16(e4m3 * m) with the scale's
-// power of two applied to the fp32 accumulator; bf16 activations are
-// converted by the caller. `plan_buf` holds launch_tc_plan's output (moe mode).
-cudaError_t launch_tc_gemm(const StreamParams& p, const void* plan_buf, int grid,
+// Operands are f16: FP8 weights dequantized as f16(e4m3 * m) with the
+// scale's power of two applied to the fp32 accumulator, NVFP4 weights as
+// e2m1 * fp16_rne(e4m3 * global); bf16 activations are converted by the
+// caller. `plan_buf` holds launch_tc_plan's output (moe mode).
+cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
                            cudaStream_t stream) {
-  static bool configured[64] = {};
+  const bool fp4 = quant == kQuantNvfp4;
+  static bool configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+  if (!configured[fp4][dev]) {
+    cudaError_t err =
+        fp4 ? cudaFuncSetAttribute(tc_gemm_kernel<true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem)
+            : cudaFuncSetAttribute(tc_gemm_kernel<false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (err != cudaSuccess) return err;
-    configured[dev] = true;
+    configured[fp4][dev] = true;
   }
-  // Weights: every 16 KiB unit is 128 rows of 128 bytes.
+  // Weights: every unit is rows of 128 bytes (FP8 128 rows, NVFP4 72), one
+  // box per unit.
+  const unsigned unit_rows = (fp4 ? kFp4UnitBytes : kFp8UnitBytes) / 128;
   const long long experts = p.sorted_ids == nullptr ? 1 : p.E;
   const unsigned long long wrows =
-      (unsigned long long)experts * (p.N / 128) * (p.K / 128) * (kUnitBytes / 128);
-  if (wrows >= (1ull << 31))
-    return cudaErrorInvalidValue;
+      (unsigned long long)experts * (p.N / 128) * (p.K / 128) * unit_rows;
+  if (wrows >= (1ull << 31)) return cudaErrorInvalidValue;
   CUtensorMap tmap_w;
-  if (!make_map(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.wq, 128, wrows, 128, 128, 128,
+  if (!make_map(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.wq, 128, wrows, 128, 128, unit_rows,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
     return cudaErrorInvalidValue;
   const int* count = reinterpret_cast<const int*>(plan_buf);
   const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
-  return launch_pdl(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan, count,
-                    tmap_w);
+  if (fp4)
+    return launch_pdl(tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
+                      count, tmap_w);
+  return launch_pdl(tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
+                    count, tmap_w);
 }
 
 }  // namespace b200

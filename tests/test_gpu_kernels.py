@@ -282,32 +282,40 @@ def test_layer_config2_decode(cuda_device, quant, tokens):
 
 
 # ------------------------------------------------- tcgen05 (prefill) path
+@pytest.mark.parametrize("quant", [_lib.QUANT_FP8_BLOCK, _lib.QUANT_NVFP4])
 @pytest.mark.parametrize("block", [64, 128, 256])
 @pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED, _lib.GATED_SPLIT])
 @pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16])
-def test_moe_gemm_tcgen05(cuda_device, block, gated_mode, x_dtype):
-    """FP8 expert GEMM on the tensor-core path: many routes per expert."""
+def test_moe_gemm_tcgen05(cuda_device, quant, block, gated_mode, x_dtype):
+    """Expert GEMM on the tensor-core path: many routes per expert."""
     experts, tokens, top_k, k, n = 5, 150, 3, 384, 512
     ids, weights = synth.route(tokens, experts, top_k, cuda_device, seed=block + gated_mode)
     ids[3, 1] = -1
     x = synth.activations(tokens, k, cuda_device, seed=9, dtype=x_dtype)
-    q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=3)
-    packed = ops.fp8_prepack(q, gated_mode != _lib.GATED_NONE)
-    dense = _stack(_dequant_fp8_bank(q, s), experts)
+    gated = gated_mode != _lib.GATED_NONE
+    if quant == _lib.QUANT_FP8_BLOCK:
+        q, s = synth.fp8_bank(experts, n, k, cuda_device, seed=3)
+        packed, scales, gs = ops.fp8_prepack(q, gated), s, None
+        dense = _stack(_dequant_fp8_bank(q, s), experts)
+    else:
+        p4, s8, gs = synth.nvfp4_bank(experts, n, k, cuda_device, seed=3)
+        packed, scales = ops.nvfp4_prepack(p4, s8, gated), None
+        dense = _stack(_dequant_nvfp4_bank(p4, s8, gs), experts)
     sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, block, experts)
     routes = tokens * top_k
     cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
     c = torch.zeros(routes, cols, dtype=x_dtype, device=cuda_device)
     mul = gated_mode == _lib.GATED_NONE
-    ops.moe_gemm(x, packed, n, quant=_lib.QUANT_FP8_BLOCK, num_experts=experts,
+    ops.moe_gemm(x, packed, n, quant=quant, num_experts=experts,
                  sorted_token_ids=sorted_ids, expert_ids=expert_ids, num_tokens_post_pad=ntpp,
-                 block_size=block, top_k=top_k, num_routes=routes, c=c, scales=s,
-                 topk_weights=weights, mul_topk_weights=mul, gated_mode=gated_mode)
+                 block_size=block, top_k=top_k, num_routes=routes, c=c, scales=scales,
+                 global_scale=gs, topk_weights=weights, mul_topk_weights=mul,
+                 gated_mode=gated_mode)
     want, written = oracle.moe_gemm_ref(
         x.cpu(), dense, sorted_ids.cpu().numpy(), expert_ids.cpu().numpy(), int(ntpp.item()),
         block, top_k, routes, weights.cpu(), mul, 1 if gated_mode == _lib.GATED_FUSED else 0,
     )
-    assert_close(c.cpu()[written], want[written], what=f"tc moe_gemm bs={block} g={gated_mode}")
+    assert_close(c.cpu()[written], want[written], what=f"tc moe_gemm q={quant} bs={block} g={gated_mode}")
     assert ops.workspace_status() == 0
 
 
@@ -367,6 +375,27 @@ def test_fp8_linear_tcgen05_scale_spread(cuda_device):
     # The 2^12 block dominates every output: compare at the outputs' scale.
     scale = float(want.abs().mean())
     assert_close(y.float().cpu() / scale, want / scale, what="tc linear scale spread")
+
+
+@pytest.mark.parametrize("m", [33, 130, 300])
+@pytest.mark.parametrize("gated_mode", [_lib.GATED_NONE, _lib.GATED_FUSED])
+def test_nvfp4_linear_tcgen05(cuda_device, m, gated_mode):
+    k, n = 768, 1024
+    p4, s8, gs = synth.nvfp4_bank(1, n, k, cuda_device, seed=m)
+    x = synth.activations(m, k, cuda_device, seed=5)
+    packed = ops.nvfp4_prepack(p4[0], s8[0], gated=gated_mode != _lib.GATED_NONE)
+    y = ops.linear(x, packed, n, quant=_lib.QUANT_NVFP4, global_scale=gs[:1], gated_mode=gated_mode)
+    want = oracle.nvfp4_linear_ref(x.cpu(), p4[0].cpu(), s8[0].cpu(), float(gs[0]),
+                                   gated=gated_mode == _lib.GATED_FUSED)
+    assert_close(y, want, what=f"tc nvfp4 linear m={m} g={gated_mode}")
+
+
+def test_layer_config3_prefill_sampled(cuda_device):
+    """The NVFP4 layer (config-2 shapes, NVFP4 weights) at 4096 tokens on the
+    tensor-core path; four tokens checked against the oracle."""
+    sample = torch.tensor([0, 1, 2047, 4095])
+    _check_layer(synth.CONFIG2, 4096, _lib.QUANT_NVFP4, cuda_device, block=64,
+                 sample_tokens=sample, rsf=1.0)
 
 
 @pytest.mark.parametrize("m", [33, 64, 130, 300])
