@@ -168,8 +168,17 @@ int run_tc(int32_t quant, StreamParams& p, WsView& ws, bool planned, cudaStream_
                     "tcgen05 GEMM launch");
 }
 
-// Dense rows above this use the tcgen05 GEMM.
+// Route count from which the layer aligns with the multi-CTA kernels.
+constexpr int64_t kAlignMultiMin = 4096;
+
+// Dense calls use the tcgen05 GEMM once M exceeds the decode range and its
+// items (192-row chunks x 128-row weight blocks, no K split) fill at least
+// half of the SMs; below that the stream GEMM's K split keeps every SM busy.
 constexpr int64_t kTcDenseMinRows = 33;
+bool use_tc_dense(int64_t m, int64_t n) {
+  const int64_t items = (m + 191) / 192 * (n / 128);
+  return m >= kTcDenseMinRows && 2 * items >= device_sm_count();
+}
 
 // Moe calls take the tcgen05 GEMM for blocks of 64 and more (the prefill
 // regime) when every group fits the plan.
@@ -343,7 +352,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     return fail(B200_ERR_INVALID, "workspace missing, misaligned or smaller than %lld bytes",
                 (long long)stream_ws_bytes());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (m >= kTcDenseMinRows) {
+  if (use_tc_dense(m, n)) {
     // Prefill-sized batch: tcgen05 tensor cores.
     int64_t used_tc = 0;
     const __half* xh = nullptr;
@@ -543,8 +552,16 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   __half* routed = reinterpret_cast<__half*>(ws.scratch + used);
   used += align_up(numel * hidden * 2);
 
-  rc = b200_moe_align_block_size(topk_ids, numel, num_experts, block_size, sorted, cap, eids,
-                                 blocks, ntpp, stream);
+  if (numel >= kAlignMultiMin && num_experts <= moe_align_max_experts()) {
+    // Many routes: the multi-CTA align, its per-segment histograms in the
+    // routed-output buffer (written only later, by the down GEMM).
+    rc = check_cuda(launch_moe_align_multi(topk_ids, numel, num_experts, block_size, sorted, cap,
+                                           eids, blocks, ntpp, reinterpret_cast<int*>(routed), st),
+                    "moe_align launch");
+  } else {
+    rc = b200_moe_align_block_size(topk_ids, numel, num_experts, block_size, sorted, cap, eids,
+                                   blocks, ntpp, stream);
+  }
   if (rc) return rc;
 
   StreamParams p{};

@@ -71,6 +71,13 @@ cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_exper
                              int* sorted_ids, long long sorted_cap, int* expert_ids,
                              long long expert_cap, int* ntpp, cudaStream_t stream);
 int moe_align_max_experts();
+// Multi-CTA variant (same output) for large route counts; `scratch` holds
+// moe_align_scratch_ints(numel, E) ints.
+long long moe_align_scratch_ints(long long numel, int num_experts);
+cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num_experts,
+                                   int block_size, int* sorted_ids, long long sorted_cap,
+                                   int* expert_ids, long long expert_cap, int* ntpp, int* scratch,
+                                   cudaStream_t stream);
 
 // Elementwise / reduction kernels.
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);

@@ -161,9 +161,199 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ multi-CTA
+// The same contract for large route counts, in three launches over
+// segments of kSeg routes (route order = segment order, so the result is
+// identical): per-segment expert histograms into `hist[segments][E]`, one
+// CTA turning them into each segment's first slot per expert (plus the
+// padded offsets, expert_ids and padding), then a stable scatter per
+// segment.
+constexpr int kSeg = 1024;
+constexpr int kSegThreads = 256;
+constexpr int kSegWarps = kSegThreads / 32;
+
+__global__ void __launch_bounds__(kSegThreads)
+    align_hist_kernel(const int* __restrict__ topk_ids, long long numel, int E,
+                      int* __restrict__ hist) {
+  extern __shared__ int hsm[];  // [E]
+  for (int e = threadIdx.x; e < E; e += kSegThreads) hsm[e] = 0;
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  __syncthreads();
+  const long long s0 = (long long)blockIdx.x * kSeg;
+  for (int i = threadIdx.x; i < kSeg; i += kSegThreads) {
+    const long long idx = s0 + i;
+    if (idx < numel) {
+      const int e = __ldg(topk_ids + idx);
+      if (e >= 0 && e < E) atomicAdd(&hsm[e], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kSegThreads)
+    hist[(long long)blockIdx.x * E + e] = hsm[e];
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    align_scan_kernel(int* __restrict__ hist, int segments, long long numel, int E, int bs,
+                      int* __restrict__ sorted_ids, long long sorted_cap,
+                      int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
+  extern __shared__ int ssm[];
+  int* off = ssm;           // [E + 1]
+  int* tot = off + E + 1;   // [E]
+  int* wsum = tot + E;      // [kWarps]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  griddep_wait();
+  if (tid == 0) griddep_launch_dependents();
+  // Per expert: exclusive scan over segments (in place) and the total.
+  for (int e = tid; e < E; e += kThreads) {
+    int run = 0;
+    for (int c = 0; c < segments; ++c) {
+      int* h = hist + (long long)c * E + e;
+      const int v = *h;
+      *h = run;
+      run += v;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  const int pad = (tid < E) ? (tot[tid] + bs - 1) / bs * bs : 0;
+  int x = pad;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int v = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    wsum[lane] = v;
+  }
+  __syncthreads();
+  const int excl = x - pad + (warp > 0 ? wsum[warp - 1] : 0);
+  if (tid < E) off[tid] = excl;
+  if (tid == E - 1) off[E] = excl + pad;
+  __syncthreads();
+  const int total = off[E];
+  if (tid == 0) ntpp[0] = total;
+  // Segment bases become absolute first slots.
+  for (int e = tid; e < E; e += kThreads)
+    for (int c = 0; c < segments; ++c) hist[(long long)c * E + e] += off[e];
+  for (long long b = tid; b < expert_cap; b += kThreads) {
+    const long long slot = b * bs;
+    int v = -1;
+    if (slot < total) {
+      int lo = 0, hi = E - 1;  // last e with off[e] <= slot
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (off[mid] <= slot) lo = mid; else hi = mid - 1;
+      }
+      v = lo;
+    }
+    expert_ids[b] = v;
+  }
+  for (int e = tid; e < E; e += kThreads) {
+    for (int p = off[e] + tot[e]; p < off[e + 1]; ++p)
+      if (p < sorted_cap) sorted_ids[p] = (int)numel;
+  }
+  for (long long p = total + tid; p < sorted_cap; p += kThreads) sorted_ids[p] = (int)numel;
+}
+
+__global__ void __launch_bounds__(kSegThreads)
+    align_scatter_kernel(const int* __restrict__ topk_ids, long long numel, int E,
+                         const int* __restrict__ base, int* __restrict__ sorted_ids,
+                         long long sorted_cap) {
+  extern __shared__ int csm[];  // [kSegWarps][E] per-warp running positions
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kSegWarps * E; i += kSegThreads) csm[i] = 0;
+  griddep_wait();
+  if (tid == 0) griddep_launch_dependents();
+  __syncthreads();
+  // Warp w owns routes s0 + w*128 .. +127 of the segment.
+  const long long s0 = (long long)blockIdx.x * kSeg + warp * (kSeg / kSegWarps);
+  int ids[kSeg / kSegWarps / 32];
+#pragma unroll
+  for (int b = 0; b < kSeg / kSegWarps / 32; ++b) {
+    const long long idx = s0 + b * 32 + lane;
+    ids[b] = idx < numel ? __ldg(topk_ids + idx) : -1;
+  }
+#pragma unroll
+  for (int b = 0; b < kSeg / kSegWarps / 32; ++b) {
+    const int e = ids[b];
+    const bool valid = e >= 0 && e < E;
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+    if (valid && lane == __ffs(peers) - 1) csm[warp * E + e] += __popc(peers);
+  }
+  __syncthreads();
+  // Exclusive scan over the warps, offset by the segment's first slot.
+  for (int e = tid; e < E; e += kSegThreads) {
+    int run = base[(long long)blockIdx.x * E + e];
+    for (int w = 0; w < kSegWarps; ++w) {
+      const int c = csm[w * E + e];
+      csm[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int b = 0; b < kSeg / kSegWarps / 32; ++b) {
+    const long long idx = s0 + b * 32 + lane;
+    const int e = ids[b];
+    const bool valid = e >= 0 && e < E;
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+    if (valid) {
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const long long pos = (long long)csm[warp * E + e] + rank;
+      if (pos < sorted_cap) sorted_ids[pos] = (int)idx;
+    }
+    __syncwarp();
+    if (valid && lane == __ffs(peers) - 1) csm[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
 }  // namespace
 
 int moe_align_max_experts() { return kMaxExperts; }
+
+long long moe_align_scratch_ints(long long numel, int num_experts) {
+  return (numel + kSeg - 1) / kSeg * (long long)num_experts;
+}
+
+cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num_experts,
+                                   int block_size, int* sorted_ids, long long sorted_cap,
+                                   int* expert_ids, long long expert_cap, int* ntpp, int* scratch,
+                                   cudaStream_t stream) {
+  const int segments = (int)((numel + kSeg - 1) / kSeg);
+  if (segments < 1) return cudaErrorInvalidValue;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(align_scatter_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)(sizeof(int) * kSegWarps * kMaxExperts));
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
+  const int E = num_experts;
+  cudaError_t err = launch_pdl(align_hist_kernel, dim3(segments), dim3(kSegThreads),
+                               sizeof(int) * E, stream, topk_ids, numel, E, scratch);
+  if (err != cudaSuccess) return err;
+  err = launch_pdl(align_scan_kernel, dim3(1), dim3(kThreads),
+                   sizeof(int) * (2 * (size_t)E + 1 + kWarps), stream, scratch, segments, numel, E,
+                   block_size, sorted_ids, sorted_cap, expert_ids, expert_cap, ntpp);
+  if (err != cudaSuccess) return err;
+  return launch_pdl(align_scatter_kernel, dim3(segments), dim3(kSegThreads),
+                    sizeof(int) * kSegWarps * E, stream, topk_ids, numel, E,
+                    (const int*)scratch, sorted_ids, sorted_cap);
+}
 
 cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_experts, int block_size,
                              int* sorted_ids, long long sorted_cap, int* expert_ids,
