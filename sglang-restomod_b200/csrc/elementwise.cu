@@ -85,15 +85,37 @@ __global__ void sum_reduce_kernel(const void* __restrict__ in, void* __restrict_
     const long long t = id / h8;
     const long long c = (id - t * h8) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < top_k; ++k) {
-      if (topk_ids != nullptr) {
-        const int e = topk_ids[t * top_k + k];
-        if (e < 0 || e >= num_experts) continue;
-      }
-      float v[8];
-      load8(in, (t * top_k + k) * hidden + c, f16, v);
+    // Four routes' rows in flight per step; a dropped route's row is never
+    // read (it was not written).
+    for (int k0 = 0; k0 < top_k; k0 += 4) {
+      uint4 raw[4];
+      bool use[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+      for (int j = 0; j < 4; ++j) {
+        const int k = k0 + j;
+        use[j] = k < top_k;
+        if (use[j] && topk_ids != nullptr) {
+          const int e = __ldg(topk_ids + t * top_k + k);
+          use[j] = e >= 0 && e < num_experts;
+        }
+        raw[j] = use[j] ? *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(in) +
+                                                          ((t * top_k + k) * hidden + c) * 2)
+                        : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f;
+          if (f16)
+            f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+          else
+            f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
+        }
+      }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] *= scale;

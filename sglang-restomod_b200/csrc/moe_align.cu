@@ -165,9 +165,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // The same contract for large route counts, in three launches over
 // segments of kSeg routes (route order = segment order, so the result is
 // identical): per-segment expert histograms into `hist[segments][E]`, one
-// CTA turning them into each segment's first slot per expert (plus the
-// padded offsets, expert_ids and padding), then a stable scatter per
-// segment.
+// CTA turning them into per-segment exclusive counts plus the padded expert
+// offsets `off[E + 1]` (stored after hist), expert_ids and padding, then a
+// stable scatter per segment at off[e] + hist[segment][e] + rank.
 constexpr int kSeg = 1024;
 constexpr int kSegThreads = 256;
 constexpr int kSegWarps = kSegThreads / 32;
@@ -204,14 +204,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   griddep_wait();
   if (tid == 0) griddep_launch_dependents();
-  // Per expert: exclusive scan over segments (in place) and the total.
+  // Per expert: exclusive scan over segments (in place) and the total,
+  // eight segments' loads in flight at a time.
   for (int e = tid; e < E; e += kThreads) {
     int run = 0;
-    for (int c = 0; c < segments; ++c) {
-      int* h = hist + (long long)c * E + e;
-      const int v = *h;
-      *h = run;
-      run += v;
+    for (int c0 = 0; c0 < segments; c0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = c0 + j < segments ? hist[(long long)(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (c0 + j < segments) hist[(long long)(c0 + j) * E + e] = run;
+        run += v[j];
+      }
     }
     tot[e] = run;
   }
@@ -241,9 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   const int total = off[E];
   if (tid == 0) ntpp[0] = total;
-  // Segment bases become absolute first slots.
-  for (int e = tid; e < E; e += kThreads)
-    for (int c = 0; c < segments; ++c) hist[(long long)c * E + e] += off[e];
+  int* goff = hist + (long long)segments * E;
+  for (int e = tid; e <= E; e += kThreads) goff[e] = off[e];
   for (long long b = tid; b < expert_cap; b += kThreads) {
     const long long slot = b * bs;
     int v = -1;
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 __global__ void __launch_bounds__(kSegThreads)
     align_scatter_kernel(const int* __restrict__ topk_ids, long long numel, int E,
-                         const int* __restrict__ base, int* __restrict__ sorted_ids,
+                         const int* __restrict__ base, int segments, int* __restrict__ sorted_ids,
                          long long sorted_cap) {
   extern __shared__ int csm[];  // [kSegWarps][E] per-warp running positions
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -292,7 +296,7 @@ __global__ void __launch_bounds__(kSegThreads)
   __syncthreads();
   // Exclusive scan over the warps, offset by the segment's first slot.
   for (int e = tid; e < E; e += kSegThreads) {
-    int run = base[(long long)blockIdx.x * E + e];
+    int run = base[(long long)segments * E + e] + base[(long long)blockIdx.x * E + e];
     for (int w = 0; w < kSegWarps; ++w) {
       const int c = csm[w * E + e];
       csm[w * E + e] = run;
@@ -322,7 +326,7 @@ __global__ void __launch_bounds__(kSegThreads)
 int moe_align_max_experts() { return kMaxExperts; }
 
 long long moe_align_scratch_ints(long long numel, int num_experts) {
-  return (numel + kSeg - 1) / kSeg * (long long)num_experts;
+  return ((numel + kSeg - 1) / kSeg + 1) * (long long)num_experts + 1;
 }
 
 cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num_experts,
@@ -352,7 +356,7 @@ cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num
   if (err != cudaSuccess) return err;
   return launch_pdl(align_scatter_kernel, dim3(segments), dim3(kSegThreads),
                     sizeof(int) * kSegWarps * E, stream, topk_ids, numel, E,
-                    (const int*)scratch, sorted_ids, sorted_cap);
+                    (const int*)scratch, segments, sorted_ids, sorted_cap);
 }
 
 cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_experts, int block_size,
