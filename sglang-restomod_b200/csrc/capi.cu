@@ -171,13 +171,13 @@ int run_tc(int32_t quant, StreamParams& p, WsView& ws, bool planned, cudaStream_
 // Route count from which the layer aligns with the multi-CTA kernels.
 constexpr int64_t kAlignMultiMin = 4096;
 
-// Dense calls use the tcgen05 GEMM once M exceeds the decode range and its
-// items (192-row chunks x 128-row weight blocks, no K split) fill at least
-// half of the SMs; below that the stream GEMM's K split keeps every SM busy.
+// Dense calls use the tcgen05 GEMM once M exceeds the decode range: measured
+// faster than the stream GEMM's 64-row tile even when its items (192-row
+// chunks x 128-row weight blocks) cover only a quarter of the SMs.
 constexpr int64_t kTcDenseMinRows = 33;
 bool use_tc_dense(int64_t m, int64_t n) {
-  const int64_t items = (m + 191) / 192 * (n / 128);
-  return m >= kTcDenseMinRows && 2 * items >= device_sm_count();
+  (void)n;
+  return m >= kTcDenseMinRows;
 }
 
 // Moe calls take the tcgen05 GEMM for blocks of 64 and more (the prefill
@@ -375,7 +375,20 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.out = y;
     p.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
     p.out_f16 = y_dtype == B200_DTYPE_F16;
-    return run_tc(quant, p, ws, false, st);
+    // Too few (row chunk, weight block) items for the SMs: split K and sum
+    // the parts in the workspace's fp32 partial region.
+    p.ksplit = 1;
+    const int64_t kch = k / 128, sms = device_sm_count();
+    const int64_t items = (m + 191) / 192 * (n / 128);
+    if (items < sms && m * n <= (int64_t)max_grid_slots() * kWsSlotFloats) {
+      const int64_t want = (2 * sms + items - 1) / items;
+      int64_t kpart = (kch + want - 1) / want;
+      if (kpart < 2) kpart = 2;
+      p.ksplit = (int)((kch + kpart - 1) / kpart);
+    }
+    rc = run_tc(quant, p, ws, false, st);
+    if (rc || p.ksplit <= 1) return rc;
+    return check_cuda(launch_tc_split_finish(p, st), "split-K finish launch");
   }
   int64_t used = 0;
   const __half* x16 = nullptr;

@@ -37,6 +37,7 @@ struct StreamParams {
   void* out;
   long long ldo;
   int out_f16;           // 1: f16 output, 0: bf16
+  int ksplit;            // tcgen05 dense mode: K ranges per item (1 = none); >1 sums into ws
   float* ws;             // split-pair partial sums, kWsSlotFloats per grid slot, zeroed
   int* ws_cnt;           // one arrival counter per grid slot, zeroed
   int* status;           // device error bits
@@ -64,6 +65,9 @@ int64_t tc_plan_bytes(int cap);
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream);
 cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
                            cudaStream_t stream);
+// After a dense tcgen05 GEMM with ksplit > 1: fp32 sums in p.ws -> output
+// (SiLU*up for a fused gated bank), and the sums back to zero.
+cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream);
 
 // moe_align_block_size: stable expert-major counting sort with per-expert
 // padding to block_size.

@@ -245,7 +245,21 @@ struct Item {
   int rb;           // 128-row weight block
   long long slot0;  // first route slot (moe) or first activation row (dense)
   int rows;         // route slots / rows covered (<= kNMax)
+  int kc0, nk;      // 128-K units kc0 .. kc0+nk-1 (all of K unless split)
 };
+
+// Dense items with K split: item g = ((chunk * nrb) + rb) * ksplit + part.
+__device__ __forceinline__ void item_k_range(const StreamParams& p, long long g, int kch,
+                                             int& kc0, int& nk) {
+  if (p.sorted_ids != nullptr || p.ksplit <= 1) {
+    kc0 = 0;
+    nk = kch;
+    return;
+  }
+  const int kpart = (kch + p.ksplit - 1) / p.ksplit;
+  kc0 = (int)(g % p.ksplit) * kpart;
+  nk = kch - kc0 < kpart ? kch - kc0 : kpart;
+}
 
 __device__ __forceinline__ int2 plan_entry(const StreamParams& p, const int2* plan, long long g,
                                            int nrb) {
@@ -253,16 +267,21 @@ __device__ __forceinline__ int2 plan_entry(const StreamParams& p, const int2* pl
   return __ldg(plan + g / nrb);
 }
 
-__device__ __forceinline__ Item make_item(const StreamParams& p, int2 pe, long long g, int nrb) {
+__device__ __forceinline__ Item make_item(const StreamParams& p, int2 pe, long long g, int nrb,
+                                          int kch) {
   Item it;
-  const long long sb = g / nrb;
-  it.rb = (int)(g - sb * nrb);
+  item_k_range(p, g, kch, it.kc0, it.nk);
   if (p.sorted_ids == nullptr) {
+    const long long gb = p.ksplit > 1 ? g / p.ksplit : g;
+    const long long sb = gb / nrb;
+    it.rb = (int)(gb - sb * nrb);
     it.e = 0;
     it.slot0 = sb * kNMax;
     const long long left = (long long)p.dense_m - it.slot0;
     it.rows = left < kNMax ? (int)left : kNMax;
   } else {
+    const long long sb = g / nrb;
+    it.rb = (int)(g - sb * nrb);
     it.e = pe.y >> 9;
     it.slot0 = pe.x;
     it.rows = pe.y & 511;
@@ -369,7 +388,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   long long items;
   if (dense) {
-    items = (long long)((p.dense_m + kNMax - 1) / kNMax) * nrb;
+    items = (long long)((p.dense_m + kNMax - 1) / kNMax) * nrb * (p.ksplit > 1 ? p.ksplit : 1);
   } else {
     items = (long long)__ldg(plan_count) * nrb;
   }
@@ -384,7 +403,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     int2 pe_next = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
     for (long long j = 0; j < my_items && ok; ++j) {
-      const Item it = make_item(p, pe_next, g0 + j * gs, nrb);
+      const Item it = make_item(p, pe_next, g0 + j * gs, nrb, kch);
       if (j + 1 < my_items) pe_next = plan_entry(p, plan, g0 + (j + 1) * gs, nrb);
       const float* stop = nullptr;
       const float* sbot = nullptr;
@@ -397,30 +416,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Lane l holds the scales of units 32c + l (window c); the row maxima
         // give the item's exponents. Runs right after the previous item's
         // last unit was issued, while the raw ring is full.
-        ct = ldg_or0(stop, lane, kch);
-        cb = ldg_or0(sbot, lane, kch);
-        float mt = fabsf(ct), mb = fabsf(cb);
-        for (int k = 32 + lane; k < kch; k += 32) {
+        float mt = 0.f, mb = 0.f;
+        for (int k = lane; k < kch; k += 32) {
           mt = fmaxf(mt, fabsf(__ldg(stop + k)));
           mb = fmaxf(mb, fabsf(__ldg(sbot + k)));
         }
         et = max_exponent(warp_max(mt));
         eb = max_exponent(warp_max(mb));
-        nt = ldg_or0(stop, 32 + lane, kch);
-        nb = ldg_or0(sbot, 32 + lane, kch);
+        // Scale windows from the item's first unit on.
+        ct = ldg_or0(stop, it.kc0 + lane, kch);
+        cb = ldg_or0(sbot, it.kc0 + lane, kch);
+        nt = ldg_or0(stop, it.kc0 + 32 + lane, kch);
+        nb = ldg_or0(sbot, it.kc0 + 32 + lane, kch);
       }
       // The unit's rows of 128 bytes in the weight tensor map.
       constexpr int kUnitRows = (kFp4 ? kFp4UnitBytes : kFp8UnitBytes) / 128;
       const int row0 = (int)(((long long)it.e * nrb + it.rb) * kch * kUnitRows);
-      for (int kc = 0; kc < kch; ++kc, ++u) {
-        if (!kFp4 && kc > 0 && (kc & 31) == 0) {
+      for (int i = 0; i < it.nk; ++i, ++u) {
+        const int kc = it.kc0 + i;
+        if (!kFp4 && i > 0 && (i & 31) == 0) {
           ct = nt;
           cb = nb;
           nt = ldg_or0(stop, kc + 32 + lane, kch);
           nb = ldg_or0(sbot, kc + 32 + lane, kch);
         }
-        const float vt = __shfl_sync(0xffffffffu, ct, kc & 31);
-        const float vb = __shfl_sync(0xffffffffu, cb, kc & 31);
+        const float vt = __shfl_sync(0xffffffffu, ct, i & 31);
+        const float vb = __shfl_sync(0xffffffffu, cb, i & 31);
         const int s = (int)(u % kRawStages);
         const uint32_t ph = (uint32_t)((u / kRawStages) & 1);
         int good = 1;
@@ -464,7 +485,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t)buf * kAccCols;
       uint32_t idesc = 0;
-      for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
+      int kc0, nk;
+      item_k_range(p, g0 + j * gs, kch, kc0, nk);
+      for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
         const int s = (int)(t % kStages);
         ok = warp_wait(&ctl->full[s], (uint32_t)((t / kStages) & 1), ctl, p.status);
         if (!ok) break;
@@ -506,7 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int2 pe_a = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
     int ids_a[kLoadPasses];
     {
-      const Item it0 = make_item(p, pe_a, g0, nrb);
+      const Item it0 = make_item(p, pe_a, g0, nrb, kch);
 #pragma unroll
       for (int q = 0; q < kLoadPasses; ++q)
         ids_a[q] = my_items > 0 ? slot_id(p, it0, q * (kLoadThreads / 2) + rsub) : -1;
@@ -527,18 +550,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Prefetch the next item's route ids and the one after's plan entry.
       int2 pe_c = make_int2(0, 0);
       if (j + 1 < my_items) {
-        const Item itn = make_item(p, pe_b, g0 + (j + 1) * gs, nrb);
+        const Item itn = make_item(p, pe_b, g0 + (j + 1) * gs, nrb, kch);
 #pragma unroll
         for (int q = 0; q < kLoadPasses; ++q)
           ids_a[q] = slot_id(p, itn, q * (kLoadThreads / 2) + rsub);
         if (j + 2 < my_items) pe_c = plan_entry(p, plan, g0 + (j + 2) * gs, nrb);
       }
-      for (int ts = 0; ts < 2 * kch; ++ts, ++t) {
+      int kc0, nk;
+      item_k_range(p, g0 + j * gs, kch, kc0, nk);
+      for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
         const int s = (int)(t % kStages);
         ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
         if (!ok) break;
         uint8_t* B = smem + kOffB + s * kBTile;
-        const long long kofs = (long long)(ts >> 1) * 128 + (ts & 1) * 64;
+        const long long kofs = (long long)(kc0 + (ts >> 1)) * 128 + (ts & 1) * 64;
 #pragma unroll
         for (int q = 0; q < kLoadPasses; ++q) {
           if (rowp[q] != nullptr) {
@@ -569,10 +594,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int r8 = m & 7;
     const int rbase = (m >> 4) * 16 + (r8 >> 1);  // 128-byte row of q = 0
     const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
-    const long long units = my_items * kch;
-    long long t = 0;
+    long long t = 0, u = 0;
     bool ok = true;
-    for (long long u = 0; u < units && ok; ++u) {
+    int nk_left = 0;  // units left in the current item
+    for (long long j = 0; ok;) {
+      if (nk_left == 0) {
+        if (j >= my_items) break;
+        int kc0;
+        item_k_range(p, g0 + j * gs, kch, kc0, nk_left);
+        ++j;
+      }
+      --nk_left;
       const int rs = (int)(u % kRawStages);
       ok = warp_wait(&ctl->raw_full[rs], (uint32_t)((u / kRawStages) & 1), ctl, p.status);
       if (!ok) break;
@@ -652,6 +684,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->raw_empty[rs]);
+      ++u;
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -667,7 +700,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int kGroups = kNMax / 32;
     for (long long j = eg; j < my_items; j += 2) {
       const long long g = g0 + j * gs;
-      const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb);
+      const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
       float fself = 1.f;  // this lane's row: 2^E (FP8), 1 (NVFP4)
       if constexpr (!kFp4) {
         const float* stop;
@@ -729,6 +762,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           // (scaled) up value of the row 8 lanes below.
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] *= fself;
+          if (p.ksplit > 1) {
+            // K split (dense): add this part's sums; the finishing kernel
+            // applies the activation. Gate and up rows land in columns j and
+            // N/2 + j of the [rows][N] fp32 buffer.
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (orw[i] >= 0) atomicAdd(p.ws + (long long)orw[i] * p.N + mycol, v[i]);
+            continue;
+          }
           if (fused) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -871,6 +913,30 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int* __restrict__ e
   griddep_launch_dependents();
 }
 
+__global__ void __launch_bounds__(256) tc_split_finish_kernel(const StreamParams p) {
+  griddep_wait();
+  const int cols = p.fuse_act ? p.N / 2 : p.N;
+  const long long total = (long long)p.dense_m * cols;
+  for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
+       id += (long long)gridDim.x * blockDim.x) {
+    const long long r = id / cols;
+    const int c = (int)(id - r * cols);
+    float* row = p.ws + r * p.N;
+    float v = row[c];
+    row[c] = 0.f;
+    if (p.fuse_act) {
+      const float up = row[p.N / 2 + c];
+      row[p.N / 2 + c] = 0.f;
+      v = silu_f32(v) * up;
+    }
+    if (p.out_f16)
+      reinterpret_cast<__half*>(p.out)[r * p.ldo + c] = __float2half_rn(v);
+    else
+      reinterpret_cast<__nv_bfloat16*>(p.out)[r * p.ldo + c] = __float2bfloat16_rn(v);
+  }
+  griddep_launch_dependents();
+}
+
 }  // namespace
 
 int64_t tc_plan_bytes(int cap) { return 256 + (int64_t)cap * (int64_t)sizeof(int2); }
@@ -887,6 +953,15 @@ cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaS
   const int vblock = p.block_m > kNMax ? p.block_m / 2 : p.block_m;
   return launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, stream, p.expert_ids, p.ntpp,
                     p.block_m, vblock, p.max_groups, p.E, kNMax / vblock, plan, count, cap);
+}
+
+cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
+  const long long work = (long long)p.dense_m * (p.fuse_act ? p.N / 2 : p.N);
+  long long blocks = (work + 255) / 256;
+  const long long cap = (long long)device_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return launch_pdl(tc_split_finish_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, p);
 }
 
 namespace {
