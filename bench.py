@@ -195,7 +195,14 @@ class MoEWorkload:
         e_local = shape.experts // world
         self.layer = QuantMoELayer.synthetic(shape, self.quant, device,
                                              first_expert=rank * e_local, num_experts=e_local)
-        self.model = ExpertParallelMoE(self.layer, shape.experts, rank, world)
+        # N > 1: the peer-memory exchange (NVLink P2P stores, no host sync) by
+        # default; --transport nccl selects the all-to-all baseline.
+        self.transport = spec.get("transport", "peer") if world > 1 else "local"
+        if self.transport == "peer":
+            self.model = ExpertParallelMoE(self.layer, shape.experts, rank, world,
+                                           transport="peer", max_tokens=self.tokens)
+        else:
+            self.model = ExpertParallelMoE(self.layer, shape.experts, rank, world)
         # Each rank's tokens are its own seeded batch.
         self.x = synth.activations(self.tokens, shape.hidden, device, seed=100 + rank)
         self.ids, self.w = synth.route(self.tokens, shape.experts, shape.top_k, device, seed=200 + rank)
@@ -224,8 +231,11 @@ class MoEWorkload:
         return h2d, self.h_out.numel() * 2
 
     def launches_per_step(self):
+        if self.transport == "peer":
+            return self.model.peer_launches_per_forward(self.x.dtype)
         # local layer (+ shared); under EP one more combine of returned rows
-        return self.layer.launches_per_forward() + (1 if self.world > 1 else 0)
+        return (self.layer.launches_per_forward(self.x.dtype, self.tokens)
+                + (1 if self.world > 1 else 0))
 
     def algorithmic(self):
         """(bytes, flops) of one step on this rank (realized routing)."""
@@ -440,7 +450,9 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4-decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--eager", action="store_true", help="no CUDA graph replay at N=1")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel exchange at N > 1")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -456,6 +468,7 @@ def main() -> int:
     rank, world, local_rank = dist_setup()
     device = torch.device("cuda", torch.cuda.current_device())
     spec = parse_workload(args.workload)
+    spec["transport"] = args.transport
     if spec["kind"] == "dense":
         wl = DenseWorkload(spec, device)
     elif spec["kind"] in ("ep", "moe"):
@@ -469,9 +482,10 @@ def main() -> int:
         wl.step()
     torch.cuda.synchronize()
     # One process per GPU replays the step as a CUDA graph, as a serving
-    # engine does at decode; under expert parallelism the all-to-all split
-    # sizes are read on the host every step, so that path runs eagerly.
-    use_graph = world == 1 and not args.eager
+    # engine does at decode. Under expert parallelism the peer transport has
+    # no host sync and is replayed too (every rank in lockstep); the NCCL
+    # transport reads its all-to-all split sizes on the host and runs eagerly.
+    use_graph = not args.eager and (world == 1 or args.transport == "peer")
     step_fn, e2e_fn = wl.step, wl.step_e2e
     if use_graph:
         for _ in range(2):

@@ -63,7 +63,8 @@ int b200_num_sms(void);
 /*
  * Device-side error bits recorded in a workspace (1 = a pipeline wait timed
  * out, 2 = an expert id >= E reached a GEMM, 4 = a route pointed past the
- * activation rows). Synchronizes `stream`; clears the bits when reset != 0.
+ * activation rows) or an expert-parallel region (8 = a wait on another rank
+ * timed out). Synchronizes `stream`; clears the bits when reset != 0.
  */
 int b200_workspace_status(void* workspace, int32_t* bits, int32_t reset, void* stream);
 
@@ -222,6 +223,70 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
                            float routed_scaling_factor, const void* shared_out,
                            int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
                            int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------- expert parallelism (peer memory) */
+
+/*
+ * Expert-parallel token exchange over NVLink peer memory, replacing the
+ * all-to-all around the expert compute. The reference's expert parallelism
+ * is upstream SGLang's dispatcher (global -> local expert ids, foreign routes
+ * -1: quant/sm70_fp8_moe/method.py:8-12, 253-283) plus the method's combine
+ * (method.py:305-309); these entry points give the same layer output with
+ * experts split contiguously, num_experts / world per rank.
+ *
+ * Every rank owns one exchange region of b200_ep_region_bytes() (zero-filled
+ * before first use, 256-byte aligned, identical arguments on every rank) and
+ * maps every peer's region (b200_ipc_get_handle / b200_ipc_open_handle, the
+ * handles exchanged by the caller). peer_regions is a DEVICE array of `world`
+ * 64-bit addresses: entry r = rank r's region as mapped in this process (its
+ * own entry = its own region). One layer forward on every rank, in this order
+ * on one stream:
+ *   b200_ep_dispatch        rows + routing to the owners (P2P stores)
+ *   b200_ep_expert_forward  wait for every source, align, gate/up + down GEMMs
+ *                           storing each weighted row into its source's region
+ *   b200_ep_combine         wait for every owner, sum the top-k rows per
+ *                           token (+ shared_out) x routed_scaling_factor
+ * No host synchronization: the three calls can be captured in a CUDA graph.
+ * Waits on other ranks are bounded (2 s) and set bit 8 in the region's status
+ * word (read it with b200_workspace_status(region, ...)). Every rank must run
+ * the same sequence of calls; calls on one region must not overlap.
+ */
+int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden);
+
+/* CUDA IPC of the allocation holding dev_ptr: a 64-byte handle plus the
+ * pointer's offset inside it; open maps a peer's allocation, close unmaps. */
+int b200_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset);
+int b200_ipc_open_handle(const void* handle, int64_t offset, void** dev_ptr);
+int b200_ipc_close_handle(void* dev_ptr, int64_t offset);
+
+/* Source side: x [tokens, hidden] bf16/f16, topk_ids / topk_weights
+ * [tokens, top_k] (global expert ids; ids outside [0, num_experts) are not
+ * sent), tokens <= max_tokens. */
+int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
+                     const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
+                     int32_t num_experts, int32_t rank, int32_t world, const uint64_t* peer_regions,
+                     void* region, int64_t max_tokens, void* stream);
+
+/* Owner side: this rank's local_experts experts (w13: gated bank
+ * [local_experts, 2*inter, hidden], w2: [local_experts, hidden, inter], as for
+ * b200_moe_layer_forward). block_size as for b200_moe_layer_forward, sized
+ * for about max_tokens * top_k routes per rank. */
+int64_t b200_ep_expert_workspace_bytes(int32_t world, int64_t max_tokens, int32_t top_k,
+                                       int64_t inter, int32_t local_experts, int32_t block_size);
+int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t local_experts,
+                           const uint8_t* w13_packed, const float* w13_scales,
+                           const float* w13_global, const uint8_t* w2_packed,
+                           const float* w2_scales, const float* w2_global, int32_t block_size,
+                           int32_t rank, int32_t world, const uint64_t* peer_regions, void* region,
+                           int64_t max_tokens, int32_t top_k, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+
+/* Source side: out [tokens, hidden] = rsf * sum_k (weighted rows returned for
+ * topk_ids[t, k]) + shared_out[t] (optional). */
+int b200_ep_combine(int64_t tokens, int64_t hidden, const int32_t* topk_ids, int32_t top_k,
+                    int32_t num_experts, float routed_scaling_factor, const void* shared_out,
+                    int32_t shared_dtype, void* out, int32_t out_dtype, int32_t world, void* region,
+                    int64_t max_tokens, void* stream);
 
 #ifdef __cplusplus
 }

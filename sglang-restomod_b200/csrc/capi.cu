@@ -3,6 +3,7 @@
 // each one replaces) in include/b200moe.h.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/b200moe.h"
@@ -632,6 +633,285 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
 
   return b200_moe_combine(routed, B200_DTYPE_F16, topk_ids, num_experts, tokens, top_k, hidden,
                           routed_scaling_factor, shared_out, shared_dtype, out, out_dtype, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------ expert parallelism
+
+namespace {
+
+using CuMemGetAddressRange = int (*)(unsigned long long*, size_t*, unsigned long long);
+
+CuMemGetAddressRange get_address_range_fn() {
+  static CuMemGetAddressRange fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CuMemGetAddressRange>(ptr);
+  }
+  return fn;
+}
+
+int check_ep_common(int32_t rank, int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden,
+                    const void* region, const uint64_t* peers) {
+  if (world < 1 || world > kEpMaxWorld)
+    return fail(B200_ERR_INVALID, "world must be in [1, %d], got %d", kEpMaxWorld, world);
+  if (rank < 0 || rank >= world) return fail(B200_ERR_INVALID, "rank %d outside [0, %d)", rank, world);
+  if (max_tokens <= 0 || top_k <= 0 || hidden <= 0 || hidden % 128)
+    return fail(B200_ERR_INVALID, "bad max_tokens=%lld top_k=%d hidden=%lld (hidden %% 128 == 0)",
+                (long long)max_tokens, top_k, (long long)hidden);
+  if ((int64_t)world * max_tokens * top_k >= (1ll << 31))
+    return fail(B200_ERR_INVALID, "world * max_tokens * top_k must stay below 2^31");
+  if (region == nullptr || (reinterpret_cast<uintptr_t>(region) % kAlign) != 0)
+    return fail(B200_ERR_INVALID, "region missing or not 256-byte aligned");
+  if (peers != nullptr && (reinterpret_cast<uintptr_t>(peers) & 7u))
+    return fail(B200_ERR_INVALID, "peer_regions must be 8-byte aligned");
+  return B200_OK;
+}
+
+// Expert-parallel owner workspace: fixed part, routing, align scratch,
+// gate_up output for every receive slot.
+struct EpWs {
+  int64_t numel, cap_a, blocks, total;
+};
+EpWs ep_ws(int32_t world, int64_t max_tokens, int32_t top_k, int64_t inter, int32_t local_experts,
+           int32_t block_size) {
+  EpWs w;
+  w.numel = (int64_t)world * max_tokens * top_k;
+  const int64_t busy = w.numel < local_experts ? w.numel : local_experts;
+  w.cap_a = w.numel + busy * (block_size - 1);
+  w.blocks = (w.cap_a + block_size - 1) / block_size;
+  w.total = stream_ws_bytes() + align_up(w.cap_a * 4) + align_up(w.blocks * 4) + align_up(4) +
+            align_up(moe_align_scratch_ints(w.numel, local_experts) * 4) +
+            align_up(w.numel * inter * 2);
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden) {
+  if (world < 1 || world > kEpMaxWorld || max_tokens <= 0 || top_k <= 0 || hidden <= 0) return -1;
+  return ep_layout(world, max_tokens * top_k, hidden).total;
+}
+
+int b200_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset) {
+  if (dev_ptr == nullptr || handle == nullptr || offset == nullptr)
+    return fail(B200_ERR_INVALID, "null argument");
+  CuMemGetAddressRange range = get_address_range_fn();
+  if (range == nullptr) return fail(B200_ERR_CUDA, "cuMemGetAddressRange is not available");
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(dev_ptr)) != 0)
+    return fail(B200_ERR_INVALID, "pointer is not device memory of this process");
+  cudaIpcMemHandle_t h;
+  int rc = check_cuda(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  if (rc) return rc;
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<unsigned long long>(dev_ptr) - base);
+  return B200_OK;
+}
+
+int b200_ipc_open_handle(const void* handle, int64_t offset, void** dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr || offset < 0)
+    return fail(B200_ERR_INVALID, "bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  int rc = check_cuda(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess),
+                      "cudaIpcOpenMemHandle");
+  if (rc) return rc;
+  *dev_ptr = static_cast<uint8_t*>(base) + offset;
+  return B200_OK;
+}
+
+int b200_ipc_close_handle(void* dev_ptr, int64_t offset) {
+  if (dev_ptr == nullptr || offset < 0) return fail(B200_ERR_INVALID, "bad argument");
+  return check_cuda(cudaIpcCloseMemHandle(static_cast<uint8_t*>(dev_ptr) - offset),
+                    "cudaIpcCloseMemHandle");
+}
+
+int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
+                     const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
+                     int32_t num_experts, int32_t rank, int32_t world, const uint64_t* peer_regions,
+                     void* region, int64_t max_tokens, void* stream) {
+  int rc = check_ep_common(rank, world, max_tokens, top_k, hidden, region, peer_regions);
+  if (rc) return rc;
+  if (!valid_dtype16(x_dtype)) return fail(B200_ERR_UNSUPPORTED, "activations must be bf16 or f16");
+  if (tokens < 0 || tokens > max_tokens)
+    return fail(B200_ERR_INVALID, "tokens %lld outside [0, max_tokens=%lld]", (long long)tokens,
+                (long long)max_tokens);
+  if (num_experts <= 0 || num_experts % world)
+    return fail(B200_ERR_INVALID, "%d experts do not split over %d ranks", num_experts, world);
+  if (peer_regions == nullptr) return fail(B200_ERR_INVALID, "null peer_regions");
+  if (tokens > 0 && (x == nullptr || topk_ids == nullptr || topk_weights == nullptr))
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (tokens > 0 && !aligned16(x)) return fail(B200_ERR_INVALID, "x must be 16-byte aligned");
+  const int64_t routes = tokens * top_k;
+  if (ep_dispatch_chunk(routes > 0 ? routes : 1) > 12288)
+    return fail(B200_ERR_UNSUPPORTED, "too many routes for one dispatch");
+  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return check_cuda(launch_ep_dispatch(x, x_dtype == B200_DTYPE_F16, tokens, hidden, topk_ids,
+                                       topk_weights, top_k, num_experts, num_experts / world, rank,
+                                       world, reinterpret_cast<const unsigned long long*>(peer_regions),
+                                       region, L, st),
+                    "ep dispatch launch");
+}
+
+int64_t b200_ep_expert_workspace_bytes(int32_t world, int64_t max_tokens, int32_t top_k,
+                                       int64_t inter, int32_t local_experts, int32_t block_size) {
+  if (world < 1 || max_tokens <= 0 || top_k <= 0 || inter <= 0 || local_experts <= 0 ||
+      block_size <= 0)
+    return -1;
+  return ep_ws(world, max_tokens, top_k, inter, local_experts, block_size).total;
+}
+
+int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t local_experts,
+                           const uint8_t* w13_packed, const float* w13_scales,
+                           const float* w13_global, const uint8_t* w2_packed,
+                           const float* w2_scales, const float* w2_global, int32_t block_size,
+                           int32_t rank, int32_t world, const uint64_t* peer_regions, void* region,
+                           int64_t max_tokens, int32_t top_k, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  int rc = check_ep_common(rank, world, max_tokens, top_k, hidden, region, peer_regions);
+  if (rc) return rc;
+  rc = check_weight_shape(quant, 2 * inter, hidden, B200_GATED_FUSED);
+  if (rc) return rc;
+  rc = check_weight_shape(quant, hidden, inter, B200_GATED_NONE);
+  if (rc) return rc;
+  if (peer_regions == nullptr || w13_packed == nullptr || w2_packed == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (local_experts <= 0 || local_experts > moe_align_max_experts())
+    return fail(B200_ERR_UNSUPPORTED, "local_experts must be in [1, %d]", moe_align_max_experts());
+  const bool tc_block = block_size >= 64 && tc_gemm_supported(block_size);
+  if (!tc_block && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
+    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32, 64, 128 or 256, got %d",
+                block_size);
+  const EpWs w = ep_ws(world, max_tokens, top_k, inter, local_experts, block_size);
+  if (workspace_bytes < w.total)
+    return fail(B200_ERR_INVALID, "workspace holds %lld bytes, needs %lld",
+                (long long)workspace_bytes, (long long)w.total);
+  WsView ws;
+  if (!carve(workspace, workspace_bytes, ws))
+    return fail(B200_ERR_INVALID, "workspace missing or misaligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  const unsigned long long* peers = reinterpret_cast<const unsigned long long*>(peer_regions);
+  uint8_t* reg = static_cast<uint8_t*>(region);
+
+  rc = check_cuda(launch_ep_receive(region, peers, world, L, local_experts, st), "ep receive launch");
+  if (rc) return rc;
+
+  const int64_t numel = w.numel;
+  int64_t used = 0;
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(w.cap_a * 4);
+  int32_t* eids = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(w.blocks * 4);
+  int32_t* ntpp = reinterpret_cast<int32_t*>(ws.scratch + used);
+  used += align_up(4);
+  int* align_scratch = reinterpret_cast<int*>(ws.scratch + used);
+  used += align_up(moe_align_scratch_ints(numel, local_experts) * 4);
+  __half* inter_out = reinterpret_cast<__half*>(ws.scratch + used);
+  used += align_up(numel * inter * 2);
+
+  const int32_t* ids = reinterpret_cast<const int32_t*>(reg + L.off_ids);
+  if (numel >= kAlignMultiMin) {
+    rc = check_cuda(launch_moe_align_multi(ids, numel, local_experts, block_size, sorted, w.cap_a,
+                                           eids, w.blocks, ntpp, align_scratch, st),
+                    "moe_align launch");
+  } else {
+    rc = check_cuda(launch_moe_align(ids, numel, local_experts, block_size, sorted, w.cap_a, eids,
+                                     w.blocks, ntpp, st),
+                    "moe_align launch");
+  }
+  if (rc) return rc;
+
+  const bool tc = use_tc_moe(quant, block_size, w.blocks);
+  StreamParams p{};
+  p.wq = w13_packed;
+  p.wscale = w13_scales;
+  p.gscale = w13_global;
+  p.x = reinterpret_cast<const __half*>(reg + L.off_recv);
+  p.ldx = hidden;
+  p.x_rows = numel;
+  p.sorted_ids = sorted;
+  p.expert_ids = eids;
+  p.ntpp = ntpp;
+  p.block_m = block_size;
+  p.max_groups = w.cap_a / block_size;
+  p.top_k = 1;
+  p.num_routes = (int)numel;
+  p.topk_w = reinterpret_cast<const float*>(reg + L.off_w);
+  p.E = local_experts;
+  p.N = (int)(2 * inter);
+  p.K = (int)hidden;
+  p.gated = 1;
+  p.fuse_act = 1;
+  p.mul_w = 0;
+  p.out = inter_out;
+  p.ldo = inter;
+  p.out_f16 = 1;
+  const int nt = block_size / 8;
+  if (tc)
+    rc = run_tc(quant, p, ws, false, st);
+  else
+    rc = run_stream(quant, nt, p, w.blocks * (2 * inter / 128) * (hidden / 128), ws, st);
+  if (rc) return rc;
+
+  StreamParams q = p;
+  q.wq = w2_packed;
+  q.wscale = w2_scales;
+  q.gscale = w2_global;
+  q.x = inter_out;
+  q.ldx = inter;
+  q.N = (int)hidden;
+  q.K = (int)inter;
+  q.gated = 0;
+  q.fuse_act = 0;
+  q.mul_w = 1;
+  q.out = nullptr;
+  q.out_rows = reinterpret_cast<const unsigned long long*>(reg + L.off_rows);
+  q.ldo = hidden;
+  q.out_f16 = 1;
+  if (tc)
+    rc = run_tc(quant, q, ws, true, st);
+  else
+    rc = run_stream(quant, nt, q, w.blocks * (hidden / 128) * (inter / 128), ws, st);
+  if (rc) return rc;
+  return check_cuda(launch_ep_signal(region, peers, rank, world, L, st), "ep signal launch");
+}
+
+int b200_ep_combine(int64_t tokens, int64_t hidden, const int32_t* topk_ids, int32_t top_k,
+                    int32_t num_experts, float routed_scaling_factor, const void* shared_out,
+                    int32_t shared_dtype, void* out, int32_t out_dtype, int32_t world, void* region,
+                    int64_t max_tokens, void* stream) {
+  int rc = check_ep_common(0, world, max_tokens, top_k, hidden, region, nullptr);
+  if (rc) return rc;
+  if (!valid_dtype16(out_dtype) || (shared_out != nullptr && !valid_dtype16(shared_dtype)))
+    return fail(B200_ERR_UNSUPPORTED, "dtypes must be bf16 or f16");
+  if (tokens < 0 || tokens > max_tokens)
+    return fail(B200_ERR_INVALID, "tokens %lld outside [0, max_tokens=%lld]", (long long)tokens,
+                (long long)max_tokens);
+  if (num_experts <= 0) return fail(B200_ERR_INVALID, "bad num_experts");
+  if (tokens > 0 && (topk_ids == nullptr || out == nullptr))
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (!aligned16(out) || (shared_out && !aligned16(shared_out)))
+    return fail(B200_ERR_INVALID, "buffers must be 16-byte aligned");
+  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  return check_cuda(launch_ep_combine(region, L, world, tokens, top_k, topk_ids, num_experts,
+                                      routed_scaling_factor, shared_out,
+                                      shared_dtype == B200_DTYPE_F16, out,
+                                      out_dtype == B200_DTYPE_F16,
+                                      reinterpret_cast<cudaStream_t>(stream)),
+                    "ep combine launch");
 }
 
 }  // extern "C"

@@ -20,6 +20,7 @@ enum DeviceError : int {
   kDevWaitTimeout = 1,   // an mbarrier wait gave up (never expected)
   kDevBadExpert = 2,     // an expert id outside [0, E) reached a GEMM
   kDevBadRoute = 4,      // a route index outside the activation rows
+  kDevPeerTimeout = 8,   // an expert-parallel wait on another rank gave up
 };
 
 // A wait that has not completed after this many nanoseconds records

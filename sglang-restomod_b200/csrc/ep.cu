@@ -1,0 +1,419 @@
+// Expert-parallel token exchange over peer memory (NVLink / NVSwitch P2P).
+//
+// Replaces the all-to-all dispatch / combine around the expert compute of an
+// expert-parallel MoE layer. The reference has no all-to-all: its expert
+// parallelism is upstream SGLang's dispatcher, which maps global expert ids to
+// local ones and marks foreign routes -1
+// (sglang_restomod/quant/sm70_fp8_moe/method.py:8-12, 253-283), and the expert
+// method's combine (method.py:305-309). Here every rank owns a contiguous
+// range of experts and one forward is four launches per rank, none of which
+// involves the host:
+//
+//   dispatch (source)  every route's activation row is converted to f16 and
+//                      stored straight into its owner's receive segment for
+//                      this source (P2P stores), with (local expert, router
+//                      weight, route index); the grid's last CTA publishes the
+//                      per-owner counts and raises the owner's dispatch flag;
+//   receive  (owner)   waits for every source's flag, marks slots past each
+//                      source's count empty and builds the table of
+//                      destination rows (the source's combine buffer);
+//   expert GEMMs       (capi.cu) align + gate/up + down, the down GEMM's
+//                      epilogue storing each route's weighted row directly
+//                      into the source's combine buffer through the table;
+//   signal   (owner)   raises each source's combine flag once the down GEMM
+//                      has completed;
+//   combine  (source)  waits for every owner's flag, sums the k rows of each
+//                      token (+ shared expert, x routed_scaling_factor) and
+//                      advances the step counter.
+//
+// Flags carry the step number (the region's local counter + 1), so nothing is
+// reset between steps; every rank runs the same steps in the same order.
+// Every wait is bounded (kWaitLimitNs) and reports kDevPeerTimeout in the
+// region's status word instead of hanging. No TMA and no multicast: peer
+// memory is touched only by plain loads and stores.
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200 {
+namespace {
+
+constexpr int kEpThreads = 256;
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int* hdr_of(uint8_t* region) { return reinterpret_cast<int*>(region); }
+
+// Current step number + 1: the value this step's flags carry.
+__device__ __forceinline__ int next_epoch(uint8_t* region) {
+  return *reinterpret_cast<volatile int*>(hdr_of(region) + kEpHdrEpoch) + 1;
+}
+
+// Thread `who` < world waits until flags[who] reaches `want` (wrap-safe
+// compare). Returns false after kWaitLimitNs, having set kDevPeerTimeout.
+__device__ bool wait_flag(const int* flag, int want, int* status) {
+  if (ld_acquire_sys(flag) - want >= 0) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_sys(flag) - want >= 0) return true;
+    if ((i & 63u) == 0u && global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(status, kDevPeerTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 raw) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+    __half2 h = __floats2half2_rn(__low2float(b), __high2float(b));
+    o[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ void st_u128(void* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+struct DispatchParams {
+  const void* x;  // [tokens, hidden] bf16 / f16
+  int x_f16;
+  long long tokens, hidden;
+  const int* ids;  // [tokens * top_k] global expert ids
+  const float* w;  // [tokens * top_k]
+  int top_k, num_experts, experts_per_rank, rank, world;
+  const unsigned long long* peers;  // [world] region bases in this process
+  uint8_t* region;                  // this rank's region
+  EpLayout L;
+  int chunk;  // routes per CTA (multiple of 32)
+};
+
+// One CTA per chunk of routes. Positions inside an owner's segment follow
+// route order (stable), so a receiver's slots are in the source's route order.
+__global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const DispatchParams p) {
+  extern __shared__ int pos[];  // [chunk]
+  __shared__ int base[kEpMaxWorld];
+  __shared__ int mine[kEpMaxWorld];
+  __shared__ int last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long routes = p.tokens * p.top_k;
+  const long long c0 = (long long)blockIdx.x * p.chunk;
+  const long long c1 = c0 + p.chunk < routes ? c0 + p.chunk : routes;
+  const int epoch = next_epoch(p.region);
+  int* hdr = hdr_of(p.region);
+  if (tid < kEpMaxWorld) {
+    base[tid] = 0;
+    mine[tid] = 0;
+  }
+  __syncthreads();
+  // Routes of earlier chunks per owner.
+  for (long long r = tid; r < c0; r += kEpThreads) {
+    const int e = __ldg(p.ids + r);
+    if (e >= 0 && e < p.num_experts) atomicAdd(&base[e / p.experts_per_rank], 1);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (long long g = c0; g < c1; g += 32) {
+      const long long r = g + lane;
+      int o = -1;
+      if (r < c1) {
+        const int e = __ldg(p.ids + r);
+        if (e >= 0 && e < p.num_experts) o = e / p.experts_per_rank;
+      }
+      int mypos = -1;
+      for (int d = 0; d < p.world; ++d) {
+        const unsigned m = __ballot_sync(0xffffffffu, o == d);
+        if (o == d) mypos = base[d] + __popc(m & ((1u << lane) - 1u));
+        __syncwarp();
+        if (lane == 0) {
+          base[d] += __popc(m);
+          mine[d] += __popc(m);
+        }
+        __syncwarp();
+      }
+      if (r < c1) pos[r - c0] = mypos;
+    }
+  }
+  __syncthreads();
+  // Rows: one warp per route, 16 bytes per lane per access.
+  const long long h8 = p.hidden / 8;
+  for (long long r = c0 + warp; r < c1; r += kEpThreads / 32) {
+    const int ps = pos[r - c0];
+    if (ps < 0) continue;
+    const int e = __ldg(p.ids + r);
+    const int o = e / p.experts_per_rank;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.peers[o]);
+    const long long slot = (long long)p.rank * p.L.cap + ps;
+    if (lane == 0) {
+      reinterpret_cast<int*>(dst + p.L.off_ids)[slot] = e - o * p.experts_per_rank;
+      reinterpret_cast<float*>(dst + p.L.off_w)[slot] = __ldg(p.w + r);
+      reinterpret_cast<int*>(dst + p.L.off_orig)[slot] = (int)r;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(p.x) + (r / p.top_k) * h8;
+    uint8_t* drow = dst + p.L.off_recv + slot * p.hidden * 2;
+    for (long long v = lane; v < h8; v += 32) {
+      uint4 val = __ldg(src + v);
+      if (!p.x_f16) val = bf16x8_to_f16x8(val);
+      st_u128(drow + v * 16, val);
+    }
+  }
+  // Publish: this CTA's per-owner counts, then (last CTA) the totals + flags.
+  if (tid < p.world && mine[tid] != 0)
+    atomicAdd(reinterpret_cast<int*>(p.region + p.L.off_cnt_local) + tid, mine[tid]);
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(hdr + kEpHdrDispatchDone, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid < p.world) {
+    const int n = atomicExch(reinterpret_cast<int*>(p.region + p.L.off_cnt_local) + tid, 0);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.peers[tid]);
+    *reinterpret_cast<volatile int*>(dst + p.L.off_count + 4 * p.rank) = n;
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<int*>(dst + p.L.off_dflag) + p.rank, epoch);
+  }
+  if (tid == 0) hdr[kEpHdrDispatchDone] = 0;
+}
+
+// Owner: wait for every source, then per slot keep (local expert, weight) or
+// mark it empty, and point the slot's output row at the source's combine
+// buffer. Every CTA takes the waits itself.
+__global__ void __launch_bounds__(kEpThreads) ep_receive_kernel(
+    uint8_t* region, const unsigned long long* peers, int world, EpLayout L, int experts_local) {
+  __shared__ int cnt[kEpMaxWorld];
+  const int tid = threadIdx.x;
+  int* hdr = hdr_of(region);
+  const int epoch = next_epoch(region);
+  if (tid < world) {
+    const int* flag = reinterpret_cast<const int*>(region + L.off_dflag) + tid;
+    int n = 0;
+    if (wait_flag(flag, epoch, hdr + kEpHdrStatus)) {
+      n = __ldcg(reinterpret_cast<const int*>(region + L.off_count) + tid);
+      n = n < 0 ? 0 : (n > L.cap ? (int)L.cap : n);
+    }
+    cnt[tid] = n;
+  }
+  __syncthreads();
+  __threadfence();
+  int* ids = reinterpret_cast<int*>(region + L.off_ids);
+  float* wts = reinterpret_cast<float*>(region + L.off_w);
+  const int* orig = reinterpret_cast<const int*>(region + L.off_orig);
+  unsigned long long* rows = reinterpret_cast<unsigned long long*>(region + L.off_rows);
+  const long long total = (long long)world * L.cap;
+  for (long long slot = blockIdx.x * (long long)kEpThreads + tid; slot < total;
+       slot += (long long)gridDim.x * kEpThreads) {
+    const int s = (int)(slot / L.cap);
+    const long long j = slot - (long long)s * L.cap;
+    int id = -1;
+    if (j < cnt[s]) {
+      const int lid = __ldcg(ids + slot);
+      const int r = __ldcg(orig + slot);
+      if (lid >= 0 && lid < experts_local && r >= 0 && r < L.cap) {
+        id = lid;
+        rows[slot] = peers[s] + (unsigned long long)L.off_comb +
+                     (unsigned long long)r * (unsigned long long)L.hidden * 2ull;
+        wts[slot] = __ldcg(wts + slot);
+      }
+    }
+    ids[slot] = id;
+  }
+}
+
+// Owner, after its down GEMM has completed (plain stream order): raise each
+// source's combine flag.
+__global__ void ep_signal_kernel(uint8_t* region, const unsigned long long* peers, int rank,
+                                 int world, EpLayout L) {
+  const int tid = threadIdx.x;
+  const int epoch = next_epoch(region);
+  __threadfence_system();
+  if (tid < world) {
+    uint8_t* dst = reinterpret_cast<uint8_t*>(peers[tid]);
+    st_release_sys(reinterpret_cast<int*>(dst + L.off_cflag) + rank, epoch);
+  }
+}
+
+struct CombineParams {
+  uint8_t* region;
+  EpLayout L;
+  int world;
+  long long tokens;
+  int top_k;
+  const int* topk_ids;  // routes with ids outside [0, E) were not dispatched
+  int num_experts;
+  float scale;
+  const void* shared_out;
+  int shared_f16;
+  void* out;
+  int out_f16;
+};
+
+// Source: wait for every owner, then out[t] = scale * sum_k rows[t*k + k] (+
+// shared[t]); the last CTA advances the step counter.
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const CombineParams p) {
+  __shared__ int last;
+  const int tid = threadIdx.x;
+  int* hdr = hdr_of(p.region);
+  const int epoch = next_epoch(p.region);
+  if (tid < p.world) {
+    const int* flag = reinterpret_cast<const int*>(p.region + p.L.off_cflag) + tid;
+    wait_flag(flag, epoch, hdr + kEpHdrStatus);
+  }
+  __syncthreads();
+  __threadfence();
+  const uint8_t* rows = p.region + p.L.off_comb;
+  const long long hidden = p.L.hidden;
+  const long long h8 = hidden / 8;
+  const long long total = p.tokens * h8;
+  for (long long id = blockIdx.x * (long long)kEpThreads + tid; id < total;
+       id += (long long)gridDim.x * kEpThreads) {
+    const long long t = id / h8;
+    const long long c = (id - t * h8) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < p.top_k; ++k) {
+      const int e = __ldg(p.topk_ids + t * p.top_k + k);
+      if (e < 0 || e >= p.num_experts) continue;
+      const uint4 raw =
+          __ldcg(reinterpret_cast<const uint4*>(rows + ((t * p.top_k + k) * hidden + c) * 2));
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= p.scale;
+    if (p.shared_out != nullptr) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const uint8_t*>(p.shared_out) + (t * hidden + c) * 2));
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f;
+        if (p.shared_f16)
+          f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        else
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (p.out_f16) {
+        __half2 h = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (t * hidden + c) * 2) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(hdr + kEpHdrCombineDone, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (last && tid == 0) {
+    hdr[kEpHdrCombineDone] = 0;
+    __threadfence();
+    atomicExch(hdr + kEpHdrEpoch, epoch);
+  }
+}
+
+int ep_grid(long long work) {
+  long long blocks = (work + kEpThreads - 1) / kEpThreads;
+  const long long cap = (long long)device_sm_count() * 4;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+}  // namespace
+
+int ep_dispatch_chunk(long long routes) {
+  const long long ctas = 2ll * device_sm_count();
+  long long chunk = (routes + ctas - 1) / ctas;
+  chunk = (chunk + 31) / 32 * 32;
+  return chunk < 32 ? 32 : (int)chunk;
+}
+
+cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
+                               const int* ids, const float* w, int top_k, int num_experts,
+                               int experts_per_rank, int rank, int world,
+                               const unsigned long long* peers, void* region, const EpLayout& L,
+                               cudaStream_t stream) {
+  // With no routes one CTA still publishes this step's (zero) counts and flags.
+  const long long routes = tokens * top_k;
+  DispatchParams p;
+  p.x = x;
+  p.x_f16 = x_f16;
+  p.tokens = tokens;
+  p.hidden = hidden;
+  p.ids = ids;
+  p.w = w;
+  p.top_k = top_k;
+  p.num_experts = num_experts;
+  p.experts_per_rank = experts_per_rank;
+  p.rank = rank;
+  p.world = world;
+  p.peers = peers;
+  p.region = static_cast<uint8_t*>(region);
+  p.L = L;
+  p.chunk = ep_dispatch_chunk(routes);
+  const int grid = routes > 0 ? (int)((routes + p.chunk - 1) / p.chunk) : 1;
+  ep_dispatch_kernel<<<grid, kEpThreads, (size_t)p.chunk * 4, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int world,
+                              const EpLayout& L, int experts_local, cudaStream_t stream) {
+  ep_receive_kernel<<<ep_grid((long long)world * L.cap), kEpThreads, 0, stream>>>(
+      static_cast<uint8_t*>(region), peers, world, L, experts_local);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_signal(void* region, const unsigned long long* peers, int rank, int world,
+                             const EpLayout& L, cudaStream_t stream) {
+  ep_signal_kernel<<<1, 32, 0, stream>>>(static_cast<uint8_t*>(region), peers, rank, world, L);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long long tokens,
+                              int top_k, const int* topk_ids, int num_experts, float scale,
+                              const void* shared_out, int shared_f16, void* out, int out_f16,
+                              cudaStream_t stream) {
+  CombineParams p;
+  p.region = static_cast<uint8_t*>(region);
+  p.L = L;
+  p.world = world;
+  p.tokens = tokens;
+  p.top_k = top_k;
+  p.topk_ids = topk_ids;
+  p.num_experts = num_experts;
+  p.scale = scale;
+  p.shared_out = shared_out;
+  p.shared_f16 = shared_f16;
+  p.out = out;
+  p.out_f16 = out_f16;
+  ep_combine_kernel<<<ep_grid(tokens * (L.hidden / 8)), kEpThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -36,6 +36,9 @@ struct StreamParams {
   int mul_w;             // multiply each route's row by topk_w[route]
   void* out;
   long long ldo;
+  // Optional: output row of route r at address out_rows[r] (expert-parallel
+  // owners store straight into the source rank's buffer); nullptr: out + r*ldo.
+  const unsigned long long* out_rows;
   int out_f16;           // 1: f16 output, 0: bf16
   int ksplit;            // tcgen05 dense mode: K ranges per item (1 = none); >1 sums into ws
   float* ws;             // split-pair partial sums, kWsSlotFloats per grid slot, zeroed
@@ -99,6 +102,55 @@ cudaError_t launch_prepack_nvfp4(const uint8_t* w, const uint8_t* scales, long l
                                  int K, int gated, uint8_t* out, cudaStream_t stream);
 
 int device_sm_count();
+
+// Expert-parallel exchange region: one per rank, identical layout on every
+// rank, mapped into every peer (CUDA IPC). Offsets in bytes, each 256-aligned.
+constexpr int kEpMaxWorld = 64;
+enum EpHdr : int { kEpHdrStatus = 0, kEpHdrEpoch = 1, kEpHdrDispatchDone = 2, kEpHdrCombineDone = 3 };
+struct EpLayout {
+  long long cap;     // routes one source may send (max tokens x top_k)
+  long long hidden;
+  long long off_dflag, off_cflag, off_count, off_cnt_local;  // [kEpMaxWorld] ints each
+  long long off_ids, off_w, off_orig;  // [world * cap]: local expert id, router weight, route index
+  long long off_rows;                  // [world * cap] u64: destination row of each slot
+  long long off_recv;                  // [world * cap][hidden] f16: received activation rows
+  long long off_comb;                  // [cap][hidden] f16: returned (weighted) rows, route order
+  long long total;
+};
+inline EpLayout ep_layout(int world, long long cap, long long hidden) {
+  auto up = [](long long v) { return (v + 255) / 256 * 256; };
+  EpLayout L;
+  L.cap = cap;
+  L.hidden = hidden;
+  long long o = 256;  // header: status, step counter, two done counters
+  L.off_dflag = o; o += up(4 * kEpMaxWorld);
+  L.off_cflag = o; o += up(4 * kEpMaxWorld);
+  L.off_count = o; o += up(4 * kEpMaxWorld);
+  L.off_cnt_local = o; o += up(4 * kEpMaxWorld);
+  const long long slots = (long long)world * cap;
+  L.off_ids = o; o += up(4 * slots);
+  L.off_w = o; o += up(4 * slots);
+  L.off_orig = o; o += up(4 * slots);
+  L.off_rows = o; o += up(8 * slots);
+  L.off_recv = o; o += up(2 * slots * hidden);
+  L.off_comb = o; o += up(2 * cap * hidden);
+  L.total = o;
+  return L;
+}
+int ep_dispatch_chunk(long long routes);
+cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
+                               const int* ids, const float* w, int top_k, int num_experts,
+                               int experts_per_rank, int rank, int world,
+                               const unsigned long long* peers, void* region, const EpLayout& L,
+                               cudaStream_t stream);
+cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int world,
+                              const EpLayout& L, int experts_local, cudaStream_t stream);
+cudaError_t launch_ep_signal(void* region, const unsigned long long* peers, int rank, int world,
+                             const EpLayout& L, cudaStream_t stream);
+cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long long tokens,
+                              int top_k, const int* topk_ids, int num_experts, float scale,
+                              const void* shared_out, int shared_f16, void* out, int out_f16,
+                              cudaStream_t stream);
 
 // Records `message` as this thread's b200_last_error() and returns `code`.
 int set_last_error(int code, const char* message);

@@ -162,12 +162,17 @@ __device__ __forceinline__ void store_pair(const StreamParams& p, long long gi, 
         v0 = vt * w;
         v1 = vb * w;
       }
+      // Both output dtypes are 2 bytes; an expert-parallel owner's row may
+      // live on another GPU (out_rows).
+      void* orow_p = p.out_rows != nullptr
+                         ? reinterpret_cast<void*>(p.out_rows[orow])
+                         : reinterpret_cast<void*>(reinterpret_cast<uint16_t*>(p.out) + orow * p.ldo);
       if (p.out_f16) {
-        __half* o = reinterpret_cast<__half*>(p.out) + orow * p.ldo;
+        __half* o = reinterpret_cast<__half*>(orow_p);
         o[c0] = __float2half_rn(v0);
         if (c1 >= 0) o[c1] = __float2half_rn(v1);
       } else {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + orow * p.ldo;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(orow_p);
         o[c0] = __float2bfloat16_rn(v0);
         if (c1 >= 0) o[c1] = __float2bfloat16_rn(v1);
       }

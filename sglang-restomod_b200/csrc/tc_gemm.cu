@@ -778,7 +778,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               v[i] = silu_f32(v[i]) * up;
             }
           }
-          if (p.out_f16) {
+          if (p.out_rows != nullptr) {
+            // Expert-parallel owner: each route's row is in its source
+            // rank's combine buffer (a peer address).
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (lane_stores && orw[i] >= 0) {
+                uint16_t* o = reinterpret_cast<uint16_t*>(__ldg(p.out_rows + orw[i]));
+                const float x = v[i] * wv[i];
+                o[mycol] = p.out_f16 ? __half_as_ushort(__float2half_rn(x))
+                                     : __bfloat16_as_ushort(__float2bfloat16_rn(x));
+              }
+          } else if (p.out_f16) {
             __half* o = reinterpret_cast<__half*>(p.out);
 #pragma unroll
             for (int i = 0; i < 16; ++i)

@@ -19,7 +19,17 @@ an all-reduce. Here each rank owns ``E / world`` experts and one forward is:
    on the rank's own tokens) and applies ``routed_scaling_factor``.
 
 The split sizes make one host read per forward (step 2); the collectives run
-on the current stream.
+on the current stream. That is the NCCL transport (``transport="nccl"``).
+
+The peer transport (``transport="peer"``, the default on GPUs) needs no host
+read and no NCCL call per forward: every rank maps every other rank's
+exchange region (:class:`PeerExchange`, CUDA IPC over NVLink) and one
+forward is three library calls on the current stream -
+``b200_ep_dispatch`` (rows stored straight into the owners' regions),
+``b200_ep_expert_forward`` (the owner's experts; the down GEMM's epilogue
+stores each weighted row into its source's region) and ``b200_ep_combine``.
+Ranks synchronize through flags in the regions, so the forward can be
+captured in a CUDA graph and replayed on every rank.
 """
 
 from __future__ import annotations
@@ -29,6 +39,54 @@ import torch.distributed as dist
 
 from . import ops
 from .layer import QuantMoELayer, block_size_for  # noqa: F401
+
+
+class PeerExchange:
+    """This rank's exchange region, and every rank's region mapped here.
+
+    ``region`` is a zero-filled buffer of ``b200_ep_region_bytes``; the CUDA IPC
+    handles are exchanged once with ``all_gather_object`` over ``group``.
+    ``peers`` (int64 [world], on the device) holds rank r's region address in
+    this process. ``regions`` lets a single process stand in for ``world``
+    ranks (tests): then no IPC is involved and every rank's peers are the
+    given local buffers.
+    """
+
+    def __init__(self, world: int, rank: int, max_tokens: int, top_k: int, hidden: int,
+                 device: torch.device, group=None, regions: list | None = None):
+        self.world, self.rank = world, rank
+        self.max_tokens, self.top_k, self.hidden = max_tokens, top_k, hidden
+        self._opened: list[tuple[int, int]] = []
+        nbytes = ops.ep_region_bytes(world, max_tokens, top_k, hidden)
+        if regions is not None:
+            self.region = regions[rank]
+            ptrs = [int(r.data_ptr()) for r in regions]
+        else:
+            self.region = ops.aligned_zeros(nbytes, device)
+            torch.cuda.synchronize(device)
+            mine = ops.ipc_get_handle(self.region)
+            gathered = [None] * world
+            dist.all_gather_object(gathered, mine, group=group)
+            ptrs = []
+            for r, (handle, offset) in enumerate(gathered):
+                if r == rank:
+                    ptrs.append(int(self.region.data_ptr()))
+                else:
+                    addr = ops.ipc_open_handle(handle, offset)
+                    self._opened.append((addr, offset))
+                    ptrs.append(addr)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        if regions is None:
+            torch.cuda.synchronize(device)
+            dist.barrier(group=group)
+
+    def status(self, reset: bool = True) -> int:
+        return ops.region_status(self.region, reset)
+
+    def close(self) -> None:
+        for addr, offset in self._opened:
+            ops.ipc_close_handle(addr, offset)
+        self._opened = []
 
 
 class ExpertParallelMoE:
@@ -41,7 +99,9 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, local: QuantMoELayer | None, num_experts: int, rank: int, world: int,
-                 group=None, local_fn=None, combine_fn=None, shared_fn=None):
+                 group=None, local_fn=None, combine_fn=None, shared_fn=None,
+                 transport: str = "nccl", max_tokens: int | None = None,
+                 exchange: PeerExchange | None = None):
         if num_experts % world:
             raise ValueError(f"{num_experts} experts do not split over {world} ranks")
         if local is not None and local.num_experts != num_experts // world:
@@ -56,6 +116,19 @@ class ExpertParallelMoE:
         self._local_fn = local_fn
         self._combine_fn = combine_fn
         self._shared_fn = shared_fn
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.exchange = exchange
+        if transport == "peer":
+            if local is None or max_tokens is None:
+                raise ValueError("the peer transport needs the local layer and max_tokens")
+            if exchange is None:
+                self.exchange = PeerExchange(world, rank, max_tokens, local.top_k, local.hidden,
+                                             local.w13.device, group=group)
+            # Each owner receives about max_tokens * top_k routes per step.
+            self.peer_block_size = local.block_size or block_size_for(
+                max_tokens * local.top_k, local.num_experts)
 
     def _run_local(self, rows, ids1, w1):
         if self._local_fn is not None:
@@ -87,6 +160,8 @@ class ExpertParallelMoE:
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         shared = self._shared(x)
+        if self.transport == "peer":
+            return self._forward_peer(x, topk_ids, topk_weights, shared, out)
         if self.world == 1 and self._local_fn is None:
             return self.local.forward(x, topk_ids, topk_weights, out=out, shared_out=shared)
 
@@ -121,3 +196,46 @@ class ExpertParallelMoE:
         routed = torch.empty_like(back)
         routed.index_copy_(0, order, back)
         return self._combine(routed, topk_ids, shared, out)
+
+    def _forward_peer(self, x, topk_ids, topk_weights, shared, out):
+        self.peer_dispatch(x, topk_ids, topk_weights)
+        self.peer_experts()
+        return self.peer_combine(topk_ids, shared, out, x.dtype)
+
+    def peer_launches_per_forward(self, x_dtype=torch.bfloat16) -> int:
+        """Kernels of one peer-transport forward: dispatch, receive, align (3
+        kernels from 4096 receive slots on), [tcgen05 plan], gate/up, down,
+        signal, combine, + the shared expert's."""
+        layer = self.local
+        slots = self.world * self.exchange.max_tokens * layer.top_k
+        n = 1 + 1 + (3 if slots >= 4096 else 1) + (1 if self.peer_block_size >= 64 else 0) + 4
+        if layer.shared is not None:
+            n += layer.shared.launches(self.exchange.max_tokens, layer.hidden, x_dtype)
+        return n
+
+    # The three steps of a peer-transport forward; every rank runs them in this
+    # order. (A single process standing in for several ranks interleaves them
+    # rank by rank: all dispatches, then all expert steps, then all combines.)
+    def peer_dispatch(self, x, topk_ids, topk_weights):
+        ex = self.exchange
+        ops.ep_dispatch(x, topk_ids, topk_weights, num_experts=self.num_experts, rank=self.rank,
+                        world=self.world, peers=ex.peers, region=ex.region,
+                        max_tokens=ex.max_tokens)
+
+    def peer_experts(self):
+        ex, layer = self.exchange, self.local
+        ops.ep_expert_forward(
+            quant=layer.quant, hidden=layer.hidden, inter=layer.inter,
+            local_experts=layer.num_experts, w13=layer.w13, w2=layer.w2,
+            w13_scales=layer.w13_scales, w2_scales=layer.w2_scales, w13_global=layer.w13_global,
+            w2_global=layer.w2_global, block_size=self.peer_block_size, rank=self.rank,
+            world=self.world, peers=ex.peers, region=ex.region, max_tokens=ex.max_tokens,
+            top_k=layer.top_k,
+        )
+
+    def peer_combine(self, topk_ids, shared=None, out=None, out_dtype=torch.bfloat16):
+        ex, layer = self.exchange, self.local
+        return ops.ep_combine(topk_ids, hidden=layer.hidden, num_experts=self.num_experts,
+                              world=self.world, region=ex.region, max_tokens=ex.max_tokens,
+                              routed_scaling_factor=layer.routed_scaling_factor,
+                              shared_out=shared, out=out, out_dtype=out_dtype)

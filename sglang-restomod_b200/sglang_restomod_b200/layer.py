@@ -53,7 +53,22 @@ class SharedExpert:
         return ops.linear(h, self.w2, x.shape[-1], quant=self.quant, scales=self.w2_scales,
                           global_scale=self.w2_global, out_dtype=x.dtype)
 
-    launches_per_forward = 3  # bf16->f16 conversion, gate/up(+SiLU), down
+    launches_per_forward = 3  # bf16->f16 conversion, gate/up(+SiLU), down (decode rows)
+
+    def launches(self, m: int, hidden: int, x_dtype=torch.bfloat16) -> int:
+        """Kernels of one forward on m rows: the library's dense linear runs
+        m > 32 on the tcgen05 GEMM and, when its items cannot fill the SMs,
+        splits K and adds a finishing kernel (the rule of b200_linear)."""
+        n = 1 if x_dtype == torch.bfloat16 else 0
+        for rows_n, k in ((2 * self.inter, hidden), (hidden, self.inter)):
+            n += 1
+            items = (m + 191) // 192 * (rows_n // 128)
+            sms = ops.num_sms()
+            if m >= 33 and items < sms and m * rows_n <= 2 * sms * 128 * 64:
+                want = (2 * sms + items - 1) // items
+                kpart = max(2, (k // 128 + want - 1) // want)
+                n += 1 if (k // 128 + kpart - 1) // kpart > 1 else 0
+        return n
 
 
 @dataclass
@@ -87,10 +102,18 @@ class QuantMoELayer:
             shared_out=shared_out, out=out,
         )
 
-    # launches of one forward: bf16->f16, align, gate/up, down, combine (+ shared)
-    def launches_per_forward(self, x_dtype=torch.bfloat16) -> int:
+    # launches of one forward on `tokens` rows: bf16->f16, align (3 kernels
+    # from 4096 routes on), [tcgen05 plan], gate/up, down, combine (+ shared)
+    def launches_per_forward(self, x_dtype=torch.bfloat16, tokens: int | None = None) -> int:
         n = 4 + (1 if x_dtype == torch.bfloat16 else 0)
-        return n + (SharedExpert.launches_per_forward if self.shared is not None else 0)
+        if tokens is not None:
+            routes = tokens * self.top_k
+            bs = self.block_size or block_size_for(routes, self.num_experts)
+            n += (2 if routes >= 4096 else 0) + (1 if bs >= 64 else 0)
+        if self.shared is not None:
+            n += (self.shared.launches(tokens, self.hidden, x_dtype) if tokens is not None
+                  else SharedExpert.launches_per_forward)
+        return n
 
     def weight_bytes_per_expert(self) -> int:
         if self.quant == _lib.QUANT_FP8_BLOCK:

@@ -308,3 +308,129 @@ def moe_layer_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: tor
         )
     )
     return out
+
+
+# ------------------------------------------------------ expert parallelism
+# Peer-memory exchange (b200_ep_*): see ep.PeerExchange for the set-up of the
+# per-rank regions and their mapping into every peer.
+def ep_region_bytes(world: int, max_tokens: int, top_k: int, hidden: int) -> int:
+    n = int(lib().b200_ep_region_bytes(world, max_tokens, top_k, hidden))
+    if n < 0:
+        raise ValueError("bad expert-parallel region shape")
+    return n
+
+
+def aligned_zeros(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Zero-filled uint8 buffer of ``nbytes`` whose base is 256-byte aligned."""
+    raw = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+    offset = (-raw.data_ptr()) % 256
+    return raw[offset : offset + nbytes]
+
+
+def ipc_get_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of t's allocation, t's offset inside it)."""
+    _cuda(t, "buffer")
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_int64(0)
+    _lib.check(lib().b200_ipc_get_handle(_vp(t), handle, ctypes.byref(offset)))
+    return handle.raw, int(offset.value)
+
+
+def ipc_open_handle(handle: bytes, offset: int) -> int:
+    """Maps a peer's allocation; returns the device address of its buffer."""
+    if len(handle) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    ptr = ctypes.c_void_p(0)
+    _lib.check(lib().b200_ipc_open_handle(ctypes.create_string_buffer(handle, 64), int(offset),
+                                          ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close_handle(address: int, offset: int) -> None:
+    _lib.check(lib().b200_ipc_close_handle(ctypes.c_void_p(address), int(offset)))
+
+
+def _peers_arg(peers: torch.Tensor, world: int):
+    _contig(peers, "peer_regions")
+    if peers.dtype != torch.int64 or peers.numel() != world:
+        raise ValueError(f"peer_regions must be int64[{world}] on the device")
+    return _vp(peers)
+
+
+def ep_dispatch(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, *,
+                num_experts: int, rank: int, world: int, peers: torch.Tensor,
+                region: torch.Tensor, max_tokens: int) -> None:
+    """Source side: this rank's routes (rows + routing) into their owners' regions."""
+    _contig(x, "x")
+    _contig(topk_ids, "topk_ids")
+    _contig(topk_weights, "topk_weights")
+    _contig(region, "region")
+    if topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32:
+        raise TypeError("topk_ids must be int32 and topk_weights float32")
+    tokens, hidden = (int(d) for d in x.shape)
+    _lib.check(
+        lib().b200_ep_dispatch(
+            _vp(x), _code(x, "x"), tokens, hidden, _vp(topk_ids), _vp(topk_weights),
+            int(topk_ids.shape[1]), num_experts, rank, world, _peers_arg(peers, world),
+            _vp(region), max_tokens, _stream(x.device),
+        )
+    )
+
+
+def ep_expert_workspace_bytes(world: int, max_tokens: int, top_k: int, inter: int,
+                              local_experts: int, block_size: int) -> int:
+    return int(lib().b200_ep_expert_workspace_bytes(world, max_tokens, top_k, inter,
+                                                    local_experts, block_size))
+
+
+def ep_expert_forward(*, quant: int, hidden: int, inter: int, local_experts: int,
+                      w13: torch.Tensor, w2: torch.Tensor, w13_scales=None, w2_scales=None,
+                      w13_global=None, w2_global=None, block_size: int, rank: int, world: int,
+                      peers: torch.Tensor, region: torch.Tensor, max_tokens: int,
+                      top_k: int) -> None:
+    """Owner side: wait for every source, run this rank's experts on what
+    arrived, store each weighted row into its source's region."""
+    _contig(region, "region")
+    ws = workspace(
+        ep_expert_workspace_bytes(world, max_tokens, top_k, inter, local_experts, block_size),
+        region.device,
+    )
+    _lib.check(
+        lib().b200_ep_expert_forward(
+            quant, hidden, inter, local_experts, _vp(w13), _vp(w13_scales), _vp(w13_global),
+            _vp(w2), _vp(w2_scales), _vp(w2_global), block_size, rank, world,
+            _peers_arg(peers, world), _vp(region), max_tokens, top_k, _vp(ws), ws.numel(),
+            _stream(region.device),
+        )
+    )
+
+
+def ep_combine(topk_ids: torch.Tensor, *, hidden: int, num_experts: int, world: int,
+               region: torch.Tensor, max_tokens: int, routed_scaling_factor: float = 1.0,
+               shared_out: torch.Tensor | None = None, out: torch.Tensor | None = None,
+               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Source side: wait for every owner, sum each token's returned rows."""
+    _contig(topk_ids, "topk_ids")
+    _contig(region, "region")
+    tokens, top_k = (int(d) for d in topk_ids.shape)
+    if out is None:
+        out = torch.empty(tokens, hidden, dtype=out_dtype, device=topk_ids.device)
+    _contig(out, "out")
+    if shared_out is not None:
+        _contig(shared_out, "shared_out")
+    _lib.check(
+        lib().b200_ep_combine(
+            tokens, hidden, _vp(topk_ids), top_k, num_experts, float(routed_scaling_factor),
+            _vp(shared_out), _code(shared_out, "shared_out") if shared_out is not None else 0,
+            _vp(out), _code(out, "out"), world, _vp(region), max_tokens, _stream(out.device),
+        )
+    )
+    return out
+
+
+def region_status(region: torch.Tensor, reset: bool = True) -> int:
+    """Error bits of an expert-parallel region (8 = a wait on a peer timed out). Synchronizes."""
+    bits = ctypes.c_int32(0)
+    _lib.check(lib().b200_workspace_status(_vp(region), ctypes.byref(bits), int(reset),
+                                           _stream(region.device)))
+    return int(bits.value)
