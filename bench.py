@@ -271,13 +271,19 @@ class MoEWorkload:
         layer = self.layer
         if self.world == 1:
             ids, x = self.ids, self.x
+        elif self.transport == "peer":
+            # the owner's gate/up GEMM on the routes its region received
+            ids, _, x = self.model.exchange.received()
         else:
             if self.model.last_recv is None:
                 return None
             x, ids, _ = self.model.last_recv
-        bs = block_size_for(ids.numel(), layer.num_experts)
+        if self.transport == "peer":
+            bs = self.model.peer_block_size
+        else:
+            bs = block_size_for(ids.numel(), layer.num_experts)
         sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, bs, layer.num_experts)
-        x16 = x.half()
+        x16 = x if x.dtype == torch.float16 else x.half()
         routes = ids.numel()
         c = torch.empty(routes, layer.inter, dtype=torch.float16, device=self.x.device)
 
@@ -288,12 +294,17 @@ class MoEWorkload:
                          top_k=ids.shape[1], num_routes=routes, c=c, scales=layer.w13_scales,
                          global_scale=layer.w13_global, gated_mode=_lib.GATED_FUSED)
 
-        touched = int(torch.unique(ids).numel())
+        valid = ids[(ids >= 0) & (ids < layer.num_experts)]
+        touched = int(torch.unique(valid).numel())
         if layer.quant == 0:
             per_expert = 2 * layer.inter * layer.hidden + (2 * layer.inter // 128) * (layer.hidden // 128) * 4
         else:
             per_expert = 2 * layer.inter * layer.hidden // 2 + 2 * layer.inter * layer.hidden // 16
-        nbytes = touched * per_expert + x.shape[0] * layer.hidden * 2 + routes * layer.inter * 2
+        nvalid = int(valid.numel())
+        if self.transport == "peer":  # only received slots are read and written
+            nbytes = touched * per_expert + nvalid * layer.hidden * 2 + nvalid * layer.inter * 2
+        else:
+            nbytes = touched * per_expert + x.shape[0] * layer.hidden * 2 + routes * layer.inter * 2
         return run, nbytes, "stream_gemm_kernel (gate/up, gated SiLU epilogue)"
 
 

@@ -253,6 +253,14 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
  */
 int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden);
 
+/* Byte offsets inside a region, for inspection: offsets[0..6] = receive slots'
+ * local expert ids (int32 [world * max_tokens * top_k], -1 = empty once
+ * received), router weights (fp32), source route indices (int32), destination
+ * row addresses (u64), received rows (f16 [slots][hidden]), returned rows
+ * (f16 [max_tokens * top_k][hidden]), total bytes. */
+int b200_ep_region_layout(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden,
+                          int64_t* offsets);
+
 /* CUDA IPC of the allocation holding dev_ptr: a 64-byte handle plus the
  * pointer's offset inside it; open maps a peer's allocation, close unmaps. */
 int b200_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset);
@@ -272,7 +280,8 @@ int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hid
  * b200_moe_layer_forward). block_size as for b200_moe_layer_forward, sized
  * for about max_tokens * top_k routes per rank. */
 int64_t b200_ep_expert_workspace_bytes(int32_t world, int64_t max_tokens, int32_t top_k,
-                                       int64_t inter, int32_t local_experts, int32_t block_size);
+                                       int64_t hidden, int64_t inter, int32_t local_experts,
+                                       int32_t block_size);
 int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t local_experts,
                            const uint8_t* w13_packed, const float* w13_scales,
                            const float* w13_global, const uint8_t* w2_packed,

@@ -366,6 +366,8 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.x = xh;
     p.ldx = k;
     p.x_rows = m;
+    p.xs = xh;  // contiguous rows: B tiles by TMA
+    p.xs_rows = m;
     p.sorted_ids = nullptr;
     p.dense_m = (int)m;
     p.E = 1;
@@ -503,10 +505,13 @@ int64_t b200_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden, int64_t i
   const int64_t busy = numel < num_experts ? numel : num_experts;
   const int64_t cap = numel + busy * (block_size - 1);
   const int64_t blocks = (cap + block_size - 1) / block_size;
-  return stream_ws_bytes() + align_up(tokens * hidden * 2)  // f16 activations
-         + align_up(cap * 4) + align_up(blocks * 4) + align_up(4)  // routing
-         + align_up(numel * inter * 2)                              // gate_up output
-         + align_up(numel * hidden * 2);                            // per-route down output
+  // Streaming path: f16 activations + gate_up output per route. tcgen05
+  // path (blocks of 64+): both operands in slot order, one row per slot.
+  const int64_t stream_ops = align_up(tokens * hidden * 2) + align_up(numel * inter * 2);
+  const int64_t tc_ops = block_size >= 64 ? align_up(cap * hidden * 2) + align_up(cap * inter * 2) : 0;
+  return stream_ws_bytes() + (stream_ops > tc_ops ? stream_ops : tc_ops)  // operands
+         + align_up(cap * 4) + align_up(blocks * 4) + align_up(4)           // routing
+         + align_up(numel * hidden * 2);                                     // per-route down output
 }
 
 int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
@@ -552,17 +557,31 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   const bool tc = use_tc_moe(quant, block_size, blocks);
   int64_t used = 0;
   const __half* x16 = nullptr;
-  rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
-  if (rc) return rc;
-  if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+  __half* xs = nullptr;  // tcgen05: activations in slot order
+  __half* inter_out = nullptr;
+  if (tc) {
+    xs = reinterpret_cast<__half*>(ws.scratch + used);
+    used += align_up(cap * hidden * 2);
+    inter_out = reinterpret_cast<__half*>(ws.scratch + used);  // slot order
+    used += align_up(cap * inter * 2);
+    const int64_t stream_ops = align_up(tokens * hidden * 2) + align_up(numel * inter * 2);
+    if (used < stream_ops) used = stream_ops;
+  } else {
+    rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
+    if (rc) return rc;
+    if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+    inter_out = reinterpret_cast<__half*>(ws.scratch + used);  // route order
+    used += align_up(numel * inter * 2);
+    const int64_t tc_ops =
+        block_size >= 64 ? align_up(cap * hidden * 2) + align_up(cap * inter * 2) : 0;
+    if (used < tc_ops) used = tc_ops;
+  }
   int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(cap * 4);
   int32_t* eids = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(blocks * 4);
   int32_t* ntpp = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(4);
-  __half* inter_out = reinterpret_cast<__half*>(ws.scratch + used);
-  used += align_up(numel * inter * 2);
   __half* routed = reinterpret_cast<__half*>(ws.scratch + used);
   used += align_up(numel * hidden * 2);
 
@@ -577,6 +596,14 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
                                    blocks, ntpp, stream);
   }
   if (rc) return rc;
+  if (tc) {
+    // One slot-ordered f16 copy of the routed rows (bf16 converted on the
+    // way): the GEMM reads it as TMA tiles instead of gathering per route.
+    rc = check_cuda(launch_permute_rows(x, x_dtype == B200_DTYPE_F16, hidden, tokens, hidden,
+                                        sorted, ntpp, cap, top_k, numel, xs, st),
+                    "permute launch");
+    if (rc) return rc;
+  }
 
   StreamParams p{};
   p.wq = w13_packed;
@@ -585,6 +612,9 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   p.x = x16;
   p.ldx = hidden;
   p.x_rows = tokens;
+  p.xs = xs;
+  p.xs_rows = cap;
+  p.out_by_slot = tc ? 1 : 0;
   p.sorted_ids = sorted;
   p.expert_ids = eids;
   p.ntpp = ntpp;
@@ -616,6 +646,9 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   q.x = inter_out;
   q.ldx = inter;
   q.x_rows = numel;
+  q.xs = tc ? inter_out : nullptr;  // written in slot order by the gate/up epilogue
+  q.xs_rows = cap;
+  q.out_by_slot = 0;
   q.top_k = 1;
   q.N = (int)hidden;
   q.K = (int)inter;
@@ -678,16 +711,21 @@ int check_ep_common(int32_t rank, int32_t world, int64_t max_tokens, int32_t top
 struct EpWs {
   int64_t numel, cap_a, blocks, total;
 };
-EpWs ep_ws(int32_t world, int64_t max_tokens, int32_t top_k, int64_t inter, int32_t local_experts,
-           int32_t block_size) {
+EpWs ep_ws(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden, int64_t inter,
+           int32_t local_experts, int32_t block_size) {
   EpWs w;
   w.numel = (int64_t)world * max_tokens * top_k;
   const int64_t busy = w.numel < local_experts ? w.numel : local_experts;
   w.cap_a = w.numel + busy * (block_size - 1);
   w.blocks = (w.cap_a + block_size - 1) / block_size;
+  // gate_up output per route (streaming path) or, for blocks of 64+, both
+  // tcgen05 operands in slot order (received rows + gate_up output).
+  const int64_t stream_ops = align_up(w.numel * inter * 2);
+  const int64_t tc_ops =
+      block_size >= 64 ? align_up(w.cap_a * hidden * 2) + align_up(w.cap_a * inter * 2) : 0;
   w.total = stream_ws_bytes() + align_up(w.cap_a * 4) + align_up(w.blocks * 4) + align_up(4) +
             align_up(moe_align_scratch_ints(w.numel, local_experts) * 4) +
-            align_up(w.numel * inter * 2);
+            (stream_ops > tc_ops ? stream_ops : tc_ops);
   return w;
 }
 
@@ -698,6 +736,17 @@ extern "C" {
 int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden) {
   if (world < 1 || world > kEpMaxWorld || max_tokens <= 0 || top_k <= 0 || hidden <= 0) return -1;
   return ep_layout(world, max_tokens * top_k, hidden).total;
+}
+
+int b200_ep_region_layout(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden,
+                          int64_t* offsets) {
+  if (world < 1 || world > kEpMaxWorld || max_tokens <= 0 || top_k <= 0 || hidden <= 0 ||
+      offsets == nullptr)
+    return fail(B200_ERR_INVALID, "bad region shape");
+  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  const int64_t v[7] = {L.off_ids, L.off_w, L.off_orig, L.off_rows, L.off_recv, L.off_comb, L.total};
+  for (int i = 0; i < 7; ++i) offsets[i] = v[i];
+  return B200_OK;
 }
 
 int b200_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset) {
@@ -766,11 +815,12 @@ int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hid
 }
 
 int64_t b200_ep_expert_workspace_bytes(int32_t world, int64_t max_tokens, int32_t top_k,
-                                       int64_t inter, int32_t local_experts, int32_t block_size) {
-  if (world < 1 || max_tokens <= 0 || top_k <= 0 || inter <= 0 || local_experts <= 0 ||
-      block_size <= 0)
+                                       int64_t hidden, int64_t inter, int32_t local_experts,
+                                       int32_t block_size) {
+  if (world < 1 || max_tokens <= 0 || top_k <= 0 || hidden <= 0 || inter <= 0 ||
+      local_experts <= 0 || block_size <= 0)
     return -1;
-  return ep_ws(world, max_tokens, top_k, inter, local_experts, block_size).total;
+  return ep_ws(world, max_tokens, top_k, hidden, inter, local_experts, block_size).total;
 }
 
 int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t local_experts,
@@ -794,7 +844,7 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   if (!tc_block && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32, 64, 128 or 256, got %d",
                 block_size);
-  const EpWs w = ep_ws(world, max_tokens, top_k, inter, local_experts, block_size);
+  const EpWs w = ep_ws(world, max_tokens, top_k, hidden, inter, local_experts, block_size);
   if (workspace_bytes < w.total)
     return fail(B200_ERR_INVALID, "workspace holds %lld bytes, needs %lld",
                 (long long)workspace_bytes, (long long)w.total);
@@ -819,8 +869,13 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   used += align_up(4);
   int* align_scratch = reinterpret_cast<int*>(ws.scratch + used);
   used += align_up(moe_align_scratch_ints(numel, local_experts) * 4);
+  const bool tc = use_tc_moe(quant, block_size, w.blocks);
+  __half* xs = nullptr;  // tcgen05: received rows in slot order
   __half* inter_out = reinterpret_cast<__half*>(ws.scratch + used);
-  used += align_up(numel * inter * 2);
+  if (tc) {
+    xs = inter_out;
+    inter_out = reinterpret_cast<__half*>(ws.scratch + used + align_up(w.cap_a * hidden * 2));
+  }
 
   const int32_t* ids = reinterpret_cast<const int32_t*>(reg + L.off_ids);
   if (numel >= kAlignMultiMin) {
@@ -833,15 +888,24 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
                     "moe_align launch");
   }
   if (rc) return rc;
+  const __half* recv = reinterpret_cast<const __half*>(reg + L.off_recv);
+  if (tc) {
+    rc = check_cuda(launch_permute_rows(recv, 1, hidden, numel, hidden, sorted, ntpp, w.cap_a, 1,
+                                        numel, xs, st),
+                    "permute launch");
+    if (rc) return rc;
+  }
 
-  const bool tc = use_tc_moe(quant, block_size, w.blocks);
   StreamParams p{};
   p.wq = w13_packed;
   p.wscale = w13_scales;
   p.gscale = w13_global;
-  p.x = reinterpret_cast<const __half*>(reg + L.off_recv);
+  p.x = recv;
   p.ldx = hidden;
   p.x_rows = numel;
+  p.xs = xs;
+  p.xs_rows = w.cap_a;
+  p.out_by_slot = tc ? 1 : 0;
   p.sorted_ids = sorted;
   p.expert_ids = eids;
   p.ntpp = ntpp;
@@ -872,6 +936,9 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   q.gscale = w2_global;
   q.x = inter_out;
   q.ldx = inter;
+  q.xs = tc ? inter_out : nullptr;  // written in slot order by the gate/up epilogue
+  q.xs_rows = w.cap_a;
+  q.out_by_slot = 0;
   q.N = (int)hidden;
   q.K = (int)inter;
   q.gated = 0;

@@ -130,6 +130,45 @@ __global__ void sum_reduce_kernel(const void* __restrict__ in, void* __restrict_
   griddep_launch_dependents();
 }
 
+// One warp per route slot, 16 bytes per lane per access. Reads the slot
+// count written by moe_align on the device, so it is graph-capturable.
+__global__ void __launch_bounds__(256) permute_rows_kernel(
+    const uint8_t* __restrict__ x, int x_f16, long long ldx, long long x_rows, long long k,
+    const int* __restrict__ sorted_ids, const int* __restrict__ ntpp, long long cap, int top_k,
+    long long num_routes, uint8_t* __restrict__ out) {
+  griddep_wait();
+  long long n = ntpp[0];
+  if (n > cap) n = cap;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long k8 = k / 8;
+  for (long long s = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); s < n;
+       s += warps) {
+    const int id = __ldg(sorted_ids + s);
+    if (id < 0 || id >= num_routes) continue;
+    const long long row = id / top_k;
+    if (row >= x_rows) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * ldx * 2);
+    uint4* dst = reinterpret_cast<uint4*>(out + s * k * 2);
+    for (long long v = lane; v < k8; v += 32) {
+      uint4 raw = __ldg(src + v);
+      if (!x_f16) {
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+          __half2 h = __floats2half2_rn(__low2float(b), __high2float(b));
+          o[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        raw = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      dst[v] = raw;
+    }
+  }
+  griddep_launch_dependents();
+}
+
 int grid_for(long long work, int threads) {
   long long blocks = (work + threads - 1) / threads;
   const long long cap = (long long)device_sm_count() * 8;
@@ -145,6 +184,18 @@ cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStrea
   if (n8 == 0) return cudaSuccess;
   return launch_pdl(bf16_to_f16_kernel, dim3(grid_for(n8, 256)), dim3(256), 0, stream,
                     reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n8);
+}
+
+cudaError_t launch_permute_rows(const void* x, int x_f16, long long ldx, long long x_rows,
+                                long long k, const int* sorted_ids, const int* ntpp, long long cap,
+                                int top_k, long long num_routes, void* out, cudaStream_t stream) {
+  if (cap <= 0) return cudaSuccess;
+  long long blocks = (cap + 7) / 8;  // 8 warps of 256 threads, one slot each
+  const long long limit = (long long)device_sm_count() * 8;
+  if (blocks > limit) blocks = limit;
+  return launch_pdl(permute_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream,
+                    static_cast<const uint8_t*>(x), x_f16, ldx, x_rows, k, sorted_ids, ntpp, cap,
+                    top_k, num_routes, static_cast<uint8_t*>(out));
 }
 
 cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,

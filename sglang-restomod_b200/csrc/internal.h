@@ -20,6 +20,12 @@ struct StreamParams {
   const float* gscale;   // NVFP4: [E] fp32 global scale
   const __half* x;       // activations, f16, rows of ldx elements
   long long ldx;
+  // tcgen05 GEMM only: activations already in slot order (row s = route slot
+  // s of the moe_align output, or dense row s), f16 rows of ldx elements;
+  // B tiles then come by 2-D TMA instead of the per-route gather.
+  const __half* xs;
+  long long xs_rows;
+  int out_by_slot;       // tcgen05 moe mode: output row = route slot, not route id
   long long x_rows;      // number of activation rows (route rows are checked against it)
   const int* sorted_ids; // nullptr: dense mode
   const int* expert_ids;
@@ -88,6 +94,11 @@ cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num
 
 // Elementwise / reduction kernels.
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);
+// out[s, :k] (f16) = x[sorted_ids[s] / top_k, :k] for the valid route slots
+// s < min(*ntpp, cap); padding slots are left as they are.
+cudaError_t launch_permute_rows(const void* x, int x_f16, long long ldx, long long x_rows,
+                                long long k, const int* sorted_ids, const int* ntpp, long long cap,
+                                int top_k, long long num_routes, void* out, cudaStream_t stream);
 cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,
                                   long long hidden, int f16, float scale, cudaStream_t stream);
 cudaError_t launch_moe_combine(const void* routed, int routed_f16, const int* topk_ids,

@@ -47,6 +47,8 @@
 // largest block scale flush) and the accumulator is multiplied by 2^E exactly.
 #include <cuda.h>  // CUtensorMap and its encoding enums (types only)
 
+#include <cstring>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -60,12 +62,13 @@ constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
 constexpr int kLoadPasses = kNMax / (kLoadThreads / 2);  // rows per gather thread
-constexpr int kStages = 4;                               // 64-K stages (A in TMEM, B in smem)
+constexpr int kStages = 4;                               // 64-K A stages in tensor memory
+constexpr int kBStages = 6;                              // 64-K B stages in shared memory
 constexpr int kRawStages = 4;                            // 16 KiB FP8 units
 constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
 constexpr uint32_t kBTile = kNMax * 128;                 // [192 rows][64 K] f16
 constexpr uint32_t kOffB = 0;
-constexpr uint32_t kOffRaw = kOffB + kStages * kBTile;
+constexpr uint32_t kOffRaw = kOffB + kBStages * kBTile;
 constexpr uint32_t kOffCtl = kOffRaw + kRawStages * kUnitBytes;
 constexpr int kInfoSlots = 8;
 constexpr uint32_t kTmemCols = 512;
@@ -77,8 +80,10 @@ static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "tensor memory");
 static_assert(kBTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
 
 struct Ctl {
-  uint64_t full[kStages];   // 4 dequant warps + the gather threads
-  uint64_t empty[kStages];  // MMA commit
+  uint64_t full[kStages];    // A stage written: the 4 dequant warps
+  uint64_t empty[kStages];   // A stage consumed: MMA commit
+  uint64_t bfull[kBStages];  // B stage landed: gather threads or the TMA issuer (+ bytes)
+  uint64_t bempty[kBStages]; // B stage consumed: MMA commit
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t raw_full[kRawStages];   // expect_tx + the unit's bytes
@@ -340,7 +345,8 @@ __device__ __forceinline__ T pick(const T (&v)[M], int g) {
 template <bool kFp4>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
-                   const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w) {
+                   const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ CUtensorMap tmap_x) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -354,9 +360,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool dense = p.sorted_ids == nullptr;
 
   if (tid == 0) {
+    // bfull: every gather thread (cp.async arrivals) or the one thread that
+    // issues the stage's TMA tiles.
+    const uint32_t b_arrivals = p.xs != nullptr ? 1u : (uint32_t)kLoadThreads;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full[s], 4 + kLoadThreads);
+      mbar_init(&ctl->full[s], 4);
       mbar_init(&ctl->empty[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&ctl->bfull[s], b_arrivals);
+      mbar_init(&ctl->bempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&ctl->acc_full[s], 1);
@@ -489,7 +502,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       item_k_range(p, g0 + j * gs, kch, kc0, nk);
       for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
         const int s = (int)(t % kStages);
-        ok = warp_wait(&ctl->full[s], (uint32_t)((t / kStages) & 1), ctl, p.status);
+        const int sb = (int)(t % kBStages);
+        ok = warp_wait(&ctl->bfull[sb], (uint32_t)((t / kBStages) & 1), ctl, p.status) &&
+             warp_wait(&ctl->full[s], (uint32_t)((t / kStages) & 1), ctl, p.status);
         if (!ok) break;
         tc_fence_after();
         if (ts == 0) {
@@ -499,13 +514,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           idesc = instr_desc_f16(n);
         }
         const uint32_t acol = tmem + kACol0 + (uint32_t)s * kAStageCols;
-        const uint32_t blo = b_lo0 + (uint32_t)s * (kBTile >> 4);
+        const uint32_t blo = b_lo0 + (uint32_t)sb * (kBTile >> 4);
         if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_ts(dcol, acol + 8u * kk, ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc,
                    (ts > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&ctl->empty[s]);
+          mma_commit(&ctl->bempty[sb]);
         }
         __syncwarp();
       }
@@ -518,6 +534,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(&ctl->done, 0u, nullptr);
     }
     __syncwarp();
+  } else if (warp < kWarpDeq && p.xs != nullptr) {
+    // ------------------------------------- B (activations) by 2-D TMA tiles
+    // The operand is already in slot order: a stage is ceil(rows / 64) boxes
+    // of 64 rows x 64 K, landing in the 128-byte-swizzled K-major layout the
+    // MMA descriptor reads. Warp 3 has nothing to do.
+    if (warp == kWarpLoad) {
+      long long t = 0;  // 64-K stages issued
+      bool ok = true;
+      for (long long j = 0; j < my_items && ok; ++j) {
+        const long long g = g0 + j * gs;
+        const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
+        // The MMA's N: slots up to the item's last valid route.
+        int nmax = 0;
+#pragma unroll
+        for (int q = 0; q < kNMax / 32; ++q) {
+          const int n = q * 32 + lane;
+          if (id_row(p, slot_id(p, it, n)) >= 0) nmax = n + 1;
+        }
+        nmax = (int)__reduce_max_sync(0xffffffffu, (unsigned)nmax);
+        if (lane == 0)
+          atomicMax(&ctl->info[j % kInfoSlots], (int)(((j & 0x3fffff) << 9) | ((nmax + 15) & ~15)));
+        const int nbox = nmax > 64 ? (nmax + 63) / 64 : 1;
+        int kc0, nk;
+        item_k_range(p, g, kch, kc0, nk);
+        for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
+          const int s = (int)(t % kBStages);
+          ok = warp_wait(&ctl->bempty[s], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl, p.status);
+          if (!ok) break;
+          if (lane == 0) {
+            uint8_t* B = smem + kOffB + s * kBTile;
+            const int kofs = (kc0 + (ts >> 1)) * 128 + (ts & 1) * 64;
+            mbar_arrive_expect_tx(&ctl->bfull[s], (uint32_t)nbox * 8192u);
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(B + b * 8192, &tmap_x, kofs, (int)(it.slot0 + 64 * b), &ctl->bfull[s]);
+          }
+          __syncwarp();
+        }
+      }
+      // After an abort, tiles still in flight land before the CTA exits.
+      if (lane == 0 && !ok) {
+        for (long long v = t > kBStages ? t - kBStages : 0; v < t; ++v)
+          mbar_wait(&ctl->bfull[v % kBStages], (uint32_t)((v / kBStages) & 1), nullptr);
+      }
+    }
   } else if (warp < kWarpDeq) {
     // ---------------------------------------------------- B (activations)
     const int ltid = tid - kWarpLoad * 32;  // 0..kLoadThreads-1
@@ -559,8 +619,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int kc0, nk;
       item_k_range(p, g0 + j * gs, kch, kc0, nk);
       for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
-        const int s = (int)(t % kStages);
-        ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
+        const int s = (int)(t % kBStages);
+        ok = warp_wait(&ctl->bempty[s], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl, p.status);
         if (!ok) break;
         uint8_t* B = smem + kOffB + s * kBTile;
         const long long kofs = (long long)(kc0 + (ts >> 1)) * 128 + (ts & 1) * 64;
@@ -575,7 +635,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
         }
-        cp_async_arrive_noinc(&ctl->full[s]);
+        cp_async_arrive_noinc(&ctl->bfull[s]);
       }
       pe_b = pe_c;
     }
@@ -733,7 +793,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (dense) {
           orow[gg] = id;
         } else if (id >= 0 && id < p.num_routes && id / p.top_k < p.x_rows) {
-          orow[gg] = id;
+          orow[gg] = p.out_by_slot ? (int)(it.slot0 + gg * 32 + lane) : id;
           if (p.mul_w) wr[gg] = __ldg(p.topk_w + id);
         }
       }
@@ -1047,13 +1107,26 @@ cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_bu
   if (!make_map(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.wq, 128, wrows, 128, 128, unit_rows,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
     return cudaErrorInvalidValue;
+  // Slot-ordered activations: boxes of 64 K (128 bytes) x 64 rows; rows past
+  // xs_rows read as zero.
+  CUtensorMap tmap_x;
+  memset(&tmap_x, 0, sizeof(tmap_x));
+  if (p.xs != nullptr) {
+    if (p.xs_rows <= 0 || p.xs_rows >= (1ll << 31) || p.ldx % 8 != 0 || p.ldx < p.K ||
+        (reinterpret_cast<uintptr_t>(p.xs) & 15u) != 0)
+      return cudaErrorInvalidValue;
+    if (!make_map(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.xs, (unsigned long long)p.K,
+                  (unsigned long long)p.xs_rows, (unsigned long long)p.ldx * 2, 64, 64,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+      return cudaErrorInvalidValue;
+  }
   const int* count = reinterpret_cast<const int*>(plan_buf);
   const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
   if (fp4)
     return launch_pdl(tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
-                      count, tmap_w);
+                      count, tmap_w, tmap_x);
   return launch_pdl(tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
-                    count, tmap_w);
+                    count, tmap_w, tmap_x);
 }
 
 }  // namespace b200

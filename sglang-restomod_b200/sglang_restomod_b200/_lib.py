@@ -92,6 +92,7 @@ SIGNATURES = {
          c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_int64, c_void_p],
     ),
     "b200_ep_region_bytes": (c_int64, [c_int32, c_int64, c_int32, c_int64]),
+    "b200_ep_region_layout": (c_int32, [c_int32, c_int64, c_int32, c_int64, ctypes.POINTER(c_int64)]),
     "b200_ipc_get_handle": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
     "b200_ipc_open_handle": (c_int32, [c_void_p, c_int64, ctypes.POINTER(c_void_p)]),
     "b200_ipc_close_handle": (c_int32, [c_void_p, c_int64]),
@@ -100,7 +101,9 @@ SIGNATURES = {
         [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int32,
          c_int32, c_void_p, c_void_p, c_int64, c_void_p],
     ),
-    "b200_ep_expert_workspace_bytes": (c_int64, [c_int32, c_int64, c_int32, c_int64, c_int32, c_int32]),
+    "b200_ep_expert_workspace_bytes": (
+        c_int64, [c_int32, c_int64, c_int32, c_int64, c_int64, c_int32, c_int32]
+    ),
     "b200_ep_expert_forward": (
         c_int32,
         [c_int32, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -80,6 +80,18 @@ class PeerExchange:
             torch.cuda.synchronize(device)
             dist.barrier(group=group)
 
+    def received(self):
+        """Views of what the last expert step received: (local ids int32
+        [slots, 1], -1 = empty; router weights fp32 [slots, 1]; rows f16
+        [slots, hidden]), slots = world * max_tokens * top_k."""
+        lay = ops.ep_region_layout(self.world, self.max_tokens, self.top_k, self.hidden)
+        slots = self.world * self.max_tokens * self.top_k
+        reg = self.region
+        ids = reg[lay["ids"] : lay["ids"] + 4 * slots].view(torch.int32).view(slots, 1)
+        w = reg[lay["weights"] : lay["weights"] + 4 * slots].view(torch.float32).view(slots, 1)
+        rows = reg[lay["recv"] : lay["recv"] + 2 * slots * self.hidden].view(torch.float16)
+        return ids, w, rows.view(slots, self.hidden)
+
     def status(self, reset: bool = True) -> int:
         return ops.region_status(self.region, reset)
 

@@ -320,6 +320,14 @@ def ep_region_bytes(world: int, max_tokens: int, top_k: int, hidden: int) -> int
     return n
 
 
+def ep_region_layout(world: int, max_tokens: int, top_k: int, hidden: int) -> dict:
+    """Byte offsets of a region's arrays (see b200_ep_region_layout)."""
+    arr = (ctypes.c_int64 * 7)()
+    _lib.check(lib().b200_ep_region_layout(world, max_tokens, top_k, hidden, arr))
+    keys = ("ids", "weights", "orig", "rows", "recv", "comb", "total")
+    return dict(zip(keys, (int(v) for v in arr)))
+
+
 def aligned_zeros(nbytes: int, device: torch.device) -> torch.Tensor:
     """Zero-filled uint8 buffer of ``nbytes`` whose base is 256-byte aligned."""
     raw = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
@@ -377,9 +385,9 @@ def ep_dispatch(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
     )
 
 
-def ep_expert_workspace_bytes(world: int, max_tokens: int, top_k: int, inter: int,
+def ep_expert_workspace_bytes(world: int, max_tokens: int, top_k: int, hidden: int, inter: int,
                               local_experts: int, block_size: int) -> int:
-    return int(lib().b200_ep_expert_workspace_bytes(world, max_tokens, top_k, inter,
+    return int(lib().b200_ep_expert_workspace_bytes(world, max_tokens, top_k, hidden, inter,
                                                     local_experts, block_size))
 
 
@@ -392,7 +400,8 @@ def ep_expert_forward(*, quant: int, hidden: int, inter: int, local_experts: int
     arrived, store each weighted row into its source's region."""
     _contig(region, "region")
     ws = workspace(
-        ep_expert_workspace_bytes(world, max_tokens, top_k, inter, local_experts, block_size),
+        ep_expert_workspace_bytes(world, max_tokens, top_k, hidden, inter, local_experts,
+                                  block_size),
         region.device,
     )
     _lib.check(
