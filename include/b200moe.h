@@ -91,6 +91,27 @@ int b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int32_t nu
                               int64_t expert_capacity, int32_t* num_tokens_post_pad,
                               void* stream);
 
+/*
+ * Router top-k: router_logits [tokens, num_experts] (bf16 / f16 / f32) ->
+ * topk_ids [tokens, top_k] int32 and topk_weights fp32, in descending order
+ * of the selection key. Replaces upstream SGLang's select_experts / fused
+ * top-k softmax, whose output (StandardTopKOutput: topk_weights, topk_ids)
+ * the quant methods consume (quant/sm70_fp8_moe/check.py:106-114; the
+ * benchmark's routing: softmax -> top-k -> renormalise).
+ * scoring B200_SCORING_SOFTMAX: weights = softmax probabilities of the chosen
+ * experts; B200_SCORING_SIGMOID: weights = sigmoid(logit), chosen by
+ * sigmoid(logit) + correction_bias[e] when correction_bias is given (fp32
+ * [num_experts]; softmax takes none). renormalize != 0 divides the chosen
+ * weights by their sum. Ties go to the lower expert id. num_experts <= 1024,
+ * top_k <= min(32, num_experts).
+ */
+#define B200_SCORING_SOFTMAX 0
+#define B200_SCORING_SIGMOID 1
+int b200_topk_route(const void* router_logits, int32_t logits_dtype, int64_t tokens,
+                    int32_t num_experts, int32_t top_k, int32_t scoring, int32_t renormalize,
+                    const float* correction_bias, int32_t* topk_ids, float* topk_weights,
+                    void* stream);
+
 /* ---------------------------------------------------------------- combine */
 
 /*

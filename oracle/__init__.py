@@ -26,7 +26,10 @@ checked by ``tests/test_oracle_golden.py``):
 ``moe_align_block_size`` lives upstream (sgl_kernel, not in the reference
 tree); its restatement here is pinned to the reference's own stable
 expert-major order (``method.py:285``) through the method fixture, and is
-otherwise "parity unpinned" against upstream's kernel.
+otherwise "parity unpinned" against upstream's kernel. The router
+(softmax / sigmoid top-k) is upstream too: its restatement follows the
+benchmark's definition (softmax -> top-k -> renormalise) and is parity
+unpinned against upstream's fused top-k kernel.
 """
 
 from .align import moe_align_block_size
@@ -50,7 +53,7 @@ from .nvfp4 import (
     nvfp4_linear_ref,
     quantize_nvfp4,
 )
-from .router import route_topk
+from .router import route_topk, route_topk_general
 
 __all__ = [
     "E2M1_GRID",
@@ -69,4 +72,5 @@ __all__ = [
     "quant_block_fp8_lm_head",
     "quantize_nvfp4",
     "route_topk",
+    "route_topk_general",
 ]

@@ -16,3 +16,27 @@ def route_topk(logits: torch.Tensor, top_k: int):
     w, ids = torch.topk(probs, top_k, dim=-1)
     w = w / w.sum(dim=-1, keepdim=True)
     return ids.to(torch.int32), w.to(torch.float32)
+
+
+def route_topk_general(logits: torch.Tensor, top_k: int, scoring: str = "softmax",
+                       renormalize: bool = True, bias: torch.Tensor | None = None):
+    """Top-k routing with a deterministic tie order (lower expert id first).
+
+    ``scoring`` "softmax": weights are softmax probabilities, chosen by
+    probability; "sigmoid": weights are sigmoid(logit), chosen by
+    sigmoid(logit) + ``bias`` (upstream SGLang's biased top-k selection, where
+    the correction bias steers the choice but not the weights). Selection is a
+    stable descending sort of the key, so equal keys keep expert order.
+    """
+    x = logits.float()
+    if scoring == "softmax":
+        scores = torch.softmax(x, dim=-1)
+        key = x  # same order as the probabilities
+    else:
+        scores = torch.sigmoid(x)
+        key = scores + (bias.float() if bias is not None else 0.0)
+    order = torch.sort(-key, dim=-1, stable=True).indices[:, :top_k]
+    w = scores.gather(1, order)
+    if renormalize:
+        w = w / w.sum(dim=-1, keepdim=True)
+    return order.to(torch.int32), w.to(torch.float32)

@@ -92,6 +92,13 @@ cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num
                                    int* expert_ids, long long expert_cap, int* ntpp, int* scratch,
                                    cudaStream_t stream);
 
+// Router top-k (softmax or sigmoid scoring, optional selection bias and
+// renormalisation); logits dtype 0 bf16, 1 f16, 2 f32.
+int router_max_experts();
+cudaError_t launch_topk_route(const void* logits, int dtype, long long tokens, int num_experts,
+                              int top_k, int scoring, int renormalize, const float* bias,
+                              int* topk_ids, float* topk_w, cudaStream_t stream);
+
 // Elementwise / reduction kernels.
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);
 // out[s, :k] (f16) = x[sorted_ids[s] / top_k, :k] for the valid route slots

@@ -29,6 +29,9 @@ DTYPE_F32 = 2
 QUANT_FP8_BLOCK = 0
 QUANT_NVFP4 = 1
 
+SCORING_SOFTMAX = 0
+SCORING_SIGMOID = 1
+
 GATED_NONE = 0
 GATED_FUSED = 1
 GATED_SPLIT = 2
@@ -50,6 +53,11 @@ SIGNATURES = {
     "b200_moe_align_block_size": (
         c_int32,
         [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    ),
+    "b200_topk_route": (
+        c_int32,
+        [c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+         c_void_p, c_void_p],
     ),
     "b200_moe_sum_reduce": (
         c_int32,

@@ -110,6 +110,14 @@ class QuantMoELayer:
             shared_out=shared_out, out=out,
         )
 
+    def forward_logits(self, x, router_logits, out=None, scoring: int = _lib.SCORING_SOFTMAX,
+                       renormalize: bool = True, correction_bias=None):
+        """Route with the library's top-k kernel, then forward (the routing of
+        the benchmark: softmax -> top-k -> renormalise)."""
+        ids, w = ops.topk_route(router_logits, self.top_k, scoring=scoring,
+                                renormalize=renormalize, correction_bias=correction_bias)
+        return self.forward(x, ids, w, out=out)
+
     # launches of one forward on `tokens` rows: bf16->f16, align (3 kernels
     # from 4096 routes on), [tcgen05 plan], gate/up, down, combine (+ shared)
     def launches_per_forward(self, x_dtype=torch.bfloat16, tokens: int | None = None) -> int:

@@ -126,6 +126,38 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
 
 
 # ----------------------------------------------------------------- combine
+_LOGIT_CODE = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
+               torch.float32: _lib.DTYPE_F32}
+
+
+def topk_route(router_logits: torch.Tensor, top_k: int, *, scoring: int = _lib.SCORING_SOFTMAX,
+               renormalize: bool = True, correction_bias: torch.Tensor | None = None,
+               out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """(topk_ids int32 [T, k], topk_weights fp32 [T, k]) from router logits [T, E]."""
+    _contig(router_logits, "router_logits")
+    try:
+        code = _LOGIT_CODE[router_logits.dtype]
+    except KeyError:
+        raise TypeError(f"router_logits must be bf16, f16 or f32, got {router_logits.dtype}") from None
+    tokens, experts = (int(d) for d in router_logits.shape)
+    if correction_bias is not None:
+        _contig(correction_bias, "correction_bias")
+        if correction_bias.dtype != torch.float32 or correction_bias.numel() != experts:
+            raise ValueError("correction_bias must be fp32 [num_experts]")
+    if out is None:
+        ids = torch.empty(tokens, top_k, dtype=torch.int32, device=router_logits.device)
+        w = torch.empty(tokens, top_k, dtype=torch.float32, device=router_logits.device)
+    else:
+        ids, w = out
+    _lib.check(
+        lib().b200_topk_route(
+            _vp(router_logits), code, tokens, experts, top_k, scoring, int(renormalize),
+            _vp(correction_bias), _vp(ids), _vp(w), _stream(router_logits.device),
+        )
+    )
+    return ids, w
+
+
 def moe_sum_reduce(input_tensor: torch.Tensor, output_tensor: torch.Tensor,
                    routed_scaling_factor: float = 1.0) -> torch.Tensor:
     """``out[t] = rsf * sum_k in[t, k]`` (``quant/sm70_fp4_moe/sum_reduce.py:84-123``)."""

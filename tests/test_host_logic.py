@@ -136,3 +136,42 @@ def test_lm_head_quantizer_matches_reference_golden():
     q, s = _quantize(head)
     assert np.array_equal(q.view(torch.uint8).numpy().reshape(-1), g["head_q"].reshape(-1))
     assert np.array_equal(s.numpy(), g["head_s"])
+
+
+def test_router_host_validation_without_a_gpu():
+    """b200_topk_route refuses bad arguments before touching the device."""
+    import ctypes
+
+    from sglang_restomod_b200 import _lib
+
+    lib = _lib.load()
+    ids = (ctypes.c_int32 * 8)()
+    w = (ctypes.c_float * 8)()
+    logits = (ctypes.c_float * 64)()
+    # top_k above 32
+    assert lib.b200_topk_route(logits, 2, 1, 64, 33, 0, 1, None, ids, w, None) == _lib.ERR_INVALID
+    # top_k above num_experts
+    assert lib.b200_topk_route(logits, 2, 1, 4, 8, 0, 1, None, ids, w, None) == _lib.ERR_INVALID
+    # correction bias with softmax scoring
+    bias = (ctypes.c_float * 64)()
+    assert lib.b200_topk_route(logits, 2, 1, 64, 8, 0, 1, bias, ids, w, None) == _lib.ERR_INVALID
+    # too many experts, bad dtype, unknown scoring
+    assert lib.b200_topk_route(logits, 2, 1, 2000, 8, 0, 1, None, ids, w, None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200_topk_route(logits, 7, 1, 64, 8, 0, 1, None, ids, w, None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200_topk_route(logits, 2, 1, 64, 8, 5, 1, None, ids, w, None) == _lib.ERR_INVALID
+    # no tokens: nothing to do
+    assert lib.b200_topk_route(None, 2, 0, 64, 8, 0, 1, None, None, None, None) == _lib.OK
+
+
+def test_router_oracle_tie_order():
+    import torch
+
+    import oracle
+
+    logits = torch.zeros(2, 8)
+    logits[:, 5] = 1.0
+    logits[:, 2] = 0.5
+    logits[:, 6] = 0.5
+    ids, w = oracle.route_topk_general(logits, 3)
+    assert ids.tolist() == [[5, 2, 6], [5, 2, 6]]
+    assert torch.allclose(w.sum(-1), torch.ones(2))
