@@ -193,8 +193,11 @@ class MoEWorkload:
         self.quant = spec["quant"]
         self.world = world
         e_local = shape.experts // world
+        # The shared expert rides in the routed GEMMs (one more expert) when its
+        # shapes and quantization match the routed experts'.
         self.layer = QuantMoELayer.synthetic(shape, self.quant, device,
-                                             first_expert=rank * e_local, num_experts=e_local)
+                                             first_expert=rank * e_local, num_experts=e_local,
+                                             fuse_shared=spec.get("fuse_shared", True))
         # N > 1: the peer-memory exchange (NVLink P2P stores, no host sync) by
         # default; --transport nccl selects the all-to-all baseline.
         self.transport = spec.get("transport", "peer") if world > 1 else "local"
@@ -464,6 +467,8 @@ def main() -> int:
     ap.add_argument("--eager", action="store_true", help="no CUDA graph replay")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange at N > 1")
+    ap.add_argument("--separate-shared", action="store_true",
+                    help="run the shared expert as its own dense MLP instead of fused")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -480,6 +485,7 @@ def main() -> int:
     device = torch.device("cuda", torch.cuda.current_device())
     spec = parse_workload(args.workload)
     spec["transport"] = args.transport
+    spec["fuse_shared"] = not args.separate_shared
     if spec["kind"] == "dense":
         wl = DenseWorkload(spec, device)
     elif spec["kind"] in ("ep", "moe"):

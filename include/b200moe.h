@@ -112,6 +112,21 @@ int b200_topk_route(const void* router_logits, int32_t logits_dtype, int64_t tok
                     const float* correction_bias, int32_t* topk_ids, float* topk_weights,
                     void* stream);
 
+/*
+ * Shared-expert fusion: ids_out / weights_out [tokens, top_k + 1] = the
+ * routes of topk_ids / topk_weights [tokens, top_k] plus one route per token
+ * to shared_id with shared_weight. With the shared expert's weights stored
+ * as expert shared_id of the routed bank (same shapes and quantization), one
+ * routed layer forward then computes the shared expert too (use
+ * shared_weight = 1 / routed_scaling_factor, since the combine scales every
+ * route). Replaces the shared expert's separate dense MLP (upstream's
+ * always-on shared expert, which the FP8 checkpoint keeps as a dense
+ * linear: docs/quantization-dispatch.md:112, 125-126).
+ */
+int b200_append_shared_route(const int32_t* topk_ids, const float* topk_weights, int64_t tokens,
+                             int32_t top_k, int32_t shared_id, float shared_weight,
+                             int32_t* ids_out, float* weights_out, void* stream);
+
 /* ---------------------------------------------------------------- combine */
 
 /*
@@ -290,11 +305,14 @@ int b200_ipc_close_handle(void* dev_ptr, int64_t offset);
 
 /* Source side: x [tokens, hidden] bf16/f16, topk_ids / topk_weights
  * [tokens, top_k] (global expert ids; ids outside [0, num_experts) are not
- * sent), tokens <= max_tokens. */
+ * sent), tokens <= max_tokens. shared_expert != 0: id num_experts is a shared
+ * expert held by every rank (appended by b200_append_shared_route); those
+ * routes stay on this rank as its local expert num_experts / world. */
 int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
                      const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
-                     int32_t num_experts, int32_t rank, int32_t world, const uint64_t* peer_regions,
-                     void* region, int64_t max_tokens, void* stream);
+                     int32_t num_experts, int32_t shared_expert, int32_t rank, int32_t world,
+                     const uint64_t* peer_regions, void* region, int64_t max_tokens,
+                     void* stream);
 
 /* Owner side: this rank's local_experts experts (w13: gated bank
  * [local_experts, 2*inter, hidden], w2: [local_experts, hidden, inter], as for

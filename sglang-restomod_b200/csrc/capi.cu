@@ -278,6 +278,19 @@ int b200_topk_route(const void* router_logits, int32_t logits_dtype, int64_t tok
                     "router launch");
 }
 
+int b200_append_shared_route(const int32_t* topk_ids, const float* topk_weights, int64_t tokens,
+                             int32_t top_k, int32_t shared_id, float shared_weight,
+                             int32_t* ids_out, float* weights_out, void* stream) {
+  if (tokens < 0 || top_k <= 0) return fail(B200_ERR_INVALID, "bad tokens/top_k");
+  if (tokens == 0) return B200_OK;
+  if (topk_ids == nullptr || topk_weights == nullptr || ids_out == nullptr || weights_out == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  return check_cuda(launch_append_shared_route(topk_ids, topk_weights, tokens, top_k, shared_id,
+                                               shared_weight, ids_out, weights_out,
+                                               reinterpret_cast<cudaStream_t>(stream)),
+                    "append shared route launch");
+}
+
 int b200_moe_sum_reduce(const void* input, void* output, int64_t tokens, int32_t top_k,
                         int64_t hidden, int32_t dtype, float routed_scaling_factor, void* stream) {
   if (!valid_dtype16(dtype)) return fail(B200_ERR_UNSUPPORTED, "dtype must be bf16 or f16");
@@ -814,8 +827,9 @@ int b200_ipc_close_handle(void* dev_ptr, int64_t offset) {
 
 int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
                      const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
-                     int32_t num_experts, int32_t rank, int32_t world, const uint64_t* peer_regions,
-                     void* region, int64_t max_tokens, void* stream) {
+                     int32_t num_experts, int32_t shared_expert, int32_t rank, int32_t world,
+                     const uint64_t* peer_regions, void* region, int64_t max_tokens,
+                     void* stream) {
   int rc = check_ep_common(rank, world, max_tokens, top_k, hidden, region, peer_regions);
   if (rc) return rc;
   if (!valid_dtype16(x_dtype)) return fail(B200_ERR_UNSUPPORTED, "activations must be bf16 or f16");
@@ -834,8 +848,9 @@ int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hid
   const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return check_cuda(launch_ep_dispatch(x, x_dtype == B200_DTYPE_F16, tokens, hidden, topk_ids,
-                                       topk_weights, top_k, num_experts, num_experts / world, rank,
-                                       world, reinterpret_cast<const unsigned long long*>(peer_regions),
+                                       topk_weights, top_k, num_experts, shared_expert != 0,
+                                       num_experts / world, rank, world,
+                                       reinterpret_cast<const unsigned long long*>(peer_regions),
                                        region, L, st),
                     "ep dispatch launch");
 }

@@ -169,6 +169,23 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(
   griddep_launch_dependents();
 }
 
+// ids_out[t, :] = (topk_ids[t, :], shared_id), w_out[t, :] = (topk_weights[t, :],
+// shared_weight): every token gains one route to the shared expert.
+__global__ void __launch_bounds__(256) append_shared_route_kernel(
+    const int* __restrict__ ids, const float* __restrict__ w, long long tokens, int top_k,
+    int shared_id, float shared_weight, int* __restrict__ ids_out, float* __restrict__ w_out) {
+  griddep_wait();
+  const long long total = tokens * (top_k + 1);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / (top_k + 1);
+    const int j = (int)(i - t * (top_k + 1));
+    ids_out[i] = j < top_k ? __ldg(ids + t * top_k + j) : shared_id;
+    w_out[i] = j < top_k ? __ldg(w + t * top_k + j) : shared_weight;
+  }
+  griddep_launch_dependents();
+}
+
 int grid_for(long long work, int threads) {
   long long blocks = (work + threads - 1) / threads;
   const long long cap = (long long)device_sm_count() * 8;
@@ -196,6 +213,15 @@ cudaError_t launch_permute_rows(const void* x, int x_f16, long long ldx, long lo
   return launch_pdl(permute_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream,
                     static_cast<const uint8_t*>(x), x_f16, ldx, x_rows, k, sorted_ids, ntpp, cap,
                     top_k, num_routes, static_cast<uint8_t*>(out));
+}
+
+cudaError_t launch_append_shared_route(const int* ids, const float* w, long long tokens,
+                                       int top_k, int shared_id, float shared_weight,
+                                       int* ids_out, float* w_out, cudaStream_t stream) {
+  const long long total = tokens * (top_k + 1);
+  if (total == 0) return cudaSuccess;
+  return launch_pdl(append_shared_route_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream,
+                    ids, w, tokens, top_k, shared_id, shared_weight, ids_out, w_out);
 }
 
 cudaError_t launch_moe_sum_reduce(const void* in, void* out, long long tokens, int top_k,

@@ -95,11 +95,28 @@ struct DispatchParams {
   const int* ids;  // [tokens * top_k] global expert ids
   const float* w;  // [tokens * top_k]
   int top_k, num_experts, experts_per_rank, rank, world;
+  int shared_expert;  // id num_experts = the shared expert: stays here as local expert experts_per_rank
   const unsigned long long* peers;  // [world] region bases in this process
   uint8_t* region;                  // this rank's region
   EpLayout L;
   int chunk;  // routes per CTA (multiple of 32)
 };
+
+// Owner rank and local expert of global expert e (-1: not sent). With a
+// fused shared expert, id num_experts is the shared expert, computed by the
+// source rank itself as its local expert experts_per_rank.
+__device__ __forceinline__ int route_owner(const DispatchParams& p, int e, int& local) {
+  if (e >= 0 && e < p.num_experts) {
+    const int o = e / p.experts_per_rank;
+    local = e - o * p.experts_per_rank;
+    return o;
+  }
+  if (p.shared_expert && e == p.num_experts) {
+    local = p.experts_per_rank;
+    return p.rank;
+  }
+  return -1;
+}
 
 // One CTA per chunk of routes. Positions inside an owner's segment follow
 // route order (stable), so a receiver's slots are in the source's route order.
@@ -121,18 +138,16 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const DispatchP
   __syncthreads();
   // Routes of earlier chunks per owner.
   for (long long r = tid; r < c0; r += kEpThreads) {
-    const int e = __ldg(p.ids + r);
-    if (e >= 0 && e < p.num_experts) atomicAdd(&base[e / p.experts_per_rank], 1);
+    int local;
+    const int o = route_owner(p, __ldg(p.ids + r), local);
+    if (o >= 0) atomicAdd(&base[o], 1);
   }
   __syncthreads();
   if (warp == 0) {
     for (long long g = c0; g < c1; g += 32) {
       const long long r = g + lane;
-      int o = -1;
-      if (r < c1) {
-        const int e = __ldg(p.ids + r);
-        if (e >= 0 && e < p.num_experts) o = e / p.experts_per_rank;
-      }
+      int o = -1, local;
+      if (r < c1) o = route_owner(p, __ldg(p.ids + r), local);
       int mypos = -1;
       for (int d = 0; d < p.world; ++d) {
         const unsigned m = __ballot_sync(0xffffffffu, o == d);
@@ -153,12 +168,12 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const DispatchP
   for (long long r = c0 + warp; r < c1; r += kEpThreads / 32) {
     const int ps = pos[r - c0];
     if (ps < 0) continue;
-    const int e = __ldg(p.ids + r);
-    const int o = e / p.experts_per_rank;
+    int local;
+    const int o = route_owner(p, __ldg(p.ids + r), local);
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.peers[o]);
     const long long slot = (long long)p.rank * p.L.cap + ps;
     if (lane == 0) {
-      reinterpret_cast<int*>(dst + p.L.off_ids)[slot] = e - o * p.experts_per_rank;
+      reinterpret_cast<int*>(dst + p.L.off_ids)[slot] = local;
       reinterpret_cast<float*>(dst + p.L.off_w)[slot] = __ldg(p.w + r);
       reinterpret_cast<int*>(dst + p.L.off_orig)[slot] = (int)r;
     }
@@ -356,7 +371,7 @@ int ep_dispatch_chunk(long long routes) {
 
 cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
                                const int* ids, const float* w, int top_k, int num_experts,
-                               int experts_per_rank, int rank, int world,
+                               int shared_expert, int experts_per_rank, int rank, int world,
                                const unsigned long long* peers, void* region, const EpLayout& L,
                                cudaStream_t stream) {
   // With no routes one CTA still publishes this step's (zero) counts and flags.
@@ -370,6 +385,7 @@ cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long 
   p.w = w;
   p.top_k = top_k;
   p.num_experts = num_experts;
+  p.shared_expert = shared_expert;
   p.experts_per_rank = experts_per_rank;
   p.rank = rank;
   p.world = world;

@@ -100,6 +100,9 @@ cudaError_t launch_topk_route(const void* logits, int dtype, long long tokens, i
                               int* topk_ids, float* topk_w, cudaStream_t stream);
 
 // Elementwise / reduction kernels.
+cudaError_t launch_append_shared_route(const int* ids, const float* w, long long tokens,
+                                       int top_k, int shared_id, float shared_weight,
+                                       int* ids_out, float* w_out, cudaStream_t stream);
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);
 // out[s, :k] (f16) = x[sorted_ids[s] / top_k, :k] for the valid route slots
 // s < min(*ntpp, cap); padding slots are left as they are.
@@ -158,7 +161,7 @@ inline EpLayout ep_layout(int world, long long cap, long long hidden) {
 int ep_dispatch_chunk(long long routes);
 cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
                                const int* ids, const float* w, int top_k, int num_experts,
-                               int experts_per_rank, int rank, int world,
+                               int shared_expert, int experts_per_rank, int rank, int world,
                                const unsigned long long* peers, void* region, const EpLayout& L,
                                cudaStream_t stream);
 cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int world,

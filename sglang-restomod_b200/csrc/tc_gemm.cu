@@ -63,8 +63,8 @@ constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
 constexpr int kLoadPasses = kNMax / (kLoadThreads / 2);  // rows per gather thread
 constexpr int kStages = 4;                               // 64-K A stages in tensor memory
-constexpr int kBStages = 6;                              // 64-K B stages in shared memory
-constexpr int kRawStages = 4;                            // 16 KiB FP8 units
+constexpr int kBStages = 4;                              // 64-K B stages in shared memory
+constexpr int kRawStages = 8;                            // 16 KiB FP8 units (weights in flight)
 constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
 constexpr uint32_t kBTile = kNMax * 128;                 // [192 rows][64 K] f16
 constexpr uint32_t kOffB = 0;

@@ -59,6 +59,9 @@ SIGNATURES = {
         [c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
          c_void_p, c_void_p],
     ),
+    "b200_append_shared_route": (
+        c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]
+    ),
     "b200_moe_sum_reduce": (
         c_int32,
         [c_void_p, c_void_p, c_int64, c_int32, c_int64, c_int32, c_float, c_void_p],
@@ -107,7 +110,7 @@ SIGNATURES = {
     "b200_ep_dispatch": (
         c_int32,
         [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int32,
-         c_int32, c_void_p, c_void_p, c_int64, c_void_p],
+         c_int32, c_int32, c_void_p, c_void_p, c_int64, c_void_p],
     ),
     "b200_ep_expert_workspace_bytes": (
         c_int64, [c_int32, c_int64, c_int32, c_int64, c_int64, c_int32, c_int32]

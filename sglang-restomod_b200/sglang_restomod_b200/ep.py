@@ -132,15 +132,25 @@ class ExpertParallelMoE:
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         self.exchange = exchange
+        self.fused = False
         if transport == "peer":
             if local is None or max_tokens is None:
                 raise ValueError("the peer transport needs the local layer and max_tokens")
+            # A fused shared expert travels as one more route per token, kept
+            # on the source rank (its local expert num_experts / world); used
+            # when the owner's GEMMs run on the tensor-core path (blocks of 64+).
+            self.fused = local.shared_fused and (local.block_size or block_size_for(
+                max_tokens * (local.top_k + 1), local.num_experts + 1)) >= 64
+            routes_k = local.top_k + (1 if self.fused else 0)
+            if exchange is not None and exchange.top_k != routes_k:
+                raise ValueError(f"exchange sized for {exchange.top_k} routes per token, "
+                                 f"this layer sends {routes_k}")
             if exchange is None:
-                self.exchange = PeerExchange(world, rank, max_tokens, local.top_k, local.hidden,
+                self.exchange = PeerExchange(world, rank, max_tokens, routes_k, local.hidden,
                                              local.w13.device, group=group)
             # Each owner receives about max_tokens * top_k routes per step.
             self.peer_block_size = local.block_size or block_size_for(
-                max_tokens * local.top_k, local.num_experts)
+                max_tokens * routes_k, local.num_experts + (1 if self.fused else 0))
 
     def _run_local(self, rows, ids1, w1):
         if self._local_fn is not None:
@@ -171,11 +181,15 @@ class ExpertParallelMoE:
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
+        if self.transport == "peer" and self.fused:
+            ids, w = self.local.fused_routes(topk_ids, topk_weights, shared_id=self.num_experts)
+            return self._forward_peer(x, ids, w, None, out)
+        if self.world == 1 and self._local_fn is None and self.transport != "peer":
+            # all experts are local: one layer forward (shared expert inside)
+            return self.local.forward(x, topk_ids, topk_weights, out=out)
         shared = self._shared(x)
         if self.transport == "peer":
             return self._forward_peer(x, topk_ids, topk_weights, shared, out)
-        if self.world == 1 and self._local_fn is None:
-            return self.local.forward(x, topk_ids, topk_weights, out=out, shared_out=shared)
 
         tokens, top_k = topk_ids.shape
         order, dest, send_counts = self.dispatch_plan(topk_ids)
@@ -219,35 +233,43 @@ class ExpertParallelMoE:
         kernels from 4096 receive slots on), [tcgen05 plan], gate/up, down,
         signal, combine, + the shared expert's."""
         layer = self.local
-        slots = self.world * self.exchange.max_tokens * layer.top_k
+        slots = self.world * self.exchange.max_tokens * self.exchange.top_k
         n = 1 + 1 + (3 if slots >= 4096 else 1) + (1 if self.peer_block_size >= 64 else 0) + 4
-        if layer.shared is not None:
+        if self.fused:
+            n += 1 + (1 if self.peer_block_size >= 64 else 0)  # route append, permute
+        elif layer.shared is not None:
             n += layer.shared.launches(self.exchange.max_tokens, layer.hidden, x_dtype)
+            n += 1 if self.peer_block_size >= 64 else 0  # permute
+        else:
+            n += 1 if self.peer_block_size >= 64 else 0
         return n
 
     # The three steps of a peer-transport forward; every rank runs them in this
     # order. (A single process standing in for several ranks interleaves them
     # rank by rank: all dispatches, then all expert steps, then all combines.)
     def peer_dispatch(self, x, topk_ids, topk_weights):
+        """topk_ids / topk_weights: [T, k], or [T, k + 1] with the shared
+        route appended when the layer's shared expert is fused."""
         ex = self.exchange
         ops.ep_dispatch(x, topk_ids, topk_weights, num_experts=self.num_experts, rank=self.rank,
                         world=self.world, peers=ex.peers, region=ex.region,
-                        max_tokens=ex.max_tokens)
+                        max_tokens=ex.max_tokens, shared_expert=self.fused)
 
     def peer_experts(self):
         ex, layer = self.exchange, self.local
         ops.ep_expert_forward(
             quant=layer.quant, hidden=layer.hidden, inter=layer.inter,
-            local_experts=layer.num_experts, w13=layer.w13, w2=layer.w2,
-            w13_scales=layer.w13_scales, w2_scales=layer.w2_scales, w13_global=layer.w13_global,
-            w2_global=layer.w2_global, block_size=self.peer_block_size, rank=self.rank,
-            world=self.world, peers=ex.peers, region=ex.region, max_tokens=ex.max_tokens,
-            top_k=layer.top_k,
+            local_experts=layer.num_experts + (1 if self.fused else 0), w13=layer.w13,
+            w2=layer.w2, w13_scales=layer.w13_scales, w2_scales=layer.w2_scales,
+            w13_global=layer.w13_global, w2_global=layer.w2_global,
+            block_size=self.peer_block_size, rank=self.rank, world=self.world, peers=ex.peers,
+            region=ex.region, max_tokens=ex.max_tokens, top_k=ex.top_k,
         )
 
     def peer_combine(self, topk_ids, shared=None, out=None, out_dtype=torch.bfloat16):
         ex, layer = self.exchange, self.local
-        return ops.ep_combine(topk_ids, hidden=layer.hidden, num_experts=self.num_experts,
+        return ops.ep_combine(topk_ids, hidden=layer.hidden,
+                              num_experts=self.num_experts + (1 if self.fused else 0),
                               world=self.world, region=ex.region, max_tokens=ex.max_tokens,
                               routed_scaling_factor=layer.routed_scaling_factor,
                               shared_out=shared, out=out, out_dtype=out_dtype)

@@ -95,10 +95,60 @@ class QuantMoELayer:
     shared: SharedExpert | None = None
     routed_scaling_factor: float = 1.0
     block_size: int | None = None
+    # The banks hold the shared expert as one more expert (index num_experts)
+    # after fuse_shared(): one routed launch computes it with the rest.
+    shared_fused: bool = False
+
+    def can_fuse_shared(self) -> bool:
+        s = self.shared
+        return s is not None and s.quant == self.quant and s.inter == self.inter and \
+            self.quant == _lib.QUANT_FP8_BLOCK
+
+    def fuse_shared(self) -> "QuantMoELayer":
+        """Append the shared expert to the routed banks (same shapes and block
+        FP8). The separate SharedExpert stays for callers that run the routed
+        experts alone (the NCCL expert-parallel transport)."""
+        if self.shared_fused or not self.can_fuse_shared():
+            return self
+        s = self.shared
+        self.w13 = torch.cat([self.w13, s.w13.reshape(1, -1)])
+        self.w2 = torch.cat([self.w2, s.w2.reshape(1, -1)])
+        self.w13_scales = torch.cat([self.w13_scales, s.w13_scales.unsqueeze(0)])
+        self.w2_scales = torch.cat([self.w2_scales, s.w2_scales.unsqueeze(0)])
+        self.shared_fused = True
+        return self
+
+    def fused_routes(self, topk_ids, topk_weights, shared_id=None):
+        """Routes plus one shared route per token (weight 1 / rsf: the combine
+        scales every route by rsf, the shared expert's output is unscaled)."""
+        sid = self.num_experts if shared_id is None else shared_id
+        return ops.append_shared_route(topk_ids, topk_weights, sid,
+                                       1.0 / self.routed_scaling_factor)
+
+    def fused_block_size(self, tokens: int, block_size=None) -> int | None:
+        """Block size of the fused forward, or None when it should not be used:
+        the shared expert only pays off inside the tensor-core GEMM (blocks of
+        64+, where its tokens form one item per weight block); with the
+        weight-streaming GEMM's 16-slot groups its weights would be streamed
+        once per 16 tokens (measured 3 % slower at 128 tokens)."""
+        if not self.shared_fused:
+            return None
+        bs = block_size or self.block_size or block_size_for(tokens * (self.top_k + 1),
+                                                             self.num_experts + 1)
+        return bs if bs >= 64 else None
 
     def forward(self, x, topk_ids, topk_weights, out=None, shared_out=None, block_size=None,
                 use_shared=True):
         tokens, top_k = topk_ids.shape
+        bs = self.fused_block_size(tokens, block_size) if use_shared and shared_out is None else None
+        if bs is not None:
+            ids, w = self.fused_routes(topk_ids, topk_weights)
+            return ops.moe_layer_forward(
+                x, ids, w, quant=self.quant, num_experts=self.num_experts + 1,
+                inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
+                w2_scales=self.w2_scales, block_size=bs,
+                routed_scaling_factor=self.routed_scaling_factor, out=out,
+            )
         if use_shared and shared_out is None and self.shared is not None:
             shared_out = self.shared.forward(x)
         bs = block_size or self.block_size or block_size_for(tokens * top_k, self.num_experts)
@@ -122,6 +172,11 @@ class QuantMoELayer:
     # from 4096 routes on), [tcgen05 plan], gate/up, down, combine (+ shared)
     def launches_per_forward(self, x_dtype=torch.bfloat16, tokens: int | None = None) -> int:
         n = 4 + (1 if x_dtype == torch.bfloat16 else 0)
+        if tokens is not None and self.fused_block_size(tokens) is not None:
+            routes = tokens * (self.top_k + 1)
+            # + the shared-route append and the tcgen05 plan; the shared expert
+            # runs inside the GEMMs
+            return n + 1 + (2 if routes >= 4096 else 0) + 1
         if tokens is not None:
             routes = tokens * self.top_k
             bs = self.block_size or block_size_for(routes, self.num_experts)
@@ -138,8 +193,11 @@ class QuantMoELayer:
 
     @classmethod
     def synthetic(cls, shape: synth.MoEShape, quant: int, device, first_expert: int = 0,
-                  num_experts: int | None = None, seed: int = 10) -> "QuantMoELayer":
-        """Random-init layer of ``shape`` holding experts [first, first + num)."""
+                  num_experts: int | None = None, seed: int = 10,
+                  fuse_shared: bool = False) -> "QuantMoELayer":
+        """Random-init layer of ``shape`` holding experts [first, first + num)
+        (the shared expert appended to the banks when ``fuse_shared`` and the
+        shapes allow)."""
         e = shape.experts if num_experts is None else num_experts
         h, i = shape.hidden, shape.inter
         if quant == _lib.QUANT_FP8_BLOCK:
@@ -169,5 +227,6 @@ class QuantMoELayer:
                 quant=_lib.QUANT_FP8_BLOCK, inter=si, w13=ops.fp8_prepack(q13[0], True),
                 w2=ops.fp8_prepack(q2[0], False), w13_scales=s13[0], w2_scales=s2[0],
             )
-        return cls(quant=quant, hidden=h, inter=i, num_experts=e, top_k=shape.top_k, w13=w13,
-                   w2=w2, shared=shared, **kw)
+        layer = cls(quant=quant, hidden=h, inter=i, num_experts=e, top_k=shape.top_k, w13=w13,
+                    w2=w2, shared=shared, **kw)
+        return layer.fuse_shared() if fuse_shared else layer

@@ -158,6 +158,22 @@ def topk_route(router_logits: torch.Tensor, top_k: int, *, scoring: int = _lib.S
     return ids, w
 
 
+def append_shared_route(topk_ids: torch.Tensor, topk_weights: torch.Tensor, shared_id: int,
+                        shared_weight: float = 1.0):
+    """[T, k] routes -> [T, k + 1] with one route per token to ``shared_id``."""
+    _contig(topk_ids, "topk_ids")
+    _contig(topk_weights, "topk_weights")
+    tokens, top_k = (int(d) for d in topk_ids.shape)
+    ids = torch.empty(tokens, top_k + 1, dtype=torch.int32, device=topk_ids.device)
+    w = torch.empty(tokens, top_k + 1, dtype=torch.float32, device=topk_ids.device)
+    _lib.check(
+        lib().b200_append_shared_route(_vp(topk_ids), _vp(topk_weights), tokens, top_k, shared_id,
+                                       float(shared_weight), _vp(ids), _vp(w),
+                                       _stream(topk_ids.device))
+    )
+    return ids, w
+
+
 def moe_sum_reduce(input_tensor: torch.Tensor, output_tensor: torch.Tensor,
                    routed_scaling_factor: float = 1.0) -> torch.Tensor:
     """``out[t] = rsf * sum_k in[t, k]`` (``quant/sm70_fp4_moe/sum_reduce.py:84-123``)."""
@@ -399,7 +415,7 @@ def _peers_arg(peers: torch.Tensor, world: int):
 
 def ep_dispatch(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, *,
                 num_experts: int, rank: int, world: int, peers: torch.Tensor,
-                region: torch.Tensor, max_tokens: int) -> None:
+                region: torch.Tensor, max_tokens: int, shared_expert: bool = False) -> None:
     """Source side: this rank's routes (rows + routing) into their owners' regions."""
     _contig(x, "x")
     _contig(topk_ids, "topk_ids")
@@ -411,8 +427,8 @@ def ep_dispatch(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
     _lib.check(
         lib().b200_ep_dispatch(
             _vp(x), _code(x, "x"), tokens, hidden, _vp(topk_ids), _vp(topk_weights),
-            int(topk_ids.shape[1]), num_experts, rank, world, _peers_arg(peers, world),
-            _vp(region), max_tokens, _stream(x.device),
+            int(topk_ids.shape[1]), num_experts, int(shared_expert), rank, world,
+            _peers_arg(peers, world), _vp(region), max_tokens, _stream(x.device),
         )
     )
 

@@ -52,6 +52,13 @@ def _worker(rank, port, results):
         max_tokens = 32
         peer = ExpertParallelMoE(local, shape.experts, rank, WORLD, transport="peer",
                                  max_tokens=max_tokens)
+        fused_local = QuantMoELayer.synthetic(shape, _lib.QUANT_FP8_BLOCK, dev,
+                                              first_expert=rank * per, num_experts=per,
+                                              fuse_shared=True)
+        fused_local.block_size = 64  # the tensor-core owner path, where fusion applies
+        peer_fused = ExpertParallelMoE(fused_local, shape.experts, rank, WORLD, transport="peer",
+                                       max_tokens=max_tokens)
+        assert peer_fused.fused
         nccl = ExpertParallelMoE(local, shape.experts, rank, WORLD, transport="nccl")
         errors = []
         for step in range(3):
@@ -61,8 +68,10 @@ def _worker(rank, port, results):
             want = full.forward(x, ids, w)
             got = peer.forward(x, ids, w)
             got_nccl = nccl.forward(x, ids, w)
+            got_fused = peer_fused.forward(x, ids, w)
             torch.cuda.synchronize()
             assert_close(got, want, what=f"peer step {step}")
+            assert_close(got_fused, want, what=f"peer fused-shared step {step}")
             assert_close(got_nccl, want, what=f"nccl step {step}")
         # CUDA graph of the peer forward, replayed in lockstep on both ranks.
         x = synth.activations(max_tokens, shape.hidden, dev, seed=7 + rank)
@@ -84,6 +93,7 @@ def _worker(rank, port, results):
         dist.barrier()
         del graph
         peer.exchange.close()
+        peer_fused.exchange.close()
         results[rank] = ("ok", "")
     except Exception:  # noqa: BLE001 - reported to the parent
         results[rank] = ("error", traceback.format_exc())

@@ -29,30 +29,40 @@ pytestmark = pytest.mark.gpu
 SHAPE = synth.MoEShape(hidden=256, inter=128, experts=16, top_k=4, shared_inter=128)
 
 
-def _setup(world, max_tokens, quant, dev, block_size=None, shape=SHAPE):
+def _setup(world, max_tokens, quant, dev, block_size=None, shape=SHAPE, fused=False):
     full = QuantMoELayer.synthetic(shape, quant, dev)
     per = shape.experts // world
-    nbytes = ops.ep_region_bytes(world, max_tokens, shape.top_k, shape.hidden)
+    routes_k = shape.top_k + (1 if fused else 0)
+    nbytes = ops.ep_region_bytes(world, max_tokens, routes_k, shape.hidden)
     regions = [ops.aligned_zeros(nbytes, dev) for _ in range(world)]
     models = []
     for r in range(world):
-        local = QuantMoELayer.synthetic(shape, quant, dev, first_expert=r * per, num_experts=per)
+        local = QuantMoELayer.synthetic(shape, quant, dev, first_expert=r * per, num_experts=per,
+                                        fuse_shared=fused)
+        assert local.shared_fused == fused
         local.block_size = block_size
-        ex = PeerExchange(world, r, max_tokens, shape.top_k, shape.hidden, dev, regions=regions)
+        ex = PeerExchange(world, r, max_tokens, routes_k, shape.hidden, dev, regions=regions)
         models.append(ExpertParallelMoE(local, shape.experts, r, world, transport="peer",
                                         max_tokens=max_tokens, exchange=ex))
     return full, models
 
 
 def _step(models, inputs):
-    """One forward of every emulated rank, interleaved on the current stream."""
+    """One forward of every emulated rank, interleaved on the current stream.
+    A fused shared expert travels as one more route per token."""
+    routed = []
     for m, (x, ids, w) in zip(models, inputs):
+        if m.fused:
+            ids, w = m.local.fused_routes(ids, w, shared_id=m.num_experts)
+        routed.append((ids, w))
         m.peer_dispatch(x, ids, w)
     for m in models:
         m.peer_experts()
     outs = []
-    for m, (x, ids, w) in zip(models, inputs):
-        shared = m.local.shared.forward(x) if m.local.shared is not None and len(x) else None
+    for m, (x, _, _), (ids, _) in zip(models, inputs, routed):
+        shared = None
+        if not m.fused and m.local.shared is not None and len(x):
+            shared = m.local.shared.forward(x)
         outs.append(m.peer_combine(ids, shared, None, x.dtype))
     return outs
 
@@ -121,6 +131,24 @@ def test_peer_ep_tensor_core_path(cuda_device):
     torch.cuda.synchronize()
     for r, ((x, ids, w), out) in enumerate(zip(inputs, outs)):
         assert_close(out, full.forward(x, ids, w), what=f"rank {r}")
+    assert ops.workspace_status() == 0
+
+
+@pytest.mark.parametrize("world,block", [(2, None), (4, None), (2, 64)])
+def test_peer_ep_fused_shared_expert(cuda_device, world, block):
+    """The shared expert as one more local route per token (kept on the source
+    rank by the dispatch), stream and tcgen05 owner GEMMs."""
+    dev = cuda_device
+    full, models = _setup(world, 64, _lib.QUANT_FP8_BLOCK, dev, block_size=block, fused=True)
+    assert all(m.fused for m in models)
+    for step in range(2):
+        inputs = [_inputs(64 - 9 * r * step, SHAPE, dev, 500 + 31 * r + step) for r in range(world)]
+        outs = _step(models, inputs)
+        torch.cuda.synchronize()
+        for r, ((x, ids, w), out) in enumerate(zip(inputs, outs)):
+            assert_close(out, full.forward(x, ids, w), what=f"fused w={world} step {step} rank {r}")
+    for m in models:
+        assert m.exchange.status() == 0
     assert ops.workspace_status() == 0
 
 

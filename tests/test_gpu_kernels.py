@@ -423,3 +423,50 @@ def test_layer_config4_prefill_sampled(cuda_device):
     sample = torch.tensor([0, 1000, 4095])
     _check_layer(synth.CONFIG4, 4096, _lib.QUANT_FP8_BLOCK, cuda_device, block=256,
                  sample_tokens=sample, rsf=1.0)
+
+
+def test_layer_config4_decode_bench_workload(cuda_device):
+    """The default bench workload itself: H=7168, I=2048, 256 experts, top-8,
+    128 tokens, 16-slot blocks (weight-streaming GEMM), sampled tokens."""
+    _check_layer(synth.CONFIG4, 128, _lib.QUANT_FP8_BLOCK, cuda_device, block=16,
+                 sample_tokens=torch.tensor([0, 77, 127]), rsf=1.0)
+
+
+# ------------------------------------------------ fused shared expert
+@pytest.mark.parametrize("tokens,block", [(1, 64), (16, 64), (128, 64), (512, 64), (512, 128)])
+@pytest.mark.parametrize("rsf", [1.0, 2.5])
+def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
+    """Shared expert appended to the routed bank (one more route per token,
+    weight 1 / rsf) gives the layer output of the separate dense MLP. Fusion
+    is taken with blocks of 64+ (the tensor-core GEMM)."""
+    from sglang_restomod_b200.layer import QuantMoELayer
+
+    shape = synth.MoEShape(hidden=512, inter=256, experts=32, top_k=4, shared_inter=256)
+    sep = QuantMoELayer.synthetic(shape, _lib.QUANT_FP8_BLOCK, cuda_device)
+    fused = QuantMoELayer.synthetic(shape, _lib.QUANT_FP8_BLOCK, cuda_device, fuse_shared=True)
+    assert fused.shared_fused and not sep.shared_fused
+    sep.routed_scaling_factor = fused.routed_scaling_factor = rsf
+    sep.block_size = fused.block_size = block
+    x = synth.activations(tokens, shape.hidden, cuda_device, seed=21)
+    ids, w = synth.route(tokens, shape.experts, shape.top_k, cuda_device, seed=22)
+    assert fused.fused_block_size(tokens) == block
+    got = fused.forward(x, ids, w)
+    want = sep.forward(x, ids, w)
+    torch.cuda.synchronize()
+    assert ops.workspace_status() == 0
+    assert_close(got, want, what=f"fused shared T={tokens} block={block} rsf={rsf}")
+    # and against the CPU oracle: routed layer + the shared MLP as a 1-expert MoE
+    q13, s13 = synth.fp8_bank(shape.experts, 2 * shape.inter, shape.hidden, cuda_device, 10)
+    q2, s2 = synth.fp8_bank(shape.experts, shape.hidden, shape.inter, cuda_device, 11)
+    d13 = torch.stack([oracle.dequant_block_fp8(q13[e].cpu(), s13[e].cpu()) for e in range(shape.experts)])
+    d2 = torch.stack([oracle.dequant_block_fp8(q2[e].cpu(), s2[e].cpu()) for e in range(shape.experts)])
+    sq13, ss13 = synth.fp8_bank(1, 2 * shape.shared_inter, shape.hidden, cuda_device, 12)
+    sq2, ss2 = synth.fp8_bank(1, shape.hidden, shape.shared_inter, cuda_device, 13)
+    sd13 = oracle.dequant_block_fp8(sq13[0].cpu(), ss13[0].cpu()).unsqueeze(0)
+    sd2 = oracle.dequant_block_fp8(sq2[0].cpu(), ss2[0].cpu()).unsqueeze(0)
+    xc = x.cpu()
+    shared = oracle.moe_layer_ref(xc, torch.zeros(tokens, 1, dtype=torch.int32),
+                                  torch.ones(tokens, 1), sd13, sd2)
+    want_o = oracle.moe_layer_ref(xc, ids.cpu(), w.cpu(), d13, d2, routed_scaling_factor=rsf,
+                                  shared_out=shared)
+    assert_close(got, want_o, what=f"fused shared vs oracle T={tokens}")
