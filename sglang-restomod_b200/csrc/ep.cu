@@ -99,7 +99,7 @@ struct DispatchParams {
   const unsigned long long* peers;  // [world] region bases in this process
   uint8_t* region;                  // this rank's region
   EpLayout L;
-  int chunk;  // routes per CTA (multiple of 32)
+  int chunk;  // routes per CTA (multiple of 8)
 };
 
 // Owner rank and local expert of global expert e (-1: not sent). With a
@@ -362,11 +362,13 @@ int ep_grid(long long work) {
 
 }  // namespace
 
+// Routes per dispatch CTA: spread over up to 4 CTAs per SM (one warp per
+// route row, eight rows in flight per CTA), at least 8 routes per CTA.
 int ep_dispatch_chunk(long long routes) {
-  const long long ctas = 2ll * device_sm_count();
+  const long long ctas = 4ll * device_sm_count();
   long long chunk = (routes + ctas - 1) / ctas;
-  chunk = (chunk + 31) / 32 * 32;
-  return chunk < 32 ? 32 : (int)chunk;
+  chunk = (chunk + 7) / 8 * 8;
+  return chunk < 8 ? 8 : (int)chunk;
 }
 
 cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,

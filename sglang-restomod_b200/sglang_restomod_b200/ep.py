@@ -139,8 +139,9 @@ class ExpertParallelMoE:
             # A fused shared expert travels as one more route per token, kept
             # on the source rank (its local expert num_experts / world); used
             # when the owner's GEMMs run on the tensor-core path (blocks of 64+).
-            self.fused = local.shared_fused and (local.block_size or block_size_for(
-                max_tokens * (local.top_k + 1), local.num_experts + 1)) >= 64
+            fbs = local.block_size or block_size_for(max_tokens * (local.top_k + 1),
+                                                     local.num_experts + 1)
+            self.fused = local.shared_fused and (fbs >= 64 or max_tokens <= fbs)
             routes_k = local.top_k + (1 if self.fused else 0)
             if exchange is not None and exchange.top_k != routes_k:
                 raise ValueError(f"exchange sized for {exchange.top_k} routes per token, "

@@ -126,16 +126,17 @@ class QuantMoELayer:
                                        1.0 / self.routed_scaling_factor)
 
     def fused_block_size(self, tokens: int, block_size=None) -> int | None:
-        """Block size of the fused forward, or None when it should not be used:
-        the shared expert only pays off inside the tensor-core GEMM (blocks of
-        64+, where its tokens form one item per weight block); with the
-        weight-streaming GEMM's 16-slot groups its weights would be streamed
-        once per 16 tokens (measured 3 % slower at 128 tokens)."""
+        """Block size of the fused forward, or None when it should not be used.
+        The shared expert's weights are streamed once per group of its tokens:
+        fused when all tokens fit one group (small decode batches, saving the
+        dense MLP's launches) or on the tensor-core GEMM (blocks of 64+, one
+        item per weight block); with several 8-16-slot groups its weights
+        would be streamed several times (measured 3 % slower at 128 tokens)."""
         if not self.shared_fused:
             return None
         bs = block_size or self.block_size or block_size_for(tokens * (self.top_k + 1),
                                                              self.num_experts + 1)
-        return bs if bs >= 64 else None
+        return bs if bs >= 64 or tokens <= bs else None
 
     def forward(self, x, topk_ids, topk_weights, out=None, shared_out=None, block_size=None,
                 use_shared=True):

@@ -433,7 +433,8 @@ def test_layer_config4_decode_bench_workload(cuda_device):
 
 
 # ------------------------------------------------ fused shared expert
-@pytest.mark.parametrize("tokens,block", [(1, 64), (16, 64), (128, 64), (512, 64), (512, 128)])
+@pytest.mark.parametrize("tokens,block", [(1, None), (8, None), (1, 64), (16, 64), (128, 64),
+                                          (512, 64), (512, 128)])
 @pytest.mark.parametrize("rsf", [1.0, 2.5])
 def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
     """Shared expert appended to the routed bank (one more route per token,
@@ -449,7 +450,9 @@ def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
     sep.block_size = fused.block_size = block
     x = synth.activations(tokens, shape.hidden, cuda_device, seed=21)
     ids, w = synth.route(tokens, shape.experts, shape.top_k, cuda_device, seed=22)
-    assert fused.fused_block_size(tokens) == block
+    # fused on the tensor-core path, or when the batch fits one stream group
+    assert fused.fused_block_size(tokens) == (block or fused.fused_block_size(tokens))
+    assert fused.fused_block_size(tokens) is not None
     got = fused.forward(x, ids, w)
     want = sep.forward(x, ids, w)
     torch.cuda.synchronize()
