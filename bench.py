@@ -44,6 +44,12 @@ FALLBACK_BF16_TFLOPS = 1590.0
 
 
 # ------------------------------------------------------------------ helpers
+def torch_empty_like(t):
+    import torch
+
+    return torch.empty_like(t)
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.is_file():
@@ -158,6 +164,47 @@ def barrier(world):
         dist.barrier()
 
 
+class PipelinedIO:
+    """Double-buffered end-to-end I/O around one workload step.
+
+    Step i computes on device buffer i % 2 while a copy stream returns step
+    i-1's result to pinned host memory and brings step i+1's inputs to the
+    device (the copy engines run beside the kernels). Every step's input copy
+    and result copy still happen inside the timed region: the first inputs
+    are copied before the first step, the last result after the last one.
+    """
+
+    def __init__(self, host_inputs, device_out, compute):
+        import torch
+
+        self.h_in = list(host_inputs)
+        self.d_in = [[torch.empty_like(t, device=device_out.device) for t in self.h_in]
+                     for _ in range(2)]
+        self.d_out = [device_out, torch.empty_like(device_out)]
+        self.h_out = [torch.empty_like(device_out, device="cpu").pin_memory() for _ in range(2)]
+        self.copy = torch.cuda.Stream(device=device_out.device)
+        self.compute = compute
+
+    def load_first(self):
+        for d, h in zip(self.d_in[0], self.h_in):
+            d.copy_(h, non_blocking=True)
+
+    def step(self, p: int):
+        import torch
+
+        main = torch.cuda.current_stream()
+        self.copy.wait_stream(main)
+        with torch.cuda.stream(self.copy):
+            self.h_out[1 - p].copy_(self.d_out[1 - p], non_blocking=True)
+            for d, h in zip(self.d_in[1 - p], self.h_in):
+                d.copy_(h, non_blocking=True)
+        self.compute(self.d_in[p], self.d_out[p])
+        main.wait_stream(self.copy)
+
+    def drain(self, p: int):
+        self.h_out[p].copy_(self.d_out[p], non_blocking=True)
+
+
 # ---------------------------------------------------------------- workloads
 def parse_workload(name: str):
     from sglang_restomod_b200 import synth
@@ -215,19 +262,14 @@ class MoEWorkload:
         self.h_ids = self.ids.cpu().pin_memory()
         self.h_w = self.w.cpu().pin_memory()
         self.h_out = torch.empty_like(self.h_x).pin_memory()
-        self.d_x = torch.empty_like(self.x)
-        self.d_ids = torch.empty_like(self.ids)
-        self.d_w = torch.empty_like(self.w)
+        self.d_out = torch.empty_like(self.x)
 
     def step(self):
         self.model.forward(self.x, self.ids, self.w, out=self.out)
 
-    def step_e2e(self):
-        self.d_x.copy_(self.h_x, non_blocking=True)
-        self.d_ids.copy_(self.h_ids, non_blocking=True)
-        self.d_w.copy_(self.h_w, non_blocking=True)
-        self.model.forward(self.d_x, self.d_ids, self.d_w, out=self.out)
-        self.h_out.copy_(self.out, non_blocking=True)
+    def e2e_io(self):
+        return PipelinedIO([self.h_x, self.h_ids, self.h_w], self.d_out,
+                           lambda d, out: self.model.forward(d[0], d[1], d[2], out=out))
 
     def io_bytes(self):
         h2d = self.h_x.numel() * 2 + self.h_ids.numel() * 4 + self.h_w.numel() * 4
@@ -327,20 +369,19 @@ class DenseWorkload:
         self.out = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=device)
         self.h_x = self.x.cpu().pin_memory()
         self.h_out = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
-        self.d_x = torch.empty_like(self.x)
 
-    def _run(self, x):
+    def _run(self, x, out=None):
         from sglang_restomod_b200 import _lib, ops
 
-        ops.linear(x, self.packed, self.n, quant=_lib.QUANT_FP8_BLOCK, scales=self.scales, out=self.out)
+        ops.linear(x, self.packed, self.n, quant=_lib.QUANT_FP8_BLOCK, scales=self.scales,
+                   out=self.out if out is None else out)
 
     def step(self):
         self._run(self.x)
 
-    def step_e2e(self):
-        self.d_x.copy_(self.h_x, non_blocking=True)
-        self._run(self.d_x)
-        self.h_out.copy_(self.out, non_blocking=True)
+    def e2e_io(self):
+        return PipelinedIO([self.h_x], torch_empty_like(self.out),
+                           lambda d, out: self._run(d[0], out))
 
     def io_bytes(self):
         return self.h_x.numel() * 2, self.h_out.numel() * 2
@@ -503,18 +544,25 @@ def main() -> int:
     # no host sync and is replayed too (every rank in lockstep); the NCCL
     # transport reads its all-to-all split sizes on the host and runs eagerly.
     use_graph = not args.eager and (world == 1 or args.transport == "peer")
-    step_fn, e2e_fn = wl.step, wl.step_e2e
+    io = wl.e2e_io()
+    step_fn = wl.step
+    e2e_fns = [lambda: io.step(0), lambda: io.step(1)]
     if use_graph:
-        for _ in range(2):
-            wl.step_e2e()
+        io.load_first()
+        for i in range(2):
+            io.step(i)
         torch.cuda.synchronize()
         g_step = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_step):
             wl.step()
-        g_e2e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e2e):
-            wl.step_e2e()
-        step_fn, e2e_fn = g_step.replay, g_e2e.replay
+        g_e2e = []
+        for i in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                io.step(i)
+            g_e2e.append(g)
+        step_fn = g_step.replay
+        e2e_fns = [g.replay for g in g_e2e]
         for _ in range(args.warmup):
             step_fn()
         torch.cuda.synchronize()
@@ -536,15 +584,21 @@ def main() -> int:
     sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
 
-    # end-to-end: pinned host inputs in, result out, every step
-    for _ in range(3):
-        e2e_fn()
+    # end-to-end: pinned host inputs in, result out, every step (double
+    # buffered: copies of step i+1's inputs and step i-1's result overlap
+    # step i's kernels; the first inputs and the last result are copied inside
+    # the timed region too)
+    io.load_first()
+    for i in range(4):
+        e2e_fns[i % 2]()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start.record(stream)
-    for _ in range(args.steps):
-        e2e_fn()
+    io.load_first()
+    for i in range(args.steps):
+        e2e_fns[i % 2]()
+    io.drain((args.steps - 1) % 2)
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
