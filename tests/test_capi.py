@@ -103,3 +103,54 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_LIB", None)
     with pytest.raises(FileNotFoundError):
         _lib.load()
+
+
+def test_ep_validation_without_a_gpu():
+    """The expert-parallel entry points refuse bad arguments on the host,
+    before any device call (so this runs without a GPU)."""
+    import ctypes
+
+    from sglang_restomod_b200 import _lib
+
+    lib = _lib.load()
+    region = ctypes.create_string_buffer(4096 + 256)
+    base = ctypes.addressof(region)
+    aligned = ctypes.c_void_p((base + 255) // 256 * 256)
+    misaligned = ctypes.c_void_p((base + 255) // 256 * 256 + 8)
+    peers = (ctypes.c_uint64 * 8)()
+    x = (ctypes.c_uint16 * 1024)()
+    ids = (ctypes.c_int32 * 64)()
+    w = (ctypes.c_float * 64)()
+    # world too large, rank outside world, hidden not a multiple of 128
+    assert lib.b200_ep_dispatch(x, 0, 4, 256, ids, w, 4, 16, 0, 0, 65, peers, aligned, 8, None) == _lib.ERR_INVALID
+    assert lib.b200_ep_dispatch(x, 0, 4, 256, ids, w, 4, 16, 0, 2, 2, peers, aligned, 8, None) == _lib.ERR_INVALID
+    assert lib.b200_ep_dispatch(x, 0, 4, 100, ids, w, 4, 16, 0, 0, 2, peers, aligned, 8, None) == _lib.ERR_INVALID
+    # more tokens than the region was sized for, experts not divisible by world
+    assert lib.b200_ep_dispatch(x, 0, 9, 256, ids, w, 4, 16, 0, 0, 2, peers, aligned, 8, None) == _lib.ERR_INVALID
+    assert lib.b200_ep_dispatch(x, 0, 4, 256, ids, w, 4, 15, 0, 0, 2, peers, aligned, 8, None) == _lib.ERR_INVALID
+    # region not 256-byte aligned, peer table missing
+    assert lib.b200_ep_dispatch(x, 0, 4, 256, ids, w, 4, 16, 0, 0, 2, peers, misaligned, 8, None) == _lib.ERR_INVALID
+    assert lib.b200_ep_dispatch(x, 0, 4, 256, ids, w, 4, 16, 0, 0, 2, None, aligned, 8, None) == _lib.ERR_INVALID
+    # unsupported activation dtype
+    assert lib.b200_ep_dispatch(x, 2, 4, 256, ids, w, 4, 16, 0, 0, 2, peers, aligned, 8, None) == _lib.ERR_UNSUPPORTED
+    # combine: tokens beyond max_tokens; expert forward: workspace too small
+    out = (ctypes.c_uint16 * 1024)()
+    assert lib.b200_ep_combine(9, 256, ids, 4, 16, 1.0, None, 0, out, 0, 2, aligned, 8, None) == _lib.ERR_INVALID
+    wq = (ctypes.c_uint8 * 16)()
+    assert lib.b200_ep_expert_forward(0, 256, 128, 8, wq, None, None, wq, None, None, 16, 0, 2,
+                                      peers, aligned, 8, 4, aligned, 16, None) == _lib.ERR_INVALID
+    assert "workspace" in lib.b200_last_error().decode()
+
+
+def test_ep_region_layout_sizes():
+    from sglang_restomod_b200 import ops
+
+    for world, tokens, k, h in [(1, 1, 1, 128), (2, 24, 4, 256), (8, 128, 9, 7168), (8, 4096, 8, 7168)]:
+        lay = ops.ep_region_layout(world, tokens, k, h)
+        assert lay["total"] == ops.ep_region_bytes(world, tokens, k, h)
+        slots = world * tokens * k
+        offs = [lay[n] for n in ("ids", "weights", "orig", "rows", "recv", "comb")]
+        assert all(o % 256 == 0 for o in offs) and offs == sorted(offs)
+        assert lay["recv"] - lay["rows"] >= 8 * slots
+        assert lay["comb"] - lay["recv"] >= 2 * slots * h
+        assert lay["total"] - lay["comb"] >= 2 * tokens * k * h

@@ -45,6 +45,8 @@ ALIGN_CASES = [
     (10, 1, 8),
     (81920, 512, 64),  # configuration 2 prefill: 8192 tokens x top-10
     (4096 * 8, 256, 64),
+    (3000, 1024, 16),  # the kernel's maximum expert count
+    (20000, 1024, 64),
     (777, 1024, 5),
 ]
 
@@ -473,3 +475,18 @@ def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
     want_o = oracle.moe_layer_ref(xc, ids.cpu(), w.cpu(), d13, d2, routed_scaling_factor=rsf,
                                   shared_out=shared)
     assert_close(got, want_o, what=f"fused shared vs oracle T={tokens}")
+
+
+def test_layer_empty_batch(cuda_device):
+    """Zero tokens: nothing launched, an empty output."""
+    from sglang_restomod_b200.layer import QuantMoELayer
+
+    shape = synth.MoEShape(hidden=256, inter=128, experts=8, top_k=2, shared_inter=128)
+    layer = QuantMoELayer.synthetic(shape, _lib.QUANT_FP8_BLOCK, cuda_device)
+    x = torch.empty(0, shape.hidden, dtype=torch.bfloat16, device=cuda_device)
+    ids = torch.empty(0, shape.top_k, dtype=torch.int32, device=cuda_device)
+    w = torch.empty(0, shape.top_k, dtype=torch.float32, device=cuda_device)
+    out = ops.moe_layer_forward(x, ids, w, quant=0, num_experts=shape.experts, inter=shape.inter,
+                                w13=layer.w13, w2=layer.w2, w13_scales=layer.w13_scales,
+                                w2_scales=layer.w2_scales)
+    assert out.shape == (0, shape.hidden)
