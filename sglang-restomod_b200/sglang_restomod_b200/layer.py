@@ -68,14 +68,21 @@ class SharedExpert:
         m > 32 on the tcgen05 GEMM and, when its items cannot fill the SMs,
         splits K and adds a finishing kernel (the rule of b200_linear)."""
         n = 1 if x_dtype == torch.bfloat16 else 0
+        sms = ops.num_sms()
         for rows_n, k in ((2 * self.inter, hidden), (hidden, self.inter)):
             n += 1
-            items = (m + 191) // 192 * (rows_n // 128)
-            sms = ops.num_sms()
-            if m >= 33 and items < sms and m * rows_n <= 2 * sms * 128 * 64:
-                want = (2 * sms + items - 1) // items
-                kpart = max(2, (k // 128 + want - 1) // want)
-                n += 1 if (k // 128 + kpart - 1) // kpart > 1 else 0
+            if m >= 33 and m * rows_n <= 2 * sms * 128 * 64:
+                kch = k // 128
+                items = (m + 191) // 192 * (rows_n // 128)
+                part_cost = 9.0 * m * rows_n * 4.0 / 16384.0 / sms
+                best, split = float((items + sms - 1) // sms * kch), False
+                for ks in range(2, min(16, kch) + 1):
+                    kpart = -(-kch // ks)
+                    parts = -(-kch // kpart)
+                    cost = (items * parts + sms - 1) // sms * kpart + part_cost * parts
+                    if cost < best * 0.97:
+                        best, split = cost, True
+                n += 1 if split else 0
         return n
 
 
