@@ -260,6 +260,27 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
                            int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
                            int64_t workspace_bytes, void* stream);
 
+/*
+ * b200_moe_layer_forward from router logits: the routing of b200_topk_route
+ * (written to topk_ids_out / topk_weights_out [tokens, top_k], which the
+ * caller keeps) followed by the layer. For up to 32 tokens the router and
+ * moe_align run as one kernel. Replaces the select_experts ->
+ * StandardTopKOutput -> quant method apply chain
+ * (quant/sm70_fp8_moe/check.py:106-114, method.py:239-309).
+ */
+int b200_moe_layer_forward_logits(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
+                                  int64_t hidden, int64_t inter, const void* router_logits,
+                                  int32_t logits_dtype, int32_t scoring, int32_t renormalize,
+                                  const float* correction_bias, int32_t top_k,
+                                  int32_t num_experts, int32_t* topk_ids_out,
+                                  float* topk_weights_out, const uint8_t* w13_packed,
+                                  const float* w13_scales, const float* w13_global,
+                                  const uint8_t* w2_packed, const float* w2_scales,
+                                  const float* w2_global, int32_t block_size,
+                                  float routed_scaling_factor, const void* shared_out,
+                                  int32_t shared_dtype, void* out, int32_t out_dtype,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ---------------------------------------- expert parallelism (peer memory) */
 
 /*

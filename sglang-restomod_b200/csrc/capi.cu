@@ -565,15 +565,27 @@ int64_t b200_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden, int64_t i
          + align_up(numel * hidden * 2);                                     // per-route down output
 }
 
-int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
-                           int64_t hidden, int64_t inter, const int32_t* topk_ids,
-                           const float* topk_weights, int32_t top_k, int32_t num_experts,
-                           const uint8_t* w13_packed, const float* w13_scales,
-                           const float* w13_global, const uint8_t* w2_packed,
-                           const float* w2_scales, const float* w2_global, int32_t block_size,
-                           float routed_scaling_factor, const void* shared_out,
-                           int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
-                           int64_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Routing from router logits (b200_moe_layer_forward_logits): the chosen
+// routes go to the caller's ids / weights buffers.
+struct RouterArgs {
+  const void* logits;
+  int32_t dtype, scoring, renormalize;
+  const float* bias;
+  int32_t* ids_out;
+  float* weights_out;
+};
+
+int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
+                  int64_t inter, const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
+                  int32_t num_experts, const uint8_t* w13_packed, const float* w13_scales,
+                  const float* w13_global, const uint8_t* w2_packed, const float* w2_scales,
+                  const float* w2_global, int32_t block_size, float routed_scaling_factor,
+                  const void* shared_out, int32_t shared_dtype, void* out, int32_t out_dtype,
+                  void* workspace, int64_t workspace_bytes, void* stream, const RouterArgs* router) {
   int rc = check_weight_shape(quant, 2 * inter, hidden, B200_GATED_FUSED);
   if (rc) return rc;
   rc = check_weight_shape(quant, hidden, inter, B200_GATED_NONE);
@@ -588,6 +600,10 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   if (!tc_block && block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64)
     return fail(B200_ERR_UNSUPPORTED,
                 "block_size must be 8, 16, 32, 64, 128 or 256, got %d", block_size);
+  if (router != nullptr) {
+    topk_ids = router->ids_out;
+    topk_weights = router->weights_out;
+  }
   if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
       w2_packed == nullptr || out == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
@@ -636,13 +652,36 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
   __half* routed = reinterpret_cast<__half*>(ws.scratch + used);
   used += align_up(numel * hidden * 2);
 
-  if (numel >= kAlignMultiMin && num_experts <= moe_align_max_experts()) {
+  if (router != nullptr && tokens <= 32 && numel < kAlignMultiMin) {
+    // Up to one token per warp: route and align in one launch. (Measured no
+    // faster than the two kernels, which programmatic dependent launch
+    // already overlaps; with more tokens the single CTA's routing is slower.)
+    rc = check_cuda(launch_route_align(router->logits, router->dtype, tokens, num_experts, top_k,
+                                       router->scoring, router->renormalize, router->bias,
+                                       router->ids_out, router->weights_out, block_size, sorted,
+                                       cap, eids, blocks, ntpp, st),
+                    "route + align launch");
+  } else if (numel >= kAlignMultiMin && num_experts <= moe_align_max_experts()) {
+    if (router != nullptr) {
+      rc = check_cuda(launch_topk_route(router->logits, router->dtype, tokens, num_experts, top_k,
+                                        router->scoring, router->renormalize, router->bias,
+                                        router->ids_out, router->weights_out, st),
+                      "router launch");
+      if (rc) return rc;
+    }
     // Many routes: the multi-CTA align, its per-segment histograms in the
     // routed-output buffer (written only later, by the down GEMM).
     rc = check_cuda(launch_moe_align_multi(topk_ids, numel, num_experts, block_size, sorted, cap,
                                            eids, blocks, ntpp, reinterpret_cast<int*>(routed), st),
                     "moe_align launch");
   } else {
+    if (router != nullptr) {
+      rc = check_cuda(launch_topk_route(router->logits, router->dtype, tokens, num_experts, top_k,
+                                        router->scoring, router->renormalize, router->bias,
+                                        router->ids_out, router->weights_out, st),
+                      "router launch");
+      if (rc) return rc;
+    }
     rc = b200_moe_align_block_size(topk_ids, numel, num_experts, block_size, sorted, cap, eids,
                                    blocks, ntpp, stream);
   }
@@ -717,6 +756,61 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
 
   return b200_moe_combine(routed, B200_DTYPE_F16, topk_ids, num_experts, tokens, top_k, hidden,
                           routed_scaling_factor, shared_out, shared_dtype, out, out_dtype, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
+                           int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                           const float* topk_weights, int32_t top_k, int32_t num_experts,
+                           const uint8_t* w13_packed, const float* w13_scales,
+                           const float* w13_global, const uint8_t* w2_packed,
+                           const float* w2_scales, const float* w2_global, int32_t block_size,
+                           float routed_scaling_factor, const void* shared_out,
+                           int32_t shared_dtype, void* out, int32_t out_dtype, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  return layer_forward(quant, x, x_dtype, tokens, hidden, inter, topk_ids, topk_weights, top_k,
+                       num_experts, w13_packed, w13_scales, w13_global, w2_packed, w2_scales,
+                       w2_global, block_size, routed_scaling_factor, shared_out, shared_dtype, out,
+                       out_dtype, workspace, workspace_bytes, stream, nullptr);
+}
+
+int b200_moe_layer_forward_logits(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
+                                  int64_t hidden, int64_t inter, const void* router_logits,
+                                  int32_t logits_dtype, int32_t scoring, int32_t renormalize,
+                                  const float* correction_bias, int32_t top_k,
+                                  int32_t num_experts, int32_t* topk_ids_out,
+                                  float* topk_weights_out, const uint8_t* w13_packed,
+                                  const float* w13_scales, const float* w13_global,
+                                  const uint8_t* w2_packed, const float* w2_scales,
+                                  const float* w2_global, int32_t block_size,
+                                  float routed_scaling_factor, const void* shared_out,
+                                  int32_t shared_dtype, void* out, int32_t out_dtype,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  if (logits_dtype != B200_DTYPE_BF16 && logits_dtype != B200_DTYPE_F16 &&
+      logits_dtype != B200_DTYPE_F32)
+    return fail(B200_ERR_UNSUPPORTED, "router logits must be bf16, f16 or f32");
+  if (num_experts <= 0 || num_experts > router_max_experts() ||
+      num_experts > moe_align_max_experts())
+    return fail(B200_ERR_UNSUPPORTED, "num_experts must be in [1, %d], got %d",
+                router_max_experts(), num_experts);
+  if (top_k <= 0 || top_k > 32 || top_k > num_experts)
+    return fail(B200_ERR_INVALID, "top_k must be in [1, min(32, num_experts)], got %d", top_k);
+  if (scoring != B200_SCORING_SOFTMAX && scoring != B200_SCORING_SIGMOID)
+    return fail(B200_ERR_INVALID, "unknown scoring %d", scoring);
+  if (correction_bias != nullptr && scoring != B200_SCORING_SIGMOID)
+    return fail(B200_ERR_INVALID, "a correction bias needs sigmoid scoring");
+  if (tokens > 0 && (router_logits == nullptr || topk_ids_out == nullptr ||
+                     topk_weights_out == nullptr))
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  const RouterArgs r{router_logits, logits_dtype, scoring, renormalize != 0, correction_bias,
+                     topk_ids_out, topk_weights_out};
+  return layer_forward(quant, x, x_dtype, tokens, hidden, inter, nullptr, nullptr, top_k,
+                       num_experts, w13_packed, w13_scales, w13_global, w2_packed, w2_scales,
+                       w2_global, block_size, routed_scaling_factor, shared_out, shared_dtype, out,
+                       out_dtype, workspace, workspace_bytes, stream, &r);
 }
 
 }  // extern "C"

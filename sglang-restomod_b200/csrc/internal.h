@@ -84,6 +84,13 @@ cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_exper
                              int* sorted_ids, long long sorted_cap, int* expert_ids,
                              long long expert_cap, int* ntpp, cudaStream_t stream);
 int moe_align_max_experts();
+// Router top-k and single-CTA align in one launch (decode-size batches):
+// writes topk_ids / topk_w and the moe_align outputs.
+cudaError_t launch_route_align(const void* logits, int dtype, long long tokens, int E, int top_k,
+                               int scoring, int renormalize, const float* bias, int* topk_ids,
+                               float* topk_w, int bs, int* sorted_ids, long long sorted_cap,
+                               int* expert_ids, long long expert_cap, int* ntpp,
+                               cudaStream_t stream);
 // Multi-CTA variant (same output) for large route counts; `scratch` holds
 // moe_align_scratch_ints(numel, E) ints.
 long long moe_align_scratch_ints(long long numel, int num_experts);

@@ -25,6 +25,7 @@
 //      offset + (earlier warps' count) + (rank among equal ids so far).
 #include "common.cuh"
 #include "internal.h"
+#include "route_topk.cuh"
 
 namespace b200 {
 namespace {
@@ -34,11 +35,22 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxExperts = 1024;
 constexpr int kBatch = 8;  // loads in flight per lane
 
-__global__ void __launch_bounds__(kThreads, 1)
-    moe_align_kernel(const int* __restrict__ topk_ids, long long numel, int E, int bs,
-                     int* __restrict__ sorted_ids, long long sorted_cap,
-                     int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
-  extern __shared__ int sm[];
+// Route ids as written by an earlier kernel (read-only path) or by this
+// kernel's own threads before a block barrier (plain coherent loads).
+template <bool kReadOnly>
+__device__ __forceinline__ int load_id(const int* p) {
+  if constexpr (kReadOnly) return __ldg(p);
+  return *p;
+}
+
+// The single-CTA align (steps 1-3 above) on `sm` (kWarps * E + 2 * E + 1 +
+// kWarps ints). The caller zeroes the per-warp counts sm[0, kWarps * E)
+// and synchronises the block first.
+template <bool kReadOnly>
+__device__ __forceinline__ void align_cta(const int* __restrict__ topk_ids, long long numel, int E,
+                                          int bs, int* __restrict__ sorted_ids, long long sorted_cap,
+                                          int* __restrict__ expert_ids, long long expert_cap,
+                                          int* __restrict__ ntpp, int* sm) {
   int* cnt = sm;                  // [kWarps][E] per-warp counts, then running bases
   int* off = cnt + kWarps * E;    // [E + 1] first padded slot of each expert
   int* tot = off + E + 1;         // [E] routes per expert
@@ -47,10 +59,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  for (int i = tid; i < kWarps * E; i += kThreads) cnt[i] = 0;
-  griddep_wait();  // topk_ids may come from the previous kernel
-  if (tid == 0) griddep_launch_dependents();
-  __syncthreads();
 
   const long long seg = (numel + kWarps - 1) / kWarps;
   const long long s0 = (long long)warp * seg;
@@ -62,7 +70,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const long long idx = base + b * 32 + lane;
-      ids[b] = (idx < s1) ? __ldg(topk_ids + idx) : -1;
+      ids[b] = (idx < s1) ? load_id<kReadOnly>(topk_ids + idx) : -1;
     }
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
@@ -141,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const long long idx = base + b * 32 + lane;
-      ids[b] = (idx < s1) ? __ldg(topk_ids + idx) : -1;
+      ids[b] = (idx < s1) ? load_id<kReadOnly>(topk_ids + idx) : -1;
     }
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
@@ -159,6 +167,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_align_kernel(const int* __restrict__ topk_ids, long long numel, int E, int bs,
+                     int* __restrict__ sorted_ids, long long sorted_cap,
+                     int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
+  extern __shared__ int sm[];
+  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
+  griddep_wait();  // topk_ids may come from the previous kernel
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  __syncthreads();
+  align_cta<true>(topk_ids, numel, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap, ntpp, sm);
+}
+
+// Router + align in one launch (decode batches): each warp routes tokens
+// warp, warp + 32, ... (route::route_token, the router kernel's code), then
+// the block aligns the ids it just wrote.
+template <int PER>
+__global__ void __launch_bounds__(kThreads, 1) route_align_kernel(
+    const void* __restrict__ logits, int dtype, long long tokens, int E, int top_k, int scoring,
+    int renormalize, const float* __restrict__ bias, int* __restrict__ topk_ids,
+    float* __restrict__ topk_w, int bs, int* __restrict__ sorted_ids, long long sorted_cap,
+    int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
+  extern __shared__ int sm[];
+  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  for (long long t = threadIdx.x >> 5; t < tokens; t += kWarps)
+    route::route_token<PER>(logits, dtype, t, E, top_k, scoring, renormalize, bias, topk_ids,
+                            topk_w);
+  __syncthreads();
+  align_cta<false>(topk_ids, tokens * top_k, E, bs, sorted_ids, sorted_cap, expert_ids,
+                   expert_cap, ntpp, sm);
 }
 
 // ------------------------------------------------------------ multi-CTA
@@ -357,6 +398,51 @@ cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num
   return launch_pdl(align_scatter_kernel, dim3(segments), dim3(kSegThreads),
                     sizeof(int) * kSegWarps * E, stream, topk_ids, numel, E,
                     (const int*)scratch, segments, sorted_ids, sorted_cap);
+}
+
+namespace {
+
+template <int PER>
+cudaError_t launch_route_align_t(const void* logits, int dtype, long long tokens, int E, int top_k,
+                                 int scoring, int renormalize, const float* bias, int* topk_ids,
+                                 float* topk_w, int bs, int* sorted_ids, long long sorted_cap,
+                                 int* expert_ids, long long expert_cap, int* ntpp,
+                                 cudaStream_t stream) {
+  const size_t smem = sizeof(int) * ((size_t)kWarps * E + 2 * E + 1 + kWarps);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const int max_smem = (int)(sizeof(int) * ((size_t)kWarps * kMaxExperts + 2 * kMaxExperts + 1 + kWarps));
+    cudaError_t err = cudaFuncSetAttribute(route_align_kernel<PER>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
+  return launch_pdl(route_align_kernel<PER>, dim3(1), dim3(kThreads), smem, stream, logits, dtype,
+                    tokens, E, top_k, scoring, renormalize, bias, topk_ids, topk_w, bs, sorted_ids,
+                    sorted_cap, expert_ids, expert_cap, ntpp);
+}
+
+}  // namespace
+
+cudaError_t launch_route_align(const void* logits, int dtype, long long tokens, int E, int top_k,
+                               int scoring, int renormalize, const float* bias, int* topk_ids,
+                               float* topk_w, int bs, int* sorted_ids, long long sorted_cap,
+                               int* expert_ids, long long expert_cap, int* ntpp,
+                               cudaStream_t stream) {
+  const int per = (E + 31) / 32;
+#define B200_ROUTE_ALIGN(P)                                                                    \
+  return launch_route_align_t<P>(logits, dtype, tokens, E, top_k, scoring, renormalize, bias,  \
+                                 topk_ids, topk_w, bs, sorted_ids, sorted_cap, expert_ids,     \
+                                 expert_cap, ntpp, stream)
+  if (per <= 1) B200_ROUTE_ALIGN(1);
+  if (per <= 4) B200_ROUTE_ALIGN(4);
+  if (per <= 8) B200_ROUTE_ALIGN(8);
+  if (per <= 16) B200_ROUTE_ALIGN(16);
+  B200_ROUTE_ALIGN(32);
+#undef B200_ROUTE_ALIGN
 }
 
 cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_experts, int block_size,

@@ -171,7 +171,21 @@ class QuantMoELayer:
     def forward_logits(self, x, router_logits, out=None, scoring: int = _lib.SCORING_SOFTMAX,
                        renormalize: bool = True, correction_bias=None):
         """Route with the library's top-k kernel, then forward (the routing of
-        the benchmark: softmax -> top-k -> renormalise)."""
+        the benchmark: softmax -> top-k -> renormalise). Without a fused
+        shared expert this is one library call, whose router and moe_align
+        share a launch for decode batches."""
+        tokens = x.shape[0]
+        if self.fused_block_size(tokens) is None:
+            shared_out = self.shared.forward(x) if self.shared is not None else None
+            bs = self.block_size or block_size_for(tokens * self.top_k, self.num_experts)
+            y, _, _ = ops.moe_layer_forward_logits(
+                x, router_logits, self.top_k, quant=self.quant, num_experts=self.num_experts,
+                inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
+                w2_scales=self.w2_scales, w13_global=self.w13_global, w2_global=self.w2_global,
+                block_size=bs, routed_scaling_factor=self.routed_scaling_factor,
+                shared_out=shared_out, scoring=scoring, renormalize=renormalize,
+                correction_bias=correction_bias, out=out)
+            return y
         ids, w = ops.topk_route(router_logits, self.top_k, scoring=scoring,
                                 renormalize=renormalize, correction_bias=correction_bias)
         return self.forward(x, ids, w, out=out)

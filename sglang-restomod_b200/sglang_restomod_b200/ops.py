@@ -358,6 +358,47 @@ def moe_layer_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: tor
     return out
 
 
+def moe_layer_forward_logits(x: torch.Tensor, router_logits: torch.Tensor, top_k: int, *,
+                             quant: int, num_experts: int, inter: int, w13: torch.Tensor,
+                             w2: torch.Tensor, w13_scales=None, w2_scales=None, w13_global=None,
+                             w2_global=None, block_size: int = 16,
+                             routed_scaling_factor: float = 1.0,
+                             shared_out: torch.Tensor | None = None,
+                             scoring: int = _lib.SCORING_SOFTMAX, renormalize: bool = True,
+                             correction_bias: torch.Tensor | None = None,
+                             out: torch.Tensor | None = None):
+    """Router top-k + layer in one library call: (out, topk_ids, topk_weights)."""
+    _contig(x, "x")
+    _contig(router_logits, "router_logits")
+    try:
+        lcode = _LOGIT_CODE[router_logits.dtype]
+    except KeyError:
+        raise TypeError(f"router_logits must be bf16, f16 or f32, got {router_logits.dtype}") from None
+    tokens, hidden = (int(d) for d in x.shape)
+    if correction_bias is not None:
+        _contig(correction_bias, "correction_bias")
+    ids = torch.empty(tokens, top_k, dtype=torch.int32, device=x.device)
+    w = torch.empty(tokens, top_k, dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty(tokens, hidden, dtype=x.dtype, device=x.device)
+    if shared_out is not None:
+        _contig(shared_out, "shared_out")
+    ws = workspace(
+        moe_layer_workspace_bytes(tokens, hidden, inter, num_experts, top_k, block_size), x.device
+    )
+    _lib.check(
+        lib().b200_moe_layer_forward_logits(
+            quant, _vp(x), _code(x, "x"), tokens, hidden, inter, _vp(router_logits), lcode,
+            scoring, int(renormalize), _vp(correction_bias), top_k, num_experts, _vp(ids), _vp(w),
+            _vp(w13), _vp(w13_scales), _vp(w13_global), _vp(w2), _vp(w2_scales), _vp(w2_global),
+            block_size, float(routed_scaling_factor), _vp(shared_out),
+            _code(shared_out, "shared_out") if shared_out is not None else 0, _vp(out),
+            _code(out, "out"), _vp(ws), ws.numel(), _stream(x.device),
+        )
+    )
+    return out, ids, w
+
+
 # ------------------------------------------------------ expert parallelism
 # Peer-memory exchange (b200_ep_*): see ep.PeerExchange for the set-up of the
 # per-rank regions and their mapping into every peer.

@@ -92,3 +92,32 @@ def test_routed_layer_from_logits(cuda_device):
 def test_empty_batch(cuda_device):
     ids, w = ops.topk_route(torch.empty(0, 16, device=cuda_device), 4)
     assert ids.shape == (0, 4) and w.shape == (0, 4)
+
+
+@pytest.mark.parametrize("tokens,experts,top_k,block", [(1, 16, 4, 8), (32, 512, 10, 16), (37, 64, 6, 16),
+                                                         (128, 256, 8, 16), (300, 512, 10, 64),
+                                                         (1000, 64, 8, 64)])
+def test_layer_forward_from_logits(cuda_device, tokens, experts, top_k, block):
+    """b200_moe_layer_forward_logits (router + align in one kernel up to 32
+    tokens, separate kernels above) gives the routes of b200_topk_route and
+    the output of the layer fed those routes."""
+    from sglang_restomod_b200 import synth
+    from tests.conftest import assert_close
+
+    shape = synth.MoEShape(hidden=256, inter=128, experts=experts, top_k=top_k)
+    q13, s13 = synth.fp8_bank(experts, 256, 256, cuda_device, 40)
+    q2, s2 = synth.fp8_bank(experts, 256, 128, cuda_device, 41)
+    bank = dict(w13=ops.fp8_prepack(q13, True), w2=ops.fp8_prepack(q2, False), w13_scales=s13,
+                w2_scales=s2)
+    x = synth.activations(tokens, 256, cuda_device, seed=tokens)
+    g = torch.Generator().manual_seed(tokens + experts)
+    logits = torch.randn(tokens, experts, generator=g).to(cuda_device)
+    out, ids, w = ops.moe_layer_forward_logits(x, logits, top_k, quant=0, num_experts=experts,
+                                               inter=128, block_size=block, **bank)
+    ref_ids, ref_w = ops.topk_route(logits, top_k)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ref_ids) and torch.equal(w, ref_w)
+    want = ops.moe_layer_forward(x, ref_ids, ref_w, quant=0, num_experts=experts, inter=128,
+                                 block_size=block, **bank)
+    assert_close(out, want, rtol=1e-3, atol=1e-3, what=f"from logits T={tokens}")
+    assert ops.workspace_status() == 0
