@@ -21,7 +21,6 @@ Replaces the same three upstream hooks as the reference
 from __future__ import annotations
 
 import logging
-import os
 
 from ... import attest
 from ..._common import is_b200, library_loadable, mode
