@@ -14,14 +14,16 @@
 //     bytes are ordered exactly as the consumer warps read them (prepack.cu).
 //     A unit is one FP8 scale block: 16 KiB of E4M3, or 8 KiB of E2M1 codes
 //     plus 1 KiB of E4M3 group scales.
-//   * A persistent grid splits the flattened (row-group, row-block, K-unit)
-//     space evenly across CTAs (stream-K). Each CTA runs one producer warp and
-//     8 consumer warps over a 4-stage shared-memory ring tracked by mbarriers.
-//     For every unit the producer issues one cp.async.bulk (TMA) of the weight
-//     unit (L2 evict-first), and its 32 lanes copy the group's activation rows
-//     (128-K slices) with 16-byte cp.async into a padded tile (row stride
-//     304 B, second half at +160 B: bank-conflict-free for the consumers'
-//     16-byte reads). Both kinds of copy complete on the stage's mbarrier.
+//   * A persistent grid splits the flattened (row-group, row-block, K-stage)
+//     space evenly across CTAs (stream-K); a stage is 1, 2 or 4 consecutive
+//     K-units of one pair. Each CTA runs one producer warp and 8 consumer
+//     warps over a shared-memory ring of up to 4 stages tracked by mbarriers.
+//     For every stage the producer issues one cp.async.bulk (TMA) of its
+//     weight units (contiguous in the prepacked bank; L2 evict-first), and
+//     its 32 lanes copy the group's activation rows (128-K slices) with
+//     16-byte cp.async into padded tiles (row stride 304 B, second half at
+//     +160 B: bank-conflict-free for the consumers' 16-byte reads). Both
+//     kinds of copy complete on the stage's mbarrier.
 //   * A consumer warp owns 16 weight rows of the unit. It converts its bytes
 //     with the hardware cvt.rn.f16x2.{e4m3x2,e2m1x2} instructions straight
 //     into m16n8k16 A fragments and multiplies them against f16 activation
@@ -57,6 +59,16 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 #ifndef B200_STREAM_DENSE_PREFETCH
 #define B200_STREAM_DENSE_PREFETCH 0
 #endif
+// K-units per pipeline stage (1, 2 or 4; fewer when two such stages would
+// not fit): consecutive K-units of a pair share one barrier wait, one unit
+// walk and one accumulate. Measured against one unit per stage: FP8 two
+// units 10 % faster (config4 decode); NVFP4 two units 10 %, four 17-20 %.
+#ifndef B200_STREAM_SUB_FP8
+#define B200_STREAM_SUB_FP8 2
+#endif
+#ifndef B200_STREAM_SUB_NVFP4
+#define B200_STREAM_SUB_NVFP4 4
+#endif
 
 constexpr int kSmemPerSm = 233472;  // 228 KiB of shared memory per SM
 constexpr int kSmemReserved = 1024; // per CTA, kept by the system
@@ -79,18 +91,36 @@ struct UnitBytes<kQuantNvfp4> {
   static constexpr uint32_t value = kFp4UnitBytes;
 };
 
-// Stage = one weight unit + its activation tile; as many stages as fit when
+template <int Q>
+struct SubUnits {
+  static constexpr int value = Q == kQuantFp8Block ? B200_STREAM_SUB_FP8 : B200_STREAM_SUB_NVFP4;
+  static_assert(value == 1 || value == 2 || value == 4, "1, 2 or 4 units per stage");
+};
+
+constexpr uint32_t stage_bytes(int sub, uint32_t w, uint32_t x) {
+  return (sub * (w + x) + 127) / 128 * 128;
+}
+
+// Stage = kSub consecutive weight units of one pair (contiguous, one bulk
+// copy) followed by their kSub activation tiles; as many stages as fit when
 // CtasPerSm<NT> CTAs share an SM, capped at B200_STREAM_MAX_STAGES.
 template <int Q, int NT>
 struct Layout {
   static constexpr uint32_t kW = UnitBytes<Q>::value;
   static constexpr uint32_t kX = 8 * NT * kRowStride;
-  static constexpr uint32_t kStage = (kW + kX + 127) / 128 * 128;
   static constexpr int kBudget = kSmemPerSm / CtasPerSm<NT>::value - kSmemReserved - 128;
+  static constexpr int kReq = SubUnits<Q>::value;
+  static constexpr int kSub =
+      kReq >= 4 && 2 * stage_bytes(4, kW, kX) <= (uint32_t)kBudget   ? 4
+      : kReq >= 2 && 2 * stage_bytes(2, kW, kX) <= (uint32_t)kBudget ? 2
+                                                                     : 1;
+  static constexpr uint32_t kXOff = kSub * kW;  // first activation tile
+  static constexpr uint32_t kStage = stage_bytes(kSub, kW, kX);
   static constexpr int kFit = kBudget / (int)kStage;
   static constexpr int kS = kFit > B200_STREAM_MAX_STAGES ? B200_STREAM_MAX_STAGES : kFit;
   static constexpr size_t kSmem = (size_t)kS * kStage + 2 * kS * sizeof(uint64_t) + 16;
   static_assert(kS >= 2, "stage does not fit");
+  static_assert(kXOff % 16 == 0 && kX % 16 == 0, "16-byte cp.async destinations");
 };
 
 __device__ __forceinline__ int chunk_pos(int j) { return j * 16 + (j >= 8 ? kHalf1 - 128 : 0); }
@@ -186,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   using L = Layout<Q, NT>;
   constexpr uint32_t UB = L::kW;
   constexpr int kRows = 8 * NT;
+  constexpr int kSub = L::kSub;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int kStages = L::kS;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * L::kStage);
@@ -196,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nrb = p.N / kUnitRows;
-  const int kch = p.K / kUnitK;
+  const int kch = p.K / kUnitK;            // K-units per (group, row block) pair
+  const int kcs = (kch + kSub - 1) / kSub;  // stages per pair; the last may hold fewer units
   const bool dense = p.sorted_ids == nullptr;
 
   if (threadIdx.x == 0) {
@@ -223,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     if (groups < 0) groups = 0;
     if (groups > p.max_groups) groups = p.max_groups;
   }
-  const long long U = groups * nrb * (long long)kch;
+  const long long U = groups * nrb * (long long)kcs;
   const long long G = gridDim.x;
   const long long u0 = (long long)blockIdx.x * U / G;
   const long long u1 = ((long long)blockIdx.x + 1) * U / G;
@@ -238,10 +270,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       // Dense units of one CTA are contiguous in memory: pull the first ones
       // into L2 while the previous kernel finishes.
       if (lane == 0) {
-        const long long pre = (u1 - u0) < 2 * kStages ? (u1 - u0) : 2 * kStages;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wq + u0 * (long long)UB),
-                     "r"((uint32_t)(pre * UB))
-                     : "memory");
+        // first K-unit of stage u0, and the units of its first 2 * kStages stages
+        const long long unit0 = (u0 / kcs) * kch + (u0 % kcs) * kSub;
+        const long long units = (long long)p.dense_m > 0 ? (long long)nrb * kch : 0;
+        long long pre = units - unit0;
+        if (pre > 2LL * kStages * kSub) pre = 2LL * kStages * kSub;
+        if (pre > 0)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.wq + unit0 * (long long)UB),
+                       "r"((uint32_t)(pre * UB))
+                       : "memory");
       }
       griddep_wait();
     }
@@ -257,9 +294,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     const int my_chunk0 = kRows >= 32 ? 0 : (lane % kLanesPerRow) * kChunks;
     const uint64_t pol_w = l2_policy_evict_first();
     const __half* rows[kRowsPerLane];
-    // (group, row block, K unit) of u0; advanced by counters, not divisions.
-    long long pair = u0 / kch;
-    int kc = (int)(u0 - pair * kch);
+    // (group, row block, stage of the pair) of u0; advanced by counters.
+    long long pair = u0 / kcs;
+    int kc = (int)(u0 - pair * kcs);
     long long gi = pair / nrb;
     int rb = (int)(pair - gi * nrb);
     bool new_pair = true;
@@ -267,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     int i = 0;
     for (long long u = u0; u < u1; ++u) {
       if (u != u0) {
-        if (++kc == kch) {
+        if (++kc == kcs) {
           kc = 0;
           new_pair = true;
           if (++rb == nrb) {
@@ -295,18 +332,26 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         if (!ok) break;
       }
       uint8_t* stage = smem + (size_t)s * L::kStage;
+      const int ku = kc * kSub;  // first K-unit of this stage
+      const int nsub = kch - ku < kSub ? kch - ku : kSub;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], UB);
-        const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + kc) * (long long)UB;
-        bulk_g2s(stage, src, UB, &full[s], pol_w);
+        mbar_arrive_expect_tx(&full[s], UB * (uint32_t)nsub);
+        const uint8_t* src = p.wq + (((long long)e * nrb + rb) * kch + ku) * (long long)UB;
+        bulk_g2s(stage, src, UB * (uint32_t)nsub, &full[s], pol_w);
       }
 #pragma unroll
       for (int r = 0; r < kRowsPerLane; ++r) {
         if (rows[r] != nullptr) {
-          const __half* src = rows[r] + (long long)kc * kUnitK + my_chunk0 * 8;
-          uint8_t* dst = stage + UB + (my_row0 + 32 * r) * kRowStride;
 #pragma unroll
-          for (int c = 0; c < kChunks; ++c) cp_async_16(dst + chunk_pos(my_chunk0 + c), src + c * 8);
+          for (int sub = 0; sub < kSub; ++sub) {
+            if (sub < nsub) {
+              const __half* src = rows[r] + (long long)(ku + sub) * kUnitK + my_chunk0 * 8;
+              uint8_t* dst = stage + L::kXOff + sub * L::kX + (my_row0 + 32 * r) * kRowStride;
+#pragma unroll
+              for (int c = 0; c < kChunks; ++c)
+                cp_async_16(dst + chunk_pos(my_chunk0 + c), src + c * 8);
+            }
+          }
         }
       }
       cp_async_arrive_noinc(&full[s]);
@@ -323,17 +368,18 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   const int cq = lane & 3;
   float acc[NT][4];
   bool valid[NT];
-  long long pair = u0 / kch;
-  int kc = (int)(u0 - pair * kch);
+  long long pair = u0 / kcs;
+  int kc = (int)(u0 - pair * kcs);
   long long gi = pair / nrb;
   int rb = (int)(pair - gi * nrb);
   bool new_pair = true;
   int e = 0;
   int i = 0;
+  float gs = 1.f;  // NVFP4 global scale of expert e
 
   for (long long u = u0; u < u1; ++u) {
     if (u != u0) {
-      if (++kc == kch) {
+      if (++kc == kcs) {
         kc = 0;
         new_pair = true;
         ++pair;
@@ -358,24 +404,11 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
         valid[nt] = slot_row<NT>(p, gi, nt * 8 + g8, dense) != nullptr;
       }
+      if constexpr (Q == kQuantNvfp4) gs = __ldg(p.gscale + e);
     }
 
-    float s_top = 1.f, s_bot = 1.f;
-    float gs = 1.f;
-    if constexpr (Q == kQuantFp8Block) {
-      const int nsr = p.N / kUnitRows;  // scale rows per expert
-      if (p.gated) {
-        const int half_rows = p.N / 2 / kUnitRows;
-        s_top = __ldg(p.wscale + ((long long)e * nsr + rb / 2) * kch + kc);
-        s_bot = __ldg(p.wscale + ((long long)e * nsr + half_rows + rb / 2) * kch + kc);
-      } else {
-        s_top = __ldg(p.wscale + ((long long)e * nsr + rb) * kch + kc);
-        s_bot = s_top;
-      }
-    } else {
-      gs = __ldg(p.gscale + e);
-    }
-
+    const int ku = kc * kSub;  // first K-unit of this stage
+    const int nsub = kch - ku < kSub ? kch - ku : kSub;
     const int s = i % kStages;
     const uint32_t parity = (uint32_t)((i / kStages) & 1);
     ++i;
@@ -386,138 +419,171 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     }
     if (ok) {
       const uint8_t* stage = smem + (size_t)s * L::kStage;
-      const uint8_t* xt = stage + UB + g8 * kRowStride;
-      auto load_b = [&](int nt, int q) -> uint4 {
-        if (!valid[nt]) return make_uint4(0u, 0u, 0u, 0u);
-        return ld_shared_u128(xt + nt * 8 * kRowStride + chunk_pos(4 * cq + q));
-      };
       // NT == 1 keeps two accumulators (even / odd K-steps) so the MMA
       // chain is half as long; wider tiles already interleave NT chains.
       constexpr int kChains = NT == 1 ? 2 : 1;
+      // Small tiles copy their activation fragments out and release the
+      // stage once the last unit's are read; wider tiles read them during
+      // the MMA loop.
+      constexpr bool kPre = NT <= B200_STREAM_PRELOAD_NT;
       float t[NT * kChains][4];
 #pragma unroll
       for (int c = 0; c < NT * kChains; ++c)
 #pragma unroll
         for (int r = 0; r < 4; ++r) t[c][r] = 0.f;
 
-      if constexpr (Q == kQuantFp8Block) {
-        uint4 wa[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          wa[q] = ld_shared_u128(stage + warp * 2048 + q * 512 + lane * 16);
-        // Small tiles copy their activation fragments out and release the
-        // stage at once; wider tiles read them during the MMA loop.
-        constexpr bool kPre = NT <= B200_STREAM_PRELOAD_NT;
-        uint4 bpre[kPre ? NT : 1][4];
-        if constexpr (kPre) {
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 b[NT];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (kPre)
-              b[nt] = bpre[nt][q];
-            else
-              b[nt] = load_b(nt, q);
+      for (int sub = 0; sub < kSub; ++sub) {
+        if (sub >= nsub) break;
+        const uint8_t* wunit = stage + sub * UB;
+        const uint8_t* xt = stage + L::kXOff + sub * L::kX + g8 * kRowStride;
+        auto load_b = [&](int nt, int q) -> uint4 {
+          if (!valid[nt]) return make_uint4(0u, 0u, 0u, 0u);
+          return ld_shared_u128(xt + nt * 8 * kRowStride + chunk_pos(4 * cq + q));
+        };
+        const bool last = sub == nsub - 1;
+
+        if constexpr (Q == kQuantFp8Block) {
+          float s_top, s_bot;
+          const int nsr = p.N / kUnitRows;  // scale rows per expert
+          if (p.gated) {
+            const int half_rows = p.N / 2 / kUnitRows;
+            s_top = __ldg(p.wscale + ((long long)e * nsr + rb / 2) * kch + ku + sub);
+            s_bot = __ldg(p.wscale + ((long long)e * nsr + half_rows + rb / 2) * kch + ku + sub);
+          } else {
+            s_top = __ldg(p.wscale + ((long long)e * nsr + rb) * kch + ku + sub);
+            s_bot = s_top;
           }
+          if (sub > 0) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t top = h ? wa[q].y : wa[q].x;
-            const uint32_t bot = h ? wa[q].w : wa[q].z;
-            uint32_t a[4];
-            a[0] = e4m3x2_to_f16x2((uint16_t)(top & 0xffffu));
-            a[1] = e4m3x2_to_f16x2((uint16_t)(bot & 0xffffu));
-            a[2] = e4m3x2_to_f16x2((uint16_t)(top >> 16));
-            a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
+            for (int c = 0; c < NT * kChains; ++c)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) t[c][r] = 0.f;
+          }
+          uint4 wa[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            wa[q] = ld_shared_u128(wunit + warp * 2048 + q * 512 + lane * 16);
+          uint4 bpre[kPre ? NT : 1][4];
+          if constexpr (kPre) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-              mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
-                        h ? b[nt].w : b[nt].y);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
+            if (last) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[s]);
+            }
           }
-        }
-        if constexpr (!kPre) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        if constexpr (kChains == 2) {
 #pragma unroll
-          for (int r = 0; r < 4; ++r) t[0][r] += t[1][r];
-        }
+          for (int q = 0; q < 4; ++q) {
+            uint4 b[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          acc[nt][0] = fmaf(s_top, t[nt][0], acc[nt][0]);
-          acc[nt][1] = fmaf(s_top, t[nt][1], acc[nt][1]);
-          acc[nt][2] = fmaf(s_bot, t[nt][2], acc[nt][2]);
-          acc[nt][3] = fmaf(s_bot, t[nt][3], acc[nt][3]);
-        }
-      } else {
-        const uint4 ct = ld_shared_u128(stage + warp * 1024 + lane * 32);
-        const uint4 cb = ld_shared_u128(stage + warp * 1024 + lane * 32 + 16);
-        const uint32_t sc = ld_shared_u32(stage + 8192 + warp * 128 + lane * 4);
-        // Small tiles copy their activation fragments out and release the
-        // stage at once; wider tiles read them during the MMA loop.
-        constexpr bool kPre = NT <= B200_STREAM_PRELOAD_NT;
-        uint4 bpre[kPre ? NT : 1][4];
-        if constexpr (kPre) {
+            for (int nt = 0; nt < NT; ++nt) {
+              if constexpr (kPre)
+                b[nt] = bpre[nt][q];
+              else
+                b[nt] = load_b(nt, q);
+            }
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t top = h ? wa[q].y : wa[q].x;
+              const uint32_t bot = h ? wa[q].w : wa[q].z;
+              uint32_t a[4];
+              a[0] = e4m3x2_to_f16x2((uint16_t)(top & 0xffffu));
+              a[1] = e4m3x2_to_f16x2((uint16_t)(bot & 0xffffu));
+              a[2] = e4m3x2_to_f16x2((uint16_t)(top >> 16));
+              a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        // Group scales: fp16_rne(float(e4m3) * global), the single rounding
-        // the reference applies (quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:40-45).
-        const uint32_t st2 = e4m3x2_to_f16x2((uint16_t)(sc & 0xffffu));
-        const uint32_t sb2 = e4m3x2_to_f16x2((uint16_t)(sc >> 16));
-        const __half2 st_h = *reinterpret_cast<const __half2*>(&st2);
-        const __half2 sb_h = *reinterpret_cast<const __half2*>(&sb2);
-        const uint32_t st[2] = {f16x2_splat(__low2float(st_h) * gs),
-                                f16x2_splat(__high2float(st_h) * gs)};
-        const uint32_t sb[2] = {f16x2_splat(__low2float(sb_h) * gs),
-                                f16x2_splat(__high2float(sb_h) * gs)};
-        const uint32_t ctw[4] = {ct.x, ct.y, ct.z, ct.w};
-        const uint32_t cbw[4] = {cb.x, cb.y, cb.z, cb.w};
+              for (int nt = 0; nt < NT; ++nt)
+                mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                          h ? b[nt].w : b[nt].y);
+            }
+          }
+          if constexpr (!kPre) {
+            if (last) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[s]);
+            }
+          }
+          if constexpr (kChains == 2) {
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          uint32_t wt[4], wb[4];
-          e2m1x8_to_f16x2x4(ctw[m], wt);
-          e2m1x8_to_f16x2x4(cbw[m], wb);
-          const uint32_t sct = st[m >> 1];
-          const uint32_t scb = sb[m >> 1];
-          uint4 b[NT];
+            for (int r = 0; r < 4; ++r) t[0][r] += t[1][r];
+          }
+          // block scales differ per unit: fold this unit's sums in now
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (kPre)
-              b[nt] = bpre[nt][m];
-            else
-              b[nt] = load_b(nt, m);
+            acc[nt][0] = fmaf(s_top, t[nt][0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_top, t[nt][1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_bot, t[nt][2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_bot, t[nt][3], acc[nt][3]);
           }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t a[4];
-            a[0] = hmul2_u32(wt[2 * h], sct);
-            a[1] = hmul2_u32(wb[2 * h], scb);
-            a[2] = hmul2_u32(wt[2 * h + 1], sct);
-            a[3] = hmul2_u32(wb[2 * h + 1], scb);
-            // k-step j = 2m + h uses activation chunk m, half h
+        } else {
+          const uint4 ct = ld_shared_u128(wunit + warp * 1024 + lane * 32);
+          const uint4 cb = ld_shared_u128(wunit + warp * 1024 + lane * 32 + 16);
+          const uint32_t sc = ld_shared_u32(wunit + 8192 + warp * 128 + lane * 4);
+          uint4 bpre[kPre ? NT : 1][4];
+          if constexpr (kPre) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-              mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
-                        h ? b[nt].w : b[nt].y);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) bpre[nt][q] = load_b(nt, q);
+            if (last) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[s]);
+            }
+          }
+          // Group scales: fp16_rne(float(e4m3) * global), the single rounding
+          // the reference applies (quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:40-45).
+          const uint32_t st2 = e4m3x2_to_f16x2((uint16_t)(sc & 0xffffu));
+          const uint32_t sb2 = e4m3x2_to_f16x2((uint16_t)(sc >> 16));
+          const __half2 st_h = *reinterpret_cast<const __half2*>(&st2);
+          const __half2 sb_h = *reinterpret_cast<const __half2*>(&sb2);
+          const uint32_t st[2] = {f16x2_splat(__low2float(st_h) * gs),
+                                  f16x2_splat(__high2float(st_h) * gs)};
+          const uint32_t sb[2] = {f16x2_splat(__low2float(sb_h) * gs),
+                                  f16x2_splat(__high2float(sb_h) * gs)};
+          const uint32_t ctw[4] = {ct.x, ct.y, ct.z, ct.w};
+          const uint32_t cbw[4] = {cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            uint32_t wt[4], wb[4];
+            e2m1x8_to_f16x2x4(ctw[m], wt);
+            e2m1x8_to_f16x2x4(cbw[m], wb);
+            const uint32_t sct = st[m >> 1];
+            const uint32_t scb = sb[m >> 1];
+            uint4 b[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if constexpr (kPre)
+                b[nt] = bpre[nt][m];
+              else
+                b[nt] = load_b(nt, m);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t a[4];
+              a[0] = hmul2_u32(wt[2 * h], sct);
+              a[1] = hmul2_u32(wb[2 * h], scb);
+              a[2] = hmul2_u32(wt[2 * h + 1], sct);
+              a[3] = hmul2_u32(wb[2 * h + 1], scb);
+              // k-step j = 2m + h uses activation chunk m, half h
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+                mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                          h ? b[nt].w : b[nt].y);
+            }
+          }
+          if constexpr (!kPre) {
+            if (last) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[s]);
+            }
           }
         }
-        if constexpr (!kPre) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-        }
+      }
+      if constexpr (Q == kQuantNvfp4) {
+        // group scales are already in the fragments: one accumulate per stage
         if constexpr (kChains == 2) {
 #pragma unroll
           for (int r = 0; r < 4; ++r) t[0][r] += t[1][r];
@@ -529,11 +595,11 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       }
     }
 
-    const bool pair_end = (kc == kch - 1) || (u == u1 - 1);
+    const bool pair_end = (kc == kcs - 1) || (u == u1 - 1);
     if (!pair_end) continue;
 
-    const long long pu0 = pair * kch;
-    const long long pu1 = pu0 + kch;
+    const long long pu0 = pair * kcs;
+    const long long pu1 = pu0 + kcs;
     if (pu0 >= u0 && pu1 <= u1) {
       if (*abort_flag == 0) store_pair<NT>(p, gi, rb, warp, lane, acc);
       continue;
@@ -556,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     named_bar_sync(1, kConsumerWarps * 32);
     if (warp == 0 && lane == 0) {
       const int old = atomicAdd(p.ws_cnt + slot, my_units);
-      *flag = (old + my_units == kch) ? 1 : 0;
+      *flag = (old + my_units == kcs) ? 1 : 0;
     }
     named_bar_sync(1, kConsumerWarps * 32);
     if (*flag != 0) {
