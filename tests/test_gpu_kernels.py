@@ -106,7 +106,7 @@ def test_moe_combine_skips_dropped_routes(cuda_device):
 
 # ----------------------------------------------------------- dense linear
 DENSE_SMALL = [(1, 256, 384), (4, 512, 256), (16, 384, 512), (64, 256, 256), (13, 1024, 640),
-               (100, 256, 384)]
+               (100, 256, 384), (2, 640, 256), (8, 128, 384)]
 
 
 @pytest.mark.parametrize("m,k,n", DENSE_SMALL)
@@ -164,7 +164,9 @@ def test_fp8_linear_lm_head_sampled(cuda_device):
     assert_close(y.cpu()[:, rows], want, what="lm_head")
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 256, 256), (8, 512, 384), (16, 1024, 256), (64, 256, 512)])
+# K = 384 and 640 leave a pipeline stage with fewer K-units than the others
+@pytest.mark.parametrize("m,k,n", [(1, 256, 256), (8, 512, 384), (16, 1024, 256), (64, 256, 512),
+                                   (4, 384, 256), (2, 640, 384), (16, 640, 128)])
 def test_nvfp4_linear(cuda_device, m, k, n):
     p, s, gs = synth.nvfp4_bank(1, n, k, cuda_device, seed=m + n)
     x = synth.activations(m, k, cuda_device, seed=7)
