@@ -261,6 +261,29 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
                            int64_t workspace_bytes, void* stream);
 
 /*
+ * b200_moe_layer_forward with the shared expert fused into the routed bank
+ * (upstream SGLang's always-on shared MLP beside the routed experts, which
+ * the reference runs as a separate dense layer): w13 / w2 hold
+ * num_experts + 1 experts, the last being the shared expert (its shapes and
+ * block-FP8 weights match the routed ones). Every token gets one more route,
+ * id num_experts, weight shared_route_weight (1 / routed_scaling_factor
+ * leaves the shared output unscaled), written with the caller's routes to
+ * topk_ids_out / topk_weights_out [tokens, top_k + 1] (distinct from the
+ * inputs). For up to 4095 extended routes the append, moe_align and the
+ * bf16 -> f16 activation conversion run as one kernel. Workspace:
+ * b200_moe_layer_workspace_bytes(tokens, hidden, inter, num_experts + 1,
+ * top_k + 1, block_size).
+ */
+int b200_moe_layer_forward_fused_shared(
+    int32_t quant, const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden, int64_t inter,
+    const int32_t* topk_ids, const float* topk_weights, int32_t top_k, int32_t num_experts,
+    float shared_route_weight, int32_t* topk_ids_out, float* topk_weights_out,
+    const uint8_t* w13_packed, const float* w13_scales, const float* w13_global,
+    const uint8_t* w2_packed, const float* w2_scales, const float* w2_global, int32_t block_size,
+    float routed_scaling_factor, void* out, int32_t out_dtype, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
+/*
  * b200_moe_layer_forward from router logits: the routing of b200_topk_route
  * (written to topk_ids_out / topk_weights_out [tokens, top_k], which the
  * caller keeps) followed by the layer. For up to 32 tokens the router and

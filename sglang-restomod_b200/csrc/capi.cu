@@ -579,13 +579,24 @@ struct RouterArgs {
   float* weights_out;
 };
 
+// The shared expert fused into the routed bank as its last expert
+// (b200_moe_layer_forward_fused_shared): one more route per token, id
+// num_experts (the routed count), weight `weight`, written with the routed
+// ones to the caller's [tokens, top_k + 1] buffers.
+struct SharedRoute {
+  float weight;
+  int32_t* ids_out;
+  float* weights_out;
+};
+
 int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden,
                   int64_t inter, const int32_t* topk_ids, const float* topk_weights, int32_t top_k,
                   int32_t num_experts, const uint8_t* w13_packed, const float* w13_scales,
                   const float* w13_global, const uint8_t* w2_packed, const float* w2_scales,
                   const float* w2_global, int32_t block_size, float routed_scaling_factor,
                   const void* shared_out, int32_t shared_dtype, void* out, int32_t out_dtype,
-                  void* workspace, int64_t workspace_bytes, void* stream, const RouterArgs* router) {
+                  void* workspace, int64_t workspace_bytes, void* stream, const RouterArgs* router,
+                  const SharedRoute* shared_route = nullptr) {
   int rc = check_weight_shape(quant, 2 * inter, hidden, B200_GATED_FUSED);
   if (rc) return rc;
   rc = check_weight_shape(quant, hidden, inter, B200_GATED_NONE);
@@ -604,7 +615,21 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
     topk_ids = router->ids_out;
     topk_weights = router->weights_out;
   }
-  if (x == nullptr || topk_ids == nullptr || topk_weights == nullptr || w13_packed == nullptr ||
+  // The caller's routes; with a fused shared expert the layer runs on the
+  // extended routes (one more per token, one more expert).
+  const int32_t* in_ids = topk_ids;
+  const float* in_w = topk_weights;
+  const int32_t in_k = top_k;
+  if (shared_route != nullptr) {
+    if (router != nullptr) return fail(B200_ERR_INVALID, "router and shared route are exclusive");
+    if (shared_route->ids_out == nullptr || shared_route->weights_out == nullptr)
+      return fail(B200_ERR_INVALID, "null pointer argument");
+    topk_ids = shared_route->ids_out;
+    topk_weights = shared_route->weights_out;
+    top_k += 1;
+    num_experts += 1;
+  }
+  if (x == nullptr || in_ids == nullptr || in_w == nullptr || w13_packed == nullptr ||
       w2_packed == nullptr || out == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
   const int64_t need = b200_moe_layer_workspace_bytes(tokens, hidden, inter, num_experts, top_k,
@@ -624,6 +649,7 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
   const bool tc = use_tc_moe(quant, block_size, blocks);
   int64_t used = 0;
   const __half* x16 = nullptr;
+  __half* x16_conv = nullptr;  // bf16 activations converted for the stream GEMM
   __half* xs = nullptr;  // tcgen05: activations in slot order
   __half* inter_out = nullptr;
   if (tc) {
@@ -634,9 +660,15 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
     const int64_t stream_ops = align_up(tokens * hidden * 2) + align_up(numel * inter * 2);
     if (used < stream_ops) used = stream_ops;
   } else {
-    rc = stage_activations(x, x_dtype, tokens * hidden, ws, used, &x16, st);
-    if (rc) return rc;
-    if (x_dtype == B200_DTYPE_F16) used += align_up(tokens * hidden * 2);
+    // f16 operand of the weight-streaming GEMM: the caller's rows, or a
+    // converted copy written below (by the preparation kernel when it runs)
+    if (x_dtype == B200_DTYPE_F16) {
+      x16 = reinterpret_cast<const __half*>(x);
+    } else {
+      x16_conv = reinterpret_cast<__half*>(ws.scratch + used);
+      x16 = x16_conv;
+    }
+    used += align_up(tokens * hidden * 2);
     inter_out = reinterpret_cast<__half*>(ws.scratch + used);  // route order
     used += align_up(numel * inter * 2);
     const int64_t tc_ops =
@@ -652,6 +684,10 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
   __half* routed = reinterpret_cast<__half*>(ws.scratch + used);
   used += align_up(numel * hidden * 2);
 
+  if (num_experts > moe_align_max_experts())
+    return fail(B200_ERR_UNSUPPORTED, "num_experts must be in [1, %d], got %d",
+                moe_align_max_experts(), num_experts);
+  bool converted = x16_conv == nullptr;
   if (router != nullptr && tokens <= 32 && numel < kAlignMultiMin) {
     // Up to one token per warp: route and align in one launch. (Measured no
     // faster than the two kernels, which programmatic dependent launch
@@ -661,12 +697,19 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
                                        router->ids_out, router->weights_out, block_size, sorted,
                                        cap, eids, blocks, ntpp, st),
                     "route + align launch");
-  } else if (numel >= kAlignMultiMin && num_experts <= moe_align_max_experts()) {
+  } else if (numel >= kAlignMultiMin) {
     if (router != nullptr) {
       rc = check_cuda(launch_topk_route(router->logits, router->dtype, tokens, num_experts, top_k,
                                         router->scoring, router->renormalize, router->bias,
                                         router->ids_out, router->weights_out, st),
                       "router launch");
+      if (rc) return rc;
+    }
+    if (shared_route != nullptr) {
+      rc = check_cuda(launch_append_shared_route(in_ids, in_w, tokens, in_k, num_experts - 1,
+                                                 shared_route->weight, shared_route->ids_out,
+                                                 shared_route->weights_out, st),
+                      "append shared route launch");
       if (rc) return rc;
     }
     // Many routes: the multi-CTA align, its per-segment histograms in the
@@ -682,10 +725,24 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
                       "router launch");
       if (rc) return rc;
     }
-    rc = b200_moe_align_block_size(topk_ids, numel, num_experts, block_size, sorted, cap, eids,
-                                   blocks, ntpp, stream);
+    // Small batches: the shared-route append, the align and the activation
+    // conversion share one launch (each is a few microseconds of latency in
+    // a decode step's chain of dependent kernels).
+    rc = check_cuda(launch_moe_prep(in_ids, in_w, tokens, in_k, num_experts,
+                                    shared_route != nullptr ? 1 : 0,
+                                    shared_route != nullptr ? shared_route->weight : 0.f,
+                                    shared_route != nullptr ? shared_route->ids_out : nullptr,
+                                    shared_route != nullptr ? shared_route->weights_out : nullptr,
+                                    block_size, sorted, cap, eids, blocks, ntpp,
+                                    converted ? nullptr : x, x16_conv, tokens * hidden, st),
+                    "moe_prep launch");
+    converted = true;
   }
   if (rc) return rc;
+  if (!converted) {
+    rc = check_cuda(launch_bf16_to_f16(x, x16_conv, tokens * hidden, st), "bf16->f16 conversion");
+    if (rc) return rc;
+  }
   if (tc) {
     // One slot-ordered f16 copy of the routed rows (bf16 converted on the
     // way): the GEMM reads it as TMA tiles instead of gathering per route.
@@ -775,6 +832,26 @@ int b200_moe_layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_
                        num_experts, w13_packed, w13_scales, w13_global, w2_packed, w2_scales,
                        w2_global, block_size, routed_scaling_factor, shared_out, shared_dtype, out,
                        out_dtype, workspace, workspace_bytes, stream, nullptr);
+}
+
+int b200_moe_layer_forward_fused_shared(
+    int32_t quant, const void* x, int32_t x_dtype, int64_t tokens, int64_t hidden, int64_t inter,
+    const int32_t* topk_ids, const float* topk_weights, int32_t top_k, int32_t num_experts,
+    float shared_route_weight, int32_t* topk_ids_out, float* topk_weights_out,
+    const uint8_t* w13_packed, const float* w13_scales, const float* w13_global,
+    const uint8_t* w2_packed, const float* w2_scales, const float* w2_global, int32_t block_size,
+    float routed_scaling_factor, void* out, int32_t out_dtype, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  if (tokens > 0 && (topk_ids_out == nullptr || topk_weights_out == nullptr))
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (tokens > 0 && (topk_ids_out == topk_ids ||
+                     (const void*)topk_weights_out == (const void*)topk_weights))
+    return fail(B200_ERR_INVALID, "the extended routes must not overwrite the input routes");
+  const SharedRoute sr{shared_route_weight, topk_ids_out, topk_weights_out};
+  return layer_forward(quant, x, x_dtype, tokens, hidden, inter, topk_ids, topk_weights, top_k,
+                       num_experts, w13_packed, w13_scales, w13_global, w2_packed, w2_scales,
+                       w2_global, block_size, routed_scaling_factor, nullptr, x_dtype, out,
+                       out_dtype, workspace, workspace_bytes, stream, nullptr, &sr);
 }
 
 int b200_moe_layer_forward_logits(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,

@@ -185,6 +185,19 @@ __device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&out)[4]
       : "r"(w));
 }
 
+// Eight bf16 to eight f16, each rounded to nearest even.
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 raw) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+    __half2 h = __floats2half2_rn(__low2float(b), __high2float(b));
+    o[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);

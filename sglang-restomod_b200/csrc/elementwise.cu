@@ -56,18 +56,8 @@ __global__ void bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restri
                                    long long n8) {
   griddep_wait();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
-       i += (long long)gridDim.x * blockDim.x) {
-    const uint4 raw = in[i];
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
-      __half2 h = __floats2half2_rn(__low2float(b), __high2float(b));
-      o[j] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    out[i] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+       i += (long long)gridDim.x * blockDim.x)
+    out[i] = bf16x8_to_f16x8(in[i]);
   griddep_launch_dependents();
 }
 

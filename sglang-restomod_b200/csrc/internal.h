@@ -111,6 +111,14 @@ cudaError_t launch_append_shared_route(const int* ids, const float* w, long long
                                        int top_k, int shared_id, float shared_weight,
                                        int* ids_out, float* w_out, cudaStream_t stream);
 cudaError_t launch_bf16_to_f16(const void* in, void* out, long long n, cudaStream_t stream);
+// Shared-route append (optional), moe_align and the bf16 -> f16 activation
+// conversion (optional: conv_in == nullptr skips it) in one launch; the
+// single-CTA align, so for route counts the single-CTA path takes.
+cudaError_t launch_moe_prep(const int* topk_ids, const float* topk_w, long long tokens, int top_k,
+                            int num_experts, int shared, float shared_w, int* ids_out,
+                            float* w_out, int block_size, int* sorted_ids, long long sorted_cap,
+                            int* expert_ids, long long expert_cap, int* ntpp, const void* conv_in,
+                            void* conv_out, long long conv_elems, cudaStream_t stream);
 // out[s, :k] (f16) = x[sorted_ids[s] / top_k, :k] for the valid route slots
 // s < min(*ntpp, cap); padding slots are left as they are.
 cudaError_t launch_permute_rows(const void* x, int x_f16, long long ldx, long long x_rows,

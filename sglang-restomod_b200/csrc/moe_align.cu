@@ -202,6 +202,47 @@ __global__ void __launch_bounds__(kThreads, 1) route_align_kernel(
                    expert_cap, ntpp, sm);
 }
 
+// Everything a small batch needs before its GEMMs, in one launch. Block 0
+// optionally appends one shared-expert route per token (id E - 1, weight
+// shared_w; the extended routes go to ids_out / w_out, [tokens, top_k + 1])
+// and aligns the routes; blocks 1.. optionally convert the bf16 activations
+// to the f16 operand of the weight-streaming GEMM (n8 groups of 8).
+__global__ void __launch_bounds__(kThreads, 1) moe_prep_kernel(
+    const int* __restrict__ topk_ids, const float* __restrict__ topk_w, long long tokens,
+    int top_k, int E, int shared, float shared_w, int* __restrict__ ids_out,
+    float* __restrict__ w_out, int bs, int* __restrict__ sorted_ids, long long sorted_cap,
+    int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp,
+    const uint4* __restrict__ conv_in, uint4* __restrict__ conv_out, long long n8) {
+  extern __shared__ int sm[];
+  if (blockIdx.x > 0) {
+    griddep_wait();  // the activations may come from the previous kernel
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    const long long stride = (long long)(gridDim.x - 1) * kThreads;
+    for (long long i = (long long)(blockIdx.x - 1) * kThreads + threadIdx.x; i < n8; i += stride)
+      conv_out[i] = bf16x8_to_f16x8(conv_in[i]);
+    return;
+  }
+  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  if (shared) {
+    const int k1 = top_k + 1;
+    for (long long i = threadIdx.x; i < tokens * k1; i += kThreads) {
+      const long long t = i / k1;
+      const int j = (int)(i - t * k1);
+      ids_out[i] = j < top_k ? __ldg(topk_ids + t * top_k + j) : E - 1;
+      w_out[i] = j < top_k ? __ldg(topk_w + t * top_k + j) : shared_w;
+    }
+    __syncthreads();  // also publishes ids_out to the whole block
+    align_cta<false>(ids_out, tokens * k1, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap,
+                     ntpp, sm);
+  } else {
+    __syncthreads();
+    align_cta<true>(topk_ids, tokens * top_k, E, bs, sorted_ids, sorted_cap, expert_ids,
+                    expert_cap, ntpp, sm);
+  }
+}
+
 // ------------------------------------------------------------ multi-CTA
 // The same contract for large route counts, in three launches over
 // segments of kSeg routes (route order = segment order, so the result is
@@ -462,6 +503,33 @@ cudaError_t launch_moe_align(const int* topk_ids, long long numel, int num_exper
   }
   return launch_pdl(moe_align_kernel, dim3(1), dim3(kThreads), smem, stream, topk_ids, numel,
                     num_experts, block_size, sorted_ids, sorted_cap, expert_ids, expert_cap, ntpp);
+}
+
+cudaError_t launch_moe_prep(const int* topk_ids, const float* topk_w, long long tokens, int top_k,
+                            int num_experts, int shared, float shared_w, int* ids_out,
+                            float* w_out, int block_size, int* sorted_ids, long long sorted_cap,
+                            int* expert_ids, long long expert_cap, int* ntpp, const void* conv_in,
+                            void* conv_out, long long conv_elems, cudaStream_t stream) {
+  const size_t smem = sizeof(int) * ((size_t)kWarps * num_experts + 2 * num_experts + 1 + kWarps);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const int max_smem = (int)(sizeof(int) * ((size_t)kWarps * kMaxExperts + 2 * kMaxExperts + 1 + kWarps));
+    cudaError_t err = cudaFuncSetAttribute(moe_prep_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
+  const long long n8 = conv_in != nullptr ? conv_elems / 8 : 0;
+  long long conv_blocks = (n8 + kThreads - 1) / kThreads;
+  const long long cap = device_sm_count();
+  if (conv_blocks > cap) conv_blocks = cap;
+  return launch_pdl(moe_prep_kernel, dim3((unsigned)(1 + conv_blocks)), dim3(kThreads), smem,
+                    stream, topk_ids, topk_w, tokens, top_k, num_experts, shared, shared_w, ids_out,
+                    w_out, block_size, sorted_ids, sorted_cap, expert_ids, expert_cap, ntpp,
+                    static_cast<const uint4*>(conv_in), static_cast<uint4*>(conv_out), n8);
 }
 
 }  // namespace b200

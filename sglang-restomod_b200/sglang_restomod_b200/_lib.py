@@ -102,6 +102,12 @@ SIGNATURES = {
          c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_float,
          c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_int64, c_void_p],
     ),
+    "b200_moe_layer_forward_fused_shared": (
+        c_int32,
+        [c_int32, c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int32,
+         c_int32, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_int32, c_float, c_void_p, c_int32, c_void_p, c_int64, c_void_p],
+    ),
     "b200_moe_layer_forward_logits": (
         c_int32,
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p, c_int32, c_int32,

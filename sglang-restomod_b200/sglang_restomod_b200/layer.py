@@ -150,13 +150,14 @@ class QuantMoELayer:
         tokens, top_k = topk_ids.shape
         bs = self.fused_block_size(tokens, block_size) if use_shared and shared_out is None else None
         if bs is not None:
-            ids, w = self.fused_routes(topk_ids, topk_weights)
-            return ops.moe_layer_forward(
-                x, ids, w, quant=self.quant, num_experts=self.num_experts + 1,
+            # the shared route is appended inside the library call
+            y, _, _ = ops.moe_layer_forward_fused_shared(
+                x, topk_ids, topk_weights, quant=self.quant, num_experts=self.num_experts,
                 inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
                 w2_scales=self.w2_scales, block_size=bs,
                 routed_scaling_factor=self.routed_scaling_factor, out=out,
             )
+            return y
         if use_shared and shared_out is None and self.shared is not None:
             shared_out = self.shared.forward(x)
         bs = block_size or self.block_size or block_size_for(tokens * top_k, self.num_experts)
@@ -190,20 +191,34 @@ class QuantMoELayer:
                                 renormalize=renormalize, correction_bias=correction_bias)
         return self.forward(x, ids, w, out=out)
 
-    # launches of one forward on `tokens` rows: bf16->f16, align (3 kernels
-    # from 4096 routes on), [tcgen05 plan], gate/up, down, combine (+ shared)
     def launches_per_forward(self, x_dtype=torch.bfloat16, tokens: int | None = None) -> int:
-        n = 4 + (1 if x_dtype == torch.bfloat16 else 0)
-        if tokens is not None and self.fused_block_size(tokens) is not None:
+        """Kernels of one forward on ``tokens`` rows, following the library's
+        rules: up to 4095 routes one preparation kernel ([shared-route
+        append +] align [+ bf16 conversion]), from 4096 on the three-kernel
+        align with the append and the conversion as their own launches;
+        blocks of 64+ run the tcgen05 GEMMs, which add their plan and the
+        slot-order copy of the activations (instead of the conversion); then
+        gate/up, down and the combine, plus the separate shared MLP when the
+        shared expert is not fused into this forward."""
+        bf16 = x_dtype == torch.bfloat16
+        fused = tokens is not None and self.fused_block_size(tokens) is not None
+        if fused:
             routes = tokens * (self.top_k + 1)
-            # + the shared-route append and the tcgen05 plan; the shared expert
-            # runs inside the GEMMs
-            return n + 1 + (2 if routes >= 4096 else 0) + 1
-        if tokens is not None:
+            bs = self.fused_block_size(tokens)
+        elif tokens is not None:
             routes = tokens * self.top_k
             bs = self.block_size or block_size_for(routes, self.num_experts)
-            n += (2 if routes >= 4096 else 0) + (1 if bs >= 64 else 0)
-        if self.shared is not None:
+        else:
+            routes, bs = 0, self.block_size or 16
+        tc = bs >= 64
+        n = 3  # gate/up, down, combine
+        if routes >= 4096:
+            n += 3 + (1 if fused else 0) + (1 if bf16 and not tc else 0)
+        else:
+            n += 1
+        if tc:
+            n += 2
+        if not fused and self.shared is not None:
             n += (self.shared.launches(tokens, self.hidden, x_dtype) if tokens is not None
                   else SharedExpert.launches_per_forward)
         return n

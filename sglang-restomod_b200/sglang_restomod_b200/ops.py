@@ -358,6 +358,49 @@ def moe_layer_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: tor
     return out
 
 
+def moe_layer_forward_fused_shared(x: torch.Tensor, topk_ids: torch.Tensor,
+                                   topk_weights: torch.Tensor, *, quant: int, num_experts: int,
+                                   inter: int, w13: torch.Tensor, w2: torch.Tensor,
+                                   w13_scales: torch.Tensor | None = None,
+                                   w2_scales: torch.Tensor | None = None, block_size: int = 16,
+                                   routed_scaling_factor: float = 1.0,
+                                   shared_route_weight: float | None = None,
+                                   out: torch.Tensor | None = None):
+    """The layer with the shared expert as the banks' last expert (index
+    ``num_experts``, the routed count): one more route per token, appended
+    inside the call. Returns (out, extended ids, extended weights), the
+    routes [T, top_k + 1] the layer ran on."""
+    _contig(x, "x")
+    _contig(topk_ids, "topk_ids")
+    _contig(topk_weights, "topk_weights")
+    if topk_ids.dtype != torch.int32:
+        raise TypeError(f"topk_ids must be int32, got {topk_ids.dtype}")
+    if topk_weights.dtype != torch.float32:
+        raise TypeError(f"topk_weights must be float32, got {topk_weights.dtype}")
+    tokens, hidden = (int(d) for d in x.shape)
+    top_k = int(topk_ids.shape[1])
+    if shared_route_weight is None:
+        shared_route_weight = 1.0 / routed_scaling_factor
+    ids = torch.empty(tokens, top_k + 1, dtype=torch.int32, device=x.device)
+    w = torch.empty(tokens, top_k + 1, dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty(tokens, hidden, dtype=x.dtype, device=x.device)
+    ws = workspace(
+        moe_layer_workspace_bytes(tokens, hidden, inter, num_experts + 1, top_k + 1, block_size),
+        x.device,
+    )
+    _lib.check(
+        lib().b200_moe_layer_forward_fused_shared(
+            quant, _vp(x), _code(x, "x"), tokens, hidden, inter, _vp(topk_ids), _vp(topk_weights),
+            top_k, num_experts, float(shared_route_weight), _vp(ids), _vp(w), _vp(w13),
+            _vp(w13_scales), None, _vp(w2), _vp(w2_scales), None, block_size,
+            float(routed_scaling_factor), _vp(out), _code(out, "out"), _vp(ws), ws.numel(),
+            _stream(x.device),
+        )
+    )
+    return out, ids, w
+
+
 def moe_layer_forward_logits(x: torch.Tensor, router_logits: torch.Tensor, top_k: int, *,
                              quant: int, num_experts: int, inter: int, w13: torch.Tensor,
                              w2: torch.Tensor, w13_scales=None, w2_scales=None, w13_global=None,

@@ -89,6 +89,23 @@ def test_gemm_validation():
     assert st == _lib.ERR_INVALID and "workspace" in _err(st)
 
 
+def test_fused_shared_validation():
+    lib = _lib.load()
+    p, q, r = ctypes.c_void_p(256), ctypes.c_void_p(512), ctypes.c_void_p(1024)
+
+    def call(ids_out, w_out):
+        return lib.b200_moe_layer_forward_fused_shared(
+            0, p, 0, 4, 256, 128, p, q, 4, 16, 1.0, ids_out, w_out, p, p, None, p, p, None, 16,
+            1.0, p, 0, p, 1 << 30, None)
+
+    st = call(None, r)
+    assert st == _lib.ERR_INVALID and "null pointer" in _err(st)
+    st = call(p, r)  # extended ids would overwrite the input ids
+    assert st == _lib.ERR_INVALID and "overwrite" in _err(st)
+    st = call(r, q)  # extended weights would overwrite the input weights
+    assert st == _lib.ERR_INVALID and "overwrite" in _err(st)
+
+
 def test_sizes():
     lib = _lib.load()
     assert lib.b200_fp8_packed_bytes(3, 256, 512) == 3 * 256 * 512

@@ -438,7 +438,7 @@ def test_layer_config4_decode_bench_workload(cuda_device):
 
 # ------------------------------------------------ fused shared expert
 @pytest.mark.parametrize("tokens,block", [(1, None), (8, None), (1, 64), (16, 64), (128, 64),
-                                          (512, 64), (512, 128)])
+                                          (512, 64), (512, 128), (1024, 64)])
 @pytest.mark.parametrize("rsf", [1.0, 2.5])
 def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
     """Shared expert appended to the routed bank (one more route per token,
@@ -477,6 +477,38 @@ def test_fused_shared_expert_matches_separate(cuda_device, tokens, block, rsf):
     want_o = oracle.moe_layer_ref(xc, ids.cpu(), w.cpu(), d13, d2, routed_scaling_factor=rsf,
                                   shared_out=shared)
     assert_close(got, want_o, what=f"fused shared vs oracle T={tokens}")
+
+
+@pytest.mark.parametrize("tokens,block,x_dtype", [(3, 8, torch.bfloat16), (3, 8, torch.float16),
+                                                  (40, 64, torch.bfloat16), (900, 16, torch.bfloat16),
+                                                  (1024, 64, torch.float16)])
+def test_layer_forward_fused_shared_entry(cuda_device, tokens, block, x_dtype):
+    """b200_moe_layer_forward_fused_shared returns the caller's routes plus
+    (E, 1 / rsf) per token, and its output is bit-identical to
+    b200_moe_layer_forward on those routes over the E + 1 expert bank: up to
+    4095 routes through the one preparation kernel (append + align + bf16
+    conversion), from 4096 through the append and the multi-CTA align."""
+    from sglang_restomod_b200.layer import QuantMoELayer
+
+    shape = synth.MoEShape(hidden=256, inter=128, experts=16, top_k=4, shared_inter=128)
+    layer = QuantMoELayer.synthetic(shape, _lib.QUANT_FP8_BLOCK, cuda_device, fuse_shared=True)
+    assert layer.shared_fused
+    rsf = 2.5
+    x = synth.activations(tokens, shape.hidden, cuda_device, seed=3, dtype=x_dtype)
+    ids, w = synth.route(tokens, shape.experts, shape.top_k, cuda_device, seed=4)
+    ids[0, 1] = -1  # an expert-parallel drop stays dropped
+    kw = dict(quant=_lib.QUANT_FP8_BLOCK, inter=shape.inter, w13=layer.w13, w2=layer.w2,
+              w13_scales=layer.w13_scales, w2_scales=layer.w2_scales, block_size=block,
+              routed_scaling_factor=rsf)
+    out, ids2, w2 = ops.moe_layer_forward_fused_shared(x, ids, w, num_experts=shape.experts, **kw)
+    want_ids = torch.cat([ids, torch.full((tokens, 1), shape.experts, dtype=torch.int32,
+                                          device=cuda_device)], 1)
+    want_w = torch.cat([w, torch.full((tokens, 1), 1.0 / rsf, device=cuda_device)], 1)
+    ref = ops.moe_layer_forward(x, want_ids, want_w, num_experts=shape.experts + 1, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(ids2, want_ids) and torch.equal(w2, want_w)
+    assert torch.equal(out, ref)
+    assert ops.workspace_status() == 0
 
 
 def test_layer_empty_batch(cuda_device):
