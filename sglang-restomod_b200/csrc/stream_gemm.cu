@@ -63,6 +63,11 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 // not fit): consecutive K-units of a pair share one barrier wait, one unit
 // walk and one accumulate. Measured against one unit per stage: FP8 two
 // units 10 % faster (config4 decode); NVFP4 two units 10 %, four 17-20 %.
+// Pairs of at most this many stages are not split across CTAs when there
+// are no more pairs than CTAs (0: always split evenly, stream-K).
+#ifndef B200_STREAM_WHOLE_PAIR_MAX_STAGES
+#define B200_STREAM_WHOLE_PAIR_MAX_STAGES 8
+#endif
 #ifndef B200_STREAM_SUB_FP8
 #define B200_STREAM_SUB_FP8 2
 #endif
@@ -255,10 +260,20 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
     if (groups < 0) groups = 0;
     if (groups > p.max_groups) groups = p.max_groups;
   }
-  const long long U = groups * nrb * (long long)kcs;
+  const long long pairs = groups * nrb;
+  const long long U = pairs * (long long)kcs;
   const long long G = gridDim.x;
-  const long long u0 = (long long)blockIdx.x * U / G;
-  const long long u1 = ((long long)blockIdx.x + 1) * U / G;
+  long long u0, u1;
+  if (pairs <= G && kcs <= B200_STREAM_WHOLE_PAIR_MAX_STAGES) {
+    // Few, short pairs (small decode batches): one whole pair per CTA, so no
+    // pair is split and none pays the workspace reduction; the pairs' first
+    // stages alone keep enough bytes in flight.
+    u0 = blockIdx.x < pairs ? (long long)blockIdx.x * kcs : U;
+    u1 = blockIdx.x < pairs ? u0 + kcs : U;
+  } else {
+    u0 = (long long)blockIdx.x * U / G;
+    u1 = ((long long)blockIdx.x + 1) * U / G;
+  }
   if (u0 >= u1) {
     if (early_producer) griddep_wait();
     return;
