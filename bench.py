@@ -16,7 +16,10 @@ and config1-<K>x<N>-M<m> (dense FP8 GEMV).
 Inputs are seeded synthetic tensors (no dataset): activations N(0,1),
 router logits N(0,1) -> softmax -> top-k -> renormalised, weights N(0,0.02)
 quantized to block FP8 (or NVFP4). Weights read per step exceed the 126 MB
-L2 in every default workload, so no L2 flush is inserted.
+L2 in the default workload. A workload whose step reads less than L2 (one-
+token decode, configuration 0) is built several times over, each copy with
+its own weights, and the timed steps rotate over the copies, so a copy's
+weights are evicted from L2 before its next step (the config says how many).
 
 ``--impl reference`` times the reference's CPU torch arithmetic (the
 oracle port of sglang-restomod's dequantize-then-matmul MoE path) on the
@@ -33,6 +36,8 @@ import sys
 import threading
 import time
 from pathlib import Path
+
+L2_BYTES = 126 * 1000 * 1000  # B200 L2
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "sglang-restomod_b200"))
@@ -264,6 +269,33 @@ class MoEWorkload:
         self.h_out = torch.empty_like(self.h_x).pin_memory()
         self.d_out = torch.empty_like(self.x)
 
+    def replica(self):
+        """This workload on its own copy of the layer's weights (same inputs
+        and routing, own output buffers); single GPU."""
+        import copy
+
+        import torch
+
+        from sglang_restomod_b200.ep import ExpertParallelMoE
+
+        assert self.world == 1
+
+        def cloned(obj):
+            c = copy.copy(obj)
+            for k, v in vars(obj).items():
+                if isinstance(v, torch.Tensor) and v.is_cuda:
+                    setattr(c, k, v.clone())
+            return c
+
+        r = copy.copy(self)
+        r.layer = cloned(self.layer)
+        if self.layer.shared is not None:
+            r.layer.shared = cloned(self.layer.shared)
+        r.model = ExpertParallelMoE(r.layer, self.shape.experts, 0, 1)
+        r.out = torch.empty_like(self.out)
+        r.d_out = torch.empty_like(self.d_out)
+        return r
+
     def step(self):
         self.model.forward(self.x, self.ids, self.w, out=self.out)
 
@@ -394,7 +426,9 @@ class DenseWorkload:
         return wbytes + self.m * (self.k + self.n) * 2, 2 * self.m * self.n * self.k, 1
 
     def dominant(self):
-        return self.step, self.algorithmic()[0], "stream_gemm_kernel (dense)"
+        # b200_linear runs 33+ rows on the tcgen05 GEMM, fewer on the stream GEMM
+        name = "tc_gemm_kernel (dense)" if self.m >= 33 else "stream_gemm_kernel (dense)"
+        return self.step, self.algorithmic()[0], name
 
 
 # -------------------------------------------------------------- CPU legs
@@ -527,44 +561,59 @@ def main() -> int:
     spec = parse_workload(args.workload)
     spec["transport"] = args.transport
     spec["fuse_shared"] = not args.separate_shared
+
     if spec["kind"] == "dense":
         wl = DenseWorkload(spec, device)
-    elif spec["kind"] in ("ep", "moe"):
+    else:
         wl = MoEWorkload(spec, rank, world, device)
+    # Steps that read less than L2 rotate over copies of the workload (own
+    # weights, same routing), enough that the copies together read twice L2.
+    step_bytes = wl.algorithmic()[0]
+    copies = 1
+    if world == 1 and step_bytes < L2_BYTES and hasattr(wl, "replica"):
+        copies = int(min(16, max(4, -(-2 * L2_BYTES // step_bytes))))
+    wls = [wl] + [wl.replica() for _ in range(copies - 1)]
     torch.cuda.synchronize()
 
     from sglang_restomod_b200 import ops
 
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        wl.step()
+        for w in wls:
+            w.step()
     torch.cuda.synchronize()
     # One process per GPU replays the step as a CUDA graph, as a serving
     # engine does at decode. Under expert parallelism the peer transport has
     # no host sync and is replayed too (every rank in lockstep); the NCCL
     # transport reads its all-to-all split sizes on the host and runs eagerly.
     use_graph = not args.eager and (world == 1 or args.transport == "peer")
-    io = wl.e2e_io()
-    step_fn = wl.step
-    e2e_fns = [lambda: io.step(0), lambda: io.step(1)]
+    ios = [w.e2e_io() for w in wls]
+    step_fns = [w.step for w in wls]
+    e2e_fns = [[(lambda io=io, p=p: io.step(p)) for p in range(2)] for io in ios]
     if use_graph:
-        io.load_first()
-        for i in range(2):
-            io.step(i)
+        for io in ios:
+            io.load_first()
+            for i in range(2):
+                io.step(i)
         torch.cuda.synchronize()
-        g_step = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_step):
-            wl.step()
-        g_e2e = []
-        for i in range(2):
+        step_fns, e2e_fns, graphs = [], [], []
+        for w, io in zip(wls, ios):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                io.step(i)
-            g_e2e.append(g)
-        step_fn = g_step.replay
-        e2e_fns = [g.replay for g in g_e2e]
+                w.step()
+            graphs.append(g)
+            step_fns.append(g.replay)
+            pair = []
+            for i in range(2):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    io.step(i)
+                graphs.append(g)
+                pair.append(g.replay)
+            e2e_fns.append(pair)
         for _ in range(args.warmup):
-            step_fn()
+            for f in step_fns:
+                f()
         torch.cuda.synchronize()
 
     sampler = ClockSampler(device.index)
@@ -575,8 +624,8 @@ def main() -> int:
     end = torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("bench_timed")
     start.record(stream)
-    for _ in range(args.steps):
-        step_fn()
+    for i in range(args.steps):
+        step_fns[i % copies]()
     end.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -588,42 +637,51 @@ def main() -> int:
     # buffered: copies of step i+1's inputs and step i-1's result overlap
     # step i's kernels; the first inputs and the last result are copied inside
     # the timed region too)
-    io.load_first()
-    for i in range(4):
-        e2e_fns[i % 2]()
+    # (with copies, step i runs copy i % copies on its buffer (i // copies) % 2)
+    def e2e_run(steps):
+        for io in ios[:min(copies, steps)]:
+            io.load_first()
+        for i in range(steps):
+            e2e_fns[i % copies][(i // copies) % 2]()
+        for r in range(min(copies, steps)):
+            last = r + (steps - 1 - r) // copies * copies
+            ios[r].drain((last // copies) % 2)
+
+    e2e_run(4 * copies)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start.record(stream)
-    io.load_first()
-    for i in range(args.steps):
-        e2e_fns[i % 2]()
-    io.drain((args.steps - 1) % 2)
+    e2e_run(args.steps)
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(start.elapsed_time(end), world)
 
     # dominant kernel alone, CUDA events on its launch stream
-    dom = wl.dominant()
+    doms = [w.dominant() for w in wls]
     roofline = None
     hbm_gbs, bf16_tflops, peak_kind = measured_peaks()
-    if dom is not None:
-        run, dom_bytes, dom_name = dom
-        for _ in range(3):
-            run()
-        torch.cuda.synchronize()
-        if use_graph:
-            g_dom = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_dom):
+    if doms[0] is not None:
+        _, dom_bytes, dom_name = doms[0]
+        runs = []
+        for run, _, _ in doms:
+            for _ in range(3):
                 run()
-            run = g_dom.replay
-            run()
             torch.cuda.synchronize()
+            if use_graph:
+                g_dom = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g_dom):
+                    run()
+                graphs.append(g_dom)
+                run = g_dom.replay
+                run()
+                torch.cuda.synchronize()
+            runs.append(run)
         reps = max(args.steps, 20)
         start.record(stream)
-        for _ in range(reps):
-            run()
+        for i in range(reps):
+            runs[i % copies]()
         end.record(stream)
         torch.cuda.synchronize()
         dom_ms = start.elapsed_time(end) / reps
@@ -657,7 +715,12 @@ def main() -> int:
                         "sample": desc}
 
     if rank == 0:
-        config = {"workload": args.workload, "l2": "weights read per step exceed the 126 MB L2; no flush"}
+        if copies == 1:
+            l2_note = "weights read per step exceed the 126 MB L2; no flush"
+        else:
+            l2_note = (f"weights read per step ({step_bytes / 1e6:.1f} MB) fit the 126 MB L2: "
+                       f"{copies} copies of the layer's weights, rotated every step")
+        config = {"workload": args.workload, "l2": l2_note, "weight_copies": copies}
         if spec["kind"] != "dense":
             s = spec["shape"]
             config.update({"hidden": s.hidden, "inter": s.inter, "experts": s.experts,
