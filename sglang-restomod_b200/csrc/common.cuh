@@ -120,6 +120,13 @@ __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
                : "memory");
 }
 
+// 4-byte asynchronous global -> shared copy (through L1), tracked like
+// cp_async_16.
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
 // The barrier's expected count must include this arrival (noinc).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {

@@ -68,6 +68,11 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 #ifndef B200_STREAM_WHOLE_PAIR_MAX_STAGES
 #define B200_STREAM_WHOLE_PAIR_MAX_STAGES 8
 #endif
+// FP8 block scales of a stage copied into the stage by the producer (one
+// 4-byte cp.async per scale) instead of loaded by every consumer warp.
+#ifndef B200_STREAM_STAGE_SCALES
+#define B200_STREAM_STAGE_SCALES 1
+#endif
 #ifndef B200_STREAM_SUB_FP8
 #define B200_STREAM_SUB_FP8 2
 #endif
@@ -102,30 +107,39 @@ struct SubUnits {
   static_assert(value == 1 || value == 2 || value == 4, "1, 2 or 4 units per stage");
 };
 
-constexpr uint32_t stage_bytes(int sub, uint32_t w, uint32_t x) {
-  return (sub * (w + x) + 127) / 128 * 128;
+// FP8 stages end with their units' block scales: (top, bottom) per unit.
+template <int Q>
+struct StageScaleBytes {
+  static constexpr uint32_t value = Q == kQuantFp8Block && B200_STREAM_STAGE_SCALES ? 8 : 0;
+};
+
+constexpr uint32_t stage_bytes(int sub, uint32_t w, uint32_t x, uint32_t sc) {
+  return (sub * (w + x + sc) + 127) / 128 * 128;
 }
 
 // Stage = kSub consecutive weight units of one pair (contiguous, one bulk
-// copy) followed by their kSub activation tiles; as many stages as fit when
+// copy) followed by their kSub activation tiles (and, FP8, their block
+// scales); as many stages as fit when
 // CtasPerSm<NT> CTAs share an SM, capped at B200_STREAM_MAX_STAGES.
 template <int Q, int NT>
 struct Layout {
   static constexpr uint32_t kW = UnitBytes<Q>::value;
   static constexpr uint32_t kX = 8 * NT * kRowStride;
+  static constexpr uint32_t kSc = StageScaleBytes<Q>::value;
   static constexpr int kBudget = kSmemPerSm / CtasPerSm<NT>::value - kSmemReserved - 128;
   static constexpr int kReq = SubUnits<Q>::value;
   static constexpr int kSub =
-      kReq >= 4 && 2 * stage_bytes(4, kW, kX) <= (uint32_t)kBudget   ? 4
-      : kReq >= 2 && 2 * stage_bytes(2, kW, kX) <= (uint32_t)kBudget ? 2
-                                                                     : 1;
-  static constexpr uint32_t kXOff = kSub * kW;  // first activation tile
-  static constexpr uint32_t kStage = stage_bytes(kSub, kW, kX);
+      kReq >= 4 && 2 * stage_bytes(4, kW, kX, kSc) <= (uint32_t)kBudget   ? 4
+      : kReq >= 2 && 2 * stage_bytes(2, kW, kX, kSc) <= (uint32_t)kBudget ? 2
+                                                                           : 1;
+  static constexpr uint32_t kXOff = kSub * kW;             // first activation tile
+  static constexpr uint32_t kScOff = kSub * (kW + kX);     // block scales
+  static constexpr uint32_t kStage = stage_bytes(kSub, kW, kX, kSc);
   static constexpr int kFit = kBudget / (int)kStage;
   static constexpr int kS = kFit > B200_STREAM_MAX_STAGES ? B200_STREAM_MAX_STAGES : kFit;
   static constexpr size_t kSmem = (size_t)kS * kStage + 2 * kS * sizeof(uint64_t) + 16;
   static_assert(kS >= 2, "stage does not fit");
-  static_assert(kXOff % 16 == 0 && kX % 16 == 0, "16-byte cp.async destinations");
+  static_assert(kXOff % 16 == 0 && kX % 16 == 0 && kScOff % 8 == 0, "cp.async destinations");
 };
 
 __device__ __forceinline__ int chunk_pos(int j) { return j * 16 + (j >= 8 ? kHalf1 - 128 : 0); }
@@ -369,6 +383,17 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
           }
         }
       }
+      if constexpr (L::kSc != 0) {
+        if (lane == 31) {
+          const int nsr = p.N / kUnitRows;  // scale rows per expert
+          const long long top = p.gated ? (long long)e * nsr + rb / 2 : (long long)e * nsr + rb;
+          const long long bot = p.gated ? top + p.N / 2 / kUnitRows : top;
+          for (int sub = 0; sub < nsub; ++sub) {
+            cp_async_4(stage + L::kScOff + sub * 8, p.wscale + top * kch + ku + sub);
+            cp_async_4(stage + L::kScOff + sub * 8 + 4, p.wscale + bot * kch + ku + sub);
+          }
+        }
+      }
       cp_async_arrive_noinc(&full[s]);
       ++i;
     }
@@ -461,7 +486,10 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
         if constexpr (Q == kQuantFp8Block) {
           float s_top, s_bot;
           const int nsr = p.N / kUnitRows;  // scale rows per expert
-          if (p.gated) {
+          if constexpr (L::kSc != 0) {
+            s_top = __uint_as_float(ld_shared_u32(stage + L::kScOff + sub * 8));
+            s_bot = __uint_as_float(ld_shared_u32(stage + L::kScOff + sub * 8 + 4));
+          } else if (p.gated) {
             const int half_rows = p.N / 2 / kUnitRows;
             s_top = __ldg(p.wscale + ((long long)e * nsr + rb / 2) * kch + ku + sub);
             s_bot = __ldg(p.wscale + ((long long)e * nsr + half_rows + rb / 2) * kch + ku + sub);
