@@ -26,17 +26,24 @@ def block_size_for(routes: int, experts: int) -> int:
     usual per-expert route count; larger blocks waste tensor-core rows,
     which the decode regime can afford (it is HBM-bound).
 
-    The 16-slot tile stays the choice up to 12 routes per expert on average:
-    the 32-slot kernel streamed 3.7 TB/s against 5.35 TB/s for the 16-slot
-    one on the same 1024 routes over 128 experts (B200, block FP8, H=7168,
-    I=2048), although a few experts then take two groups. Above that, blocks
-    of 64 go to the tensor-core GEMM, which beat the 32-slot kernel at 20
-    routes per expert (0.61 against 0.74 ms for the 1024-token E=512 layer).
+    Measured on B200 (block FP8, H=7168, I=2048, 1024 routes spread evenly
+    over 256 / 128 / 64 / 32 experts, graph replay, ms per layer):
+
+    ============  =====  =====  =====  =====
+    routes/expert   4      8     16     32
+    blocks of 8   1.765  1.291  1.090  0.874
+    blocks of 16  1.843  0.994  0.729  0.639
+    blocks of 32  2.929  1.592  0.888  0.778
+    blocks of 64  2.941  1.563  0.806  0.443
+    ============  =====  =====  =====  =====
+
+    so 8-slot groups up to 5 routes per expert on average, 16-slot groups up
+    to 16, and above that blocks of 64 on the tensor-core GEMM.
     """
     avg = routes / max(experts, 1)
-    if 2.5 * avg <= 8:
+    if avg <= 5:
         return 8
-    if avg <= 12:
+    if avg <= 16:
         return 16
     return 64
 
