@@ -37,11 +37,14 @@ def block_size_for(routes: int, experts: int) -> int:
     blocks of 64  2.941  1.563  0.806  0.443
     ============  =====  =====  =====  =====
 
-    so 8-slot groups up to 5 routes per expert on average, 16-slot groups up
-    to 16, and above that blocks of 64 on the tensor-core GEMM.
+    and on the E=512 bank (H=2048, I=512, top-10; FP8 / NVFP4): 8 slots
+    0.300 / 0.262 against 16 slots 0.309 / 0.302 ms at 5 routes per expert,
+    0.377 / 0.328 against 0.331 / 0.329 ms at 7.5, so 8-slot groups up to 6
+    routes per expert on average, 16-slot groups up to 16, and above that
+    blocks of 64 on the tensor-core GEMM.
     """
     avg = routes / max(experts, 1)
-    if avg <= 5:
+    if avg <= 6:
         return 8
     if avg <= 16:
         return 16
