@@ -419,26 +419,32 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     p.out_f16 = y_dtype == B200_DTYPE_F16;
     // Items (192-row chunk x 128-row weight block) are dealt round-robin over
     // the SMs, each streaming its K range. Split K (parts summed in fp32 in
-    // the workspace, then a finishing kernel) when that lowers the busiest
-    // SM's 128-K unit count, each part charged for its m*n fp32 atomic adds:
-    // measured on B200 at ~9x the time of streaming the same bytes of weights
-    // (64 x 25600 x 5120: 64 us unsplit, 88 us in two parts).
+    // the workspace, then a finishing kernel) when that cuts the busiest SM's
+    // 128-K unit count by a quarter or more, each part charged for its m*n
+    // fp32 atomic adds at 3x the time of streaming the same bytes of weights.
+    // Measured on B200: a split that only evens out waves is slower
+    // (64 x 25600 x 5120: 64 us unsplit, 87 us in two parts), one that fills
+    // idle SMs is faster (128 x 4096 x 7168: 43 us in three parts, 35 us in
+    // four; 64 x 5120 x 25600: 64 us in three, 60 us in seven).
     p.ksplit = 1;
     const int64_t kch = k / 128, sms = device_sm_count();
     const int64_t items = (m + 191) / 192 * (n / 128);
     if (m * n <= (int64_t)max_grid_slots() * kWsSlotFloats) {
-      const double part_cost = 9.0 * (double)m * (double)n * 4.0 / 16384.0 / (double)sms;
-      double best = (double)((items + sms - 1) / sms * kch);
+      const double part_cost = 3.0 * (double)m * (double)n * 4.0 / 16384.0 / (double)sms;
+      const double whole = (double)((items + sms - 1) / sms * kch);
+      double best = whole;
+      int best_parts = 1;
       for (int64_t ks = 2; ks <= 16 && ks <= kch; ++ks) {
         const int64_t kpart = (kch + ks - 1) / ks;
         const int64_t parts = (kch + kpart - 1) / kpart;
         const double cost =
             (double)((items * parts + sms - 1) / sms * kpart) + part_cost * (double)parts;
-        if (cost < best * 0.97) {
+        if (cost < best) {
           best = cost;
-          p.ksplit = (int)parts;
+          best_parts = (int)parts;
         }
       }
+      if (best < 0.75 * whole) p.ksplit = best_parts;
     }
     rc = run_tc(quant, p, ws, false, st);
     if (rc || p.ksplit <= 1) return rc;

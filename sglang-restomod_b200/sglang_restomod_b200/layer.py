@@ -84,15 +84,14 @@ class SharedExpert:
             if m >= 33 and m * rows_n <= 2 * sms * 128 * 64:
                 kch = k // 128
                 items = (m + 191) // 192 * (rows_n // 128)
-                part_cost = 9.0 * m * rows_n * 4.0 / 16384.0 / sms
-                best, split = float((items + sms - 1) // sms * kch), False
+                part_cost = 3.0 * m * rows_n * 4.0 / 16384.0 / sms
+                whole = float((items + sms - 1) // sms * kch)
+                best = whole
                 for ks in range(2, min(16, kch) + 1):
                     kpart = -(-kch // ks)
                     parts = -(-kch // kpart)
-                    cost = (items * parts + sms - 1) // sms * kpart + part_cost * parts
-                    if cost < best * 0.97:
-                        best, split = cost, True
-                n += 1 if split else 0
+                    best = min(best, (items * parts + sms - 1) // sms * kpart + part_cost * parts)
+                n += 1 if best < 0.75 * whole else 0
         return n
 
 
