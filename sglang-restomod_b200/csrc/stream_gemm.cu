@@ -15,15 +15,18 @@
 //     A unit is one FP8 scale block: 16 KiB of E4M3, or 8 KiB of E2M1 codes
 //     plus 1 KiB of E4M3 group scales.
 //   * A persistent grid splits the flattened (row-group, row-block, K-stage)
-//     space evenly across CTAs (stream-K); a stage is 1, 2 or 4 consecutive
-//     K-units of one pair. Each CTA runs one producer warp and 8 consumer
+//     space evenly across CTAs (stream-K), or, when there are no more
+//     (row-group, row-block) pairs than CTAs and they are short, gives each
+//     CTA one whole pair; a stage is 1, 2 or 4 consecutive K-units of one
+//     pair. Each CTA runs one producer warp and 8 consumer
 //     warps over a shared-memory ring of up to 4 stages tracked by mbarriers.
 //     For every stage the producer issues one cp.async.bulk (TMA) of its
 //     weight units (contiguous in the prepacked bank; L2 evict-first), and
 //     its 32 lanes copy the group's activation rows (128-K slices) with
 //     16-byte cp.async into padded tiles (row stride 304 B, second half at
-//     +160 B: bank-conflict-free for the consumers' 16-byte reads). Both
-//     kinds of copy complete on the stage's mbarrier.
+//     +160 B: bank-conflict-free for the consumers' 16-byte reads); one lane
+//     copies the units' FP8 block scales (4-byte cp.async). All the copies
+//     complete on the stage's mbarrier.
 //   * A consumer warp owns 16 weight rows of the unit. It converts its bytes
 //     with the hardware cvt.rn.f16x2.{e4m3x2,e2m1x2} instructions straight
 //     into m16n8k16 A fragments and multiplies them against f16 activation
