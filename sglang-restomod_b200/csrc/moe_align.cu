@@ -43,6 +43,46 @@ __device__ __forceinline__ int load_id(const int* p) {
   return *p;
 }
 
+// The same result for at most 32 routes (decode steps of one to three
+// tokens) from one warp, without the shared-memory histogram: lane i holds
+// route i; equal experts are found with match_any, an expert's first slot is
+// the sum of the padded counts of the smaller experts present, and a route's
+// place inside its expert is its rank among the equal lanes below it. The
+// whole block first writes the sentinels and the -1 blocks, then warp 0 the
+// routes and the experts' blocks.
+template <bool kReadOnly>
+__device__ __forceinline__ void align_warp(const int* __restrict__ topk_ids, int numel, int E,
+                                           int bs, int* __restrict__ sorted_ids,
+                                           long long sorted_cap, int* __restrict__ expert_ids,
+                                           long long expert_cap, int* __restrict__ ntpp) {
+  const int tid = threadIdx.x;
+  for (long long p = tid; p < sorted_cap; p += kThreads) sorted_ids[p] = numel;
+  for (long long b = tid; b < expert_cap; b += kThreads) expert_ids[b] = -1;
+  __syncthreads();  // orders the fills before warp 0's writes (same block)
+  if (tid >= 32) return;
+  const int lane = tid;
+  const int e = lane < numel ? load_id<kReadOnly>(topk_ids + lane) : -1;
+  const bool valid = e >= 0 && e < E;
+  const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+  const bool leader = valid && lane == __ffs(peers) - 1;
+  const int pad = leader ? (__popc(peers) + bs - 1) / bs * bs : 0;
+  int off = 0, total = 0;
+#pragma unroll 4
+  for (int j = 0; j < 32; ++j) {
+    const int pj = __shfl_sync(0xffffffffu, pad, j);
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    total += pj;
+    if (pj > 0 && ej < e) off += pj;
+  }
+  if (valid) {
+    const long long pos = (long long)off + __popc(peers & ((1u << lane) - 1u));
+    if (pos < sorted_cap) sorted_ids[pos] = lane;
+  }
+  if (leader)
+    for (int b = off / bs; b < (off + pad) / bs && b < expert_cap; ++b) expert_ids[b] = e;
+  if (lane == 0) ntpp[0] = total;
+}
+
 // The single-CTA align (steps 1-3 above) on `sm` (kWarps * E + 2 * E + 1 +
 // kWarps ints). The caller zeroes the per-warp counts sm[0, kWarps * E)
 // and synchronises the block first.
@@ -174,6 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                      int* __restrict__ sorted_ids, long long sorted_cap,
                      int* __restrict__ expert_ids, long long expert_cap, int* __restrict__ ntpp) {
   extern __shared__ int sm[];
+  if (numel <= 32) {
+    griddep_wait();  // topk_ids may come from the previous kernel
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    align_warp<true>(topk_ids, (int)numel, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap,
+                     ntpp);
+    return;
+  }
   for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
   griddep_wait();  // topk_ids may come from the previous kernel
   if (threadIdx.x == 0) griddep_launch_dependents();
@@ -222,7 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prep_kernel(
       conv_out[i] = bf16x8_to_f16x8(conv_in[i]);
     return;
   }
-  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
+  const long long numel = tokens * (top_k + (shared ? 1 : 0));
+  if (numel > 32)
+    for (int i = threadIdx.x; i < kWarps * E; i += kThreads) sm[i] = 0;
   griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
   if (shared) {
@@ -234,12 +283,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prep_kernel(
       w_out[i] = j < top_k ? __ldg(topk_w + t * top_k + j) : shared_w;
     }
     __syncthreads();  // also publishes ids_out to the whole block
-    align_cta<false>(ids_out, tokens * k1, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap,
-                     ntpp, sm);
+    if (numel <= 32)
+      align_warp<false>(ids_out, (int)numel, E, bs, sorted_ids, sorted_cap, expert_ids,
+                        expert_cap, ntpp);
+    else
+      align_cta<false>(ids_out, numel, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap,
+                       ntpp, sm);
   } else {
     __syncthreads();
-    align_cta<true>(topk_ids, tokens * top_k, E, bs, sorted_ids, sorted_cap, expert_ids,
-                    expert_cap, ntpp, sm);
+    if (numel <= 32)
+      align_warp<true>(topk_ids, (int)numel, E, bs, sorted_ids, sorted_cap, expert_ids,
+                       expert_cap, ntpp);
+    else
+      align_cta<true>(topk_ids, numel, E, bs, sorted_ids, sorted_cap, expert_ids, expert_cap,
+                      ntpp, sm);
   }
 }
 

@@ -48,6 +48,14 @@ ALIGN_CASES = [
     (3000, 1024, 16),  # the kernel's maximum expert count
     (20000, 1024, 64),
     (777, 1024, 5),
+    # up to 32 routes: the one-warp align
+    (11, 513, 8),    # a one-token config2 step with the shared route
+    (32, 64, 16),
+    (24, 8, 64),
+    (32, 1024, 8),
+    (17, 3, 4),
+    (32, 2, 5),
+    (33, 16, 8),     # one past it
 ]
 
 
