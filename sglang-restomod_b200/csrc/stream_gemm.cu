@@ -269,6 +269,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   if (!early_producer) griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
 
+  // The producer reads the expert of group blockIdx.x / nrb together with the
+  // group count: when each CTA takes one whole pair (small batches) that is
+  // its first pair's expert, and its first weight copy then waits for one
+  // load instead of two in a row. (In bounds: expert_ids holds max_groups
+  // entries; the value is used only for a group below the aligned count.)
+  const long long gi_first = (long long)blockIdx.x / nrb;
+  int e_first = -1;
+  if (!dense && warp == kConsumerWarps && gi_first < p.max_groups) e_first = p.expert_ids[gi_first];
+
   long long groups;
   if (dense) {
     groups = (long long)(p.dense_m + kRows - 1) / kRows;
@@ -345,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
           }
         }
       }
-      if (new_pair) e = dense ? 0 : p.expert_ids[gi];
+      if (new_pair) e = dense ? 0 : (gi == gi_first ? e_first : p.expert_ids[gi]);
       if (e < 0 || e >= p.E) {
         new_pair = false;
         continue;
