@@ -419,7 +419,13 @@ class DenseWorkload:
         return self.h_x.numel() * 2, self.h_out.numel() * 2
 
     def launches_per_step(self):
-        return 2
+        """bf16 -> f16 conversion and the GEMM (stream GEMM up to 32 rows;
+        tcgen05 beyond, plus its finishing kernel when K is split)."""
+        from sglang_restomod_b200 import ops
+        from sglang_restomod_b200.layer import dense_k_parts
+
+        split = self.m >= 33 and dense_k_parts(self.m, self.n, self.k, ops.num_sms()) > 1
+        return 3 if split else 2
 
     def algorithmic(self):
         wbytes = self.n * self.k + (self.n // 128) * (self.k // 128) * 4

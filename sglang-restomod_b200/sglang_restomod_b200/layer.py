@@ -75,24 +75,38 @@ class SharedExpert:
 
     def launches(self, m: int, hidden: int, x_dtype=torch.bfloat16) -> int:
         """Kernels of one forward on m rows: the library's dense linear runs
-        m > 32 on the tcgen05 GEMM and, when its items cannot fill the SMs,
-        splits K and adds a finishing kernel (the rule of b200_linear)."""
+        m > 32 on the tcgen05 GEMM and, when splitting K pays, adds a
+        finishing kernel (the rule of b200_linear, `dense_k_parts`)."""
         n = 1 if x_dtype == torch.bfloat16 else 0
         sms = ops.num_sms()
         for rows_n, k in ((2 * self.inter, hidden), (hidden, self.inter)):
             n += 1
-            if m >= 33 and m * rows_n <= 2 * sms * 128 * 64:
-                kch = k // 128
-                items = (m + 191) // 192 * (rows_n // 128)
-                part_cost = 3.0 * m * rows_n * 4.0 / 16384.0 / sms
-                whole = float((items + sms - 1) // sms * kch)
-                best = whole
-                for ks in range(2, min(16, kch) + 1):
-                    kpart = -(-kch // ks)
-                    parts = -(-kch // kpart)
-                    best = min(best, (items * parts + sms - 1) // sms * kpart + part_cost * parts)
-                n += 1 if best < 0.75 * whole else 0
+            if m >= 33:
+                n += 1 if dense_k_parts(m, rows_n, k, sms) > 1 else 0
         return n
+
+
+def dense_k_parts(m: int, n: int, k: int, sms: int) -> int:
+    """K parts b200_linear's tcgen05 path uses for [m, k] x [n, k]^T (the
+    library's rule, restated for launch accounting): items of 192 rows x 128
+    weight rows go round-robin over the SMs; K is split when that cuts the
+    busiest SM's 128-K units by a quarter or more, each part charged 3x the
+    streaming time of its m*n fp32 partial sums, and only while the partials
+    fit the workspace (2 CTAs per SM x 128 x 64 floats)."""
+    if m * n > 2 * sms * 128 * 64:
+        return 1
+    kch = k // 128
+    items = (m + 191) // 192 * (n // 128)
+    part_cost = 3.0 * m * n * 4.0 / 16384.0 / sms
+    whole = float((items + sms - 1) // sms * kch)
+    best, best_parts = whole, 1
+    for ks in range(2, min(16, kch) + 1):
+        kpart = -(-kch // ks)
+        parts = -(-kch // kpart)
+        cost = (items * parts + sms - 1) // sms * kpart + part_cost * parts
+        if cost < best:
+            best, best_parts = cost, parts
+    return best_parts if best < 0.75 * whole else 1
 
 
 @dataclass

@@ -175,3 +175,31 @@ def test_router_oracle_tie_order():
     ids, w = oracle.route_topk_general(logits, 3)
     assert ids.tolist() == [[5, 2, 6], [5, 2, 6]]
     assert torch.allclose(w.sum(-1), torch.ones(2))
+
+
+def test_block_size_rule_follows_the_measured_crossovers():
+    """8-slot groups up to 6 routes per expert, 16-slot up to 16, then the
+    tcgen05 blocks of 64 (the B200 measurements in block_size_for's doc)."""
+    from sglang_restomod_b200.layer import block_size_for
+
+    assert block_size_for(1024, 256) == 8      # config4 decode, 4 per expert
+    assert block_size_for(2816, 513) == 8      # config2 T=256 with the shared route
+    assert block_size_for(600, 100) == 8       # 6.0
+    assert block_size_for(601, 100) == 16
+    assert block_size_for(1024, 64) == 16      # 16 per expert
+    assert block_size_for(1025, 64) == 64
+    assert block_size_for(1024, 32) == 64      # expert-parallel owner at 8 ranks
+    assert block_size_for(0, 512) == 8
+
+
+def test_dense_split_rule_matches_the_measured_choices():
+    """The split-K choices b200_linear makes on 148 SMs for the shapes it was
+    measured on (restated in layer.dense_k_parts for launch accounting)."""
+    from sglang_restomod_b200.layer import dense_k_parts
+
+    assert dense_k_parts(64, 25600, 5120, 148) == 1    # evening out waves: slower split
+    assert dense_k_parts(33, 25600, 5120, 148) == 1
+    assert dense_k_parts(128, 4096, 7168, 148) == 4    # shared expert gate/up: fills idle SMs
+    assert dense_k_parts(128, 7168, 2048, 148) == 1    # shared expert down
+    assert dense_k_parts(64, 5120, 25600, 148) == 7
+    assert dense_k_parts(64, 152064, 5120, 148) == 1   # partials beyond the workspace
