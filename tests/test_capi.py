@@ -30,6 +30,19 @@ def test_library_exports_every_declared_symbol():
     assert lib.b200_abi_version() == 1
 
 
+def test_ctypes_signatures_match_the_header_arity():
+    """Every declaration's parameter count equals its ctypes signature's, so a
+    binding cannot silently shift arguments."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    decls = re.findall(r"^(?:int|int64_t|const char\*)\s+(b200_\w+)\(([^;]*?)\);", text,
+                       re.M | re.S)
+    assert {name for name, _ in decls} == set(declared_functions())
+    for name, params in decls:
+        p = params.strip()
+        count = 0 if p in ("", "void") else len(p.split(","))
+        assert count == len(_lib.SIGNATURES[name][1]), name
+
+
 def test_library_has_no_torch_dependency():
     """The C ABI .so stands alone: no libtorch / libc10 in its dependencies."""
     import subprocess
