@@ -23,6 +23,8 @@
 //      counts gives every expert's first slot;
 //   3. each warp re-reads its segment in order and scatters route indices at
 //      offset + (earlier warps' count) + (rank among equal ids so far).
+// Up to 32 routes (one- to three-token decode steps) one warp does the same
+// with warp shuffles alone (align_warp below).
 #include "common.cuh"
 #include "internal.h"
 #include "route_topk.cuh"
