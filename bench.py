@@ -75,7 +75,7 @@ class ClockSampler:
         0x2: "applications_clocks_setting",
     }
 
-    def __init__(self, device_index: int, period: float = 0.05):
+    def __init__(self, device_index: int, period: float = 0.01):
         self.samples = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -232,7 +232,7 @@ def parse_workload(name: str):
 class MoEWorkload:
     """One MoE layer forward per step on this rank's tokens."""
 
-    def __init__(self, spec, rank, world, device):
+    def __init__(self, spec, rank, world, device, layer=None):
         import torch
 
         from sglang_restomod_b200 import synth
@@ -246,10 +246,11 @@ class MoEWorkload:
         self.world = world
         e_local = shape.experts // world
         # The shared expert rides in the routed GEMMs (one more expert) when its
-        # shapes and quantization match the routed experts'.
-        self.layer = QuantMoELayer.synthetic(shape, self.quant, device,
-                                             first_expert=rank * e_local, num_experts=e_local,
-                                             fuse_shared=spec.get("fuse_shared", True))
+        # shapes and quantization match the routed experts'. ``layer`` reuses
+        # an already built layer of the same shape (the sweep's prefill point).
+        self.layer = layer if layer is not None else QuantMoELayer.synthetic(
+            shape, self.quant, device, first_expert=rank * e_local, num_experts=e_local,
+            fuse_shared=spec.get("fuse_shared", True))
         # N > 1: the peer-memory exchange (NVLink P2P stores, no host sync) by
         # default; --transport nccl selects the all-to-all baseline.
         self.transport = spec.get("transport", "peer") if world > 1 else "local"
@@ -382,7 +383,10 @@ class MoEWorkload:
             nbytes = touched * per_expert + nvalid * layer.hidden * 2 + nvalid * layer.inter * 2
         else:
             nbytes = touched * per_expert + x.shape[0] * layer.hidden * 2 + routes * layer.inter * 2
-        return run, nbytes, "stream_gemm_kernel (gate/up, gated SiLU epilogue)"
+        flops = 2 * nvalid * 2 * layer.inter * layer.hidden
+        name = ("tc_gemm_kernel (gate/up, gated SiLU epilogue)" if bs >= 64 else
+                "stream_gemm_kernel (gate/up, gated SiLU epilogue)")
+        return run, nbytes, name, flops
 
 
 class DenseWorkload:
@@ -434,106 +438,267 @@ class DenseWorkload:
     def dominant(self):
         # b200_linear runs 33+ rows on the tcgen05 GEMM, fewer on the stream GEMM
         name = "tc_gemm_kernel (dense)" if self.m >= 33 else "stream_gemm_kernel (dense)"
-        return self.step, self.algorithmic()[0], name
+        return self.step, self.algorithmic()[0], name, 2 * self.m * self.n * self.k
 
 
 # -------------------------------------------------------------- CPU legs
-def cpu_sample_tokens_per_s(workload_name: str, spec, sample_tokens: int, repeats: int,
-                            threads: int):
-    """Time the oracle (the reference's CPU torch arithmetic) on a token sample."""
+def cpu_reference_step(spec, threads: int):
+    """One step of the reference's CPU arithmetic on the GPU arm's own batch.
+
+    The oracle port of sglang-restomod's dequantize-then-matmul path (the
+    reference's CPU torch path; its kernels are closed V100 binaries) on the
+    same seeded inputs rank 0 of the GPU arm runs: the same tokens, routing
+    and weights (generated with the same seeds; on the GPU when one is
+    present, where the GPU arm generates them, then moved to host memory).
+    Inside the step every touched expert - and the shared expert - is
+    dequantized from its checkpoint format and applied, as the reference's
+    CPU path does. Returns (step, tokens, description).
+    """
     import torch
 
     import oracle
-    from sglang_restomod_b200 import quant as _q  # noqa: F401
-    from sglang_restomod_b200.quant.quantize import quantize_block_fp8, quantize_nvfp4
+    from sglang_restomod_b200 import synth
 
     torch.set_num_threads(threads)
-    gen = torch.Generator().manual_seed(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
     if spec["kind"] == "dense":
-        k, n = spec["k"], spec["n"]
-        m = min(spec["m"], sample_tokens)
-        rows = min(n, 4096)  # a slice of the weight; scaled to the full N below
-        w = torch.randn(rows, k, generator=gen) * 0.02
-        q, s = quantize_block_fp8(w)
-        x = torch.randn(m, k, generator=gen).bfloat16()
-        times = []
-        for _ in range(repeats):
-            t0 = time.perf_counter()
-            oracle.fp8_linear_ref(x, q, s)
-            times.append(time.perf_counter() - t0)
-        t = statistics.median(times) * (n / rows)
-        return m / t, f"{m} rows x K={k} through a {rows}-row slice of W, scaled to N={n}"
+        k, n, m = spec["k"], spec["n"], spec["m"]
+        q, s = synth.fp8_bank(1, n, k, dev, seed=1)
+        q, s = q[0].cpu(), s[0].cpu()
+        x = synth.activations(m, k, dev, seed=2).cpu()
 
-    shape = spec["shape"]
+        def step():
+            return oracle.fp8_linear_ref(x, q, s)
+
+        return step, m, f"{m} rows x [{n}, {k}] block-FP8 weight, dequantized inside the step"
+
+    shape, tokens, quant = spec["shape"], spec["tokens"], spec["quant"]
     h, i, e_all, top_k = shape.hidden, shape.inter, shape.experts, shape.top_k
-    x = torch.randn(sample_tokens, h, generator=gen).bfloat16()
-    probs = torch.softmax(torch.randn(sample_tokens, e_all, generator=gen), dim=-1)
-    wts, ids = torch.topk(probs, top_k, dim=-1)
-    wts = wts / wts.sum(-1, keepdim=True)
-    experts = torch.unique(ids).tolist()
-    remap = torch.full((e_all,), -1, dtype=torch.int64)
-    remap[experts] = torch.arange(len(experts))
-    ids_m = remap[ids]
-    # checkpoint-format weights of the touched experts (dequantized inside the timed step)
-    bank13, bank2 = [], []
-    for _ in experts:
-        w13 = torch.randn(2 * i, h, generator=gen) * 0.02
-        w2 = torch.randn(h, i, generator=gen) * 0.02
-        if spec["quant"] == 0:
-            bank13.append(quantize_block_fp8(w13))
-            bank2.append(quantize_block_fp8(w2))
+    x = synth.activations(tokens, h, dev, seed=100).cpu()
+    ids, wts = synth.route(tokens, e_all, top_k, dev, seed=200)
+    ids, wts = ids.cpu(), wts.cpu()
+    seed = 10  # QuantMoELayer.synthetic's default
+    bank = {}
+    for e in torch.unique(ids).tolist():
+        if quant == 0:
+            q13, s13 = synth.fp8_bank(1, 2 * i, h, dev, seed, e)
+            q2, s2 = synth.fp8_bank(1, h, i, dev, seed + 1, e)
+            bank[e] = ((q13[0].cpu(), s13[0].cpu()), (q2[0].cpu(), s2[0].cpu()))
         else:
-            p13, s13, g13 = quantize_nvfp4(w13)
-            p2, s2, g2 = quantize_nvfp4(w2)
-            bank13.append((p13, s13, float(g13)))
-            bank2.append((p2, s2, float(g2)))
+            p13, s13, g13 = synth.nvfp4_bank(1, 2 * i, h, dev, seed, e)
+            p2, s2, g2 = synth.nvfp4_bank(1, h, i, dev, seed + 1, e)
+            bank[e] = ((p13[0].cpu(), s13[0].cpu(), float(g13[0])),
+                       (p2[0].cpu(), s2[0].cpu(), float(g2[0])))
+    shared = None
+    if shape.shared_inter:
+        si = shape.shared_inter
+        sq13, ss13 = synth.fp8_bank(1, 2 * si, h, dev, seed + 2, 0)
+        sq2, ss2 = synth.fp8_bank(1, h, si, dev, seed + 3, 0)
+        shared = ((sq13[0].cpu(), ss13[0].cpu()), (sq2[0].cpu(), ss2[0].cpu()))
 
-    def deq(item):
-        if spec["quant"] == 0:
-            return oracle.dequant_block_fp8(*item)
-        return oracle.dequant_nvfp4(*item)
+    def deq(item, fp8):
+        return oracle.dequant_block_fp8(*item) if fp8 else oracle.dequant_nvfp4(*item)
 
     def fetch(e):  # dequantized inside the timed step, one expert at a time
-        return deq(bank13[e]), deq(bank2[e])
+        a, b = bank[e]
+        return deq(a, quant == 0), deq(b, quant == 0)
 
-    times = []
-    for _ in range(repeats):
-        t0 = time.perf_counter()
-        oracle.moe_layer_ref(x, ids_m.to(torch.int32), wts, fetch, len(experts))
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return sample_tokens / t, (
-        f"{sample_tokens} tokens x top-{top_k} ({len(experts)} experts dequantized and applied)"
-        f" per step, oracle port of the reference's CPU dequantize-then-matmul path"
+    ones_ids = torch.zeros(tokens, 1, dtype=torch.int32)
+    ones_w = torch.ones(tokens, 1)
+
+    def step():
+        out = oracle.moe_layer_ref(x, ids, wts, fetch, e_all)
+        if shared is not None:
+            out = out + oracle.moe_layer_ref(
+                x, ones_ids, ones_w, lambda _e: (deq(shared[0], True), deq(shared[1], True)), 1)
+        return out
+
+    extra = " + the shared expert" if shared is not None else ""
+    return step, tokens, (
+        f"the full {tokens}-token batch x top-{top_k} ({len(bank)} touched experts{extra} "
+        f"dequantized and applied per step): oracle port of the reference's CPU "
+        f"dequantize-then-matmul path"
     )
 
 
 def reference_arm(args, rank, world):
     """--impl reference: the reference's CPU torch path on host cores, rank 0 only.
 
-    One step is one token of the workload through the oracle port (its
-    experts dequantized and applied); W untimed steps, then min(K, 10) timed
-    steps so the run stays within minutes.
+    Each step is the GPU arm's whole per-rank batch (same workload, same
+    inputs) through the oracle port, on every host thread. One untimed
+    warm-up step; then up to K timed steps, stopping early once 150 s of CPU
+    time have passed (the line's ``steps`` says how many ran).
     """
     if rank != 0:
         return
     spec = parse_workload(args.workload)
     threads = os.cpu_count() or 1
-    cpu_sample_tokens_per_s(args.workload, spec, 1, 1, threads)  # warm-up
-    timed = max(1, min(args.steps, 10))
-    value, desc = cpu_sample_tokens_per_s(args.workload, spec, 1, timed, threads)
+    step, tokens, desc = cpu_reference_step(spec, threads)
+    step()  # warm-up
+    times = []
+    budget = time.perf_counter() + 150.0
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > budget:
+            break
+    mean_s = sum(times) / len(times)
+    value = tokens / mean_s
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": timed, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+        "steps": len(times), "warmup": 1, "ms_per_step": 1000.0 * mean_s,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 (dequantized weights) x bf16", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": args.workload},
+        "config": {"workload": args.workload, "tokens_per_step": tokens},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------- sweep and EP check
+SWEEP = (
+    "config1-5120x25600-M1", "config1-5120x25600-M64", "config1-25600x5120-M64",
+    "config1-5120x152064-M1", "config2-T1", "config2-T64", "config2-T8192", "config3-T1",
+    "config3-T128", "config3-T4096", "config4-prefill",
+)
+
+
+def weight_copies(wl, step_bytes: int, world: int) -> int:
+    """Steps that read less than twice the L2 rotate over copies of the
+    workload (own weights, same inputs), enough that the copies together
+    read at least twice the L2: a copy's weights are evicted before its next
+    step."""
+    if world == 1 and step_bytes < 2 * L2_BYTES and hasattr(wl, "replica"):
+        return int(min(16, max(2, -(-2 * L2_BYTES // step_bytes))))
+    return 1
+
+
+def sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse=None):
+    """One configuration on one GPU: step time (CUDA graph replay, CUDA
+    events) and its dominant kernel's time and roofline fractions."""
+    import torch
+
+    spec = parse_workload(name)
+    spec["transport"] = "local"
+    spec["fuse_shared"] = True
+    if spec["kind"] == "dense":
+        wl = DenseWorkload(spec, device)
+    else:
+        wl = MoEWorkload(spec, 0, 1, device, layer=reuse)
+    step_bytes, step_flops, touched = wl.algorithmic()
+    copies = weight_copies(wl, step_bytes, 1)
+    wls = [wl] + [wl.replica() for _ in range(copies - 1)]
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        for w in wls:
+            w.step()
+    torch.cuda.synchronize()
+    graphs, fns = [], []
+    for w in wls:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            w.step()
+        graphs.append(g)
+        fns.append(g.replay)
+    doms = [w.dominant() for w in wls]
+    dom_fns = []
+    for run, _, _, _ in doms:
+        run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        graphs.append(g)
+        dom_fns.append(g.replay)
+    for f in fns + dom_fns:
+        f()
+    torch.cuda.synchronize()
+    reps = max(20, min(args.steps, 200))
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(reps):
+        fns[i % copies]()
+    end.record(stream)
+    torch.cuda.synchronize()
+    step_ms = start.elapsed_time(end) / reps
+    start.record(stream)
+    for i in range(reps):
+        dom_fns[i % copies]()
+    end.record(stream)
+    torch.cuda.synchronize()
+    dom_ms = start.elapsed_time(end) / reps
+    _, dom_bytes, dom_name, dom_flops = doms[0]
+    hbm_frac = dom_bytes / (dom_ms * 1e-3) / 1e9 / hbm_gbs
+    tensor_frac = dom_flops / (dom_ms * 1e-3) / 1e12 / bf16_tflops
+    prefill = wl.tokens >= 2048
+    point = {
+        "ms_per_step": step_ms, "tokens_per_s": wl.tokens / (step_ms * 1e-3),
+        "layer_hbm_frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm_gbs,
+        "dominant": dom_name, "dominant_us": dom_ms * 1e3,
+        "bound": "tensor" if prefill else "hbm",
+        "frac": tensor_frac if prefill else hbm_frac,
+        "dominant_hbm_frac": hbm_frac, "dominant_tensor_frac": tensor_frac,
+        "weight_copies": copies,
+    }
+    del graphs, fns, dom_fns, doms, wls, wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return point
+
+
+def run_sweep(args, device, hbm_gbs, bf16_tflops, reuse_config4=None):
+    """The headline configurations besides the main workload, each measured
+    the same way (prefill points against the bf16 tensor burst peak, decode
+    points against HBM)."""
+    out = {}
+    for name in SWEEP:
+        if name == args.workload:
+            continue
+        reuse = reuse_config4 if name.startswith("config4") else None
+        try:
+            out[name] = sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse)
+        except Exception as exc:  # noqa: BLE001 - a failed point is reported, not fatal
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    return out
+
+
+def ep_check(wl, device, world):
+    """This rank's last output of the expert-parallel step against the same
+    tokens through a single-GPU layer holding all experts (built from the
+    same per-expert seeds); every token, rtol / atol 2e-2. Max over ranks."""
+    import torch
+
+    from sglang_restomod_b200.layer import QuantMoELayer
+
+    full = QuantMoELayer.synthetic(wl.shape, wl.quant, device, first_expert=0,
+                                   num_experts=wl.shape.experts, fuse_shared=False)
+    want = full.forward(wl.x, wl.ids, wl.w).float()
+    got = wl.out.float()
+    torch.cuda.synchronize()
+    err = (got - want).abs()
+    bad = int((err > 2e-2 + 2e-2 * want.abs()).sum())
+    stats = torch.tensor([float(err.max()), float(bad)], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    del full
+    torch.cuda.empty_cache()
+    return {"tokens": int(wl.tokens), "ranks": world, "max_err": float(stats[0]),
+            "bad_elements_max_rank": int(stats[1]), "rtol": 2e-2, "atol": 2e-2,
+            "ok": int(stats[1]) == 0}
+
+
+def dist_teardown(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 # -------------------------------------------------------------------- main
@@ -550,6 +715,10 @@ def main() -> int:
                     help="expert-parallel exchange at N > 1")
     ap.add_argument("--separate-shared", action="store_true",
                     help="run the shared expert as its own dense MLP instead of fused")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the other configurations' points (N=1)")
+    ap.add_argument("--no-ep-check", action="store_true",
+                    help="skip the untimed expert-parallel correctness pass (N>1)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -572,12 +741,8 @@ def main() -> int:
         wl = DenseWorkload(spec, device)
     else:
         wl = MoEWorkload(spec, rank, world, device)
-    # Steps that read less than L2 rotate over copies of the workload (own
-    # weights, same routing), enough that the copies together read twice L2.
     step_bytes = wl.algorithmic()[0]
-    copies = 1
-    if world == 1 and step_bytes < L2_BYTES and hasattr(wl, "replica"):
-        copies = int(min(16, max(4, -(-2 * L2_BYTES // step_bytes))))
+    copies = weight_copies(wl, step_bytes, world)
     wls = [wl] + [wl.replica() for _ in range(copies - 1)]
     torch.cuda.synchronize()
 
@@ -594,6 +759,7 @@ def main() -> int:
     # transport reads its all-to-all split sizes on the host and runs eagerly.
     use_graph = not args.eager and (world == 1 or args.transport == "peer")
     ios = [w.e2e_io() for w in wls]
+    graphs = []
     step_fns = [w.step for w in wls]
     e2e_fns = [[(lambda io=io, p=p: io.step(p)) for p in range(2)] for io in ios]
     if use_graph:
@@ -622,6 +788,8 @@ def main() -> int:
                 f()
         torch.cuda.synchronize()
 
+    # clocks sampled over the whole timed phase: device-timed, e2e and
+    # dominant-kernel legs
     sampler = ClockSampler(device.index)
     sampler.start()
     barrier(world)
@@ -636,7 +804,6 @@ def main() -> int:
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
-    sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
 
     # end-to-end: pinned host inputs in, result out, every step (double
@@ -667,11 +834,12 @@ def main() -> int:
     # dominant kernel alone, CUDA events on its launch stream
     doms = [w.dominant() for w in wls]
     roofline = None
+    runs = []
     hbm_gbs, bf16_tflops, peak_kind = measured_peaks()
     if doms[0] is not None:
-        _, dom_bytes, dom_name = doms[0]
+        _, dom_bytes, dom_name, _ = doms[0]
         runs = []
-        for run, _, _ in doms:
+        for run, _, _, _ in doms:
             for _ in range(3):
                 run()
             torch.cuda.synchronize()
@@ -700,10 +868,31 @@ def main() -> int:
                     "unit": "GB/s", "frac": achieved / hbm_gbs, "traffic": traffic,
                     "peak_source": peak_kind, "algorithmic_bytes": dom_bytes,
                     "launch_us": dom_ms * 1e3}
+    sampler.stop()
 
     status = ops.workspace_status()
     if status != 0:
         raise SystemExit(f"kernels reported device error bits {status}")
+
+    # Untimed correctness pass under expert parallelism: this rank's tokens
+    # through one GPU's full-bank layer, compared with what the exchange gave.
+    ep_result = None
+    if world > 1 and spec["kind"] != "dense" and not args.no_ep_check:
+        ep_result = ep_check(wl, device, world)
+    # release every CUDA graph (and the closures replaying them)
+    del graphs, step_fns, e2e_fns, runs
+    if ep_result is not None and not ep_result["ok"]:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "error": "ep_check failed", "ep_check": ep_result}),
+                  flush=True)
+        dist_teardown(world)
+        return 1
+
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        reuse = wl.layer if args.workload == "config4-decode" else None
+        del wls, ios, doms
+        sweep = run_sweep(args, device, hbm_gbs, bf16_tflops, reuse)
 
     alg_bytes, alg_flops, touched = wl.algorithmic()
     total_tokens = wl.tokens * world
@@ -715,10 +904,12 @@ def main() -> int:
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        sample = 4 if spec["kind"] != "dense" else 1
-        cpu_value, desc = cpu_sample_tokens_per_s(args.workload, spec, sample, 3, threads)
-        cpu_baseline = {"value": cpu_value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                        "sample": desc}
+        cpu_step, cpu_tokens, desc = cpu_reference_step(spec, threads)
+        t0 = time.perf_counter()
+        cpu_step()
+        cpu_s = time.perf_counter() - t0
+        cpu_baseline = {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": threads,
+                        "kind": "port", "sample": "one step: " + desc}
 
     if rank == 0:
         if copies == 1:
@@ -751,11 +942,12 @@ def main() -> int:
             "cuda_graph": use_graph,
             "gpu_launches": wl.launches_per_step() * args.steps,
         }
+        if ep_result is not None:
+            line["ep_check"] = ep_result
+        if sweep is not None:
+            line["sweep"] = sweep
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    dist_teardown(world)
     return 0
 
 

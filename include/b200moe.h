@@ -202,18 +202,31 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
  * with no access to the device allocator). No counterpart in the reference:
  * this entry point exists only for such callers. Same arguments and result
  * as b200_linear, without the workspace: it uses a 16 MiB array compiled
- * into the library (held on every device that loads it, until exit), which
- * covers the fixed workspace on a 148-SM B200 plus up to about 3.5 M bf16
- * activation elements (M*K) to convert; larger bf16 calls are refused with
- * B200_ERR_INVALID (f16 activations need no conversion room). The array is
- * shared: calls on one device must not overlap on the GPU. The first call
- * on each device looks up the array's address (cudaGetSymbolAddress); make
- * it before any stream capture. Calls no cudaMalloc / cudaFree.
+ * into the library (held on every device that loads it, until exit). The
+ * array holds the fixed workspace, b200_gemm_workspace_bytes(0) on the
+ * current device, and room for
+ * (b200_linear_noalloc_scratch_bytes() - b200_gemm_workspace_bytes(0)) / 2
+ * bf16 activation elements (M*K) to convert: 3,405,568 on a 148-SM B200.
+ * Larger bf16 calls are refused with B200_ERR_INVALID (f16 activations need
+ * no conversion room). The array is shared: calls on one device must not
+ * overlap on the GPU. The first call on each device looks up the array's
+ * address (cudaGetSymbolAddress) and clears it; make that call before any
+ * stream capture. cudaDeviceReset after it is not supported. Calls no
+ * cudaMalloc / cudaFree.
  */
 int64_t b200_linear_noalloc_scratch_bytes(void);
 int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
                         const uint8_t* w_packed, const float* w_scales, const float* global_scale,
                         int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* stream);
+
+/*
+ * Device-side error bits of b200_linear_noalloc calls on the current device
+ * (the bits of b200_workspace_status, kept in the static array, which the
+ * caller cannot address). The bits are sticky across calls until read with
+ * reset != 0, which also clears the array's partial sums when bits were set.
+ * Synchronizes `stream`. No counterpart in the reference.
+ */
+int b200_linear_noalloc_status(int32_t* bits, int32_t reset, void* stream);
 
 /*
  * Grouped expert GEMM routed by moe_align_block_size output, with the

@@ -196,6 +196,9 @@ int b200::set_last_error(int code, const char* message) {
   return code;
 }
 
+int64_t b200::ws_head_bytes() { return kStatusBytes + kCounterBytes; }
+int64_t b200::ws_fixed_bytes() { return stream_ws_bytes(); }
+
 extern "C" {
 
 int b200_abi_version(void) { return 1; }

@@ -191,4 +191,10 @@ cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long l
 // Records `message` as this thread's b200_last_error() and returns `code`.
 int set_last_error(int code, const char* message);
 
+// GEMM workspace layout (capi.cu): the status word and the arrival counters
+// sit at the front, in ws_head_bytes(); the fixed part (head, tcgen05 plan,
+// split partial sums) is ws_fixed_bytes() on the current device.
+int64_t ws_head_bytes();
+int64_t ws_fixed_bytes();
+
 }  // namespace b200

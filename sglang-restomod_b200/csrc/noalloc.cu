@@ -11,15 +11,27 @@
 // allocating library routine.
 //
 // The array is shared by every call on a device and keeps whatever the last
-// call left in it, so each call first clears the part that must start at
-// zero (status, counters, partial sums) with cudaMemsetAsync on the caller's
-// stream. Two calls that overlap on the GPU (different streams, no ordering
-// between them) race on the array and produce wrong results; order them.
+// call left in it. The kernels return every arrival counter and partial sum
+// they touch to zero when they finish, and a static device array starts
+// zero-filled, so a call needs no clearing beyond:
+//   * the first call on a device clears the whole fixed part (status word,
+//     counters, tcgen05 plan, partial sums) once;
+//   * every call clears the arrival counters (4 KiB), so a call that gave up
+//     part-way (a timed-out pipeline wait) cannot skew the next call's
+//     reductions;
+//   * b200_linear_noalloc_status(.., reset != 0) that finds error bits set
+//     clears the whole fixed part again (the partial sums of an aborted call).
+// The status word is sticky: calls never clear it, so an error any earlier
+// call recorded stays visible until the caller reads it with reset.
+// Two calls that overlap on the GPU (different streams, no ordering between
+// them) race on the array and produce wrong results; order them.
 //
 // In host code the array's name does not denote device memory. The first
 // call on each device looks up the array's device address with
-// cudaGetSymbolAddress while that device is current; make that first call
-// before capturing the calls into a CUDA graph.
+// cudaGetSymbolAddress while that device is current, and keeps it for the
+// life of the process; make that first call before capturing the calls into
+// a CUDA graph. cudaDeviceReset after the first call on a device is not
+// supported (the kept address would be stale).
 #include <cstdio>
 #include <mutex>
 
@@ -29,31 +41,37 @@
 namespace {
 
 constexpr int64_t kScratchBytes = 16ll << 20;
+constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) uint8_t g_linear_scratch[kScratchBytes];
 
 std::mutex g_mu;
-void* g_scratch_dev[64] = {};
+void* g_scratch_dev[kMaxDevices] = {};
+bool g_cleared[kMaxDevices] = {};
 
-// Device address of g_linear_scratch on the current device, looked up once.
-int scratch_for_current_device(void** out) {
+int cuda_fail(const char* what, cudaError_t err) {
+  char msg[256];
+  snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(err));
+  return b200::set_last_error(B200_ERR_CUDA, msg);
+}
+
+// Device address of g_linear_scratch on the current device (looked up once)
+// and the device ordinal.
+int scratch_for_current_device(void** out, int* dev_out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess || dev < 0 || dev >= 64)
+  if (err != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return b200::set_last_error(B200_ERR_CUDA, "b200_linear_noalloc: no usable current device");
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_scratch_dev[dev] == nullptr) {
     void* ptr = nullptr;
     err = cudaGetSymbolAddress(&ptr, g_linear_scratch);
-    if (err != cudaSuccess || ptr == nullptr) {
-      char msg[256];
-      snprintf(msg, sizeof(msg), "b200_linear_noalloc: cudaGetSymbolAddress failed: %s",
-               cudaGetErrorString(err));
-      return b200::set_last_error(B200_ERR_CUDA, msg);
-    }
+    if (err != cudaSuccess || ptr == nullptr)
+      return cuda_fail("b200_linear_noalloc: cudaGetSymbolAddress failed", err);
     g_scratch_dev[dev] = ptr;
   }
   *out = g_scratch_dev[dev];
+  *dev_out = dev;
   return B200_OK;
 }
 
@@ -79,17 +97,51 @@ extern "C" int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype
   }
   if (m == 0) return B200_OK;
   void* scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  int dev = 0;
+  int rc = scratch_for_current_device(&scratch, &dev);
   if (rc != B200_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t zeroed = b200_gemm_workspace_bytes(0);  // status, counters, partials
-  cudaError_t err = cudaMemsetAsync(scratch, 0, (size_t)zeroed, st);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  bool first = false;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    first = !g_cleared[dev];
+    g_cleared[dev] = true;
+  }
+  cudaError_t err;
+  if (first) {
+    err = cudaMemsetAsync(base, 0, (size_t)b200::ws_fixed_bytes(), st);
+  } else {
+    // counters only: they follow the 256-byte status block
+    const int64_t status_bytes = 256;
+    err = cudaMemsetAsync(base + status_bytes, 0, (size_t)(b200::ws_head_bytes() - status_bytes),
+                          st);
+  }
   if (err != cudaSuccess) {
-    char msg[256];
-    snprintf(msg, sizeof(msg), "b200_linear_noalloc: clearing the scratch failed: %s",
-             cudaGetErrorString(err));
-    return b200::set_last_error(B200_ERR_CUDA, msg);
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (first) g_cleared[dev] = false;
+    return cuda_fail("b200_linear_noalloc: clearing the scratch failed", err);
   }
   return b200_linear(quant, x, x_dtype, m, k, w_packed, w_scales, global_scale, n, gated_mode, y,
                      y_dtype, scratch, kScratchBytes, stream);
+}
+
+extern "C" int b200_linear_noalloc_status(int32_t* bits, int32_t reset, void* stream) {
+  if (bits == nullptr) return b200::set_last_error(B200_ERR_INVALID, "null argument");
+  void* scratch = nullptr;
+  int dev = 0;
+  int rc = scratch_for_current_device(&scratch, &dev);
+  if (rc != B200_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t host = 0;
+  cudaError_t err = cudaMemcpyAsync(&host, scratch, sizeof(host), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  if (err != cudaSuccess) return cuda_fail("b200_linear_noalloc_status: status read", err);
+  *bits = host;
+  if (reset && host != 0) {
+    // An errored call may have left partial sums behind: clear the fixed part.
+    err = cudaMemsetAsync(scratch, 0, (size_t)b200::ws_fixed_bytes(), st);
+    if (err != cudaSuccess) return cuda_fail("b200_linear_noalloc_status: reset", err);
+  }
+  return B200_OK;
 }

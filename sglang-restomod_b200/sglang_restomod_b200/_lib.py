@@ -89,6 +89,7 @@ SIGNATURES = {
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
          c_int32, c_void_p, c_int32, c_void_p],
     ),
+    "b200_linear_noalloc_status": (c_int32, [ctypes.POINTER(c_int32), c_int32, c_void_p]),
     "b200_moe_gemm": (
         c_int32,
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int32,

@@ -12,7 +12,20 @@ import torch
 
 import oracle
 from sglang_restomod_b200 import _lib, ops, synth
+from sglang_restomod_b200.layer import block_size_for
 from tests.conftest import assert_close
+
+
+def wide_sample(tokens: int, n: int = 256, seed: int = 0) -> torch.Tensor:
+    """n token indices: the first and last n/4 (the first and last route
+    slots of every expert's run, so the first and last tcgen05 items) and n/2
+    drawn from the rest."""
+    if tokens <= n:
+        return torch.arange(tokens)
+    q = n // 4
+    edge = torch.cat([torch.arange(q), torch.arange(tokens - q, tokens)])
+    middle = q + torch.randperm(tokens - 2 * q, generator=torch.Generator().manual_seed(seed))[: n - 2 * q]
+    return torch.cat([edge, middle]).sort().values
 
 pytestmark = pytest.mark.gpu
 
@@ -249,13 +262,15 @@ def _layer_inputs(shape, tokens, quant, device, seed=0):
         q2, s2 = synth.fp8_bank(shape.experts, shape.hidden, shape.inter, device, seed=11)
         bank = dict(w13=ops.fp8_prepack(q13, True), w2=ops.fp8_prepack(q2, False),
                     w13_scales=s13, w2_scales=s2)
-        deq = lambda es: (_dequant_fp8_bank(q13, s13, es), _dequant_fp8_bank(q2, s2, es))  # noqa: E731
+        deq = lambda e: (oracle.dequant_block_fp8(q13[e].cpu(), s13[e].cpu()),  # noqa: E731
+                         oracle.dequant_block_fp8(q2[e].cpu(), s2[e].cpu()))
     else:
         p13, s13, g13 = synth.nvfp4_bank(shape.experts, 2 * shape.inter, shape.hidden, device, seed=10)
         p2, s2, g2 = synth.nvfp4_bank(shape.experts, shape.hidden, shape.inter, device, seed=11)
         bank = dict(w13=ops.nvfp4_prepack(p13, s13, True), w2=ops.nvfp4_prepack(p2, s2, False),
                     w13_global=g13, w2_global=g2)
-        deq = lambda es: (_dequant_nvfp4_bank(p13, s13, g13, es), _dequant_nvfp4_bank(p2, s2, g2, es))  # noqa: E731
+        deq = lambda e: (oracle.dequant_nvfp4(p13[e].cpu(), s13[e].cpu(), float(g13[e])),  # noqa: E731
+                         oracle.dequant_nvfp4(p2[e].cpu(), s2[e].cpu(), float(g2[e])))
     return x, ids, weights, bank, deq
 
 
@@ -268,15 +283,8 @@ def _check_layer(shape, tokens, quant, device, block, sample_tokens=None, rsf=1.
     assert ops.workspace_status() == 0
     sel = torch.arange(tokens) if sample_tokens is None else sample_tokens
     ids_c = ids.cpu()[sel]
-    experts = torch.unique(ids_c[ids_c >= 0]).tolist()
-    d13, d2 = deq(experts)
-    # Only the touched experts are dequantized; renumber them compactly.
-    remap = torch.full((shape.experts,), -1, dtype=torch.int32)
-    remap[experts] = torch.arange(len(experts), dtype=torch.int32)
-    ids_m = torch.where(ids_c >= 0, remap[ids_c.clamp(min=0).long()], -1)
-    w13 = torch.stack([d13[e] for e in experts])
-    w2 = torch.stack([d2[e] for e in experts])
-    want = oracle.moe_layer_ref(x.cpu()[sel], ids_m, weights.cpu()[sel], w13, w2,
+    # The touched experts are dequantized one at a time, inside the oracle.
+    want = oracle.moe_layer_ref(x.cpu()[sel], ids_c, weights.cpu()[sel], deq, shape.experts,
                                 routed_scaling_factor=rsf)
     assert_close(out.cpu()[sel], want, what=f"layer q={quant} T={tokens}")
 
@@ -289,8 +297,10 @@ def test_layer_config0(cuda_device, quant):
 @pytest.mark.parametrize("quant", [_lib.QUANT_FP8_BLOCK, _lib.QUANT_NVFP4])
 @pytest.mark.parametrize("tokens", [1, 8, 64, 256])
 def test_layer_config2_decode(cuda_device, quant, tokens):
-    sample = None if tokens <= 8 else torch.tensor([0, tokens // 3, tokens - 1])
-    _check_layer(synth.CONFIG2, tokens, quant, cuda_device, block=16, sample_tokens=sample, rsf=2.0)
+    # every token checked; the layer's own block rule (8-slot groups up to 6
+    # routes per expert, 16-slot above) and 16-slot groups for comparison
+    for block in sorted({16, block_size_for(tokens * synth.CONFIG2.top_k, synth.CONFIG2.experts)}):
+        _check_layer(synth.CONFIG2, tokens, quant, cuda_device, block=block, rsf=2.0)
 
 
 # ------------------------------------------------- tcgen05 (prefill) path
@@ -404,8 +414,8 @@ def test_nvfp4_linear_tcgen05(cuda_device, m, gated_mode):
 
 def test_layer_config3_prefill_sampled(cuda_device):
     """The NVFP4 layer (config-2 shapes, NVFP4 weights) at 4096 tokens on the
-    tensor-core path; four tokens checked against the oracle."""
-    sample = torch.tensor([0, 1, 2047, 4095])
+    tensor-core path; 256 tokens checked against the oracle."""
+    sample = wide_sample(4096)
     _check_layer(synth.CONFIG2, 4096, _lib.QUANT_NVFP4, cuda_device, block=64,
                  sample_tokens=sample, rsf=1.0)
 
@@ -424,24 +434,17 @@ def test_fp8_linear_tcgen05(cuda_device, m, gated_mode):
 
 @pytest.mark.parametrize("tokens,block", [(8192, 256), (2048, 64)])
 def test_layer_config2_prefill(cuda_device, tokens, block):
-    sample = torch.tensor([0, 1, tokens // 2, tokens - 1])
+    sample = wide_sample(tokens)
     _check_layer(synth.CONFIG2, tokens, _lib.QUANT_FP8_BLOCK, cuda_device, block=block,
                  sample_tokens=sample, rsf=1.0)
 
 
 def test_layer_config4_prefill_sampled(cuda_device):
     """Expert-parallel layer shape (H=7168, I=2048, 256 experts, top-8) at 4096
-    tokens on one GPU; four tokens checked against the oracle."""
-    sample = torch.tensor([0, 1000, 4095])
+    tokens on one GPU; 256 tokens checked against the oracle."""
+    sample = wide_sample(4096)
     _check_layer(synth.CONFIG4, 4096, _lib.QUANT_FP8_BLOCK, cuda_device, block=256,
                  sample_tokens=sample, rsf=1.0)
-
-
-def test_layer_config4_decode_bench_workload(cuda_device):
-    """The default bench workload itself: H=7168, I=2048, 256 experts, top-8,
-    128 tokens, 16-slot blocks (weight-streaming GEMM), sampled tokens."""
-    _check_layer(synth.CONFIG4, 128, _lib.QUANT_FP8_BLOCK, cuda_device, block=16,
-                 sample_tokens=torch.tensor([0, 77, 127]), rsf=1.0)
 
 
 # ------------------------------------------------ fused shared expert
