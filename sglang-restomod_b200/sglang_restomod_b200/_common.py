@@ -28,6 +28,16 @@ def is_b200() -> bool:
         return False
 
 
+def b200_ops():
+    """``torch.ops.b200_moe``: the library's ops registered as torch custom ops
+    (registration happens on the first call)."""
+    import torch
+
+    from . import torch_ops  # noqa: F401
+
+    return torch.ops.b200_moe
+
+
 def library_loadable() -> bool:
     try:
         from . import _lib

@@ -38,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layer import QuantMoELayer, block_size_for  # noqa: F401
+from .layer import B, QuantMoELayer, block_size_for  # noqa: F401
 
 
 class PeerExchange:
@@ -163,8 +163,12 @@ class ExpertParallelMoE:
         if self._combine_fn is not None:
             return self._combine_fn(routed, topk_ids, shared)
         # every route was computed by its owner: no id is dropped here
-        return ops.moe_combine(routed, topk_ids.clamp(min=0), self.num_experts, 1.0,
-                               shared_out=shared, out=out, out_dtype=routed.dtype)
+        y = B.moe_combine(routed, topk_ids.clamp(min=0), self.num_experts, 1.0, shared,
+                          routed.dtype)
+        if out is None:
+            return y
+        out.copy_(y)
+        return out
 
     def _shared(self, x):
         if self._shared_fn is not None:
@@ -252,25 +256,22 @@ class ExpertParallelMoE:
         """topk_ids / topk_weights: [T, k], or [T, k + 1] with the shared
         route appended when the layer's shared expert is fused."""
         ex = self.exchange
-        ops.ep_dispatch(x, topk_ids, topk_weights, num_experts=self.num_experts, rank=self.rank,
-                        world=self.world, peers=ex.peers, region=ex.region,
-                        max_tokens=ex.max_tokens, shared_expert=self.fused)
+        B.ep_dispatch(x, topk_ids, topk_weights, self.num_experts, self.rank, self.world,
+                      ex.peers, ex.region, ex.max_tokens, self.fused)
 
     def peer_experts(self):
         ex, layer = self.exchange, self.local
-        ops.ep_expert_forward(
-            quant=layer.quant, hidden=layer.hidden, inter=layer.inter,
-            local_experts=layer.num_experts + (1 if self.fused else 0), w13=layer.w13,
-            w2=layer.w2, w13_scales=layer.w13_scales, w2_scales=layer.w2_scales,
-            w13_global=layer.w13_global, w2_global=layer.w2_global,
-            block_size=self.peer_block_size, rank=self.rank, world=self.world, peers=ex.peers,
-            region=ex.region, max_tokens=ex.max_tokens, top_k=ex.top_k,
-        )
+        B.ep_expert_forward(
+            layer.quant, layer.hidden, layer.inter, layer.num_experts + (1 if self.fused else 0),
+            layer.w13, layer.w2, layer.w13_scales, layer.w2_scales, layer.w13_global,
+            layer.w2_global, self.peer_block_size, self.rank, self.world, ex.peers, ex.region,
+            ex.max_tokens, ex.top_k)
 
     def peer_combine(self, topk_ids, shared=None, out=None, out_dtype=torch.bfloat16):
         ex, layer = self.exchange, self.local
-        return ops.ep_combine(topk_ids, hidden=layer.hidden,
-                              num_experts=self.num_experts + (1 if self.fused else 0),
-                              world=self.world, region=ex.region, max_tokens=ex.max_tokens,
-                              routed_scaling_factor=layer.routed_scaling_factor,
-                              shared_out=shared, out=out, out_dtype=out_dtype)
+        if out is None:
+            out = torch.empty(topk_ids.shape[0], layer.hidden, dtype=out_dtype,
+                              device=topk_ids.device)
+        B.ep_combine(topk_ids, layer.hidden, self.num_experts + (1 if self.fused else 0),
+                     self.world, ex.region, ex.max_tokens, layer.routed_scaling_factor, shared, out)
+        return out

@@ -1,8 +1,10 @@
 """A quantized fused-MoE layer (routed experts + optional shared expert).
 
 This is the object the method classes and the benchmark drive: it holds the
-prepacked banks and runs one forward through the C ABI
-(``b200_moe_layer_forward`` plus the shared expert's two dense calls).
+prepacked banks and runs one forward through the torch custom ops
+``torch.ops.b200_moe.*`` (:mod:`.torch_ops`), whose CUDA implementations call
+the C ABI (``b200_moe_layer_forward`` plus the shared expert's two dense
+calls).
 Semantics follow ``SM70Fp8MoEMethod.apply``
 (``sglang_restomod/quant/sm70_fp8_moe/method.py:239-309``): stable
 expert-major routing, gated SiLU*up, router-weighted down projection,
@@ -16,7 +18,9 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib, ops, synth
+from . import _lib, ops, synth, torch_ops  # noqa: F401 - torch_ops registers torch.ops.b200_moe
+
+B = torch.ops.b200_moe
 
 
 def block_size_for(routes: int, experts: int) -> int:
@@ -65,11 +69,10 @@ class SharedExpert:
     w2_global: torch.Tensor | None = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        h = ops.linear(x, self.w13, 2 * self.inter, quant=self.quant, scales=self.w13_scales,
-                       global_scale=self.w13_global, gated_mode=_lib.GATED_FUSED,
-                       out_dtype=torch.float16)
-        return ops.linear(h, self.w2, x.shape[-1], quant=self.quant, scales=self.w2_scales,
-                          global_scale=self.w2_global, out_dtype=x.dtype)
+        h = B.linear(x, self.w13, 2 * self.inter, self.quant, self.w13_scales, self.w13_global,
+                     _lib.GATED_FUSED, torch.float16)
+        return B.linear(h, self.w2, x.shape[-1], self.quant, self.w2_scales, self.w2_global,
+                        _lib.GATED_NONE, x.dtype)
 
     launches_per_forward = 3  # bf16->f16 conversion, gate/up(+SiLU), down (decode rows)
 
@@ -152,8 +155,7 @@ class QuantMoELayer:
         """Routes plus one shared route per token (weight 1 / rsf: the combine
         scales every route by rsf, the shared expert's output is unscaled)."""
         sid = self.num_experts if shared_id is None else shared_id
-        return ops.append_shared_route(topk_ids, topk_weights, sid,
-                                       1.0 / self.routed_scaling_factor)
+        return B.append_shared_route(topk_ids, topk_weights, sid, 1.0 / self.routed_scaling_factor)
 
     def fused_block_size(self, tokens: int, block_size=None) -> int | None:
         """Block size of the fused forward, or None when it should not be used.
@@ -174,23 +176,23 @@ class QuantMoELayer:
         bs = self.fused_block_size(tokens, block_size) if use_shared and shared_out is None else None
         if bs is not None:
             # the shared route is appended inside the library call
-            y, _, _ = ops.moe_layer_forward_fused_shared(
-                x, topk_ids, topk_weights, quant=self.quant, num_experts=self.num_experts,
-                inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
-                w2_scales=self.w2_scales, block_size=bs,
-                routed_scaling_factor=self.routed_scaling_factor, out=out,
-            )
-            return y
+            if out is None:
+                out = torch.empty_like(x)
+            B.moe_layer_forward_fused_shared(
+                x, topk_ids, topk_weights, self.quant, self.num_experts, self.inter, self.w13,
+                self.w2, self.w13_scales, self.w2_scales, bs, self.routed_scaling_factor,
+                1.0 / self.routed_scaling_factor, out)
+            return out
         if use_shared and shared_out is None and self.shared is not None:
             shared_out = self.shared.forward(x)
         bs = block_size or self.block_size or block_size_for(tokens * top_k, self.num_experts)
-        return ops.moe_layer_forward(
-            x, topk_ids, topk_weights, quant=self.quant, num_experts=self.num_experts,
-            inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
-            w2_scales=self.w2_scales, w13_global=self.w13_global, w2_global=self.w2_global,
-            block_size=bs, routed_scaling_factor=self.routed_scaling_factor,
-            shared_out=shared_out, out=out,
-        )
+        args = (x, topk_ids, topk_weights, self.quant, self.num_experts, self.inter, self.w13,
+                self.w2, self.w13_scales, self.w2_scales, self.w13_global, self.w2_global, bs,
+                self.routed_scaling_factor, shared_out)
+        if out is None:
+            return B.moe_layer_forward(*args)
+        B.moe_layer_forward_out(*args, out)
+        return out
 
     def forward_logits(self, x, router_logits, out=None, scoring: int = _lib.SCORING_SOFTMAX,
                        renormalize: bool = True, correction_bias=None):
@@ -202,16 +204,15 @@ class QuantMoELayer:
         if self.fused_block_size(tokens) is None:
             shared_out = self.shared.forward(x) if self.shared is not None else None
             bs = self.block_size or block_size_for(tokens * self.top_k, self.num_experts)
-            y, _, _ = ops.moe_layer_forward_logits(
-                x, router_logits, self.top_k, quant=self.quant, num_experts=self.num_experts,
-                inter=self.inter, w13=self.w13, w2=self.w2, w13_scales=self.w13_scales,
-                w2_scales=self.w2_scales, w13_global=self.w13_global, w2_global=self.w2_global,
-                block_size=bs, routed_scaling_factor=self.routed_scaling_factor,
-                shared_out=shared_out, scoring=scoring, renormalize=renormalize,
-                correction_bias=correction_bias, out=out)
-            return y
-        ids, w = ops.topk_route(router_logits, self.top_k, scoring=scoring,
-                                renormalize=renormalize, correction_bias=correction_bias)
+            if out is None:
+                out = torch.empty_like(x)
+            B.moe_layer_forward_logits(
+                x, router_logits, self.top_k, self.quant, self.num_experts, self.inter, self.w13,
+                self.w2, self.w13_scales, self.w2_scales, self.w13_global, self.w2_global, bs,
+                self.routed_scaling_factor, shared_out, scoring, renormalize, correction_bias,
+                out)
+            return out
+        ids, w = B.topk_route(router_logits, self.top_k, scoring, renormalize, correction_bias)
         return self.forward(x, ids, w, out=out)
 
     def launches_per_forward(self, x_dtype=torch.bfloat16, tokens: int | None = None) -> int:
@@ -262,18 +263,18 @@ class QuantMoELayer:
         h, i = shape.hidden, shape.inter
         if quant == _lib.QUANT_FP8_BLOCK:
             q13, s13 = synth.fp8_bank(e, 2 * i, h, device, seed, first_expert)
-            w13 = ops.fp8_prepack(q13, True)
+            w13 = B.fp8_prepack(q13, True)
             del q13
             q2, s2 = synth.fp8_bank(e, h, i, device, seed + 1, first_expert)
-            w2 = ops.fp8_prepack(q2, False)
+            w2 = B.fp8_prepack(q2, False)
             del q2
             kw = dict(w13_scales=s13, w2_scales=s2)
         else:
             p13, s13, g13 = synth.nvfp4_bank(e, 2 * i, h, device, seed, first_expert)
-            w13 = ops.nvfp4_prepack(p13, s13, True)
+            w13 = B.nvfp4_prepack(p13, s13, True)
             del p13, s13
             p2, s2, g2 = synth.nvfp4_bank(e, h, i, device, seed + 1, first_expert)
-            w2 = ops.nvfp4_prepack(p2, s2, False)
+            w2 = B.nvfp4_prepack(p2, s2, False)
             del p2, s2
             kw = dict(w13_global=g13, w2_global=g2)
         shared = None
@@ -284,8 +285,8 @@ class QuantMoELayer:
             q13, s13 = synth.fp8_bank(1, 2 * si, h, device, seed + 2, 0)
             q2, s2 = synth.fp8_bank(1, h, si, device, seed + 3, 0)
             shared = SharedExpert(
-                quant=_lib.QUANT_FP8_BLOCK, inter=si, w13=ops.fp8_prepack(q13[0], True),
-                w2=ops.fp8_prepack(q2[0], False), w13_scales=s13[0], w2_scales=s2[0],
+                quant=_lib.QUANT_FP8_BLOCK, inter=si, w13=B.fp8_prepack(q13[0], True),
+                w2=B.fp8_prepack(q2[0], False), w13_scales=s13[0], w2_scales=s2[0],
             )
         layer = cls(quant=quant, hidden=h, inter=i, num_experts=e, top_k=shape.top_k, w13=w13,
                     w2=w2, shared=shared, **kw)

@@ -27,13 +27,13 @@ def moe_align_block_size(topk_ids, block_size: int, num_experts: int, expert_map
     """
     import torch
 
-    from .. import ops
+    from .._common import b200_ops
 
     ids = topk_ids
     if expert_map is not None:
         ids = expert_map[ids.long()]
     ids = ids.to(torch.int32).contiguous()
-    return ops.moe_align_block_size(ids, int(block_size), int(num_experts))
+    return b200_ops().moe_align_block_size(ids, int(block_size), int(num_experts))
 
 
 _ORIGINAL = None

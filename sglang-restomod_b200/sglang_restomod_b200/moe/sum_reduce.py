@@ -16,9 +16,10 @@ logger = logging.getLogger(__name__)
 
 
 def moe_sum_reduce(input_tensor, output_tensor, routed_scaling_factor=1.0):
-    from .. import ops
+    from .._common import b200_ops
 
-    return ops.moe_sum_reduce(input_tensor, output_tensor, float(routed_scaling_factor))
+    b200_ops().moe_sum_reduce(input_tensor, output_tensor, float(routed_scaling_factor))
+    return output_tensor
 
 
 def install() -> bool:

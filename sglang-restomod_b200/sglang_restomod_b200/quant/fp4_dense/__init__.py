@@ -16,7 +16,7 @@ def prepare_b200_nvfp4_linear(layer) -> None:
     ``weight_scale_2`` fp32 (one value, or one per fused shard - equal)."""
     import torch
 
-    from ... import ops
+    from ..._common import b200_ops
 
     w, s, g = layer.weight, layer.weight_scale, layer.weight_scale_2
     n, half_k = (int(d) for d in w.shape)
@@ -25,19 +25,20 @@ def prepare_b200_nvfp4_linear(layer) -> None:
         # Several fused shards with different global scales: keep the largest
         # and rescale nothing - refuse instead of approximating.
         raise RuntimeError("B200 NVFP4 dense needs one global scale per matrix")
-    layer.b200_nvfp4_packed = ops.nvfp4_prepack(w.data.contiguous(), s.data.contiguous(), gated=False)
+    layer.b200_nvfp4_packed = b200_ops().nvfp4_prepack(w.data.contiguous(), s.data.contiguous(), gated=False)
     layer.b200_nvfp4_global = gs[:1].contiguous()
     layer.b200_nvfp4_shape = (n, 2 * half_k)
 
 
 def apply_b200_nvfp4_linear(layer, x, bias=None):
-    from ... import _lib, ops
+    from ... import _lib
+    from ..._common import b200_ops
 
     n, k = layer.b200_nvfp4_shape
     x_2d = x.reshape(-1, x.shape[-1]).contiguous()
     if x_2d.shape[-1] != k:
         raise RuntimeError(f"B200 NVFP4 dense: activation K {x_2d.shape[-1]} != prepared K {k}")
-    out = ops.linear(x_2d, layer.b200_nvfp4_packed, n, quant=_lib.QUANT_NVFP4,
+    out = b200_ops().linear(x_2d, layer.b200_nvfp4_packed, n, quant=_lib.QUANT_NVFP4,
                      global_scale=layer.b200_nvfp4_global, out_dtype=x.dtype)
     if bias is not None:
         out.add_(bias)

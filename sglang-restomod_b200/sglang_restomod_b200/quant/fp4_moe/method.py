@@ -74,7 +74,7 @@ def prepare_moe_nvfp4(layer, group_size: int | None = None) -> None:
     """Replace the ModelOpt expert layout with the B200 streamed layout."""
     import torch
 
-    from ... import ops
+    from ..._common import b200_ops
 
     if getattr(layer, "params_dtype", torch.bfloat16) not in (torch.bfloat16, torch.float16):
         raise RuntimeError(f"B200 NVFP4 MoE needs bf16 or fp16 activations, got {layer.params_dtype}")
@@ -102,7 +102,7 @@ def prepare_moe_nvfp4(layer, group_size: int | None = None) -> None:
         experts, size_n, half_k = (int(d) for d in weight.shape)
         check_expert_shape(size_n, 2 * half_k)
         gs = _global_scale(getattr(layer, prefix + "_weight_scale_2"), prefix)
-        packed = ops.nvfp4_prepack(weight.data.contiguous(), scales.data.contiguous(), gated=gated)
+        packed = b200_ops().nvfp4_prepack(weight.data.contiguous(), scales.data.contiguous(), gated=gated)
         setattr(packed, _MARK, {"gated": gated, "n": size_n, "k": 2 * half_k, "experts": experts})
         _rebind(layer, prefix + "_weight", packed)
         getattr(layer, prefix + "_weight").__dict__[_MARK] = {
@@ -159,7 +159,8 @@ def moe_wna16_marlin_gemm(
     """
     import torch
 
-    from ... import _lib, ops
+    from ... import _lib
+    from ..._common import b200_ops
 
     if is_ep:
         raise RuntimeError(
@@ -193,7 +194,7 @@ def moe_wna16_marlin_gemm(
     if block not in _SUPPORTED_BLOCKS:
         sorted_ids, e_ids, ntpp, block = _regroup(sorted_ids, e_ids, ntpp, block, routes)
     gated_mode = _lib.GATED_SPLIT if info["gated"] else _lib.GATED_NONE
-    ops.moe_gemm(a.contiguous(), b_q_weight, size_n, quant=_lib.QUANT_NVFP4,
+    b200_ops().moe_gemm(a.contiguous(), b_q_weight, size_n, quant=_lib.QUANT_NVFP4,
                  num_experts=info["experts"], sorted_token_ids=sorted_ids.contiguous(),
                  expert_ids=e_ids.contiguous(), num_tokens_post_pad=ntpp.contiguous(),
                  block_size=block, top_k=int(top_k), num_routes=routes, c=c,

@@ -46,7 +46,7 @@ def _check_activation_k(layer, x_2d) -> None:
 
 def prepare_b200_fp8_linear(layer, gated_silu: bool = False) -> None:
     """Prepack ``layer.weight`` ([N, K] e4m3, scales ``weight_scale_inv``)."""
-    from ... import ops
+    from ..._common import b200_ops
 
     w = layer.weight
     s = layer.weight_scale_inv
@@ -54,7 +54,7 @@ def prepare_b200_fp8_linear(layer, gated_silu: bool = False) -> None:
     _check_dense_weight_shape(n, k, gated=gated_silu)
     if tuple(s.shape) != (n // GROUP, k // GROUP):
         raise RuntimeError(f"B200 FP8 dense scales must be [{n // GROUP}, {k // GROUP}], got {tuple(s.shape)}")
-    layer.b200_fp8_packed = ops.fp8_prepack(w.data.contiguous(), gated=gated_silu)
+    layer.b200_fp8_packed = b200_ops().fp8_prepack(w.data.contiguous(), gated=gated_silu)
     layer.b200_fp8_scales = s.data.float().contiguous()
     layer.b200_fp8_in_features = k
     layer.b200_fp8_out_features = n
@@ -64,7 +64,8 @@ def prepare_b200_fp8_linear(layer, gated_silu: bool = False) -> None:
 def apply_b200_fp8_linear(layer, x, bias=None):
     """``y = x . dequant(W)^T (+ bias)``; the ordinary linear contract (a gated
     bank still returns ``[gate | up]``)."""
-    from ... import _lib, ops
+    from ... import _lib
+    from ..._common import b200_ops
 
     x_2d = x.reshape(-1, x.shape[-1])
     if x_2d.stride(-1) != 1 or not x_2d.is_contiguous():
@@ -72,7 +73,7 @@ def apply_b200_fp8_linear(layer, x, bias=None):
     _check_activation_k(layer, x_2d)
     n = layer.b200_fp8_out_features
     mode_ = _lib.GATED_SPLIT if layer.b200_fp8_gated else _lib.GATED_NONE
-    out = ops.linear(x_2d, layer.b200_fp8_packed, n, quant=_lib.QUANT_FP8_BLOCK,
+    out = b200_ops().linear(x_2d, layer.b200_fp8_packed, n, quant=_lib.QUANT_FP8_BLOCK,
                      scales=layer.b200_fp8_scales, gated_mode=mode_, out_dtype=x.dtype)
     if bias is not None:
         out.add_(bias)
@@ -82,14 +83,15 @@ def apply_b200_fp8_linear(layer, x, bias=None):
 def apply_b200_fp8_fused_silu_and_mul(layer, x):
     """Gate/up projection and ``silu(gate) * up`` in one GEMM (None when the
     layer was not prepared gated)."""
-    from ... import _lib, ops
+    from ... import _lib
+    from ..._common import b200_ops
 
     if not getattr(layer, "b200_fp8_gated", False):
         return None
     x_2d = x.reshape(-1, x.shape[-1]).contiguous()
     _check_activation_k(layer, x_2d)
     n = layer.b200_fp8_out_features
-    out = ops.linear(x_2d, layer.b200_fp8_packed, n, quant=_lib.QUANT_FP8_BLOCK,
+    out = b200_ops().linear(x_2d, layer.b200_fp8_packed, n, quant=_lib.QUANT_FP8_BLOCK,
                      scales=layer.b200_fp8_scales, gated_mode=_lib.GATED_FUSED, out_dtype=x.dtype)
     return out.reshape(*x.shape[:-1], n // 2)
 

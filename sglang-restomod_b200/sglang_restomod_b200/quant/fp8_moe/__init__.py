@@ -52,7 +52,7 @@ class Experts:
 def prepare_experts(weights, scales, *, group_size: int = GROUP,
                     interleave_gated_silu: bool = True) -> Experts:
     """``weights`` ``[E, N, K]`` e4m3, ``scales`` ``[E, N/128, K/128]`` fp32."""
-    from ... import ops
+    from ..._common import b200_ops
 
     experts, n, k = (int(d) for d in weights.shape)
     _check_gemm_shape(k, n, group_size, gated=interleave_gated_silu)
@@ -61,7 +61,7 @@ def prepare_experts(weights, scales, *, group_size: int = GROUP,
             f"B200 FP8 MoE scales must be [{experts}, {n // group_size}, {k // group_size}], "
             f"got {tuple(scales.shape)}"
         )
-    packed = ops.fp8_prepack(weights.contiguous(), gated=interleave_gated_silu)
+    packed = b200_ops().fp8_prepack(weights.contiguous(), gated=interleave_gated_silu)
     return Experts(packed=packed, scales=scales.float().contiguous(), num_experts=experts, k=k,
                    n=n, group_size=group_size, gated=interleave_gated_silu)
 
@@ -79,7 +79,8 @@ def gemm(out, sorted_input, expert_offsets, experts: Experts, *, k, n, gated_sil
     """Expert GEMM over expert-sorted rows into ``out`` (sorted order)."""
     import torch
 
-    from ... import _lib, ops
+    from ... import _lib
+    from ..._common import b200_ops
 
     k, n = int(k), int(n)
     _check_gemm_shape(k, n, experts.group_size, gated=gated_silu)
@@ -94,9 +95,9 @@ def gemm(out, sorted_input, expert_offsets, experts: Experts, *, k, n, gated_sil
     row_expert = torch.searchsorted(offsets[1:].contiguous(),
                                     torch.arange(rows, device=offsets.device, dtype=torch.int32),
                                     right=True).to(torch.int32)
-    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(row_expert, block_size,
+    sorted_ids, expert_ids, ntpp = b200_ops().moe_align_block_size(row_expert, block_size,
                                                             experts.num_experts)
-    ops.moe_gemm(sorted_input.contiguous(), experts.packed, n, quant=_lib.QUANT_FP8_BLOCK,
+    b200_ops().moe_gemm(sorted_input.contiguous(), experts.packed, n, quant=_lib.QUANT_FP8_BLOCK,
                  num_experts=experts.num_experts, sorted_token_ids=sorted_ids,
                  expert_ids=expert_ids, num_tokens_post_pad=ntpp, block_size=block_size, top_k=1,
                  num_routes=rows, c=out, scales=experts.scales,

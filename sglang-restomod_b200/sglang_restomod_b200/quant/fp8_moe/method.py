@@ -58,7 +58,8 @@ class B200Fp8MoEMethod(_Base):
     def process_weights_after_loading(self, layer) -> None:
         import torch
 
-        from ... import _lib, ops
+        from ... import _lib
+        from ..._common import b200_ops
         from ...layer import QuantMoELayer
         from . import _check_gemm_shape
 
@@ -80,8 +81,8 @@ class B200Fp8MoEMethod(_Base):
             )
         _check_gemm_shape(hidden, n13, gated=True)
         _check_gemm_shape(inter, hidden)
-        packed13 = ops.fp8_prepack(w13.data.contiguous(), gated=True)
-        packed2 = ops.fp8_prepack(w2.data.contiguous(), gated=False)
+        packed13 = b200_ops().fp8_prepack(w13.data.contiguous(), gated=True)
+        packed2 = b200_ops().fp8_prepack(w2.data.contiguous(), gated=False)
         scales13 = s13.data.float().contiguous()
         scales2 = s2.data.float().contiguous()
         # Release the checkpoint layout through the parameters themselves (the
