@@ -38,6 +38,25 @@ def b200_ops():
     return torch.ops.b200_moe
 
 
+def rebind_everywhere(attr: str, original, replacement) -> int:
+    """Point every loaded module whose ``attr`` is ``original`` at
+    ``replacement`` (modules that did ``from x import name`` before a hook was
+    installed keep their own reference). Returns how many were rebound."""
+    import sys
+
+    count = 0
+    for module in list(sys.modules.values()):
+        if module is None:
+            continue
+        try:
+            if getattr(module, attr, None) is original:
+                setattr(module, attr, replacement)
+                count += 1
+        except Exception:  # noqa: BLE001 - half-imported or proxy modules
+            continue
+    return count
+
+
 def library_loadable() -> bool:
     try:
         from . import _lib

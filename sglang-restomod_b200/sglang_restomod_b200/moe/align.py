@@ -53,5 +53,9 @@ def register() -> None:
         attest.inactive("moe_align_sm70", f"upstream module not importable: {exc}")
         return
     if _ORIGINAL is None:
+        from .._common import rebind_everywhere
+
         _ORIGINAL = upstream.moe_align_block_size
         upstream.moe_align_block_size = moe_align_block_size
+        # modules that imported the function by name before this ran
+        rebind_everywhere("moe_align_block_size", _ORIGINAL, moe_align_block_size)

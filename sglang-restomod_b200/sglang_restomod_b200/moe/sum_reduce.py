@@ -10,7 +10,6 @@ taking another path.
 from __future__ import annotations
 
 import logging
-import sys
 
 logger = logging.getLogger(__name__)
 
@@ -25,6 +24,8 @@ def moe_sum_reduce(input_tensor, output_tensor, routed_scaling_factor=1.0):
 def install() -> bool:
     """Bind the replacement wherever the installed sgl_kernel lacks the op,
     including modules that imported the name before this ran."""
+    from .._common import rebind_everywhere
+
     try:
         import sgl_kernel
         import sgl_kernel.moe as sgl_moe
@@ -34,12 +35,5 @@ def install() -> bool:
     sgl_kernel.moe_sum_reduce = moe_sum_reduce
     sgl_moe.moe_sum_reduce = moe_sum_reduce
     if original is not None:
-        for module in list(sys.modules.values()):
-            if module is None:
-                continue
-            try:
-                if getattr(module, "moe_sum_reduce", None) is original:
-                    setattr(module, "moe_sum_reduce", moe_sum_reduce)
-            except Exception:  # noqa: BLE001 - partially imported modules
-                continue
+        rebind_everywhere("moe_sum_reduce", original, moe_sum_reduce)
     return True

@@ -1,14 +1,17 @@
-"""Component registry: which hooks this package installs into SGLang.
+"""Which of this package's hooks get installed into SGLang.
 
-The selection variable and the component names are the reference's
-(``sglang_restomod/plugins.py:26-104``), restricted to the quantized MoE and
-decode-GEMM path this package implements, so an existing launch profile
-(``SGLANG_RESTOMOD_COMPONENTS=fp8_moe,fp8_dense,...``) selects the B200
-kernels unchanged. Components outside this path are refused by name.
+A launch profile names components in ``SGLANG_RESTOMOD_COMPONENTS``
+(comma-separated). The variable and the component names are the reference
+plugin's (``sglang_restomod/plugins.py``), restricted to the quantized MoE
+and decode-GEMM path built here, so a profile written for the reference
+selects the B200 kernels unchanged; the reference's other components are
+refused by name with a pointer to why.
 
-Each selected component is imported and registered on its own: a failure is
-recorded in :mod:`.attest` and does not stop the others (SGLang wraps plugin
-loading in ``except Exception``, so a raise would silently drop everything).
+Activation runs one component at a time through three steps - import its
+module, find its ``register()``, call it - and the first step that does not
+succeed decides the component's state in :mod:`.attest`. One component's
+failure never stops the next (SGLang itself swallows plugin exceptions, so a
+raise here would silently drop every component after it).
 """
 
 from __future__ import annotations
@@ -17,11 +20,15 @@ import importlib
 import logging
 import os
 from dataclasses import dataclass
-from typing import Mapping, Sequence
+from typing import Callable, Mapping, Sequence
+
+from . import attest
 
 logger = logging.getLogger(__name__)
 
 ENV_COMPONENTS = "SGLANG_RESTOMOD_COMPONENTS"
+
+_PKG = __name__.rsplit(".", 1)[0]
 
 
 @dataclass(frozen=True)
@@ -30,8 +37,6 @@ class Component:
     module: str
     description: str
 
-
-_PKG = "sglang_restomod_b200"
 
 COMPONENTS: dict[str, Component] = {
     c.name: c
@@ -53,65 +58,71 @@ COMPONENTS: dict[str, Component] = {
     )
 }
 
-# Names the reference also knows but that are outside this path.
-OUT_OF_SCOPE = ("attention_v100", "lsa_sm70", "sm70_marlin_v100", "ple_sm70", "spec_sm70",
-                "gdn_tilelang_sm70")
+# Reference components that are not on this path (refused with that reason).
+NOT_ON_THIS_PATH = frozenset({"attention_v100", "lsa_sm70", "sm70_marlin_v100", "ple_sm70",
+                              "spec_sm70", "gdn_tilelang_sm70"})
+
+
+class UnknownComponent(ValueError):
+    """A selected name this package does not provide."""
+
+
+def parse_selection(text: str) -> list[str]:
+    """Names in ``text`` in first-seen order, blanks and repeats dropped."""
+    return list(dict.fromkeys(part.strip() for part in text.split(",") if part.strip()))
 
 
 def selection(env: Mapping[str, str] | None = None) -> list[str]:
-    """Selected component names, validated and de-duplicated (order kept)."""
-    raw = (env if env is not None else os.environ).get(ENV_COMPONENTS, "")
-    names: list[str] = []
-    for item in raw.split(","):
-        name = item.strip()
-        if name and name not in names:
-            names.append(name)
+    """The selected component names; unknown ones raise :class:`UnknownComponent`."""
+    names = parse_selection((os.environ if env is None else env).get(ENV_COMPONENTS, ""))
     unknown = [n for n in names if n not in COMPONENTS]
-    if unknown:
-        scoped = [n for n in unknown if n in OUT_OF_SCOPE]
-        hint = f" ({', '.join(scoped)} is not part of the B200 MoE/GEMV path)" if scoped else ""
-        raise ValueError(
-            f"unknown component(s) in {ENV_COMPONENTS}: {', '.join(unknown)}{hint}; "
-            f"known: {', '.join(sorted(COMPONENTS))}"
-        )
-    return names
+    if not unknown:
+        return names
+    elsewhere = sorted(set(unknown) & NOT_ON_THIS_PATH)
+    why = (f"; {', '.join(elsewhere)} is not part of the B200 MoE/GEMV path" if elsewhere else "")
+    raise UnknownComponent(
+        f"unknown component(s) in {ENV_COMPONENTS}: {', '.join(unknown)}{why} "
+        f"(this package provides: {', '.join(sorted(COMPONENTS))})")
 
 
 def is_enabled(name: str, env: Mapping[str, str] | None = None) -> bool:
     return name in selection(env)
 
 
-def load_enabled(env: Mapping[str, str] | None = None) -> Sequence[str]:
-    """Import and register every selected component; return the loaded names."""
-    from . import attest
+def _describe(exc: BaseException) -> str:
+    return f"{type(exc).__name__}: {exc}"
 
-    selected = selection(env)
-    attest.set_selected(selected)
-    loaded: list[str] = []
-    for name in selected:
-        comp = COMPONENTS[name]
-        try:
-            module = importlib.import_module(comp.module)
-        except Exception as exc:  # noqa: BLE001 - isolate each component
-            attest.inactive(name, f"import failed: {type(exc).__name__}: {exc}")
-            logger.warning("component %s failed to import", name, exc_info=True)
-            continue
-        register = getattr(module, "register", None)
-        if register is None:
-            attest.inactive(name, f"imported {comp.module} but it has no register()")
-            continue
-        try:
-            register()
-        except Exception as exc:  # noqa: BLE001
-            attest.record(name, False, f"{type(exc).__name__}: {exc}")
-            logger.warning("component %s failed to register", name, exc_info=True)
-            continue
-        attest.record(name, True)
-        loaded.append(name)
-    recorded = attest.snapshot()["components"]
-    for name in sorted(set(selected) - set(recorded)):
-        attest.inactive(name, "selected but never registered")
+
+def activate(component: Component) -> bool:
+    """Import and register one component; its outcome goes to the ledger.
+    True when it registered (it may still have reported itself inactive)."""
+    try:
+        module = importlib.import_module(component.module)
+    except Exception as exc:  # noqa: BLE001 - the next component still loads
+        attest.record(component.name, False, "import failed: " + _describe(exc))
+        logger.warning("component %s: import failed", component.name, exc_info=True)
+        return False
+    register: Callable[[], object] | None = getattr(module, "register", None)
+    if not callable(register):
+        attest.record(component.name, False, f"{component.module} defines no register()")
+        return False
+    try:
+        register()
+    except Exception as exc:  # noqa: BLE001
+        attest.record(component.name, False, _describe(exc))
+        logger.warning("component %s: register() raised", component.name, exc_info=True)
+        return False
+    attest.record(component.name, True)
+    return True
+
+
+def load_enabled(env: Mapping[str, str] | None = None) -> Sequence[str]:
+    """Activate every selected component in order; return the ones that
+    registered. The ledger is written to ``$SGLANG_RESTOMOD_ATTEST`` at the end."""
+    names = selection(env)
+    attest.set_selected(names)
+    registered = [n for n in names if activate(COMPONENTS[n])]
     attest.write()
-    logger.info("sglang-restomod-b200: %d/%d components active (%s)", len(loaded),
-                len(selected), ", ".join(loaded) or "none")
-    return loaded
+    logger.info("sglang-restomod-b200: %d of %d selected components registered (%s)",
+                len(registered), len(names), ", ".join(registered) or "none")
+    return registered

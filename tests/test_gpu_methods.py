@@ -195,3 +195,28 @@ def test_nvfp4_dense(cuda_device):
     want = oracle.nvfp4_linear_ref(x.cpu(), p[0].cpu(), s[0].cpu(), float(gs[0]))
     assert_close(apply_b200_nvfp4_linear(layer, x), want, what="nvfp4 dense")
     assert ops.workspace_status() == 0
+
+
+def test_dense_quant_converts_admitted_linears(cuda_device):
+    """fp8_dense_quant after load: admitted bf16 linears are quantized with the
+    LM-head rule and served by the B200 GEMV; refused ones keep their path."""
+    from sglang_restomod_b200.quant.fp8_dense_quant import quantize_dense_linears
+    from sglang_restomod_b200.quant.fp8_lm_head import _quantize
+
+    torch.manual_seed(0)
+    model = torch.nn.Module()
+    model.up = torch.nn.Linear(512, 768, bias=True)
+    model.odd = torch.nn.Linear(200, 256, bias=False)
+    model.lm_head = torch.nn.Linear(512, 384, bias=False)
+    for p in model.parameters():
+        p.data.normal_(0, 0.02)
+    model = model.to(cuda_device, torch.bfloat16)
+    w_up = model.up.weight.detach().clone()
+    outcome = quantize_dense_linears(model)
+    assert outcome["converted"] == 1 and outcome["lm_head"] == 1 and outcome["shape:256x200"] == 1
+    assert model.up.weight.numel() == 0 and model.lm_head.weight.numel() > 0
+    x = synth.activations(3, 512, cuda_device, seed=9)
+    y = model.up(x)
+    q, s = _quantize(w_up.to(torch.float16))
+    want = oracle.fp8_linear_ref(x.cpu(), q.cpu(), s.cpu()) + model.up.bias.float().cpu()
+    assert_close(y, want, what="converted linear")

@@ -203,3 +203,99 @@ def test_dense_split_rule_matches_the_measured_choices():
     assert dense_k_parts(128, 7168, 2048, 148) == 1    # shared expert down
     assert dense_k_parts(64, 5120, 25600, 148) == 7
     assert dense_k_parts(64, 152064, 5120, 148) == 1   # partials beyond the workspace
+
+
+# ------------------------------------------------ fp8_dense_quant admission
+def test_dense_quant_admission_reasons():
+    from sglang_restomod_b200.quant.fp8_dense_quant import refusal
+
+    class ReplicatedLinear(torch.nn.Linear):
+        pass
+
+    lin = torch.nn.Linear(256, 384, bias=False).to(torch.bfloat16)
+    assert refusal("model.layers.0.mlp.down_proj", lin) is None
+    assert refusal("", lin) == "unnamed"
+    assert refusal("model.layers.0.mlp.experts.w2", lin) == "expert"
+    assert refusal("model.layers.0.mlp.shared_experts.down_proj", lin) == "expert"
+    assert refusal("lm_head", lin) == "lm_head"
+    assert refusal("model.gate", ReplicatedLinear(256, 384).to(torch.bfloat16)) == "router"
+    assert refusal("x", torch.nn.Linear(256, 384)) == "dtype"  # fp32
+    assert refusal("x", torch.nn.Linear(200, 384).to(torch.bfloat16)) == "shape:384x200"
+    assert refusal("x", torch.nn.LayerNorm(256).to(torch.bfloat16)) == "no-2d-weight"
+
+    class EngineLinear(torch.nn.Module):  # duck-typed engine linear
+        def __init__(self, method):
+            super().__init__()
+            self.weight = torch.nn.Parameter(torch.zeros(256, 256, dtype=torch.bfloat16))
+            self.quant_method = method
+            self.input_size_per_partition = 256
+
+    class UnquantizedLinearMethod:
+        pass
+
+    class Fp8LinearMethod:
+        pass
+
+    assert refusal("a.b", EngineLinear(UnquantizedLinearMethod())) is None
+    assert refusal("a.b", EngineLinear(Fp8LinearMethod())) == "quantized:Fp8LinearMethod"
+
+
+def test_dense_quant_hooks_load_model_once():
+    from sglang_restomod_b200.quant.fp8_dense_quant import hook_load_model
+
+    seen = []
+
+    class Runner:
+        def load_model(self):
+            self.model = "the model"
+            return "loaded"
+
+    assert hook_load_model(Runner, convert_all=lambda m: seen.append(m) or {"converted": 1})
+    assert not hook_load_model(Runner, convert_all=lambda m: seen.append(("again", m)))
+    assert Runner().load_model() == "loaded"
+    assert seen == ["the model"]
+
+    class Broken:
+        def load_model(self):
+            self.model = None
+
+    hook_load_model(Broken, convert_all=lambda m: 1 / 0)
+    Broken().load_model()  # a failing conversion leaves the server up
+
+
+def test_rebind_reaches_modules_that_imported_the_name(monkeypatch):
+    import sys
+    import types
+
+    from sglang_restomod_b200._common import rebind_everywhere
+
+    def original():
+        return "upstream"
+
+    def replacement():
+        return "b200"
+
+    consumer = types.ModuleType("fake_consumer_of_align")
+    consumer.moe_align_block_size = original
+    monkeypatch.setitem(sys.modules, "fake_consumer_of_align", consumer)
+    other = types.ModuleType("fake_unrelated")
+    other.moe_align_block_size = lambda: "someone else's"
+    monkeypatch.setitem(sys.modules, "fake_unrelated", other)
+    assert rebind_everywhere("moe_align_block_size", original, replacement) == 1
+    assert consumer.moe_align_block_size is replacement
+    assert other.moe_align_block_size() == "someone else's"
+
+
+def test_attest_failure_overrides_inactive_and_write_is_atomic(tmp_path):
+    attest.set_selected(["a", "b", "c"])
+    attest.inactive("a", "no GPU")
+    attest.record("a", False, "RuntimeError: boom")
+    attest.record("b", True)
+    snap = attest.snapshot()
+    assert snap["failed"] == ["a"] and snap["loaded"] == ["b"] and snap["missing"] == ["c"]
+    assert snap["components"]["a"] == {"ok": False, "detail": "RuntimeError: boom"}
+    path = tmp_path / "out.json"
+    assert attest.write(str(path)) == str(path)
+    assert json.loads(path.read_text())["selected"] == ["a", "b", "c"]
+    assert [p.name for p in tmp_path.iterdir()] == ["out.json"]
+    assert attest.write(str(tmp_path / "missing-dir" / "x.json")) is None
