@@ -639,6 +639,7 @@ def sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse=None):
     point = {
         "ms_per_step": step_ms, "tokens_per_s": wl.tokens / (step_ms * 1e-3),
         "layer_hbm_frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm_gbs,
+        "layer_tensor_frac": step_flops / (step_ms * 1e-3) / 1e12 / bf16_tflops,
         "dominant": dom_name, "dominant_us": dom_ms * 1e3,
         "bound": "tensor" if prefill else "hbm",
         "frac": tensor_frac if prefill else hbm_frac,
@@ -649,6 +650,104 @@ def sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse=None):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return point
+
+
+def measure_fp8_peak(device) -> float:
+    """Dense FP8 tensor peak on this GPU: cuBLASLt e4m3 GEMM (torch._scaled_mm)
+    at 8192^3, best of 10, CUDA events (TFLOP/s)."""
+    import torch
+
+    n = 8192
+    a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=device)
+    for _ in range(3):
+        torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    best = float("inf")
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        start.record()
+        torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        end.record()
+        torch.cuda.synchronize()
+        best = min(best, start.elapsed_time(end))
+    del a, b
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def w8a8_points(args, device, fp8_tflops, bf16_tflops):
+    """The opt-in W8A8 block-FP8 GEMMs (quantized activations) at prefill
+    shapes: the config-2 gate/up expert GEMM at 8192 tokens (blocks of 64) and
+    a dense 8192 x 7168 x 4096 GEMM; kernel time per call including the
+    activation quantization, CUDA graph replay, CUDA events."""
+    import torch
+
+    from sglang_restomod_b200 import _lib, ops, synth
+
+    out = {}
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / reps
+        del g
+        return ms
+
+    reps = max(20, min(args.steps, 100))
+    shape = synth.CONFIG2
+    tokens = 8192
+    ids, _ = synth.route(tokens, shape.experts, shape.top_k, device, seed=200)
+    x = synth.activations(tokens, shape.hidden, device, seed=100)
+    q, s = synth.fp8_bank(shape.experts, 2 * shape.inter, shape.hidden, device, seed=10)
+    sorted_ids, expert_ids, ntpp = ops.moe_align_block_size(ids, 64, shape.experts)
+    routes = tokens * shape.top_k
+    c = torch.empty(routes, shape.inter, dtype=torch.float16, device=device)
+
+    def moe():
+        ops.w8a8_moe_gemm(x, q, s, num_experts=shape.experts, sorted_token_ids=sorted_ids,
+                          expert_ids=expert_ids, num_tokens_post_pad=ntpp, block_size=64,
+                          top_k=shape.top_k, num_routes=routes, c=c,
+                          gated_mode=_lib.GATED_FUSED)
+
+    ms = timed(moe, reps)
+    flops = 2 * routes * 2 * shape.inter * shape.hidden
+    out["config2-T8192-gateup"] = {
+        "us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12,
+        "fp8_frac": flops / (ms * 1e-3) / 1e12 / fp8_tflops,
+        "bf16_frac": flops / (ms * 1e-3) / 1e12 / bf16_tflops}
+    del q, s, c, x
+    m, k, n = 8192, 7168, 4096
+    qd, sd = synth.fp8_bank(1, n, k, device, seed=3)
+    xd = synth.activations(m, k, device, seed=4)
+    yd = torch.empty(m, n // 2, dtype=torch.bfloat16, device=device)
+
+    def dense():
+        ops.w8a8_linear(xd, qd[0], sd[0], gated_mode=_lib.GATED_FUSED, out=yd)
+
+    ms = timed(dense, reps)
+    flops = 2 * m * n * k
+    out["dense-8192x7168x4096-gated"] = {
+        "us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12,
+        "fp8_frac": flops / (ms * 1e-3) / 1e12 / fp8_tflops,
+        "bf16_frac": flops / (ms * 1e-3) / 1e12 / bf16_tflops}
+    del qd, sd, xd, yd
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_sweep(args, device, hbm_gbs, bf16_tflops, reuse_config4=None):
@@ -664,6 +763,12 @@ def run_sweep(args, device, hbm_gbs, bf16_tflops, reuse_config4=None):
             out[name] = sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse)
         except Exception as exc:  # noqa: BLE001 - a failed point is reported, not fatal
             out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    try:
+        fp8 = measure_fp8_peak(device)
+        out["w8a8"] = {"fp8_peak_tflops": fp8, "fp8_peak_source": "torch._scaled_mm 8192^3 here",
+                       **w8a8_points(args, device, fp8, bf16_tflops)}
+    except Exception as exc:  # noqa: BLE001
+        out["w8a8"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     return out
 
 

@@ -317,6 +317,58 @@ int b200_moe_layer_forward_logits(int32_t quant, const void* x, int32_t x_dtype,
                                   int32_t shared_dtype, void* out, int32_t out_dtype,
                                   void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ------------------------------------------- W8A8 block FP8 (opt-in path) */
+
+/*
+ * FP8 x FP8 prefill GEMMs on the tcgen05 tensor cores (kind::f8f6f4). The
+ * reference has no such path (its FP8 linears and experts are W8A16:
+ * quant/sm70_fp8_dense/_method.py:713-863 and the TurboMind expert GEMM of
+ * quant/sm70_fp8_moe/method.py:303-304); this is upstream SGLang's
+ * block-FP8 W8A8 arithmetic: activations quantized per (row, 128-K group) to
+ * e4m3 with scale = max(amax / 448, 1e-8) (the block rule of
+ * quant/sm70_fp8_lm_head/__init__.py:33-41), the checkpoint's e4m3 weights
+ * with fp32 scales per 128x128 block, y = sum over 128-K blocks of
+ * sa * sw * (qa . qw), fp32 accumulation. Quantizing the activations changes
+ * results against the W8A16 entry points, so these are separate calls.
+ * Weights are the checkpoint's ROW-MAJOR e4m3 [E][N][K] (no prepack); a
+ * gate/up bank keeps its [gate | up] row order and gated_mode
+ * B200_GATED_FUSED yields silu(gate) * up, N / 2 wide (B200_GATED_SPLIT and
+ * B200_GATED_NONE both give all N rows). K % 128 == 0, N % 128 == 0.
+ */
+
+/* Workspace of b200_w8a8_linear (slots = M) or b200_w8a8_moe_gemm (slots =
+ * expert_capacity * block_size); zero-filled before first use. */
+int64_t b200_w8a8_workspace_bytes(int64_t slots, int64_t k);
+
+/* Per-(row, 128-K group) quantization of x [rows, k] (bf16 / f16): q [rows, k]
+ * e4m3, scales[(k / 128) * scales_ld] fp32 with scale of (row r, group g) at
+ * g * scales_ld + r ("column-major" scales, scales_ld >= rows). Replaces
+ * upstream SGLang's per_token_group_quant_fp8 (group 128). */
+int b200_fp8_act_quant(const void* x, int32_t x_dtype, int64_t rows, int64_t k, uint8_t* q,
+                       float* scales, int64_t scales_ld, void* stream);
+
+/* Dense y [m, n or n/2] = W8A8(x [m, k], w). Replaces, opt-in, the W8A16
+ * apply_sm70_turbomind_fp8_linear (quant/sm70_fp8_dense/_method.py:713-784). */
+int b200_w8a8_linear(const void* x, int32_t x_dtype, int64_t m, int64_t k, const uint8_t* w_e4m3,
+                     const float* w_scales, int64_t n, int32_t gated_mode, void* y,
+                     int32_t y_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Grouped expert GEMM with the routing of b200_moe_gemm
+ * (moe_wna16_marlin_gemm semantics: slot p of block b multiplies activation
+ * row sorted_token_ids[p] / top_k by expert expert_ids[b] and writes output
+ * row sorted_token_ids[p], times topk_weights when mul_topk_weights), W8A8:
+ * the activations are quantized straight into slot order first. Replaces,
+ * opt-in, the W8A16 TurboMind expert GEMM (quant/sm70_fp8_moe/method.py:
+ * 303-304). */
+int b200_w8a8_moe_gemm(const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+                       const uint8_t* w_e4m3, const float* w_scales, int32_t num_experts,
+                       int64_t n, int32_t gated_mode, const int32_t* sorted_token_ids,
+                       const int32_t* expert_ids, int64_t expert_capacity,
+                       const int32_t* num_tokens_post_pad, int32_t block_size, int32_t top_k,
+                       int64_t num_routes, const float* topk_weights, int32_t mul_topk_weights,
+                       void* c, int32_t c_dtype, int64_t ldc, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
 /* ---------------------------------------- expert parallelism (peer memory) */
 
 /*

@@ -54,8 +54,13 @@ from .nvfp4 import (
     quantize_nvfp4,
 )
 from .router import route_topk, route_topk_general
+from .w8a8 import act_dequant_fp8, act_quant_fp8, quantized_activations, w8a8_linear_ref
 
 __all__ = [
+    "act_dequant_fp8",
+    "act_quant_fp8",
+    "quantized_activations",
+    "w8a8_linear_ref",
     "E2M1_GRID",
     "dequant_block_fp8",
     "dequant_nvfp4",

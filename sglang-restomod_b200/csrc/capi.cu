@@ -1215,3 +1215,189 @@ int b200_ep_combine(int64_t tokens, int64_t hidden, const int32_t* topk_ids, int
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- W8A8 block FP8 (opt-in)
+
+namespace {
+
+// Scale rows per 128-K group: the activation rows (or slots) rounded up to 4
+// (16-byte aligned bulk copies) plus one item of slack (a 128-row copy that
+// starts at the last slot).
+int64_t w8_scale_ld(int64_t slots) { return (slots + 3) / 4 * 4 + 128; }
+
+struct W8Ws {
+  uint8_t* q;
+  float* scales;
+  int64_t ld;
+};
+
+bool carve_w8(WsView& ws, int64_t slots, int64_t k, W8Ws& out) {
+  const int64_t ld = w8_scale_ld(slots);
+  const int64_t need = align_up(slots * k) + align_up((k / 128) * ld * 4);
+  if (need > ws.scratch_bytes) return false;
+  out.q = ws.scratch;
+  out.scales = reinterpret_cast<float*>(ws.scratch + align_up(slots * k));
+  out.ld = ld;
+  return true;
+}
+
+int check_w8_weights(int64_t n, int64_t k, int32_t gated_mode) {
+  int rc = check_weight_shape(B200_QUANT_FP8_BLOCK, n, k, gated_mode);
+  if (rc) return rc;
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t b200_w8a8_workspace_bytes(int64_t slots, int64_t k) {
+  if (slots < 0 || k <= 0 || k % 128) return -1;
+  return stream_ws_bytes() + align_up(slots * k) + align_up((k / 128) * w8_scale_ld(slots) * 4);
+}
+
+int b200_fp8_act_quant(const void* x, int32_t x_dtype, int64_t rows, int64_t k, uint8_t* q,
+                       float* scales, int64_t scales_ld, void* stream) {
+  if (!valid_dtype16(x_dtype)) return fail(B200_ERR_UNSUPPORTED, "x must be bf16 or f16");
+  if (rows < 0 || rows >= (1ll << 31) || k <= 0 || k % 128 || k >= (1ll << 31))
+    return fail(B200_ERR_INVALID, "needs K a multiple of the 128-wide quantization group, got K=%lld",
+                (long long)k);
+  if (scales_ld < rows) return fail(B200_ERR_INVALID, "scales_ld %lld < rows %lld",
+                                    (long long)scales_ld, (long long)rows);
+  if (rows == 0) return B200_OK;
+  if (x == nullptr || q == nullptr || scales == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if ((reinterpret_cast<uintptr_t>(x) & 7u) || (reinterpret_cast<uintptr_t>(q) & 3u) ||
+      (reinterpret_cast<uintptr_t>(scales) & 3u))
+    return fail(B200_ERR_INVALID, "x must be 8-byte aligned, q and scales 4-byte aligned");
+  return check_cuda(launch_fp8_act_quant(x, x_dtype == B200_DTYPE_F16, rows, (int)k, nullptr, 1,
+                                         0, rows, q, scales, scales_ld, nullptr,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                    "activation quantization launch");
+}
+
+int b200_w8a8_linear(const void* x, int32_t x_dtype, int64_t m, int64_t k, const uint8_t* w_e4m3,
+                     const float* w_scales, int64_t n, int32_t gated_mode, void* y,
+                     int32_t y_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_w8_weights(n, k, gated_mode);
+  if (rc) return rc;
+  if (!valid_dtype16(x_dtype) || !valid_dtype16(y_dtype))
+    return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
+  if (m < 0 || m >= (1ll << 31)) return fail(B200_ERR_INVALID, "bad M %lld", (long long)m);
+  if (m == 0) return B200_OK;
+  if (x == nullptr || w_e4m3 == nullptr || w_scales == nullptr || y == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (!aligned16(x) || !aligned16(w_e4m3))
+    return fail(B200_ERR_INVALID, "x and weights must be 16-byte aligned");
+  WsView ws;
+  W8Ws w8;
+  if (!carve(workspace, workspace_bytes, ws) || !carve_w8(ws, m, k, w8))
+    return fail(B200_ERR_INVALID, "workspace smaller than b200_w8a8_workspace_bytes(%lld, %lld)",
+                (long long)m, (long long)k);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = check_cuda(launch_fp8_act_quant(x, x_dtype == B200_DTYPE_F16, m, (int)k, nullptr, 1, 0, m,
+                                       w8.q, w8.scales, w8.ld, ws.status, st),
+                  "activation quantization launch");
+  if (rc) return rc;
+  W8Launch L{};
+  L.w = w_e4m3;
+  L.wscale = w_scales;
+  L.xq = w8.q;
+  L.xscale = w8.scales;
+  L.xs_ld = w8.ld;
+  L.rows = m;
+  L.E = 1;
+  L.N = (int)n;
+  L.K = (int)k;
+  L.gated = gated_mode == B200_GATED_FUSED;
+  L.out = y;
+  L.ldo = gated_mode == B200_GATED_FUSED ? n / 2 : n;
+  L.out_f16 = y_dtype == B200_DTYPE_F16;
+  L.status = ws.status;
+  return check_cuda(launch_w8a8_gemm(L, st), "W8A8 GEMM launch");
+}
+
+int b200_w8a8_moe_gemm(const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+                       const uint8_t* w_e4m3, const float* w_scales, int32_t num_experts,
+                       int64_t n, int32_t gated_mode, const int32_t* sorted_token_ids,
+                       const int32_t* expert_ids, int64_t expert_capacity,
+                       const int32_t* num_tokens_post_pad, int32_t block_size, int32_t top_k,
+                       int64_t num_routes, const float* topk_weights, int32_t mul_topk_weights,
+                       void* c, int32_t c_dtype, int64_t ldc, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
+  int rc = check_w8_weights(n, k, gated_mode);
+  if (rc) return rc;
+  if (!valid_dtype16(a_dtype) || !valid_dtype16(c_dtype))
+    return fail(B200_ERR_UNSUPPORTED, "activations and output must be bf16 or f16");
+  if (block_size != 8 && block_size != 16 && block_size != 32 && block_size != 64 &&
+      block_size != 128 && block_size != 256)
+    return fail(B200_ERR_UNSUPPORTED, "block_size must be 8, 16, 32, 64, 128 or 256, got %d",
+                block_size);
+  if (num_experts <= 0 || num_experts >= (1 << 23))
+    return fail(B200_ERR_INVALID, "num_experts must be in [1, 2^23)");
+  if (top_k <= 0) return fail(B200_ERR_INVALID, "top_k must be positive");
+  if (a_rows < 0 || num_routes < 0 || num_routes >= (1ll << 31) || expert_capacity < 0)
+    return fail(B200_ERR_INVALID, "bad row counts");
+  const int64_t out_cols = gated_mode == B200_GATED_FUSED ? n / 2 : n;
+  if (ldc < out_cols) return fail(B200_ERR_INVALID, "ldc %lld < output width %lld",
+                                  (long long)ldc, (long long)out_cols);
+  if (expert_capacity == 0 || num_routes == 0 || a_rows == 0) return B200_OK;
+  if (a == nullptr || w_e4m3 == nullptr || w_scales == nullptr || c == nullptr ||
+      sorted_token_ids == nullptr || expert_ids == nullptr || num_tokens_post_pad == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  if (mul_topk_weights && topk_weights == nullptr)
+    return fail(B200_ERR_INVALID, "mul_topk_weights needs topk_weights");
+  if (!aligned16(a) || !aligned16(w_e4m3))
+    return fail(B200_ERR_INVALID, "activations and weights must be 16-byte aligned");
+  const int64_t slots = expert_capacity * block_size;
+  if (slots >= (1ll << 31)) return fail(B200_ERR_INVALID, "too many route slots");
+  const int plan_per_group = block_size > w8a8_item_slots() ? 2 : 1;
+  if (expert_capacity * plan_per_group > kTcPlanCap)
+    return fail(B200_ERR_UNSUPPORTED, "more than %d route-slot groups", kTcPlanCap / plan_per_group);
+  WsView ws;
+  W8Ws w8;
+  if (!carve(workspace, workspace_bytes, ws) || !carve_w8(ws, slots, k, w8))
+    return fail(B200_ERR_INVALID, "workspace smaller than b200_w8a8_workspace_bytes(%lld, %lld)",
+                (long long)slots, (long long)k);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Activations quantized straight into slot order (padding slots zero).
+  rc = check_cuda(launch_fp8_act_quant(a, a_dtype == B200_DTYPE_F16, a_rows, (int)k,
+                                       sorted_token_ids, top_k, num_routes, slots, w8.q,
+                                       w8.scales, w8.ld, ws.status, st),
+                  "activation quantization launch");
+  if (rc) return rc;
+  StreamParams pp{};
+  pp.expert_ids = expert_ids;
+  pp.ntpp = num_tokens_post_pad;
+  pp.block_m = block_size;
+  pp.max_groups = expert_capacity;
+  pp.E = num_experts;
+  rc = check_cuda(launch_tc_plan_slots(pp, ws.plan, kTcPlanCap, w8a8_item_slots(), st),
+                  "W8A8 plan launch");
+  if (rc) return rc;
+  W8Launch L{};
+  L.w = w_e4m3;
+  L.wscale = w_scales;
+  L.xq = w8.q;
+  L.xscale = w8.scales;
+  L.xs_ld = w8.ld;
+  L.rows = slots;
+  L.sorted_ids = sorted_token_ids;
+  L.ntpp = num_tokens_post_pad;
+  L.num_routes = (int)num_routes;
+  L.topk_w = topk_weights;
+  L.mul_w = mul_topk_weights != 0;
+  L.E = num_experts;
+  L.N = (int)n;
+  L.K = (int)k;
+  L.gated = gated_mode == B200_GATED_FUSED;
+  L.out = c;
+  L.ldo = ldc;
+  L.out_f16 = c_dtype == B200_DTYPE_F16;
+  L.status = ws.status;
+  L.plan_buf = ws.plan;
+  L.plan_cap = (int)(expert_capacity * plan_per_group);
+  return check_cuda(launch_w8a8_gemm(L, st), "W8A8 GEMM launch");
+}
+
+}  // extern "C"

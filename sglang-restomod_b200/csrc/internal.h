@@ -74,6 +74,10 @@ int64_t tc_plan_bytes(int cap);
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream);
 cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
                            cudaStream_t stream);
+// The same plan with items of at most max_slots route slots (blocks larger
+// than max_slots are cut in half first).
+cudaError_t launch_tc_plan_slots(const StreamParams& p, void* plan_buf, int cap, int max_slots,
+                                 cudaStream_t stream);
 // After a dense tcgen05 GEMM with ksplit > 1: fp32 sums in p.ws -> output
 // (SiLU*up for a fused gated bank), and the sums back to zero.
 cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream);
@@ -187,6 +191,43 @@ cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long l
                               int top_k, const int* topk_ids, int num_experts, float scale,
                               const void* shared_out, int shared_f16, void* out, int out_f16,
                               cudaStream_t stream);
+
+// W8A8 block-FP8 GEMM (w8a8.cu): e4m3 weights [E][N][K] row-major with fp32
+// scales per 128x128 block, times e4m3 activations [rows][K] with fp32 scales
+// per (row, 128-K group) stored [K/128][xs_ld]. Dense (sorted_ids == nullptr):
+// output row = activation row. Moe: activation rows are route slots in
+// moe_align order, items from launch_tc_plan_slots(.., w8a8_item_slots()),
+// output row = route id (times topk_w[route] when mul_w). gated: the bank is
+// [gate | up] and the output is silu(gate) * up, N / 2 wide.
+struct W8Launch {
+  const uint8_t* w;
+  const float* wscale;
+  const uint8_t* xq;
+  const float* xscale;
+  long long xs_ld;
+  long long rows;
+  const int* sorted_ids;
+  const int* ntpp;
+  int num_routes;
+  const float* topk_w;
+  int mul_w;
+  int E, N, K, gated;
+  void* out;
+  long long ldo;
+  int out_f16;
+  int* status;
+  const void* plan_buf;  // moe mode: the plan (count + entries)
+  int plan_cap;          // moe mode: plan entries the buffer holds
+};
+cudaError_t launch_w8a8_gemm(const W8Launch& L, cudaStream_t stream);
+int w8a8_item_slots();
+// Per (row, 128-K group) e4m3 quantization: q [out_rows][K], scales
+// [K/128][ld] (rows out_rows .. ld-1 zeroed). ids != nullptr: row s quantizes
+// activation row ids[s] / top_k (zeros for padding ids >= num_routes).
+cudaError_t launch_fp8_act_quant(const void* x, int x_f16, long long x_rows, int K,
+                                 const int* ids, int top_k, long long num_routes,
+                                 long long out_rows, uint8_t* q, float* scales, long long ld,
+                                 int* status, cudaStream_t stream);
 
 // Records `message` as this thread's b200_last_error() and returns `code`.
 int set_last_error(int code, const char* message);

@@ -51,9 +51,13 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "tcgen05.cuh"
 
 namespace b200 {
 namespace {
+
+using namespace tcg;
+using namespace tcg_host;
 
 constexpr int kNMax = 192;  // route slots (MMA N) per item
 // 16 warps: four per SM sub-partition, so each thread may hold 128 registers.
@@ -97,29 +101,12 @@ struct Ctl {
 static_assert(sizeof(Ctl) <= 1024, "control block");
 static_assert(kTcSmem <= 232448, "shared memory");
 
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO),
-  // LBO field 1 (unused by swizzled K-major), version 1, layout type 2.
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
-  return d;
-}
 
 __device__ __forceinline__ uint32_t instr_desc_f16(int n) {
   // f32 accumulate, A/B f16, both K-major, M = 128, N = n.
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
 
 // D[tmem] (+)= A[tmem] . B[smem descriptor]^T
 __device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
@@ -134,39 +121,8 @@ __device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_
       : "memory");
 }
 
-// One lane of the (fully active) warp; the others get false.
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n"
-      "  .reg .b32 rx;\n"
-      "  .reg .pred px;\n"
-      "  elect.sync rx|px, %1;\n"
-      "  @px mov.s32 %0, 1;\n"
-      "}\n"
-      : "+r"(pred)
-      : "r"(0xffffffffu));
-  return pred != 0;
-}
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 // Lane i of the warp writes v[0..31] to lane (taddr.lane + i), columns
 // taddr.col .. +31; returns once the stores have completed.
@@ -189,15 +145,6 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int c16) {
   return (uint32_t)row * 128u + (uint32_t)((c16 ^ (row & 7)) << 4);
 }
 
-// 2-D tiled TMA load of one box at (x, y); completion as transaction bytes.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Bounded wait that also gives up once another role of the CTA has aborted.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
@@ -1018,12 +965,18 @@ bool tc_gemm_supported(int block) {
 
 int tc_plan_slots_per_group(int block) { return block > kNMax ? 2 : 1; }
 
-cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream) {
+cudaError_t launch_tc_plan_slots(const StreamParams& p, void* plan_buf, int cap, int max_slots,
+                                cudaStream_t stream) {
   int* count = reinterpret_cast<int*>(plan_buf);
   int2* plan = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(plan_buf) + 256);
-  const int vblock = p.block_m > kNMax ? p.block_m / 2 : p.block_m;
+  const int vblock = p.block_m > max_slots ? p.block_m / 2 : p.block_m;
+  if (vblock > max_slots || vblock <= 0) return cudaErrorInvalidValue;
   return launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, stream, p.expert_ids, p.ntpp,
-                    p.block_m, vblock, p.max_groups, p.E, kNMax / vblock, plan, count, cap);
+                    p.block_m, vblock, p.max_groups, p.E, max_slots / vblock, plan, count, cap);
+}
+
+cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream) {
+  return launch_tc_plan_slots(p, plan_buf, cap, kNMax, stream);
 }
 
 cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
@@ -1035,46 +988,6 @@ cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
   return launch_pdl(tc_split_finish_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, p);
 }
 
-namespace {
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// dependency on libcuda).
-EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
-// 2-D map over `rows` rows of `row_bytes` (stride `stride` bytes), box
-// `box_x` elements x `box_y` rows, 128-byte swizzle.
-bool make_map(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base,
-              unsigned long long row_elems, unsigned long long rows, unsigned long long stride,
-              unsigned box_x, unsigned box_y, CUtensorMapL2promotion promo) {
-  EncodeTiledFn fn = encode_tiled();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {row_elems, rows};
-  const cuuint64_t strides[1] = {stride};
-  const cuuint32_t box[2] = {box_x, box_y};
-  const cuuint32_t estr[2] = {1, 1};
-  (void)elem_bytes;
-  return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-}  // namespace
 
 // Operands are f16: FP8 weights dequantized as f16(e4m3 * m) with the
 // scale's power of two applied to the fp32 accumulator, NVFP4 weights as

@@ -116,6 +116,21 @@ SIGNATURES = {
          c_void_p, c_void_p, c_void_p, c_int32, c_float, c_void_p, c_int32, c_void_p, c_int32,
          c_void_p, c_int64, c_void_p],
     ),
+    "b200_w8a8_workspace_bytes": (c_int64, [c_int64, c_int64]),
+    "b200_fp8_act_quant": (
+        c_int32, [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p]
+    ),
+    "b200_w8a8_linear": (
+        c_int32,
+        [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_void_p,
+         c_int32, c_void_p, c_int64, c_void_p],
+    ),
+    "b200_w8a8_moe_gemm": (
+        c_int32,
+        [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_int32, c_int64, c_int32,
+         c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_int32,
+         c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p],
+    ),
     "b200_ep_region_bytes": (c_int64, [c_int32, c_int64, c_int32, c_int64]),
     "b200_ep_region_layout": (c_int32, [c_int32, c_int64, c_int32, c_int64, ctypes.POINTER(c_int64)]),
     "b200_ipc_get_handle": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),

@@ -575,3 +575,87 @@ def region_status(region: torch.Tensor, reset: bool = True) -> int:
     _lib.check(lib().b200_workspace_status(_vp(region), ctypes.byref(bits), int(reset),
                                            _stream(region.device)))
     return int(bits.value)
+
+
+# ------------------------------------------- W8A8 block FP8 (opt-in path)
+# FP8 x FP8 on the tensor cores; the activations are quantized per (row,
+# 128-K group), so results differ from the W8A16 ops above. Weights are the
+# checkpoint's row-major e4m3 [E, N, K] with fp32 scales [E, N/128, K/128].
+def w8a8_workspace_bytes(slots: int, k: int) -> int:
+    n = int(lib().b200_w8a8_workspace_bytes(int(slots), int(k)))
+    if n < 0:
+        raise ValueError(f"bad W8A8 workspace shape slots={slots} k={k}")
+    return n
+
+
+def fp8_act_quant(x: torch.Tensor, scales_ld: int | None = None):
+    """(q e4m3 [rows, K], scales fp32 [K/128, scales_ld]) of bf16/f16 ``x``:
+    scale = max(amax / 448, 1e-8) per (row, 128-K group)."""
+    _contig(x, "x")
+    rows, k = (int(d) for d in x.shape)
+    ld = rows if scales_ld is None else int(scales_ld)
+    q = torch.empty(rows, k, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(k // 128, ld, dtype=torch.float32, device=x.device)
+    _lib.check(lib().b200_fp8_act_quant(_vp(x), _code(x, "x"), rows, k, _vp(q), _vp(s), ld,
+                                        _stream(x.device)))
+    return q, s
+
+
+def _w8_weights(w: torch.Tensor, w_scales: torch.Tensor):
+    _contig(w, "weight")
+    _contig(w_scales, "weight scales")
+    if w.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"W8A8 weights must be float8_e4m3fn, got {w.dtype}")
+    if w_scales.dtype != torch.float32:
+        raise TypeError(f"W8A8 weight scales must be float32, got {w_scales.dtype}")
+
+
+def w8a8_linear(x: torch.Tensor, w: torch.Tensor, w_scales: torch.Tensor, *,
+                gated_mode: int = _lib.GATED_NONE, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``y = W8A8(x, W)`` with W row-major e4m3 ``[N, K]`` and scales ``[N/128, K/128]``."""
+    _contig(x, "x")
+    _w8_weights(w, w_scales)
+    x2 = x.reshape(-1, x.shape[-1])
+    m, k = (int(d) for d in x2.shape)
+    n = int(w.shape[-2])
+    cols = n // 2 if gated_mode == _lib.GATED_FUSED else n
+    if out is None:
+        out = torch.empty(m, cols, dtype=out_dtype or x.dtype, device=x.device)
+    ws = workspace(w8a8_workspace_bytes(m, k), x.device)
+    _lib.check(
+        lib().b200_w8a8_linear(_vp(x2), _code(x2, "x"), m, k, _vp(w), _vp(w_scales), n, gated_mode,
+                               _vp(out), _code(out, "out"), _vp(ws), ws.numel(), _stream(x.device))
+    )
+    return out.reshape(*x.shape[:-1], cols)
+
+
+def w8a8_moe_gemm(a: torch.Tensor, w: torch.Tensor, w_scales: torch.Tensor, *, num_experts: int,
+                  sorted_token_ids: torch.Tensor, expert_ids: torch.Tensor,
+                  num_tokens_post_pad: torch.Tensor, block_size: int, top_k: int, num_routes: int,
+                  c: torch.Tensor, topk_weights: torch.Tensor | None = None,
+                  mul_topk_weights: bool = False, gated_mode: int = _lib.GATED_NONE) -> torch.Tensor:
+    """Grouped W8A8 expert GEMM with ``moe_wna16_marlin_gemm`` routing semantics;
+    ``w`` e4m3 ``[E, N, K]`` row-major, ``w_scales`` ``[E, N/128, K/128]``."""
+    _contig(a, "a")
+    _contig(c, "c")
+    _w8_weights(w, w_scales)
+    a_rows, k = (int(d) for d in a.reshape(-1, a.shape[-1]).shape)
+    n = int(w.shape[-2])
+    if topk_weights is not None:
+        topk_weights = topk_weights.reshape(-1).float().contiguous()
+    if c.shape[0] < num_routes:
+        raise ValueError(f"c has {c.shape[0]} rows, the routes need {num_routes}")
+    if mul_topk_weights and (topk_weights is None or topk_weights.numel() < num_routes):
+        raise ValueError("mul_topk_weights needs one topk weight per route")
+    groups = min(expert_ids.numel(), sorted_token_ids.numel() // block_size)
+    ws = workspace(w8a8_workspace_bytes(groups * block_size, k), a.device)
+    _lib.check(
+        lib().b200_w8a8_moe_gemm(
+            _vp(a), _code(a, "a"), a_rows, k, _vp(w), _vp(w_scales), num_experts, n, gated_mode,
+            _vp(sorted_token_ids), _vp(expert_ids), groups, _vp(num_tokens_post_pad), block_size,
+            top_k, num_routes, _vp(topk_weights), int(mul_topk_weights), _vp(c), _code(c, "c"),
+            c.shape[-1], _vp(ws), ws.numel(), _stream(a.device),
+        )
+    )
+    return c

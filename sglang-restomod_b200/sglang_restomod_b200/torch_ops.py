@@ -88,6 +88,16 @@ _SCHEMAS = {
         " Tensor? w2_scales, Tensor? w13_global, Tensor? w2_global, int block_size,"
         " float routed_scaling_factor, Tensor? shared_out, int scoring, bool renormalize,"
         " Tensor? correction_bias, Tensor(a!) out) -> (Tensor, Tensor)",
+    # W8A8 block FP8 (opt-in: quantizes the activations)
+    "fp8_act_quant": "fp8_act_quant(Tensor x, int? scales_ld=None) -> (Tensor, Tensor)",
+    "w8a8_linear":
+        "w8a8_linear(Tensor x, Tensor w, Tensor w_scales, int gated_mode=0,"
+        " ScalarType? out_dtype=None) -> Tensor",
+    "w8a8_moe_gemm":
+        "w8a8_moe_gemm(Tensor a, Tensor w, Tensor w_scales, int num_experts,"
+        " Tensor sorted_token_ids, Tensor expert_ids, Tensor num_tokens_post_pad, int block_size,"
+        " int top_k, int num_routes, Tensor(a!) c, Tensor? topk_weights=None,"
+        " bool mul_topk_weights=False, int gated_mode=0) -> ()",
     # expert parallelism over peer memory
     "ep_dispatch":
         "ep_dispatch(Tensor x, Tensor topk_ids, Tensor topk_weights, int num_experts, int rank,"
@@ -330,6 +340,49 @@ def _layer_logits_fake(x, router_logits, top_k, quant, num_experts, inter, w13, 
                        shared_out, scoring, renormalize, correction_bias, out):
     t = x.shape[0]
     return (x.new_empty(t, top_k, dtype=torch.int32), x.new_empty(t, top_k, dtype=torch.float32))
+
+
+# ------------------------------------------------------------------- W8A8
+@_impl("fp8_act_quant")
+def _act_quant_cuda(x, scales_ld=None):
+    return ops.fp8_act_quant(x, scales_ld)
+
+
+@_fake("fp8_act_quant")
+def _act_quant_fake(x, scales_ld=None):
+    rows, k = x.shape
+    ld = rows if scales_ld is None else scales_ld
+    return (x.new_empty(rows, k, dtype=torch.float8_e4m3fn),
+            x.new_empty(k // 128, ld, dtype=torch.float32))
+
+
+@_impl("w8a8_linear")
+def _w8a8_linear_cuda(x, w, w_scales, gated_mode=0, out_dtype=None):
+    return ops.w8a8_linear(x, w, w_scales, gated_mode=gated_mode, out_dtype=out_dtype)
+
+
+@_fake("w8a8_linear")
+def _w8a8_linear_fake(x, w, w_scales, gated_mode=0, out_dtype=None):
+    return x.new_empty(*x.shape[:-1], _linear_cols(w.shape[-2], gated_mode),
+                       dtype=out_dtype or x.dtype)
+
+
+@_impl("w8a8_moe_gemm")
+def _w8a8_moe_cuda(a, w, w_scales, num_experts, sorted_token_ids, expert_ids,
+                   num_tokens_post_pad, block_size, top_k, num_routes, c, topk_weights=None,
+                   mul_topk_weights=False, gated_mode=0):
+    ops.w8a8_moe_gemm(a, w, w_scales, num_experts=num_experts, sorted_token_ids=sorted_token_ids,
+                      expert_ids=expert_ids, num_tokens_post_pad=num_tokens_post_pad,
+                      block_size=block_size, top_k=top_k, num_routes=num_routes, c=c,
+                      topk_weights=topk_weights, mul_topk_weights=mul_topk_weights,
+                      gated_mode=gated_mode)
+
+
+@_fake("w8a8_moe_gemm")
+def _w8a8_moe_fake(a, w, w_scales, num_experts, sorted_token_ids, expert_ids,
+                   num_tokens_post_pad, block_size, top_k, num_routes, c, topk_weights=None,
+                   mul_topk_weights=False, gated_mode=0):
+    return None
 
 
 # ------------------------------------------------------ expert parallelism

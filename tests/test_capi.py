@@ -185,3 +185,23 @@ def test_ep_region_layout_sizes():
         assert lay["recv"] - lay["rows"] >= 8 * slots
         assert lay["comb"] - lay["recv"] >= 2 * slots * h
         assert lay["total"] - lay["comb"] >= 2 * tokens * k * h
+
+
+def test_w8a8_validation():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    assert lib.b200_w8a8_workspace_bytes(10, 100) == -1
+    assert lib.b200_w8a8_workspace_bytes(10, 256) > lib.b200_gemm_workspace_bytes(0)
+    st = lib.b200_w8a8_linear(p, _lib.DTYPE_BF16, 4, 200, p, p, 256, 0, p, _lib.DTYPE_BF16, p,
+                              1 << 30, None)
+    assert st == _lib.ERR_INVALID and "128-wide quantization group" in _err(st)
+    # workspace smaller than the quantized activations need
+    need = lib.b200_w8a8_workspace_bytes(64, 512)
+    st = lib.b200_w8a8_linear(p, _lib.DTYPE_BF16, 64, 512, p, p, 256, 0, p, _lib.DTYPE_BF16, p,
+                              need - 4096, None)
+    assert st == _lib.ERR_INVALID and "b200_w8a8_workspace_bytes" in _err(st)
+    st = lib.b200_w8a8_moe_gemm(p, _lib.DTYPE_BF16, 4, 256, p, p, 4, 256, 0, p, p, 1, p, 12, 1, 4,
+                                None, 0, p, _lib.DTYPE_BF16, 256, p, 1 << 30, None)
+    assert st == _lib.ERR_UNSUPPORTED and "block_size" in _err(st)
+    st = lib.b200_fp8_act_quant(p, _lib.DTYPE_BF16, 4, 256, p, p, 2, None)
+    assert st == _lib.ERR_INVALID and "scales_ld" in _err(st)

