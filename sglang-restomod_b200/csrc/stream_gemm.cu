@@ -420,6 +420,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   const int cq = lane & 3;
   float acc[NT][4];
   bool valid[NT];
+  // 8-row tiles with no valid row at all (the padding at the end of a
+  // group): their MMAs are skipped (warp-uniform).
+  bool tile_live[NT];
   long long pair = u0 / kcs;
   int kc = (int)(u0 - pair * kcs);
   long long gi = pair / nrb;
@@ -455,6 +458,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
         valid[nt] = slot_row<NT>(p, gi, nt * 8 + g8, dense) != nullptr;
+        tile_live[nt] = __any_sync(0xffffffffu, valid[nt]);
       }
       if constexpr (Q == kQuantNvfp4) gs = __ldg(p.gscale + e);
     }
@@ -551,8 +555,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
               a[3] = e4m3x2_to_f16x2((uint16_t)(bot >> 16));
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
-                mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
-                          h ? b[nt].w : b[nt].y);
+                if (NT == 1 || tile_live[nt])
+                  mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                            h ? b[nt].w : b[nt].y);
             }
           }
           if constexpr (!kPre) {
@@ -625,8 +630,9 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
               // k-step j = 2m + h uses activation chunk m, half h
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
-                mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
-                          h ? b[nt].w : b[nt].y);
+                if (NT == 1 || tile_live[nt])
+                  mma_16816(t[nt * kChains + (kChains == 2 ? h : 0)], a, h ? b[nt].z : b[nt].x,
+                            h ? b[nt].w : b[nt].y);
             }
           }
           if constexpr (!kPre) {
