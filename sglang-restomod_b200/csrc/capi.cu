@@ -181,10 +181,14 @@ bool use_tc_dense(int64_t m, int64_t n) {
   return m >= kTcDenseMinRows;
 }
 
-// Moe calls take the tcgen05 GEMM for blocks of 64 and more (the prefill
-// regime) when every group fits the plan.
+// Moe calls take the tcgen05 GEMM for blocks of B200_TC_MOE_MIN_BLOCK (64)
+// and more (the prefill regime) when every group fits the plan.
+#ifndef B200_TC_MOE_MIN_BLOCK
+#define B200_TC_MOE_MIN_BLOCK 64
+#endif
 bool use_tc_moe(int32_t quant, int32_t block_size, int64_t groups) {
-  return (quant == B200_QUANT_FP8_BLOCK || quant == B200_QUANT_NVFP4) && block_size >= 64 &&
+  return (quant == B200_QUANT_FP8_BLOCK || quant == B200_QUANT_NVFP4) &&
+         block_size >= B200_TC_MOE_MIN_BLOCK &&
          tc_gemm_supported(block_size) &&
          groups * tc_plan_slots_per_group(block_size) <= kTcPlanCap;
 }
@@ -1267,9 +1271,9 @@ int b200_fp8_act_quant(const void* x, int32_t x_dtype, int64_t rows, int64_t k, 
   if (rows == 0) return B200_OK;
   if (x == nullptr || q == nullptr || scales == nullptr)
     return fail(B200_ERR_INVALID, "null pointer argument");
-  if ((reinterpret_cast<uintptr_t>(x) & 7u) || (reinterpret_cast<uintptr_t>(q) & 3u) ||
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) ||
       (reinterpret_cast<uintptr_t>(scales) & 3u))
-    return fail(B200_ERR_INVALID, "x must be 8-byte aligned, q and scales 4-byte aligned");
+    return fail(B200_ERR_INVALID, "x must be 16-byte aligned, q 8-byte and scales 4-byte aligned");
   return check_cuda(launch_fp8_act_quant(x, x_dtype == B200_DTYPE_F16, rows, (int)k, nullptr, 1,
                                          0, rows, q, scales, scales_ld, nullptr,
                                          reinterpret_cast<cudaStream_t>(stream)),

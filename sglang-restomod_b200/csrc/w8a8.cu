@@ -19,15 +19,17 @@
 // quantized activations both arrive by 2-D TMA with 128-byte swizzle, the
 // K-major layout the MMA's shared-memory descriptors read; the stage's 128
 // activation scales come with them (a 512-byte bulk copy). The four
-// K=32 MMAs of a block write a fresh fp32 partial into one of two tensor-
-// memory buffers; the epilogue warps load it, multiply it by sa * sw and add
-// it to their register accumulators (packed f32x2 math) while the MMAs of
-// the next block fill the other buffer.
+// K=32 MMAs of a block write a fresh fp32 partial into one of four tensor-
+// memory buffers (all 512 columns); the epilogue warps load it, release the
+// buffer at once, then multiply it by sa * sw and add it to their register
+// accumulators (packed f32x2 math), so the MMAs run up to three blocks ahead
+// of the promotion.
 //
 // Warps: 0-7 epilogue (warp w reads tensor-memory lanes 32 * (w % 4) ..,
 // columns 64 * (w / 4) ..), 8 TMA producer, 9 MMA issuer (one elected lane)
-// and tensor-memory owner. Every wait is bounded; a timeout sets the status
-// bit and every role stops.
+// and tensor-memory owner, 10 item metadata (each output column's row and
+// router weight, staged in shared memory ahead of the item's stores). Every
+// wait is bounded; a timeout sets the status bit and every role stops.
 //
 // A gated gate/up bank (rows [gate | up], the checkpoint layout) is tiled so
 // that one tile holds 64 gate rows and the 64 matching up rows: TMEM lanes
@@ -47,18 +49,20 @@ using namespace tcg;
 using namespace tcg_host;
 
 constexpr int kW8N = 128;  // MMA N (tokens / route slots) per item
-constexpr int kW8Warps = 10;
+constexpr int kW8Warps = 11;
 constexpr int kW8Threads = kW8Warps * 32;
 constexpr int kWarpEpiCount = 8;
-constexpr int kWarpProd = 8, kWarpMma8 = 9;
+constexpr int kWarpProd = 8, kWarpMma8 = 9, kWarpMeta8 = 10;
+constexpr int kW8PBufs = 4;  // tensor-memory partial buffers
 constexpr int kW8Stages = 6;
 constexpr uint32_t kW8ATile = 128 * 128;  // 128 weight rows x 128 K e4m3
 constexpr uint32_t kW8BTile = 128 * 128;  // 128 tokens x 128 K e4m3
 constexpr uint32_t kW8SaBytes = kW8N * 4;
 constexpr uint32_t kW8StageBytes = kW8ATile + kW8BTile + 1024;  // + scales, 1024-aligned
 constexpr uint32_t kW8OffCtl = kW8Stages * kW8StageBytes;
-constexpr size_t kW8Smem = kW8OffCtl + 1024 + 1024;  // control block + alignment slack
-constexpr uint32_t kW8TmemCols = 256;                  // two 128-column partial buffers
+constexpr uint32_t kW8OffMeta = kW8OffCtl + 1024;     // [2][kW8N] out rows, [2][kW8N] weights
+constexpr size_t kW8Smem = kW8OffMeta + 4 * kW8N * 4 + 1024;  // + alignment slack
+constexpr uint32_t kW8TmemCols = kW8PBufs * kW8N;           // 512: four partial buffers
 constexpr uint32_t kW8StageTx = kW8ATile + kW8BTile + kW8SaBytes;
 static_assert(kW8Smem <= 232448, "shared memory");
 static_assert(kW8StageBytes % 1024 == 0, "stages stay 1024-byte aligned");
@@ -84,8 +88,10 @@ struct W8Params {
 struct W8Ctl {
   uint64_t full[kW8Stages];   // A + B + scales landed (transaction bytes)
   uint64_t empty[kW8Stages];  // MMA commit + the 8 epilogue warps (scales read)
-  uint64_t pfull[2];          // partial buffer written (MMA commit)
-  uint64_t pempty[2];         // partial buffer read (8 epilogue warps)
+  uint64_t pfull[kW8PBufs];   // partial buffer written (MMA commit)
+  uint64_t pempty[kW8PBufs];  // partial buffer read (8 epilogue warps)
+  uint64_t mfull[2];          // item metadata staged (metadata warp)
+  uint64_t mempty[2];         // item metadata used (8 epilogue warps)
   uint64_t done;
   uint32_t tmem;
   int abort;
@@ -187,6 +193,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   W8Ctl* ctl = reinterpret_cast<W8Ctl*>(smem + kW8OffCtl);
+  int* meta_row = reinterpret_cast<int*>(smem + kW8OffMeta);                  // [2][kW8N]
+  float* meta_w = reinterpret_cast<float*>(smem + kW8OffMeta + 2 * kW8N * 4);  // [2][kW8N]
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -199,9 +207,13 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1 + kWarpEpiCount);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kW8PBufs; ++b) {
       mbar_init(&ctl->pfull[b], 1);
       mbar_init(&ctl->pempty[b], kWarpEpiCount);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->mfull[b], 1);
+      mbar_init(&ctl->mempty[b], kWarpEpiCount);
     }
     mbar_init(&ctl->done, 1);
     ctl->abort = 0;
@@ -287,9 +299,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       const uint32_t idesc = instr_desc_e4m3(n);
       for (int kb = 0; kb < kch; ++kb, ++t) {
         const int s = (int)(t % kW8Stages);
-        const int pb = (int)(t & 1);
+        const int pb = (int)(t % kW8PBufs);
         ok = w8_warp_wait(&ctl->full[s], (uint32_t)((t / kW8Stages) & 1), ctl, p.status) &&
-             w8_warp_wait(&ctl->pempty[pb], (uint32_t)(((t >> 1) & 1) ^ 1), ctl, p.status);
+             w8_warp_wait(&ctl->pempty[pb], (uint32_t)(((t / kW8PBufs) & 1) ^ 1), ctl,
+                          p.status);
         if (!ok) break;
         tc_fence_after();
         const uint32_t alo = lo0 + (uint32_t)(s * kW8StageBytes >> 4);
@@ -311,6 +324,39 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       mbar_wait(&ctl->done, 0u, nullptr);
     }
     __syncwarp();
+  } else if (warp == kWarpMeta8) {
+    // ---------------------------------------------------- item metadata
+    // Output row (-1: nothing to store) and router weight of each column of
+    // the item, at most one item ahead of the stores.
+    bool ok = true;
+    for (long long j = 0; j < my_items && ok; ++j) {
+      const W8Item it = w8_item(p, plan, g0 + j * gs, ntiles, mchunks);
+      const int mb = (int)(j & 1);
+      ok = w8_warp_wait(&ctl->mempty[mb], (uint32_t)(((j >> 1) & 1) ^ 1), ctl, p.status);
+      if (!ok) break;
+#pragma unroll
+      for (int i = 0; i < kW8N / 32; ++i) {
+        const int col = 32 * i + lane;
+        int orow = -1;
+        float wt = 1.f;
+        if (col < it.rows) {
+          const long long slot = it.slot0 + col;
+          if (dense) {
+            orow = (int)slot;
+          } else {
+            const int id = __ldg(p.sorted_ids + slot);
+            if (id >= 0 && id < p.num_routes) {
+              orow = id;
+              if (p.mul_w) wt = __ldg(p.topk_w + id);
+            }
+          }
+        }
+        meta_row[mb * kW8N + col] = orow;
+        meta_w[mb * kW8N + col] = wt;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->mfull[mb]);
+    }
   } else if (warp < kWarpEpiCount) {
     // ------------------------------------------- promotion and epilogue
     const int q = warp & 3;          // tensor-memory lanes 32q .. 32q + 31
@@ -332,38 +378,47 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       uint64_t acc[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) acc[i] = 0ull;
+      float sw_next = __ldg(swp);
       for (int kb = 0; kb < kch; ++kb, ++t) {
         const int s = (int)(t % kW8Stages);
-        const int pb = (int)(t & 1);
-        const float sw = __ldg(swp + kb);
-        ok = w8_warp_wait(&ctl->pfull[pb], (uint32_t)((t >> 1) & 1), ctl, p.status) &&
+        const int pb = (int)(t % kW8PBufs);
+        const float sw = sw_next;
+        if (kb + 1 < kch) sw_next = __ldg(swp + kb + 1);
+        ok = w8_warp_wait(&ctl->pfull[pb], (uint32_t)((t / kW8PBufs) & 1), ctl, p.status) &&
              w8_warp_wait(&ctl->full[s], (uint32_t)((t / kW8Stages) & 1), ctl, p.status);
         if (!ok) break;
         tc_fence_after();
-        uint32_t v[32];
+        uint32_t v0[32], v1[32];
+        tmem_ld32_nowait(lane_base + (uint32_t)pb * kW8N, v0);
+        tmem_ld32_nowait(lane_base + (uint32_t)pb * kW8N + 32u, v1);
+        tmem_ld_wait();
+        // the partial is in registers: hand its buffer back to the MMAs
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->pempty[pb]);
         const float* sa = reinterpret_cast<const float*>(smem + s * kW8StageBytes + kW8ATile +
                                                          kW8BTile) + 64 * h;
         const uint64_t sw2 = pack2(sw, sw);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld32_nowait(lane_base + (uint32_t)pb * kW8N + 32u * half, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float2 s2 = *reinterpret_cast<const float2*>(sa + 32 * half + 2 * c);
-            fma_f32x2(acc[16 * half + c], pack2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1])),
-                      pack2(s2.x, s2.y), sw2);
-          }
+        for (int c = 0; c < 16; ++c) {
+          const float4 s4 = *reinterpret_cast<const float4*>(sa + 4 * c);
+          const uint32_t* v = c < 8 ? v0 : v1;
+          const int o = (c & 7) * 4;
+          fma_f32x2(acc[2 * c], pack2(__uint_as_float(v[o]), __uint_as_float(v[o + 1])),
+                    pack2(s4.x, s4.y), sw2);
+          fma_f32x2(acc[2 * c + 1], pack2(__uint_as_float(v[o + 2]), __uint_as_float(v[o + 3])),
+                    pack2(s4.z, s4.w), sw2);
         }
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&ctl->pempty[pb]);
-          mbar_arrive(&ctl->empty[s]);
-        }
+        if (lane == 0) mbar_arrive(&ctl->empty[s]);
       }
       if (!ok) break;
       // ---- store: column c = token / slot 64h + c of the item
+      const int mb = (int)(j & 1);
+      ok = w8_warp_wait(&ctl->mfull[mb], (uint32_t)((j >> 1) & 1), ctl, p.status);
+      if (!ok) break;
+      const int* mrow = meta_row + mb * kW8N + 64 * h;
+      const float* mw = meta_w + mb * kW8N + 64 * h;
       long long ocol;
       bool stores = true;
       if (p.gated) {
@@ -375,32 +430,27 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 #pragma unroll
       for (int c2 = 0; c2 < 32; ++c2) {
         const float2 a2 = unpack2(acc[c2]);
+        const int2 r2 = *reinterpret_cast<const int2*>(mrow + 2 * c2);
+        const float2 w2 = *reinterpret_cast<const float2*>(mw + 2 * c2);
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
-          const int col = 64 * h + 2 * c2 + w;  // uniform across the warp
           float val = w ? a2.y : a2.x;
           if (p.gated) {
             const float up = __shfl_down_sync(0xffffffffu, val, 16);
             val = silu_f32(val) * up;
           }
-          if (col >= it.rows) continue;
-          const long long slot = it.slot0 + col;
-          long long orow = slot;
-          float wt = 1.f;
-          if (!dense) {
-            const int id = __ldg(p.sorted_ids + slot);
-            if (id < 0 || id >= p.num_routes) continue;
-            orow = id;
-            if (p.mul_w) wt = __ldg(p.topk_w + id);
-          }
-          if (!stores) continue;
-          const float y = val * wt;
+          const int orow = w ? r2.y : r2.x;  // uniform across the warp
+          if (orow < 0 || !stores) continue;
+          const float y = val * (w ? w2.y : w2.x);
           if (p.out_f16)
-            reinterpret_cast<__half*>(p.out)[orow * p.ldo + ocol] = __float2half_rn(y);
+            reinterpret_cast<__half*>(p.out)[(long long)orow * p.ldo + ocol] = __float2half_rn(y);
           else
-            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + ocol] = __float2bfloat16_rn(y);
+            reinterpret_cast<__nv_bfloat16*>(p.out)[(long long)orow * p.ldo + ocol] =
+                __float2bfloat16_rn(y);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->mempty[mb]);
     }
   }
 
@@ -415,43 +465,49 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 }
 
 // ------------------------------------------------ activation quantization
-// One warp per (output row, 128-K group): amax over the group, scale =
-// max(amax / 448, 1e-8), e4m3 = rn_satfinite(x / scale). With a gather
-// (sorted_ids) output row s takes activation row sorted_ids[s] / top_k, and
-// rows whose id is padding are written as zeros. Scale rows [out_rows, ld)
-// are zeroed too.
+// One half-warp per (output row, 128-K group), 8 elements (16 bytes) per
+// lane: amax over the group, scale = max(amax / 448, 1e-8), e4m3 =
+// rn_satfinite(x / scale). With a gather (sorted_ids) output row s takes
+// activation row sorted_ids[s] / top_k, and rows whose id is padding are
+// written as zeros. Scale rows [out_rows, ld) are zeroed too.
 __global__ void __launch_bounds__(256) fp8_act_quant_kernel(
     const void* __restrict__ x, int x_f16, long long x_rows, int K, const int* __restrict__ ids,
     int top_k, long long num_routes, long long out_rows, uint8_t* __restrict__ q,
     float* __restrict__ scales, long long ld, int* status) {
   griddep_wait();
   const int kch = K / 128;
+  const int hl = threadIdx.x & 15;  // lane within the half-warp
+  const int half = (threadIdx.x >> 4) & 1;
+  // Warp-uniform loop over pairs of groups (the shuffles below need every
+  // lane of the warp): half-warp `half` takes group 2 * pair + half.
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const int lane = threadIdx.x & 31;
-  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       w < ld * kch; w += warps) {
-    const long long r = w / kch;
-    const int kb = (int)(w - r * kch);
-    if (r >= out_rows) {
-      if (lane == 0) scales[(long long)kb * ld + r] = 0.f;
-      continue;
-    }
-    long long src = r;
-    if (ids != nullptr) {
+  const long long groups = ld * kch;
+  for (long long pair = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       2 * pair < groups; pair += warps) {
+    const long long gid = 2 * pair + half;
+    const bool in = gid < groups;
+    const long long r = in ? gid / kch : 0;
+    const int kb = in ? (int)(gid - r * kch) : 0;
+    const bool row = in && r < out_rows;
+    if (in && !row && hl == 0) scales[(long long)kb * ld + r] = 0.f;
+    long long src = row ? r : -1;
+    if (row && ids != nullptr) {
       const int id = __ldg(ids + r);
       src = (id >= 0 && id < num_routes) ? id / top_k : -1;
       if (src >= x_rows) {
-        if (lane == 0 && status) atomicOr(status, kDevBadRoute);
+        if (hl == 0 && status) atomicOr(status, kDevBadRoute);
         src = -1;
       }
     }
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (src >= 0) {
-      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(
-          reinterpret_cast<const uint16_t*>(x) + src * K + kb * 128 + lane * 4));
-      const uint32_t wds[2] = {raw.x, raw.y};
+    float v[8];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    if (src >= 0) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const uint16_t*>(x) + src * K + kb * 128 + hl * 8));
+      const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
         if (x_f16) {
           const __half2 hh = *reinterpret_cast<const __half2*>(&wds[i]);
           v[2 * i] = __low2float(hh);
@@ -463,15 +519,29 @@ __global__ void __launch_bounds__(256) fp8_act_quant_kernel(
         }
       }
     }
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    float amax = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    // the half-warp's 16 lanes hold the group (xor offsets below 16 stay in it)
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float scale = fmaxf(amax / 448.f, 1e-8f);
-    uint16_t lo, hi;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[1] / scale), "f"(v[0] / scale));
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[3] / scale), "f"(v[2] / scale));
-    *reinterpret_cast<uint32_t*>(q + r * K + kb * 128 + lane * 4) = (uint32_t)lo | ((uint32_t)hi << 16);
-    if (lane == 0) scales[(long long)kb * ld + r] = scale;
+    uint32_t packed[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint16_t lo, hi;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
+          : "=h"(lo)
+          : "f"(v[4 * i + 1] / scale), "f"(v[4 * i] / scale));
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
+          : "=h"(hi)
+          : "f"(v[4 * i + 3] / scale), "f"(v[4 * i + 2] / scale));
+      packed[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    if (row) {
+      *reinterpret_cast<uint2*>(q + r * K + kb * 128 + hl * 8) = make_uint2(packed[0], packed[1]);
+      if (hl == 0) scales[(long long)kb * ld + r] = scale;
+    }
   }
   griddep_launch_dependents();
 }
@@ -483,7 +553,7 @@ cudaError_t launch_fp8_act_quant(const void* x, int x_f16, long long x_rows, int
                                  long long out_rows, uint8_t* q, float* scales, long long ld,
                                  int* status, cudaStream_t stream) {
   const long long groups = ld * (K / 128);
-  long long blocks = (groups + 7) / 8;
+  long long blocks = (groups + 15) / 16;  // 16 half-warps per block
   const long long cap = (long long)device_sm_count() * 16;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
