@@ -113,6 +113,25 @@ int b200_topk_route(const void* router_logits, int32_t logits_dtype, int64_t tok
                     void* stream);
 
 /*
+ * Grouped router top-k: b200_topk_route restricted to the topk_group best of
+ * num_expert_group contiguous expert groups, as upstream SGLang's
+ * grouped_topk / biased_grouped_topk (select_experts with num_expert_group /
+ * topk_group), whose StandardTopKOutput the quant methods consume
+ * (quant/sm70_fp8_moe/check.py:106-114). A group's score is its largest
+ * selection key (softmax: logit; sigmoid: sigmoid(logit)), or with a
+ * correction_bias the sum of its two largest sigmoid(logit) + bias keys;
+ * ties go to the lower group and the lower expert. Weights as in
+ * b200_topk_route (unbiased scores, renormalised on request).
+ * num_experts % num_expert_group == 0, num_expert_group <= 32,
+ * top_k <= topk_group * num_experts / num_expert_group.
+ */
+int b200_topk_route_grouped(const void* router_logits, int32_t logits_dtype, int64_t tokens,
+                            int32_t num_experts, int32_t top_k, int32_t scoring,
+                            int32_t renormalize, const float* correction_bias,
+                            int32_t num_expert_group, int32_t topk_group, int32_t* topk_ids,
+                            float* topk_weights, void* stream);
+
+/*
  * Shared-expert fusion: ids_out / weights_out [tokens, top_k + 1] = the
  * routes of topk_ids / topk_weights [tokens, top_k] plus one route per token
  * to shared_id with shared_weight. With the shared expert's weights stored

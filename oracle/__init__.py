@@ -53,7 +53,7 @@ from .nvfp4 import (
     nvfp4_linear_ref,
     quantize_nvfp4,
 )
-from .router import route_topk, route_topk_general
+from .router import route_topk, route_topk_general, route_topk_grouped
 from .w8a8 import act_dequant_fp8, act_quant_fp8, quantized_activations, w8a8_linear_ref
 
 __all__ = [
@@ -78,4 +78,5 @@ __all__ = [
     "quantize_nvfp4",
     "route_topk",
     "route_topk_general",
+    "route_topk_grouped",
 ]

@@ -285,6 +285,46 @@ int b200_topk_route(const void* router_logits, int32_t logits_dtype, int64_t tok
                     "router launch");
 }
 
+int b200_topk_route_grouped(const void* router_logits, int32_t logits_dtype, int64_t tokens,
+                            int32_t num_experts, int32_t top_k, int32_t scoring,
+                            int32_t renormalize, const float* correction_bias,
+                            int32_t num_expert_group, int32_t topk_group, int32_t* topk_ids,
+                            float* topk_weights, void* stream) {
+  if (num_expert_group <= 0 || num_expert_group > 32 || num_experts % num_expert_group)
+    return fail(B200_ERR_INVALID,
+                "num_expert_group must divide num_experts and be in [1, 32], got %d for %d experts",
+                num_expert_group, num_experts);
+  if (topk_group <= 0 || topk_group > num_expert_group)
+    return fail(B200_ERR_INVALID, "topk_group must be in [1, num_expert_group], got %d", topk_group);
+  const int32_t per_group = num_experts / num_expert_group;
+  if (top_k > topk_group * per_group)
+    return fail(B200_ERR_INVALID, "top_k %d exceeds the %d experts of the kept groups", top_k,
+                topk_group * per_group);
+  if (correction_bias != nullptr && per_group < 2)
+    return fail(B200_ERR_INVALID, "biased grouped top-k needs two experts per group");
+  if (logits_dtype != B200_DTYPE_BF16 && logits_dtype != B200_DTYPE_F16 &&
+      logits_dtype != B200_DTYPE_F32)
+    return fail(B200_ERR_UNSUPPORTED, "router logits must be bf16, f16 or f32");
+  if (tokens < 0) return fail(B200_ERR_INVALID, "bad tokens %lld", (long long)tokens);
+  if (num_experts <= 0 || num_experts > router_max_experts())
+    return fail(B200_ERR_UNSUPPORTED, "num_experts must be in [1, %d], got %d",
+                router_max_experts(), num_experts);
+  if (top_k <= 0 || top_k > 32 || top_k > num_experts)
+    return fail(B200_ERR_INVALID, "top_k must be in [1, min(32, num_experts)], got %d", top_k);
+  if (scoring != B200_SCORING_SOFTMAX && scoring != B200_SCORING_SIGMOID)
+    return fail(B200_ERR_INVALID, "unknown scoring %d", scoring);
+  if (correction_bias != nullptr && scoring != B200_SCORING_SIGMOID)
+    return fail(B200_ERR_INVALID, "a correction bias needs sigmoid scoring");
+  if (tokens == 0) return B200_OK;
+  if (router_logits == nullptr || topk_ids == nullptr || topk_weights == nullptr)
+    return fail(B200_ERR_INVALID, "null pointer argument");
+  return check_cuda(launch_topk_route(router_logits, logits_dtype, tokens, num_experts, top_k,
+                                      scoring, renormalize != 0, correction_bias, topk_ids,
+                                      topk_weights, reinterpret_cast<cudaStream_t>(stream),
+                                      num_expert_group, topk_group),
+                    "grouped router launch");
+}
+
 int b200_append_shared_route(const int32_t* topk_ids, const float* topk_weights, int64_t tokens,
                              int32_t top_k, int32_t shared_id, float shared_weight,
                              int32_t* ids_out, float* weights_out, void* stream) {

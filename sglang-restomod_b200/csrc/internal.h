@@ -106,9 +106,12 @@ cudaError_t launch_moe_align_multi(const int* topk_ids, long long numel, int num
 // Router top-k (softmax or sigmoid scoring, optional selection bias and
 // renormalisation); logits dtype 0 bf16, 1 f16, 2 f32.
 int router_max_experts();
+// groups > 0: only the topk_group best of `groups` contiguous expert groups
+// are selectable (upstream SGLang's grouped top-k).
 cudaError_t launch_topk_route(const void* logits, int dtype, long long tokens, int num_experts,
                               int top_k, int scoring, int renormalize, const float* bias,
-                              int* topk_ids, float* topk_w, cudaStream_t stream);
+                              int* topk_ids, float* topk_w, cudaStream_t stream, int groups = 0,
+                              int topk_group = 0);
 
 // Elementwise / reduction kernels.
 cudaError_t launch_append_shared_route(const int* ids, const float* w, long long tokens,

@@ -59,6 +59,11 @@ SIGNATURES = {
         [c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
          c_void_p, c_void_p],
     ),
+    "b200_topk_route_grouped": (
+        c_int32,
+        [c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
+         c_int32, c_void_p, c_void_p, c_void_p],
+    ),
     "b200_append_shared_route": (
         c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]
     ),

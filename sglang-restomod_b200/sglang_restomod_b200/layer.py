@@ -131,6 +131,10 @@ class QuantMoELayer:
     # The banks hold the shared expert as one more expert (index num_experts)
     # after fuse_shared(): one routed launch computes it with the rest.
     shared_fused: bool = False
+    # Grouped routing for forward_logits (upstream's num_expert_group /
+    # topk_group): only the topk_group best expert groups are selectable.
+    num_expert_group: int | None = None
+    topk_group: int | None = None
 
     def can_fuse_shared(self) -> bool:
         s = self.shared
@@ -201,6 +205,11 @@ class QuantMoELayer:
         shared expert this is one library call, whose router and moe_align
         share a launch for decode batches."""
         tokens = x.shape[0]
+        if self.num_expert_group:
+            ids, w = B.topk_route_grouped(router_logits, self.top_k, self.num_expert_group,
+                                          self.topk_group or self.num_expert_group, scoring,
+                                          renormalize, correction_bias)
+            return self.forward(x, ids, w, out=out)
         if self.fused_block_size(tokens) is None:
             shared_out = self.shared.forward(x) if self.shared is not None else None
             bs = self.block_size or block_size_for(tokens * self.top_k, self.num_experts)

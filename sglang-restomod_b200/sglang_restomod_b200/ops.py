@@ -158,6 +158,33 @@ def topk_route(router_logits: torch.Tensor, top_k: int, *, scoring: int = _lib.S
     return ids, w
 
 
+def topk_route_grouped(router_logits: torch.Tensor, top_k: int, num_expert_group: int,
+                       topk_group: int, *, scoring: int = _lib.SCORING_SOFTMAX,
+                       renormalize: bool = True, correction_bias: torch.Tensor | None = None):
+    """Grouped top-k (upstream grouped_topk / biased_grouped_topk): only the
+    ``topk_group`` best of ``num_expert_group`` expert groups are selectable."""
+    _contig(router_logits, "router_logits")
+    try:
+        code = _LOGIT_CODE[router_logits.dtype]
+    except KeyError:
+        raise TypeError(f"router_logits must be bf16, f16 or f32, got {router_logits.dtype}") from None
+    tokens, experts = (int(d) for d in router_logits.shape)
+    if correction_bias is not None:
+        _contig(correction_bias, "correction_bias")
+        if correction_bias.dtype != torch.float32 or correction_bias.numel() != experts:
+            raise ValueError("correction_bias must be fp32 [num_experts]")
+    ids = torch.empty(tokens, top_k, dtype=torch.int32, device=router_logits.device)
+    w = torch.empty(tokens, top_k, dtype=torch.float32, device=router_logits.device)
+    _lib.check(
+        lib().b200_topk_route_grouped(
+            _vp(router_logits), code, tokens, experts, top_k, scoring, int(renormalize),
+            _vp(correction_bias), int(num_expert_group), int(topk_group), _vp(ids), _vp(w),
+            _stream(router_logits.device),
+        )
+    )
+    return ids, w
+
+
 def append_shared_route(topk_ids: torch.Tensor, topk_weights: torch.Tensor, shared_id: int,
                         shared_weight: float = 1.0):
     """[T, k] routes -> [T, k + 1] with one route per token to ``shared_id``."""

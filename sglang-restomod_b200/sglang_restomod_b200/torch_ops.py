@@ -41,6 +41,9 @@ _SCHEMAS = {
     "topk_route":
         "topk_route(Tensor router_logits, int top_k, int scoring=0, bool renormalize=True,"
         " Tensor? correction_bias=None) -> (Tensor, Tensor)",
+    "topk_route_grouped":
+        "topk_route_grouped(Tensor router_logits, int top_k, int num_expert_group, int topk_group,"
+        " int scoring=0, bool renormalize=True, Tensor? correction_bias=None) -> (Tensor, Tensor)",
     "append_shared_route":
         "append_shared_route(Tensor topk_ids, Tensor topk_weights, int shared_id,"
         " float shared_weight) -> (Tensor, Tensor)",
@@ -151,6 +154,22 @@ def _topk_cuda(router_logits, top_k, scoring=0, renormalize=True, correction_bia
 
 @_fake("topk_route")
 def _topk_fake(router_logits, top_k, scoring=0, renormalize=True, correction_bias=None):
+    t = router_logits.shape[0]
+    return (router_logits.new_empty(t, top_k, dtype=torch.int32),
+            router_logits.new_empty(t, top_k, dtype=torch.float32))
+
+
+@_impl("topk_route_grouped")
+def _topk_grouped_cuda(router_logits, top_k, num_expert_group, topk_group, scoring=0,
+                       renormalize=True, correction_bias=None):
+    return ops.topk_route_grouped(router_logits, top_k, num_expert_group, topk_group,
+                                  scoring=scoring, renormalize=renormalize,
+                                  correction_bias=correction_bias)
+
+
+@_fake("topk_route_grouped")
+def _topk_grouped_fake(router_logits, top_k, num_expert_group, topk_group, scoring=0,
+                       renormalize=True, correction_bias=None):
     t = router_logits.shape[0]
     return (router_logits.new_empty(t, top_k, dtype=torch.int32),
             router_logits.new_empty(t, top_k, dtype=torch.float32))

@@ -205,3 +205,14 @@ def test_w8a8_validation():
     assert st == _lib.ERR_UNSUPPORTED and "block_size" in _err(st)
     st = lib.b200_fp8_act_quant(p, _lib.DTYPE_BF16, 4, 256, p, p, 2, None)
     assert st == _lib.ERR_INVALID and "scales_ld" in _err(st)
+
+
+def test_grouped_router_validation():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    st = lib.b200_topk_route_grouped(p, _lib.DTYPE_F32, 4, 100, 8, 0, 1, None, 8, 2, p, p, None)
+    assert st == _lib.ERR_INVALID and "divide" in _err(st)
+    st = lib.b200_topk_route_grouped(p, _lib.DTYPE_F32, 4, 64, 8, 0, 1, None, 8, 9, p, p, None)
+    assert st == _lib.ERR_INVALID and "topk_group" in _err(st)
+    st = lib.b200_topk_route_grouped(p, _lib.DTYPE_F32, 4, 64, 20, 0, 1, None, 8, 2, p, p, None)
+    assert st == _lib.ERR_INVALID and "kept groups" in _err(st)

@@ -121,3 +121,45 @@ def test_layer_forward_from_logits(cuda_device, tokens, experts, top_k, block):
                                  block_size=block, **bank)
     assert_close(out, want, rtol=1e-3, atol=1e-3, what=f"from logits T={tokens}")
     assert ops.workspace_status() == 0
+
+
+# --------------------------------------------- grouped (expert-group) top-k
+@pytest.mark.parametrize("experts,groups,topk_group,top_k,scoring,with_bias",
+                         [(256, 8, 4, 8, "sigmoid", True),    # DeepSeek-V3's routing
+                          (256, 8, 4, 8, "sigmoid", False),
+                          (64, 8, 3, 6, "softmax", False),
+                          (160, 32, 6, 12, "softmax", False),
+                          (96, 4, 1, 4, "sigmoid", True)])
+def test_grouped_topk_matches_oracle(cuda_device, experts, groups, topk_group, top_k, scoring,
+                                     with_bias):
+    g = torch.Generator().manual_seed(experts + groups + top_k)
+    logits = torch.randn(77, experts, generator=g)
+    bias = torch.randn(experts, generator=g) * 0.5 if with_bias else None
+    code = _lib.SCORING_SIGMOID if scoring == "sigmoid" else _lib.SCORING_SOFTMAX
+    got = ops.topk_route_grouped(logits.to(cuda_device), top_k, groups, topk_group, scoring=code,
+                                 correction_bias=None if bias is None else bias.to(cuda_device))
+    want = oracle.route_topk_grouped(logits, top_k, groups, topk_group, scoring=scoring,
+                                     bias=bias)
+    _check(got, want, f"grouped {experts}/{groups}/{topk_group}/{top_k} {scoring}")
+    # every chosen expert lies in one of the topk_group kept groups
+    per = experts // groups
+    chosen_groups = got[0].cpu().long() // per
+    assert int(max(len(set(r.tolist())) for r in chosen_groups)) <= topk_group
+
+
+def test_grouped_topk_groups_matter(cuda_device):
+    """One group holds the single best expert but weak others; with a top-2
+    group score it loses to groups whose two best are strong."""
+    experts, groups = 16, 4
+    logits = torch.full((1, experts), -4.0)
+    logits[0, 0] = 4.0          # group 0: one strong expert
+    logits[0, 4:6] = 3.0        # group 1: two good experts
+    logits[0, 8:10] = 2.9       # group 2
+    bias = torch.zeros(experts)
+    ids, _ = ops.topk_route_grouped(logits.to(cuda_device), 2, groups, 1,
+                                    scoring=_lib.SCORING_SIGMOID,
+                                    correction_bias=bias.to(cuda_device))
+    assert sorted(ids[0].tolist()) == [4, 5]
+    ids_max, _ = ops.topk_route_grouped(logits.to(cuda_device), 2, groups, 1,
+                                        scoring=_lib.SCORING_SIGMOID)
+    assert ids_max[0].tolist()[0] == 0  # by group maximum, group 0 wins

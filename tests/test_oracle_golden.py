@@ -156,3 +156,20 @@ def test_align_oracle_properties():
             assert all(ids[r] == expert_ids[b] for r in real)
         assert (expert_ids[total // bs :] == -1).all()
         assert (sorted_ids[total:] == numel).all()
+
+
+def test_grouped_router_oracle_known_case():
+    """Group score by maximum vs by top-2 sum (biased grouped top-k)."""
+    logits = torch.full((1, 16), -4.0)
+    logits[0, 0] = 4.0
+    logits[0, 4:6] = 3.0
+    logits[0, 8:10] = 2.9
+    ids, w = oracle.route_topk_grouped(logits, 2, 4, 1, scoring="sigmoid", bias=torch.zeros(16))
+    assert ids[0].tolist() == [4, 5] and abs(float(w.sum()) - 1.0) < 1e-6
+    ids, _ = oracle.route_topk_grouped(logits, 2, 4, 1, scoring="sigmoid")
+    assert ids[0].tolist() == [0, 1]
+    # with every group kept it is the plain top-k
+    x = torch.randn(5, 32, generator=torch.Generator().manual_seed(1))
+    a = oracle.route_topk_grouped(x, 4, 4, 4)
+    b = oracle.route_topk_general(x, 4)
+    assert torch.equal(a[0], b[0]) and torch.allclose(a[1], b[1])
