@@ -248,6 +248,21 @@ int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m
 int b200_linear_noalloc_status(int32_t* bits, int32_t reset, void* stream);
 
 /*
+ * Which kernel a call takes (for census and profiling; no counterpart in the
+ * reference, whose dispatcher decides the same question in Python,
+ * quant/sm70_fp4_moe/decode_gemv.py:183-219). Returns B200_PATH_STREAM (the
+ * weight-streaming decode GEMM; *tile_rows = rows per weight pass) or
+ * B200_PATH_TCGEN05 (the tensor-core GEMM; *tile_rows = 192, *k_parts = K
+ * split of a dense call), or an error status (negative never; check > 10).
+ * b200_linear_path: b200_linear with m rows of [n, k]. b200_moe_path:
+ * b200_moe_gemm / the layer forward with this block size and group count.
+ */
+#define B200_PATH_STREAM 16
+#define B200_PATH_TCGEN05 17
+int b200_linear_path(int64_t m, int64_t n, int64_t k, int32_t* tile_rows, int32_t* k_parts);
+int b200_moe_path(int32_t quant, int32_t block_size, int64_t expert_capacity, int32_t* tile_rows);
+
+/*
  * Grouped expert GEMM routed by moe_align_block_size output, with the
  * semantics of moe_wna16_marlin_gemm (quant/sm70_fp4_moe/method.py:385-564):
  * route slot p of block b multiplies activation row sorted_token_ids[p] /

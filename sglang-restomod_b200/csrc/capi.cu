@@ -181,6 +181,36 @@ bool use_tc_dense(int64_t m, int64_t n) {
   return m >= kTcDenseMinRows;
 }
 
+// K parts of a dense tcgen05 call. Items (192-row chunk x 128-row weight
+// block) are dealt round-robin over the SMs, each streaming its K range.
+// Split K (parts summed in fp32 in the workspace, then a finishing kernel)
+// when that cuts the busiest SM's 128-K unit count by a quarter or more, each
+// part charged for its m*n fp32 atomic adds at 3x the time of streaming the
+// same bytes of weights. Measured on B200: a split that only evens out waves
+// is slower (64 x 25600 x 5120: 64 us unsplit, 87 us in two parts), one that
+// fills idle SMs is faster (128 x 4096 x 7168: 43 us in three parts, 35 us in
+// four; 64 x 5120 x 25600: 64 us in three, 60 us in seven).
+int dense_k_parts(int64_t m, int64_t n, int64_t k) {
+  const int64_t kch = k / 128, sms = device_sm_count();
+  const int64_t items = (m + 191) / 192 * (n / 128);
+  if (m * n > (int64_t)max_grid_slots() * kWsSlotFloats) return 1;
+  const double part_cost = 3.0 * (double)m * (double)n * 4.0 / 16384.0 / (double)sms;
+  const double whole = (double)((items + sms - 1) / sms * kch);
+  double best = whole;
+  int best_parts = 1;
+  for (int64_t ks = 2; ks <= 16 && ks <= kch; ++ks) {
+    const int64_t kpart = (kch + ks - 1) / ks;
+    const int64_t parts = (kch + kpart - 1) / kpart;
+    const double cost =
+        (double)((items * parts + sms - 1) / sms * kpart) + part_cost * (double)parts;
+    if (cost < best) {
+      best = cost;
+      best_parts = (int)parts;
+    }
+  }
+  return best < 0.75 * whole ? best_parts : 1;
+}
+
 // Moe calls take the tcgen05 GEMM for blocks of B200_TC_MOE_MIN_BLOCK (64)
 // and more (the prefill regime) when every group fits the plan.
 #ifndef B200_TC_MOE_MIN_BLOCK
@@ -473,26 +503,7 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     // (64 x 25600 x 5120: 64 us unsplit, 87 us in two parts), one that fills
     // idle SMs is faster (128 x 4096 x 7168: 43 us in three parts, 35 us in
     // four; 64 x 5120 x 25600: 64 us in three, 60 us in seven).
-    p.ksplit = 1;
-    const int64_t kch = k / 128, sms = device_sm_count();
-    const int64_t items = (m + 191) / 192 * (n / 128);
-    if (m * n <= (int64_t)max_grid_slots() * kWsSlotFloats) {
-      const double part_cost = 3.0 * (double)m * (double)n * 4.0 / 16384.0 / (double)sms;
-      const double whole = (double)((items + sms - 1) / sms * kch);
-      double best = whole;
-      int best_parts = 1;
-      for (int64_t ks = 2; ks <= 16 && ks <= kch; ++ks) {
-        const int64_t kpart = (kch + ks - 1) / ks;
-        const int64_t parts = (kch + kpart - 1) / kpart;
-        const double cost =
-            (double)((items * parts + sms - 1) / sms * kpart) + part_cost * (double)parts;
-        if (cost < best) {
-          best = cost;
-          best_parts = (int)parts;
-        }
-      }
-      if (best < 0.75 * whole) p.ksplit = best_parts;
-    }
+    p.ksplit = dense_k_parts(m, n, k);
     rc = run_tc(quant, p, ws, false, st);
     if (rc || p.ksplit <= 1) return rc;
     return check_cuda(launch_tc_split_finish(p, st), "split-K finish launch");
@@ -524,6 +535,36 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
   const long long groups = (m + 8 * nt - 1) / (8 * nt);
   const long long units = groups * (n / 128) * (k / 128);
   return run_stream(quant, nt, p, units, ws, st);
+}
+
+int b200_linear_path(int64_t m, int64_t n, int64_t k, int32_t* tile_rows, int32_t* k_parts) {
+  if (m <= 0 || n <= 0 || k <= 0 || n % 128 || k % 128)
+    return fail(B200_ERR_INVALID, "bad shape m=%lld n=%lld k=%lld", (long long)m, (long long)n,
+                (long long)k);
+  int32_t rows = 0, parts = 1;
+  int path = B200_PATH_STREAM;
+  if (use_tc_dense(m, n)) {
+    path = B200_PATH_TCGEN05;
+    rows = 192;
+    parts = dense_k_parts(m, n, k);
+  } else {
+    rows = 8 * nt_for_rows(m);
+  }
+  if (tile_rows) *tile_rows = rows;
+  if (k_parts) *k_parts = parts;
+  return path;
+}
+
+int b200_moe_path(int32_t quant, int32_t block_size, int64_t expert_capacity, int32_t* tile_rows) {
+  if (quant != B200_QUANT_FP8_BLOCK && quant != B200_QUANT_NVFP4)
+    return fail(B200_ERR_INVALID, "unknown quant %d", quant);
+  if (block_size <= 0 || expert_capacity < 0) return fail(B200_ERR_INVALID, "bad block size");
+  if (use_tc_moe(quant, block_size, expert_capacity)) {
+    if (tile_rows) *tile_rows = 192;
+    return B200_PATH_TCGEN05;
+  }
+  if (tile_rows) *tile_rows = block_size;
+  return B200_PATH_STREAM;
 }
 
 int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,

@@ -36,6 +36,9 @@ GATED_NONE = 0
 GATED_FUSED = 1
 GATED_SPLIT = 2
 
+PATH_STREAM = 16
+PATH_TCGEN05 = 17
+
 _LOCK = threading.Lock()
 _LIB = None
 
@@ -95,6 +98,10 @@ SIGNATURES = {
          c_int32, c_void_p, c_int32, c_void_p],
     ),
     "b200_linear_noalloc_status": (c_int32, [ctypes.POINTER(c_int32), c_int32, c_void_p]),
+    "b200_linear_path": (
+        c_int32, [c_int64, c_int64, c_int64, ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]
+    ),
+    "b200_moe_path": (c_int32, [c_int32, c_int32, c_int64, ctypes.POINTER(c_int32)]),
     "b200_moe_gemm": (
         c_int32,
         [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int32,

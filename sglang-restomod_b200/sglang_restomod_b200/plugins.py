@@ -122,6 +122,9 @@ def load_enabled(env: Mapping[str, str] | None = None) -> Sequence[str]:
     names = selection(env)
     attest.set_selected(names)
     registered = [n for n in names if activate(COMPONENTS[n])]
+    from . import census
+
+    census.install_profile()  # only when SGLANG_B200_PROFILE asks for it
     attest.write()
     logger.info("sglang-restomod-b200: %d of %d selected components registered (%s)",
                 len(registered), len(names), ", ".join(registered) or "none")

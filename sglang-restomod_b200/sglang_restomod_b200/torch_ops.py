@@ -27,7 +27,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib, ops
+from . import _lib, census, ops
 
 NAMESPACE = "b200_moe"
 
@@ -242,6 +242,7 @@ def _linear_cols(n, gated_mode):
 @_impl("linear")
 def _linear_cuda(x, packed, n, quant, scales=None, global_scale=None, gated_mode=0,
                  out_dtype=None):
+    census.note_linear("linear", x.numel() // max(x.shape[-1], 1), n, x.shape[-1])
     return ops.linear(x, packed, n, quant=quant, scales=scales, global_scale=global_scale,
                       gated_mode=gated_mode, out_dtype=out_dtype)
 
@@ -254,6 +255,7 @@ def _linear_fake(x, packed, n, quant, scales=None, global_scale=None, gated_mode
 
 @_impl("linear_out")
 def _linear_out_cuda(x, packed, n, quant, scales, global_scale, gated_mode, out):
+    census.note_linear("linear", x.numel() // max(x.shape[-1], 1), n, x.shape[-1])
     ops.linear(x, packed, n, quant=quant, scales=scales, global_scale=global_scale,
                gated_mode=gated_mode, out=out)
 
@@ -267,6 +269,9 @@ def _linear_out_fake(x, packed, n, quant, scales, global_scale, gated_mode, out)
 def _moe_gemm_cuda(a, packed, n, quant, num_experts, sorted_token_ids, expert_ids,
                    num_tokens_post_pad, block_size, top_k, num_routes, c, scales=None,
                    global_scale=None, topk_weights=None, mul_topk_weights=False, gated_mode=0):
+    census.note_moe("moe_gemm", quant, a.shape[0], num_routes, num_experts, block_size,
+                    min(expert_ids.numel(), sorted_token_ids.numel() // block_size), n,
+                    a.shape[-1])
     ops.moe_gemm(a, packed, n, quant=quant, num_experts=num_experts,
                  sorted_token_ids=sorted_token_ids, expert_ids=expert_ids,
                  num_tokens_post_pad=num_tokens_post_pad, block_size=block_size, top_k=top_k,
@@ -283,6 +288,12 @@ def _moe_gemm_fake(a, packed, n, quant, num_experts, sorted_token_ids, expert_id
 
 
 # ---------------------------------------------------------------- the layer
+def _note_layer(op, quant, topk_ids, num_experts, block_size, inter, hidden):
+    t, k = topk_ids.shape
+    census.note_moe(op, quant, t, t * k, num_experts, block_size,
+                    ops.align_capacity(t * k, num_experts, block_size)[1], 2 * inter, hidden)
+
+
 def _layer_kw(quant, num_experts, inter, w13, w2, w13_scales, w2_scales, w13_global, w2_global,
               block_size, routed_scaling_factor, shared_out):
     return dict(quant=quant, num_experts=num_experts, inter=inter, w13=w13, w2=w2,
@@ -295,6 +306,7 @@ def _layer_kw(quant, num_experts, inter, w13, w2, w13_scales, w2_scales, w13_glo
 def _layer_cuda(x, topk_ids, topk_weights, quant, num_experts, inter, w13, w2, w13_scales=None,
                 w2_scales=None, w13_global=None, w2_global=None, block_size=16,
                 routed_scaling_factor=1.0, shared_out=None):
+    _note_layer("moe_layer", quant, topk_ids, num_experts, block_size, inter, x.shape[-1])
     return ops.moe_layer_forward(x, topk_ids, topk_weights, **_layer_kw(
         quant, num_experts, inter, w13, w2, w13_scales, w2_scales, w13_global, w2_global,
         block_size, routed_scaling_factor, shared_out))
@@ -311,6 +323,7 @@ def _layer_fake(x, topk_ids, topk_weights, quant, num_experts, inter, w13, w2, w
 def _layer_out_cuda(x, topk_ids, topk_weights, quant, num_experts, inter, w13, w2, w13_scales,
                     w2_scales, w13_global, w2_global, block_size, routed_scaling_factor,
                     shared_out, out):
+    _note_layer("moe_layer", quant, topk_ids, num_experts, block_size, inter, x.shape[-1])
     ops.moe_layer_forward(x, topk_ids, topk_weights, out=out, **_layer_kw(
         quant, num_experts, inter, w13, w2, w13_scales, w2_scales, w13_global, w2_global,
         block_size, routed_scaling_factor, shared_out))
@@ -326,6 +339,10 @@ def _layer_out_fake(x, topk_ids, topk_weights, quant, num_experts, inter, w13, w
 @_impl("moe_layer_forward_fused_shared")
 def _layer_fused_cuda(x, topk_ids, topk_weights, quant, num_experts, inter, w13, w2, w13_scales,
                       w2_scales, block_size, routed_scaling_factor, shared_route_weight, out):
+    t, k = topk_ids.shape
+    census.note_moe("moe_layer+shared", quant, t, t * (k + 1), num_experts + 1, block_size,
+                    ops.align_capacity(t * (k + 1), num_experts + 1, block_size)[1], 2 * inter,
+                    x.shape[-1])
     _, ids, w = ops.moe_layer_forward_fused_shared(
         x, topk_ids, topk_weights, quant=quant, num_experts=num_experts, inter=inter, w13=w13,
         w2=w2, w13_scales=w13_scales, w2_scales=w2_scales, block_size=block_size,
@@ -377,6 +394,8 @@ def _act_quant_fake(x, scales_ld=None):
 
 @_impl("w8a8_linear")
 def _w8a8_linear_cuda(x, w, w_scales, gated_mode=0, out_dtype=None):
+    census.note("w8a8_linear", f"m={x.numel() // max(x.shape[-1], 1)}", f"n={w.shape[-2]}",
+                f"k={x.shape[-1]}")
     return ops.w8a8_linear(x, w, w_scales, gated_mode=gated_mode, out_dtype=out_dtype)
 
 
@@ -390,6 +409,8 @@ def _w8a8_linear_fake(x, w, w_scales, gated_mode=0, out_dtype=None):
 def _w8a8_moe_cuda(a, w, w_scales, num_experts, sorted_token_ids, expert_ids,
                    num_tokens_post_pad, block_size, top_k, num_routes, c, topk_weights=None,
                    mul_topk_weights=False, gated_mode=0):
+    census.note("w8a8_moe_gemm", f"routes={num_routes}", f"experts={num_experts}",
+                f"block={block_size}", f"n={w.shape[-2]}", f"k={a.shape[-1]}")
     ops.w8a8_moe_gemm(a, w, w_scales, num_experts=num_experts, sorted_token_ids=sorted_token_ids,
                       expert_ids=expert_ids, num_tokens_post_pad=num_tokens_post_pad,
                       block_size=block_size, top_k=top_k, num_routes=num_routes, c=c,

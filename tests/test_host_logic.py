@@ -3,6 +3,7 @@ test strategy: registry, attestation, mode switches, shape guards)."""
 
 from __future__ import annotations
 
+import ctypes
 import json
 from types import SimpleNamespace
 
@@ -299,3 +300,72 @@ def test_attest_failure_overrides_inactive_and_write_is_atomic(tmp_path):
     assert json.loads(path.read_text())["selected"] == ["a", "b", "c"]
     assert [p.name for p in tmp_path.iterdir()] == ["out.json"]
     assert attest.write(str(tmp_path / "missing-dir" / "x.json")) is None
+
+
+# ------------------------------------------------------- census and profile
+def test_census_records_the_library_path_decision():
+    from sglang_restomod_b200 import _lib, census
+
+    lib = _lib.load()
+    rows = ctypes.c_int32(0)
+    parts = ctypes.c_int32(0)
+    assert lib.b200_linear_path(1, 25600, 5120, ctypes.byref(rows), ctypes.byref(parts)) == \
+        _lib.PATH_STREAM and rows.value == 8
+    assert lib.b200_linear_path(64, 1024, 5120, ctypes.byref(rows), ctypes.byref(parts)) == \
+        _lib.PATH_TCGEN05 and parts.value > 1
+    assert lib.b200_moe_path(0, 8, 100, ctypes.byref(rows)) == _lib.PATH_STREAM and rows.value == 8
+    assert lib.b200_moe_path(0, 64, 100, ctypes.byref(rows)) == _lib.PATH_TCGEN05
+    census.reset()
+    census.enable(True)
+    try:
+        census.note_linear("linear", 4, 25600, 5120)
+        census.note_linear("linear", 4, 25600, 5120)
+        census.note_moe("moe_layer", 0, 128, 1024, 256, 8, 200, 4096, 7168)
+        line = census.report()
+    finally:
+        census.enable(False)
+        census.reset()
+    assert "linear stream/8rows m=4 n=25600 k=5120 x2" in line
+    assert "moe_layer stream/8rows q=0 tokens=128 routes/expert=4.0 block=8" in line
+    census.note_linear("linear", 4, 25600, 5120)  # disabled: nothing recorded
+    assert census.tally() == {}
+
+
+def test_profile_window_wraps_forward_once(monkeypatch, tmp_path):
+    from sglang_restomod_b200 import census
+
+    class FakeProfile:
+        def __init__(self, activities):
+            self.entered = False
+
+        def __enter__(self):
+            self.entered = True
+
+        def __exit__(self, *a):
+            pass
+
+        def key_averages(self):
+            return type("T", (), {"table": lambda self, **kw: "kernel table"})()
+
+    monkeypatch.setattr(torch.profiler, "profile", FakeProfile)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda: None)
+    out = tmp_path / "prof.txt"
+    monkeypatch.setenv(census.ENV_PROFILE, "2")
+    monkeypatch.setenv(census.ENV_PROFILE_OUT, str(out))
+
+    class Runner:
+        calls = 0
+
+        def forward(self, x):
+            Runner.calls += 1
+            return x + 1
+
+    assert census.install_profile(Runner)
+    assert not census.install_profile(Runner)  # already wrapped
+    r = Runner()
+    for i in range(3):
+        assert r.forward(i) == i + 1
+        assert out.exists() == (i == 2)  # forwards 1 and 2 profiled, written after the second
+    assert out.read_text() == "kernel table"
+    monkeypatch.setenv(census.ENV_PROFILE, "zero")
+    assert not census.install_profile(Runner)
