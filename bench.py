@@ -339,8 +339,9 @@ class MoEWorkload:
             flops += 2 * self.tokens * 3 * shape.hidden * shape.shared_inter
         return wbytes + act, flops, touched
 
-    def dominant(self):
-        """Closure timing the gate/up expert GEMM alone (the largest kernel)."""
+    def dominant(self, loads_only: bool = False):
+        """Closure timing the gate/up expert GEMM alone (the largest kernel);
+        ``loads_only``: its data-movement floor (same copies, no math)."""
         import torch
 
         from sglang_restomod_b200 import _lib, ops
@@ -370,7 +371,8 @@ class MoEWorkload:
                          num_experts=layer.num_experts, sorted_token_ids=sorted_ids,
                          expert_ids=expert_ids, num_tokens_post_pad=ntpp, block_size=bs,
                          top_k=ids.shape[1], num_routes=routes, c=c, scales=layer.w13_scales,
-                         global_scale=layer.w13_global, gated_mode=_lib.GATED_FUSED)
+                         global_scale=layer.w13_global, gated_mode=_lib.GATED_FUSED,
+                         loads_only=loads_only)
 
         valid = ids[(ids >= 0) & (ids < layer.num_experts)]
         touched = int(torch.unique(valid).numel())
@@ -406,11 +408,11 @@ class DenseWorkload:
         self.h_x = self.x.cpu().pin_memory()
         self.h_out = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
 
-    def _run(self, x, out=None):
+    def _run(self, x, out=None, loads_only=False):
         from sglang_restomod_b200 import _lib, ops
 
         ops.linear(x, self.packed, self.n, quant=_lib.QUANT_FP8_BLOCK, scales=self.scales,
-                   out=self.out if out is None else out)
+                   out=self.out if out is None else out, loads_only=loads_only)
 
     def step(self):
         self._run(self.x)
@@ -435,10 +437,11 @@ class DenseWorkload:
         wbytes = self.n * self.k + (self.n // 128) * (self.k // 128) * 4
         return wbytes + self.m * (self.k + self.n) * 2, 2 * self.m * self.n * self.k, 1
 
-    def dominant(self):
+    def dominant(self, loads_only: bool = False):
         # b200_linear runs 33+ rows on the tcgen05 GEMM, fewer on the stream GEMM
         name = "tc_gemm_kernel (dense)" if self.m >= 33 else "stream_gemm_kernel (dense)"
-        return self.step, self.algorithmic()[0], name, 2 * self.m * self.n * self.k
+        run = (lambda: self._run(self.x, loads_only=True)) if loads_only else self.step
+        return run, self.algorithmic()[0], name, 2 * self.m * self.n * self.k
 
 
 # -------------------------------------------------------------- CPU legs
@@ -633,6 +636,24 @@ def sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse=None):
     torch.cuda.synchronize()
     dom_ms = start.elapsed_time(end) / reps
     _, dom_bytes, dom_name, dom_flops = doms[0]
+    # the same kernel's loads-only twin: the floor set by moving its bytes
+    floor_run = wls[0].dominant(loads_only=True)[0]
+    floor_ms = None
+    if floor_run is not None:
+        floor_run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            floor_run()
+        graphs.append(g)
+        g.replay()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        floor_ms = start.elapsed_time(end) / reps
     hbm_frac = dom_bytes / (dom_ms * 1e-3) / 1e9 / hbm_gbs
     tensor_frac = dom_flops / (dom_ms * 1e-3) / 1e12 / bf16_tflops
     prefill = wl.tokens >= 2048
@@ -645,6 +666,7 @@ def sweep_point(name, args, device, hbm_gbs, bf16_tflops, reuse=None):
         "frac": tensor_frac if prefill else hbm_frac,
         "dominant_hbm_frac": hbm_frac, "dominant_tensor_frac": tensor_frac,
         "weight_copies": copies,
+        "dominant_loads_only_us": None if floor_ms is None else floor_ms * 1e3,
     }
     del graphs, fns, dom_fns, doms, wls, wl
     torch.cuda.synchronize()

@@ -248,6 +248,31 @@ int b200_linear_noalloc(int32_t quant, const void* x, int32_t x_dtype, int64_t m
 int b200_linear_noalloc_status(int32_t* bits, int32_t reset, void* stream);
 
 /*
+ * The data-movement floor of b200_linear / b200_moe_gemm, for measurement:
+ * the same arguments and launches, every weight and activation copy and
+ * every pipeline barrier hand-off, but no conversion, MMA or store (y / c
+ * are left untouched). The reference keeps the same instrument as a
+ * kCompute=false instantiation of its NVFP4 decode GEMV
+ * (quant/sm70_fp4_moe/csrc/decode_gemv_qpn2.cu:63-200); timing a call
+ * against its loads-only twin separates the cost of moving the bytes from
+ * the cost of the math.
+ */
+int b200_linear_loads_only(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                           const uint8_t* w_packed, const float* w_scales,
+                           const float* global_scale, int64_t n, int32_t gated_mode, void* y,
+                           int32_t y_dtype, void* workspace, int64_t workspace_bytes,
+                           void* stream);
+int b200_moe_gemm_loads_only(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
+                             int64_t k, const uint8_t* w_packed, const float* w_scales,
+                             const float* global_scale, int32_t num_experts, int64_t n,
+                             int32_t gated_mode, const int32_t* sorted_token_ids,
+                             const int32_t* expert_ids, int64_t expert_capacity,
+                             const int32_t* num_tokens_post_pad, int32_t block_size,
+                             int32_t top_k, int64_t num_routes, const float* topk_weights,
+                             int32_t mul_topk_weights, void* c, int32_t c_dtype, int64_t ldc,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Which kernel a call takes (for census and profiling; no counterpart in the
  * reference, whose dispatcher decides the same question in Python,
  * quant/sm70_fp4_moe/decode_gemv.py:183-219). Returns B200_PATH_STREAM (the

@@ -446,10 +446,14 @@ int64_t b200_gemm_workspace_bytes(int64_t convert_elems) {
   return stream_ws_bytes() + align_up(convert_elems * 2);
 }
 
-int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+}  // extern "C"
+
+namespace {
+
+int linear_impl(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
                 const uint8_t* w_packed, const float* w_scales, const float* global_scale,
                 int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* workspace,
-                int64_t workspace_bytes, void* stream) {
+                int64_t workspace_bytes, void* stream, bool loads_only) {
   int rc = check_weight_shape(quant, n, k, gated_mode);
   if (rc) return rc;
   if (!valid_dtype16(x_dtype) || !valid_dtype16(y_dtype))
@@ -504,8 +508,9 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     // idle SMs is faster (128 x 4096 x 7168: 43 us in three parts, 35 us in
     // four; 64 x 5120 x 25600: 64 us in three, 60 us in seven).
     p.ksplit = dense_k_parts(m, n, k);
+    p.loads_only = loads_only ? 1 : 0;
     rc = run_tc(quant, p, ws, false, st);
-    if (rc || p.ksplit <= 1) return rc;
+    if (rc || p.ksplit <= 1 || loads_only) return rc;
     return check_cuda(launch_tc_split_finish(p, st), "split-K finish launch");
   }
   int64_t used = 0;
@@ -532,9 +537,31 @@ int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
   p.out_f16 = y_dtype == B200_DTYPE_F16;
   const int nt = nt_for_rows(m);
   p.dense_m = (int)m;
+  p.loads_only = loads_only ? 1 : 0;
   const long long groups = (m + 8 * nt - 1) / (8 * nt);
   const long long units = groups * (n / 128) * (k / 128);
   return run_stream(quant, nt, p, units, ws, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_linear(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                int64_t n, int32_t gated_mode, void* y, int32_t y_dtype, void* workspace,
+                int64_t workspace_bytes, void* stream) {
+  return linear_impl(quant, x, x_dtype, m, k, w_packed, w_scales, global_scale, n, gated_mode, y,
+                     y_dtype, workspace, workspace_bytes, stream, false);
+}
+
+int b200_linear_loads_only(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_t k,
+                           const uint8_t* w_packed, const float* w_scales,
+                           const float* global_scale, int64_t n, int32_t gated_mode, void* y,
+                           int32_t y_dtype, void* workspace, int64_t workspace_bytes,
+                           void* stream) {
+  return linear_impl(quant, x, x_dtype, m, k, w_packed, w_scales, global_scale, n, gated_mode, y,
+                     y_dtype, workspace, workspace_bytes, stream, true);
 }
 
 int b200_linear_path(int64_t m, int64_t n, int64_t k, int32_t* tile_rows, int32_t* k_parts) {
@@ -567,14 +594,19 @@ int b200_moe_path(int32_t quant, int32_t block_size, int64_t expert_capacity, in
   return B200_PATH_STREAM;
 }
 
-int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+}  // extern "C"
+
+namespace {
+
+int moe_gemm_impl(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
                   const uint8_t* w_packed, const float* w_scales, const float* global_scale,
                   int32_t num_experts, int64_t n, int32_t gated_mode,
                   const int32_t* sorted_token_ids, const int32_t* expert_ids,
                   int64_t expert_capacity, const int32_t* num_tokens_post_pad,
                   int32_t block_size, int32_t top_k, int64_t num_routes,
                   const float* topk_weights, int32_t mul_topk_weights, void* c, int32_t c_dtype,
-                  int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream) {
+                  int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream,
+                  bool loads_only) {
   int rc = check_weight_shape(quant, n, k, gated_mode);
   if (rc) return rc;
   if (!valid_dtype16(a_dtype) || !valid_dtype16(c_dtype))
@@ -637,9 +669,45 @@ int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.out = c;
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
+  p.loads_only = loads_only ? 1 : 0;
   if (tc) return run_tc(quant, p, ws, false, st);
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_moe_gemm(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows, int64_t k,
+                  const uint8_t* w_packed, const float* w_scales, const float* global_scale,
+                  int32_t num_experts, int64_t n, int32_t gated_mode,
+                  const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                  int64_t expert_capacity, const int32_t* num_tokens_post_pad,
+                  int32_t block_size, int32_t top_k, int64_t num_routes,
+                  const float* topk_weights, int32_t mul_topk_weights, void* c, int32_t c_dtype,
+                  int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream) {
+  return moe_gemm_impl(quant, a, a_dtype, a_rows, k, w_packed, w_scales, global_scale,
+                       num_experts, n, gated_mode, sorted_token_ids, expert_ids, expert_capacity,
+                       num_tokens_post_pad, block_size, top_k, num_routes, topk_weights,
+                       mul_topk_weights, c, c_dtype, ldc, workspace, workspace_bytes, stream,
+                       false);
+}
+
+int b200_moe_gemm_loads_only(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
+                             int64_t k, const uint8_t* w_packed, const float* w_scales,
+                             const float* global_scale, int32_t num_experts, int64_t n,
+                             int32_t gated_mode, const int32_t* sorted_token_ids,
+                             const int32_t* expert_ids, int64_t expert_capacity,
+                             const int32_t* num_tokens_post_pad, int32_t block_size,
+                             int32_t top_k, int64_t num_routes, const float* topk_weights,
+                             int32_t mul_topk_weights, void* c, int32_t c_dtype, int64_t ldc,
+                             void* workspace, int64_t workspace_bytes, void* stream) {
+  return moe_gemm_impl(quant, a, a_dtype, a_rows, k, w_packed, w_scales, global_scale,
+                       num_experts, n, gated_mode, sorted_token_ids, expert_ids, expert_capacity,
+                       num_tokens_post_pad, block_size, top_k, num_routes, topk_weights,
+                       mul_topk_weights, c, c_dtype, ldc, workspace, workspace_bytes, stream,
+                       true);
 }
 
 int64_t b200_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,

@@ -50,6 +50,9 @@ struct StreamParams {
   float* ws;             // split-pair partial sums, kWsSlotFloats per grid slot, zeroed
   int* ws_cnt;           // one arrival counter per grid slot, zeroed
   int* status;           // device error bits
+  // Loads only (pipeline floor, for measurement): every copy and barrier
+  // hand-off of the call runs, the conversions, MMAs and stores do not.
+  int loads_only;
 };
 
 constexpr int kWsSlotFloats = 128 * 64;

@@ -473,6 +473,12 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
       *abort_flag = 1;
       ok = false;
     }
+    if (p.loads_only) {
+      // pipeline floor: release the stage unread; no math, no stores
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&empty[s]);
+      continue;
+    }
     if (ok) {
       const uint8_t* stage = smem + (size_t)s * L::kStage;
       // NT == 1 keeps two accumulators (even / odd K-steps) so the MMA

@@ -463,10 +463,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t acol = tmem + kACol0 + (uint32_t)s * kAStageCols;
         const uint32_t blo = b_lo0 + (uint32_t)sb * (kBTile >> 4);
         if (elect_one()) {
+          if (!p.loads_only) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_ts(dcol, acol + 8u * kk, ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc,
-                   (ts > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ts(dcol, acol + 8u * kk, ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc,
+                     (ts > 0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit(&ctl->empty[s]);
           mma_commit(&ctl->bempty[sb]);
         }
@@ -621,6 +623,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint8_t* raw = smem + kOffRaw + rs * kUnitBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        if (p.loads_only) {
+          // pipeline floor: hand the A stage on without dequantizing into it
+          const int s0 = (int)(t % kStages);
+          ok = warp_wait(&ctl->empty[s0], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->full[s0]);
+          ++t;
+          continue;
+        }
         uint32_t v[32];
         int s = 0;
         if constexpr (kFp4) {
@@ -746,7 +760,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (!warp_wait(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl, p.status)) break;
       tc_fence_after();
-      const int ngroups = (it.rows + 31) >> 5;
+      const int ngroups = p.loads_only ? 0 : (it.rows + 31) >> 5;
       for (int gg = 0; gg < ngroups; ++gg) {
         const int og = pick(orow, gg);
         const float wg = pick(wr, gg);

@@ -98,6 +98,17 @@ SIGNATURES = {
          c_int32, c_void_p, c_int32, c_void_p],
     ),
     "b200_linear_noalloc_status": (c_int32, [ctypes.POINTER(c_int32), c_int32, c_void_p]),
+    "b200_linear_loads_only": (
+        c_int32,
+        [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
+         c_int32, c_void_p, c_int32, c_void_p, c_int64, c_void_p],
+    ),
+    "b200_moe_gemm_loads_only": (
+        c_int32,
+        [c_int32, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int32,
+         c_int64, c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int64,
+         c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p],
+    ),
     "b200_linear_path": (
         c_int32, [c_int64, c_int64, c_int64, ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]
     ),

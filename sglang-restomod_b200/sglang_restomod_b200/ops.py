@@ -293,8 +293,9 @@ def gemm_workspace_bytes(convert_elems: int) -> int:
 def linear(x: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int,
            scales: torch.Tensor | None = None, global_scale: torch.Tensor | None = None,
            gated_mode: int = _lib.GATED_NONE, out: torch.Tensor | None = None,
-           out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """Dense ``y = x . dequant(W)^T`` on a prepacked bank (one expert)."""
+           out_dtype: torch.dtype | None = None, loads_only: bool = False) -> torch.Tensor:
+    """Dense ``y = x . dequant(W)^T`` on a prepacked bank (one expert).
+    ``loads_only``: the call's data-movement floor (no math, ``out`` untouched)."""
     _contig(x, "x")
     x2 = x.reshape(-1, x.shape[-1])
     m, k = (int(d) for d in x2.shape)
@@ -302,8 +303,9 @@ def linear(x: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int,
     if out is None:
         out = torch.empty(m, cols, dtype=out_dtype or x.dtype, device=x.device)
     ws = workspace(gemm_workspace_bytes(m * k if x.dtype == torch.bfloat16 else 0), x.device)
+    fn = lib().b200_linear_loads_only if loads_only else lib().b200_linear
     _lib.check(
-        lib().b200_linear(
+        fn(
             quant, _vp(x2), _code(x2, "x"), m, k, _vp(packed), _vp(scales), _vp(global_scale), n,
             gated_mode, _vp(out), _code(out, "out"), _vp(ws), ws.numel(), _stream(x.device),
         )
@@ -316,8 +318,10 @@ def moe_gemm(a: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int, num_e
              num_tokens_post_pad: torch.Tensor, block_size: int, top_k: int, num_routes: int,
              c: torch.Tensor, scales: torch.Tensor | None = None,
              global_scale: torch.Tensor | None = None, topk_weights: torch.Tensor | None = None,
-             mul_topk_weights: bool = False, gated_mode: int = _lib.GATED_NONE) -> torch.Tensor:
-    """Grouped expert GEMM with ``moe_wna16_marlin_gemm`` routing semantics."""
+             mul_topk_weights: bool = False, gated_mode: int = _lib.GATED_NONE,
+             loads_only: bool = False) -> torch.Tensor:
+    """Grouped expert GEMM with ``moe_wna16_marlin_gemm`` routing semantics.
+    ``loads_only``: the call's data-movement floor (no math, ``c`` untouched)."""
     _contig(a, "a")
     _contig(c, "c")
     a_rows, k = (int(d) for d in a.reshape(-1, a.shape[-1]).shape)
@@ -331,8 +335,9 @@ def moe_gemm(a: torch.Tensor, packed: torch.Tensor, n: int, *, quant: int, num_e
         raise ValueError("mul_topk_weights needs one topk weight per route")
     groups = min(expert_ids.numel(), sorted_token_ids.numel() // block_size)
     ws = workspace(gemm_workspace_bytes(a_rows * k if a.dtype == torch.bfloat16 else 0), a.device)
+    fn = lib().b200_moe_gemm_loads_only if loads_only else lib().b200_moe_gemm
     _lib.check(
-        lib().b200_moe_gemm(
+        fn(
             quant, _vp(a), _code(a, "a"), a_rows, k, _vp(packed), _vp(scales), _vp(global_scale),
             num_experts, n, gated_mode, _vp(sorted_token_ids), _vp(expert_ids), groups,
             _vp(num_tokens_post_pad), block_size, top_k, num_routes, _vp(topk_weights),
