@@ -149,9 +149,19 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
   p.status = ws.status;
   long long grid = (long long)max_grid_slots();
   if (nt >= 4) grid = (long long)stream_gemm_ctas_per_sm(nt) * device_sm_count();
+  // A few short (group, row block) pairs - at most one per SM, each of at
+  // most the whole-pair stage count - stream one pair per CTA; then one CTA
+  // per SM with a deeper ring keeps more of each pair's bytes in flight.
+  const int sms = device_sm_count();
+  const long long kch = p.K / 128;
+  const long long kcs = (kch + stream_gemm_stage_units(quant) - 1) / stream_gemm_stage_units(quant);
+  const long long max_pairs = max_units / (kch > 0 ? kch : 1);
+  const bool solo = nt <= 2 && max_pairs <= sms && kcs <= stream_gemm_whole_pair_max_stages();
+  if (solo) grid = sms;
   if (grid > max_units) grid = max_units;
   if (grid < 1) grid = 1;
-  return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream), "stream GEMM launch");
+  return check_cuda(launch_stream_gemm(quant, nt, p, (int)grid, stream, solo),
+                    "stream GEMM launch");
 }
 
 // tcgen05 GEMM; in moe mode the plan is built first unless `planned` (the

@@ -63,8 +63,12 @@ constexpr int kUnitK = 128;
 constexpr uint32_t kFp8UnitBytes = kUnitRows * kUnitK;                       // 16 KiB
 constexpr uint32_t kFp4UnitBytes = kUnitRows * kUnitK / 2 + kUnitRows * 8;   // 9 KiB
 
+// solo: one CTA per SM with a deeper stage ring, for calls whose (group, row
+// block) pairs each fit one CTA (grid <= SMs; nt <= 2, else ignored).
 cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int grid,
-                               cudaStream_t stream);
+                               cudaStream_t stream, bool solo = false);
+int stream_gemm_whole_pair_max_stages();
+int stream_gemm_stage_units(int quant);
 int stream_gemm_ctas_per_sm(int nt);
 
 // tcgen05 grouped GEMM (FP8 or NVFP4 weights, f16 activations). Moe mode first runs

@@ -56,6 +56,13 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 #ifndef B200_STREAM_MAX_STAGES
 #define B200_STREAM_MAX_STAGES 4
 #endif
+// Stages of the one-CTA-per-SM launch used when a call has no more
+// (group, row block) pairs than SMs and each is short (small decode
+// batches): the whole pair streams through one CTA, so the bytes it keeps
+// in flight are what its latency is divided by.
+#ifndef B200_STREAM_SOLO_MAX_STAGES
+#define B200_STREAM_SOLO_MAX_STAGES 6
+#endif
 #ifndef B200_STREAM_PRELOAD_NT
 #define B200_STREAM_PRELOAD_NT 1
 #endif
@@ -123,13 +130,14 @@ constexpr uint32_t stage_bytes(int sub, uint32_t w, uint32_t x, uint32_t sc) {
 // Stage = kSub consecutive weight units of one pair (contiguous, one bulk
 // copy) followed by their kSub activation tiles (and, FP8, their block
 // scales); as many stages as fit when
-// CtasPerSm<NT> CTAs share an SM, capped at B200_STREAM_MAX_STAGES.
-template <int Q, int NT>
+// CPS CTAs share an SM, capped at B200_STREAM_MAX_STAGES (CPS = 1, the
+// launch for a few short pairs, at B200_STREAM_SOLO_MAX_STAGES).
+template <int Q, int NT, int CPS = CtasPerSm<NT>::value>
 struct Layout {
   static constexpr uint32_t kW = UnitBytes<Q>::value;
   static constexpr uint32_t kX = 8 * NT * kRowStride;
   static constexpr uint32_t kSc = StageScaleBytes<Q>::value;
-  static constexpr int kBudget = kSmemPerSm / CtasPerSm<NT>::value - kSmemReserved - 128;
+  static constexpr int kBudget = kSmemPerSm / CPS - kSmemReserved - 128;
   static constexpr int kReq = SubUnits<Q>::value;
   static constexpr int kSub =
       kReq >= 4 && 2 * stage_bytes(4, kW, kX, kSc) <= (uint32_t)kBudget   ? 4
@@ -139,7 +147,8 @@ struct Layout {
   static constexpr uint32_t kScOff = kSub * (kW + kX);     // block scales
   static constexpr uint32_t kStage = stage_bytes(kSub, kW, kX, kSc);
   static constexpr int kFit = kBudget / (int)kStage;
-  static constexpr int kS = kFit > B200_STREAM_MAX_STAGES ? B200_STREAM_MAX_STAGES : kFit;
+  static constexpr int kCap = CPS == 1 ? B200_STREAM_SOLO_MAX_STAGES : B200_STREAM_MAX_STAGES;
+  static constexpr int kS = kFit > kCap ? kCap : kFit;
   static constexpr size_t kSmem = (size_t)kS * kStage + 2 * kS * sizeof(uint64_t) + 16;
   static_assert(kS >= 2, "stage does not fit");
   static_assert(kXOff % 16 == 0 && kX % 16 == 0 && kScOff % 8 == 0, "cp.async destinations");
@@ -232,10 +241,10 @@ __device__ __forceinline__ void store_pair(const StreamParams& p, long long gi, 
   }
 }
 
-template <int Q, int NT>
-__global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
+template <int Q, int NT, int CPS>
+__global__ void __launch_bounds__(kThreads, CPS)
     stream_gemm_kernel(const StreamParams p) {
-  using L = Layout<Q, NT>;
+  using L = Layout<Q, NT, CPS>;
   constexpr uint32_t UB = L::kW;
   constexpr int kRows = 8 * NT;
   constexpr int kSub = L::kSub;
@@ -710,28 +719,43 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<NT>::value)
   }
 }
 
-template <int Q, int NT>
+template <int Q, int NT, int CPS = CtasPerSm<NT>::value>
 cudaError_t launch_one(const StreamParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = Layout<Q, NT>::kSmem;
+  const size_t smem = Layout<Q, NT, CPS>::kSmem;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(stream_gemm_kernel<Q, NT>,
+    cudaError_t err = cudaFuncSetAttribute(stream_gemm_kernel<Q, NT, CPS>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
-  return launch_pdl(stream_gemm_kernel<Q, NT>, dim3(grid), dim3(kThreads), smem, stream, p);
+  return launch_pdl(stream_gemm_kernel<Q, NT, CPS>, dim3(grid), dim3(kThreads), smem, stream, p);
 }
 
 }  // namespace
 
+int stream_gemm_whole_pair_max_stages() { return B200_STREAM_WHOLE_PAIR_MAX_STAGES; }
+
+// K-units per stage of the nt <= 2 layouts (the same at one or two CTAs per SM).
+int stream_gemm_stage_units(int quant) {
+  return quant == kQuantFp8Block ? Layout<kQuantFp8Block, 1>::kSub : Layout<kQuantNvfp4, 1>::kSub;
+}
+
 int stream_gemm_ctas_per_sm(int nt) { return nt >= 8 ? CtasPerSm<8>::value : CtasPerSm<1>::value; }
 
 cudaError_t launch_stream_gemm(int quant, int nt, const StreamParams& p, int grid,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, bool solo) {
+  if (solo && nt <= 2) {
+    // one CTA per SM, deeper ring (few short pairs, one per CTA)
+    if (quant == kQuantFp8Block)
+      return nt == 1 ? launch_one<kQuantFp8Block, 1, 1>(p, grid, stream)
+                     : launch_one<kQuantFp8Block, 2, 1>(p, grid, stream);
+    return nt == 1 ? launch_one<kQuantNvfp4, 1, 1>(p, grid, stream)
+                   : launch_one<kQuantNvfp4, 2, 1>(p, grid, stream);
+  }
   if (quant == kQuantFp8Block) {
     switch (nt) {
       case 1: return launch_one<kQuantFp8Block, 1>(p, grid, stream);
