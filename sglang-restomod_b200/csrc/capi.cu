@@ -166,17 +166,31 @@ int run_stream(int32_t quant, int nt, StreamParams& p, long long max_units, WsVi
 
 // tcgen05 GEMM; in moe mode the plan is built first unless `planned` (the
 // layer's second GEMM reuses the first one's plan).
-int run_tc(int32_t quant, StreamParams& p, WsView& ws, bool planned, cudaStream_t stream) {
+int run_tc(int32_t quant, StreamParams& p, WsView& ws, bool planned, cudaStream_t stream,
+           bool narrow = false) {
   p.ws = ws.partials;
   p.ws_cnt = ws.counters;
   p.status = ws.status;
   if (p.sorted_ids != nullptr && !planned) {
-    int rc = check_cuda(launch_tc_plan(p, ws.plan, kTcPlanCap, stream), "tcgen05 plan launch");
+    int rc = check_cuda(narrow ? launch_tc_plan_slots(p, ws.plan, kTcPlanCap, tc_narrow_slots(),
+                                                      stream)
+                               : launch_tc_plan(p, ws.plan, kTcPlanCap, stream),
+                        "tcgen05 plan launch");
     if (rc) return rc;
   }
   return check_cuda(launch_tc_gemm(quant == B200_QUANT_NVFP4 ? kQuantNvfp4 : kQuantFp8Block, p,
-                                   ws.plan, device_sm_count(), stream),
+                                   ws.plan, device_sm_count(), stream, narrow),
                     "tcgen05 GEMM launch");
+}
+
+// The narrow tcgen05 configuration (items of at most 64 slots, a deeper
+// weight ring) for blocks of 64 with few routes per expert: each expert's
+// routes then fit one or two such items anyway, and the wide configuration's
+// 192-row activation ring only takes shared memory from the weights in
+// flight. Measured on the expert-parallel owner shape (H=7168, I=2048, ~32
+// routes per expert): its loads-only twin took 256 of its 286 us there.
+bool narrow_moe(int32_t block_size, int64_t routes, int64_t experts) {
+  return block_size == 64 && routes <= 40 * experts;
 }
 
 // Route count from which the layer aligns with the multi-CTA kernels.
@@ -519,7 +533,7 @@ int linear_impl(int32_t quant, const void* x, int32_t x_dtype, int64_t m, int64_
     // four; 64 x 5120 x 25600: 64 us in three, 60 us in seven).
     p.ksplit = dense_k_parts(m, n, k);
     p.loads_only = loads_only ? 1 : 0;
-    rc = run_tc(quant, p, ws, false, st);
+    rc = run_tc(quant, p, ws, false, st, m <= tc_narrow_slots());
     if (rc || p.ksplit <= 1 || loads_only) return rc;
     return check_cuda(launch_tc_split_finish(p, st), "split-K finish launch");
   }
@@ -680,7 +694,7 @@ int moe_gemm_impl(int32_t quant, const void* a, int32_t a_dtype, int64_t a_rows,
   p.ldo = ldc;
   p.out_f16 = c_dtype == B200_DTYPE_F16;
   p.loads_only = loads_only ? 1 : 0;
-  if (tc) return run_tc(quant, p, ws, false, st);
+  if (tc) return run_tc(quant, p, ws, false, st, narrow_moe(block_size, num_routes, num_experts));
   const long long units = (long long)expert_capacity * (n / 128) * (k / 128);
   return run_stream(quant, block_size / 8, p, units, ws, st);
 }
@@ -953,7 +967,7 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
   p.out_f16 = 1;
   const int nt = block_size / 8;
   if (tc)
-    rc = run_tc(quant, p, ws, false, st);
+    rc = run_tc(quant, p, ws, false, st, narrow_moe(block_size, numel, num_experts));
   else
     rc = run_stream(quant, nt, p, blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
@@ -978,7 +992,7 @@ int layer_forward(int32_t quant, const void* x, int32_t x_dtype, int64_t tokens,
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
-    rc = run_tc(quant, q, ws, true, st);
+    rc = run_tc(quant, q, ws, true, st, narrow_moe(block_size, numel, num_experts));
   else
     rc = run_stream(quant, nt, q, blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;
@@ -1321,7 +1335,8 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   p.out_f16 = 1;
   const int nt = block_size / 8;
   if (tc)
-    rc = run_tc(quant, p, ws, false, st);
+    rc = run_tc(quant, p, ws, false, st,
+                narrow_moe(block_size, max_tokens * top_k, local_experts));
   else
     rc = run_stream(quant, nt, p, w.blocks * (2 * inter / 128) * (hidden / 128), ws, st);
   if (rc) return rc;
@@ -1345,7 +1360,8 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
-    rc = run_tc(quant, q, ws, true, st);
+    rc = run_tc(quant, q, ws, true, st,
+                narrow_moe(block_size, max_tokens * top_k, local_experts));
   else
     rc = run_stream(quant, nt, q, w.blocks * (hidden / 128) * (inter / 128), ws, st);
   if (rc) return rc;

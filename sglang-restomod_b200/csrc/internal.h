@@ -79,8 +79,12 @@ bool tc_gemm_supported(int block);  // block_m in {16, 32, 64, 128, 256}
 int tc_plan_slots_per_group(int block);  // plan entries a moe_align group may need
 int64_t tc_plan_bytes(int cap);
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream);
+// narrow: items of at most tc_narrow_slots() route slots / rows with a deeper
+// weight ring (few routes per expert, dense M <= 64); the moe plan must then
+// come from launch_tc_plan_slots(.., tc_narrow_slots(), ..).
 cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
-                           cudaStream_t stream);
+                           cudaStream_t stream, bool narrow = false);
+int tc_narrow_slots();
 // The same plan with items of at most max_slots route slots (blocks larger
 // than max_slots are cut in half first).
 cudaError_t launch_tc_plan_slots(const StreamParams& p, void* plan_buf, int cap, int max_slots,

@@ -59,47 +59,60 @@ namespace {
 using namespace tcg;
 using namespace tcg_host;
 
-constexpr int kNMax = 192;  // route slots (MMA N) per item
 // 16 warps: four per SM sub-partition, so each thread may hold 128 registers.
 constexpr int kTcWarps = 16;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
-constexpr int kLoadPasses = kNMax / (kLoadThreads / 2);  // rows per gather thread
 constexpr int kStages = 4;                               // 64-K A stages in tensor memory
 constexpr int kBStages = 4;                              // 64-K B stages in shared memory
-constexpr int kRawStages = 8;                            // 16 KiB FP8 units (weights in flight)
 constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
-constexpr uint32_t kBTile = kNMax * 128;                 // [192 rows][64 K] f16
-constexpr uint32_t kOffB = 0;
-constexpr uint32_t kOffRaw = kOffB + kBStages * kBTile;
-constexpr uint32_t kOffCtl = kOffRaw + kRawStages * kUnitBytes;
 constexpr int kInfoSlots = 8;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCols = kNMax;                     // per accumulator buffer
-constexpr uint32_t kACol0 = 2 * kAccCols;                // first A-stage column
 constexpr uint32_t kAStageCols = 32;                     // 64 K f16 = 32 columns
-constexpr size_t kTcSmem = kOffCtl + 1024 + 1024;        // control block + base alignment slack
-static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "tensor memory");
-static_assert(kBTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+constexpr int kNMaxWide = 192;   // route slots (MMA N) per item: the prefill tiles
+constexpr int kNMaxNarrow = 64;  // items of few routes (expert-parallel owners, dense M <= 64)
 
-struct Ctl {
+// Tile configuration by the item width NMAX. The narrow one gives the B ring
+// a quarter of the wide one's shared memory and the weight ring four more
+// 16 KiB units in flight: with ~32 routes per expert the call is bound by how
+// many weight bytes each SM keeps in flight (its loads-only twin takes 90 %
+// of its time at the wide configuration).
+template <int NMAX>
+struct TcCfg {
+  static constexpr int kNMax = NMAX;
+  static constexpr int kLoadPasses = NMAX / (kLoadThreads / 2);  // rows per gather thread
+  static constexpr int kRawStages = NMAX > 64 ? 8 : 12;            // 16 KiB units in flight
+  static constexpr uint32_t kBTile = NMAX * 128;                   // [NMAX rows][64 K] f16
+  static constexpr uint32_t kOffB = 0;
+  static constexpr uint32_t kOffRaw = kOffB + kBStages * kBTile;
+  static constexpr uint32_t kOffCtl = kOffRaw + kRawStages * kUnitBytes;
+  static constexpr uint32_t kAccCols = NMAX;                       // per accumulator buffer
+  static constexpr uint32_t kACol0 = 2 * kAccCols;                 // first A-stage column
+  static constexpr size_t kTcSmem = kOffCtl + 1024 + 1024;  // control block + alignment slack
+  static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "tensor memory");
+  static_assert(kBTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+  static_assert(kTcSmem <= 232448, "shared memory");
+  static_assert(NMAX % 64 == 0 && kLoadPasses * (kLoadThreads / 2) == NMAX, "item width");
+};
+
+template <int R>
+struct CtlT {
   uint64_t full[kStages];    // A stage written: the 4 dequant warps
   uint64_t empty[kStages];   // A stage consumed: MMA commit
   uint64_t bfull[kBStages];  // B stage landed: gather threads or the TMA issuer (+ bytes)
   uint64_t bempty[kBStages]; // B stage consumed: MMA commit
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
-  uint64_t raw_full[kRawStages];   // expect_tx + the unit's bytes
-  uint64_t raw_empty[kRawStages];  // 4 dequant warps
+  uint64_t raw_full[R];      // expect_tx + the unit's bytes
+  uint64_t raw_empty[R];     // 4 dequant warps
   uint64_t done;
-  uint2 raw_mult[kRawStages];      // f16x2 multipliers: top 8 rows of every 16, bottom 8
-  int info[kInfoSlots];  // (item << 9) | N of the item's MMAs, atomicMax-combined
+  uint2 raw_mult[R];         // f16x2 multipliers: top 8 rows of every 16, bottom 8
+  int info[kInfoSlots];      // (item << 9) | N of the item's MMAs, atomicMax-combined
   uint32_t tmem;
   int abort;
 };
-static_assert(sizeof(Ctl) <= 1024, "control block");
-static_assert(kTcSmem <= 232448, "shared memory");
+static_assert(sizeof(CtlT<12>) <= 1024, "control block");
 
 
 __device__ __forceinline__ uint32_t instr_desc_f16(int n) {
@@ -147,6 +160,7 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int c16) {
 
 
 // Bounded wait that also gives up once another role of the CTA has aborted.
+template <class Ctl>
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
@@ -164,6 +178,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ct
 }
 
 // The same wait, taken by every lane of the warp, with one shared outcome.
+template <class Ctl>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
   return __all_sync(0xffffffffu, wait_bar(bar, parity, ctl, status));
 }
@@ -196,7 +211,7 @@ struct Item {
   int e;            // expert (0 for dense)
   int rb;           // 128-row weight block
   long long slot0;  // first route slot (moe) or first activation row (dense)
-  int rows;         // route slots / rows covered (<= kNMax)
+  int rows;         // route slots / rows covered (<= the item width)
   int kc0, nk;      // 128-K units kc0 .. kc0+nk-1 (all of K unless split)
 };
 
@@ -219,6 +234,7 @@ __device__ __forceinline__ int2 plan_entry(const StreamParams& p, const int2* pl
   return __ldg(plan + g / nrb);
 }
 
+template <int kNMax>
 __device__ __forceinline__ Item make_item(const StreamParams& p, int2 pe, long long g, int nrb,
                                           int kch) {
   Item it;
@@ -289,11 +305,22 @@ __device__ __forceinline__ T pick(const T (&v)[M], int g) {
 
 // kFp4: NVFP4 units (9 KiB: codes, then per-16-K E4M3 scales; weights
 // e2m1 * fp16_rne(e4m3 * global)), else block-FP8 units (16 KiB).
-template <bool kFp4>
+template <bool kFp4, int NMAX>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
                    const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x) {
+  using C = TcCfg<NMAX>;
+  using Ctl = CtlT<C::kRawStages>;
+  constexpr int kNMax = C::kNMax;
+  constexpr int kLoadPasses = C::kLoadPasses;
+  constexpr int kRawStages = C::kRawStages;
+  constexpr uint32_t kBTile = C::kBTile;
+  constexpr uint32_t kOffB = C::kOffB;
+  constexpr uint32_t kOffRaw = C::kOffRaw;
+  constexpr uint32_t kOffCtl = C::kOffCtl;
+  constexpr uint32_t kAccCols = C::kAccCols;
+  constexpr uint32_t kACol0 = C::kACol0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -363,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     int2 pe_next = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
     for (long long j = 0; j < my_items && ok; ++j) {
-      const Item it = make_item(p, pe_next, g0 + j * gs, nrb, kch);
+      const Item it = make_item<kNMax>(p, pe_next, g0 + j * gs, nrb, kch);
       if (j + 1 < my_items) pe_next = plan_entry(p, plan, g0 + (j + 1) * gs, nrb);
       const float* stop = nullptr;
       const float* sbot = nullptr;
@@ -493,7 +520,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (long long j = 0; j < my_items && ok; ++j) {
         const long long g = g0 + j * gs;
-        const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
+        const Item it = make_item<kNMax>(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
         // The MMA's N: slots up to the item's last valid route.
         int nmax = 0;
 #pragma unroll
@@ -538,7 +565,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int2 pe_a = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
     int ids_a[kLoadPasses];
     {
-      const Item it0 = make_item(p, pe_a, g0, nrb, kch);
+      const Item it0 = make_item<kNMax>(p, pe_a, g0, nrb, kch);
 #pragma unroll
       for (int q = 0; q < kLoadPasses; ++q)
         ids_a[q] = my_items > 0 ? slot_id(p, it0, q * (kLoadThreads / 2) + rsub) : -1;
@@ -559,7 +586,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Prefetch the next item's route ids and the one after's plan entry.
       int2 pe_c = make_int2(0, 0);
       if (j + 1 < my_items) {
-        const Item itn = make_item(p, pe_b, g0 + (j + 1) * gs, nrb, kch);
+        const Item itn = make_item<kNMax>(p, pe_b, g0 + (j + 1) * gs, nrb, kch);
 #pragma unroll
         for (int q = 0; q < kLoadPasses; ++q)
           ids_a[q] = slot_id(p, itn, q * (kLoadThreads / 2) + rsub);
@@ -721,7 +748,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int kGroups = kNMax / 32;
     for (long long j = eg; j < my_items; j += 2) {
       const long long g = g0 + j * gs;
-      const Item it = make_item(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
+      const Item it = make_item<kNMax>(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
       float fself = 1.f;  // this lane's row: 2^E (FP8), 1 (NVFP4)
       if constexpr (!kFp4) {
         const float* stop;
@@ -894,7 +921,8 @@ __device__ __forceinline__ int block_excl_sum(int v, int* sh, int& total) {
 }
 
 // Items of the grouped GEMM. The route slots are cut into virtual blocks of
-// `vblock` (the moe_align block, or half of it when the block exceeds kNMax);
+// `vblock` (the moe_align block, or half of it when the block exceeds the
+// item width);
 // every run of consecutive virtual blocks of the same (valid) expert is cut
 // into items of at most nb_max of them.
 // plan[i] = {first slot, expert << 9 | slots}; *count = number of items.
@@ -977,7 +1005,9 @@ bool tc_gemm_supported(int block) {
   return block == 16 || block == 32 || block == 64 || block == 128 || block == 256;
 }
 
-int tc_plan_slots_per_group(int block) { return block > kNMax ? 2 : 1; }
+int tc_plan_slots_per_group(int block) { return block > kNMaxWide ? 2 : 1; }
+
+int tc_narrow_slots() { return kNMaxNarrow; }
 
 cudaError_t launch_tc_plan_slots(const StreamParams& p, void* plan_buf, int cap, int max_slots,
                                 cudaStream_t stream) {
@@ -990,7 +1020,7 @@ cudaError_t launch_tc_plan_slots(const StreamParams& p, void* plan_buf, int cap,
 }
 
 cudaError_t launch_tc_plan(const StreamParams& p, void* plan_buf, int cap, cudaStream_t stream) {
-  return launch_tc_plan_slots(p, plan_buf, cap, kNMax, stream);
+  return launch_tc_plan_slots(p, plan_buf, cap, kNMaxWide, stream);
 }
 
 cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
@@ -1007,22 +1037,32 @@ cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
 // scale's power of two applied to the fp32 accumulator, NVFP4 weights as
 // e2m1 * fp16_rne(e4m3 * global); bf16 activations are converted by the
 // caller. `plan_buf` holds launch_tc_plan's output (moe mode).
-cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
-                           cudaStream_t stream) {
-  const bool fp4 = quant == kQuantNvfp4;
-  static bool configured[2][64] = {};
+namespace {
+
+template <bool kFp4, int NMAX>
+cudaError_t launch_tc_config(const StreamParams& p, const int2* plan, const int* count, int grid,
+                             const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                             cudaStream_t stream) {
+  static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[fp4][dev]) {
-    cudaError_t err =
-        fp4 ? cudaFuncSetAttribute(tc_gemm_kernel<true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem)
-            : cudaFuncSetAttribute(tc_gemm_kernel<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+  constexpr size_t smem = TcCfg<NMAX>::kTcSmem;
+  if (!configured[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<kFp4, NMAX>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    configured[fp4][dev] = true;
+    configured[dev] = true;
   }
+  return launch_pdl(tc_gemm_kernel<kFp4, NMAX>, dim3(grid), dim3(kTcThreads), smem, stream, p,
+                    plan, count, tmap_w, tmap_x);
+}
+
+}  // namespace
+
+cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_buf, int grid,
+                           cudaStream_t stream, bool narrow) {
+  const bool fp4 = quant == kQuantNvfp4;
   // Weights: every unit is rows of 128 bytes (FP8 128 rows, NVFP4 72), one
   // box per unit.
   const unsigned unit_rows = (fp4 ? kFp4UnitBytes : kFp8UnitBytes) / 128;
@@ -1050,10 +1090,10 @@ cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_bu
   const int* count = reinterpret_cast<const int*>(plan_buf);
   const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
   if (fp4)
-    return launch_pdl(tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
-                      count, tmap_w, tmap_x);
-  return launch_pdl(tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), kTcSmem, stream, p, plan,
-                    count, tmap_w, tmap_x);
+    return narrow ? launch_tc_config<true, kNMaxNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream)
+                  : launch_tc_config<true, kNMaxWide>(p, plan, count, grid, tmap_w, tmap_x, stream);
+  return narrow ? launch_tc_config<false, kNMaxNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream)
+                : launch_tc_config<false, kNMaxWide>(p, plan, count, grid, tmap_w, tmap_x, stream);
 }
 
 }  // namespace b200
