@@ -65,7 +65,6 @@ constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
 constexpr int kStages = 4;                               // 64-K A stages in tensor memory
-constexpr int kBStages = 4;                              // 64-K B stages in shared memory
 constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
 constexpr int kInfoSlots = 8;
 constexpr uint32_t kTmemCols = 512;
@@ -73,16 +72,18 @@ constexpr uint32_t kAStageCols = 32;                     // 64 K f16 = 32 column
 constexpr int kNMaxWide = 192;   // route slots (MMA N) per item: the prefill tiles
 constexpr int kNMaxNarrow = 64;  // items of few routes (expert-parallel owners, dense M <= 64)
 
-// Tile configuration by the item width NMAX. The narrow one gives the B ring
-// a quarter of the wide one's shared memory and the weight ring four more
-// 16 KiB units in flight: with ~32 routes per expert the call is bound by how
-// many weight bytes each SM keeps in flight (its loads-only twin takes 90 %
-// of its time at the wide configuration).
+// Tile configuration by the item width NMAX. Every 64-K stage waits for its
+// activation (B) tile, so the B ring's depth over the copy latency bounds the
+// stage rate even with no math at all: at ~32 routes per expert the wide
+// configuration's loads-only twin takes 90 % of its time, ~1240 clocks per
+// 16 KiB weight unit. The narrow configuration's B tiles are a third the
+// size, so it holds three times as many stages in the same shared memory.
 template <int NMAX>
 struct TcCfg {
   static constexpr int kNMax = NMAX;
   static constexpr int kLoadPasses = NMAX / (kLoadThreads / 2);  // rows per gather thread
-  static constexpr int kRawStages = NMAX > 64 ? 8 : 12;            // 16 KiB units in flight
+  static constexpr int kRawStages = 8;                             // 16 KiB units in flight
+  static constexpr int kBStages = NMAX > 64 ? 4 : 12;              // 64-K B stages
   static constexpr uint32_t kBTile = NMAX * 128;                   // [NMAX rows][64 K] f16
   static constexpr uint32_t kOffB = 0;
   static constexpr uint32_t kOffRaw = kOffB + kBStages * kBTile;
@@ -96,7 +97,7 @@ struct TcCfg {
   static_assert(NMAX % 64 == 0 && kLoadPasses * (kLoadThreads / 2) == NMAX, "item width");
 };
 
-template <int R>
+template <int R, int kBStages>
 struct CtlT {
   uint64_t full[kStages];    // A stage written: the 4 dequant warps
   uint64_t empty[kStages];   // A stage consumed: MMA commit
@@ -112,7 +113,7 @@ struct CtlT {
   uint32_t tmem;
   int abort;
 };
-static_assert(sizeof(CtlT<12>) <= 1024, "control block");
+static_assert(sizeof(CtlT<8, 12>) <= 1024, "control block");
 
 
 __device__ __forceinline__ uint32_t instr_desc_f16(int n) {
@@ -311,8 +312,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x) {
   using C = TcCfg<NMAX>;
-  using Ctl = CtlT<C::kRawStages>;
+  using Ctl = CtlT<C::kRawStages, C::kBStages>;
   constexpr int kNMax = C::kNMax;
+  constexpr int kBStages = C::kBStages;
   constexpr int kLoadPasses = C::kLoadPasses;
   constexpr int kRawStages = C::kRawStages;
   constexpr uint32_t kBTile = C::kBTile;
