@@ -20,25 +20,42 @@
 // mbarrier rings (every wait bounded, no named barriers):
 //   warp 0       weights: per 16 KiB FP8 unit (one 128x128 block of
 //                prepack.cu's streamed layout) its two f16 scale multipliers
-//                and a 2-D TMA copy (128-byte swizzle) into a 4-deep raw ring;
-//   warp 1       MMA: one elected lane issues tcgen05.mma (M=128, N<=192,
-//                K=16, A from tensor memory, B from shared memory, f16 x f16
-//                -> f32), four per 64-K stage, and commits stage releases and
-//                accumulator-ready barriers;
-//   warps 2-3    activations: gather the item's rows (through
-//                sorted_token_ids) with 16-byte cp.async into a 4-deep ring
-//                of [192 rows][64 K] 128-byte-swizzled tiles; the stage's full
-//                barrier completes as the copies land (the TMA gather4 path
-//                measured about 60 cycles per four-row copy, slower than this);
+//                and a 2-D TMA copy (128-byte swizzle) into an 8-deep raw ring;
+//                the warp computes 32 units' multipliers at a time and lane 0
+//                issues their copies;
+//   warp 1       MMA: lane 0 alone runs the main loop - per stage its B tile
+//                (`bfull`) and A columns (`full`), tested one stage ahead,
+//                tcgen05.mma (M=128, N<=192, K=16, A from tensor memory, B
+//                from shared memory, f16 x f16 -> f32), four per 64 K, and one
+//                tcgen05.commit that releases the stage (its A columns and its
+//                B tile) to the producers;
+//   warps 2-3    activations: the item's rows as 2-D TMA tiles of a
+//                slot-ordered copy (lane 0 of warp 2), or gathered through
+//                sorted_token_ids with 16-byte cp.async (both warps), into
+//                128-byte-swizzled [rows][64 K] sub-tiles; the copies land on
+//                the stage's `bfull` barrier;
 //   warps 4-7    dequant: lane = weight row; each reads its row's FP8 bytes
 //                from the swizzled raw unit (conflict-free 8-byte reads),
-//                f16(e4m3) * m with one hmul2 per two values, and writes the
-//                stage's 64 K values into tensor memory (tcgen05.st);
-//   warps 8-15   epilogue: tcgen05.ld of a double-buffered accumulator (two
-//                192-column buffers), 2^E, SiLU*up, router weight and store,
-//                overlapping the next item's main loop; warps 8-11 drain
-//                buffer 0 (even items), warps 12-15 buffer 1.
-// Tensor memory: columns [0, 384) accumulators, [384, 512) four A stages.
+//                f16(e4m3) * m with one hmul2 per two values, and writes them
+//                into the stage's tensor-memory columns (tcgen05.st), then
+//                arrive on the stage's `full` barrier (4 arrivals);
+//   warps 8-15   epilogue: tcgen05.ld of a double-buffered accumulator, 2^E,
+//                SiLU*up, router weight and store, overlapping the next item's
+//                main loop; warps 8-11 drain buffer 0 (even items), warps 12-15
+//                buffer 1.
+// The MMA thread's loop is the pipeline's critical path. Measured on B200 with
+// a per-stage timeline of every role: the producers ran ~2,000 clocks ahead
+// while a warp-wide loop with separate A and B barriers spent 650-800 clocks
+// per 64-K stage on control (warp votes, two commits, 64-bit ring arithmetic)
+// against ~100 for its four MMAs; a barrier poll whose result feeds a branch
+// costs ~190 clocks; and an N = 192 MMA issues at about the tensor rate, so
+// nothing the MMA thread does besides issuing MMAs is hidden. Hence one
+// thread, one commit per stage, 32-bit ring counters, 128-K stages, and the
+// next stage's barriers tested while this stage's MMAs issue. (A separate
+// "scout" warp that polled the barriers and published a ready count, so that
+// the MMA thread never polled, measured 10-25 % slower on the wide tiles: its
+// extra hop lands on the dequant refill chain that bounds them.)
+// Tensor memory: accumulators in columns [0, 2 NMAX), then the A stages.
 //
 // Block scales. A 128x128 block's scale s is split as s = m * 2^E with one
 // power of two E per (expert, 128-row scale block) - the exponent of the
@@ -64,56 +81,83 @@ constexpr int kTcWarps = 16;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kWarpMeta = 0, kWarpMma = 1, kWarpLoad = 2, kWarpDeq = 4, kWarpEpi = 8;
 constexpr int kLoadThreads = (kWarpDeq - kWarpLoad) * 32;
-constexpr int kStages = 4;                               // 64-K A stages in tensor memory
 constexpr uint32_t kUnitBytes = kFp8UnitBytes;           // 16 KiB
 constexpr int kInfoSlots = 8;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAStageCols = 32;                     // 64 K f16 = 32 columns
+constexpr uint32_t kSubCols = 32;                        // 64 K f16 = 32 tensor-memory columns
 constexpr int kNMaxWide = 192;   // route slots (MMA N) per item: the prefill tiles
 constexpr int kNMaxNarrow = 64;  // items of few routes (expert-parallel owners, dense M <= 64)
 
-// Tile configuration by the item width NMAX. Every 64-K stage waits for its
-// activation (B) tile, so the B ring's depth over the copy latency bounds the
-// stage rate even with no math at all: at ~32 routes per expert the wide
-// configuration's loads-only twin takes 90 % of its time, ~1240 clocks per
-// 16 KiB weight unit. The narrow configuration's B tiles are a third the
-// size, so it holds three times as many stages in the same shared memory.
+// Tile configuration by the item width NMAX. A stage is kSub 64-K sub-tiles:
+// its A columns in tensor memory (a ring of kAStages) and its B tile
+// ([NMAX rows][64 K] f16 per sub-tile) in shared memory (a ring of kBStages
+// >= kAStages). Stage t uses A slot t % kAStages and B slot t % kBStages, and
+// the MMA thread's one commit per stage lands on empty[t % kBStages]: the B
+// producer reuses its slot after stage t - kBStages, the dequant warps theirs
+// after stage t - kAStages. Stages are 128 K (one weight unit): measured per
+// stage on B200, the MMA thread spends ~400 clocks per stage on its barrier
+// tests, commit and loop whatever the stage's size, against 96 clocks of
+// tensor work per N = 192 MMA, so a 64-K stage (four MMAs) left the tensor
+// pipe idle about half the time. The wide configuration's two 192-column
+// accumulators leave tensor memory for two 128-K A stages (the dequant warps
+// refill a slot in ~250 clocks, well inside the other stage's ~770 of MMAs);
+// its B tiles come from L2 ~2,000 clocks after they are asked for, so three
+// 48 KiB B stages are in flight, and five raw weight units. The narrow
+// configuration's 64-column accumulators leave room for six A stages.
 template <int NMAX>
 struct TcCfg {
   static constexpr int kNMax = NMAX;
   static constexpr int kLoadPasses = NMAX / (kLoadThreads / 2);  // rows per gather thread
-  static constexpr int kRawStages = 8;                             // 16 KiB units in flight
-  static constexpr int kBStages = NMAX > 64 ? 4 : 12;              // 64-K B stages
-  static constexpr uint32_t kBTile = NMAX * 128;                   // [NMAX rows][64 K] f16
+  static constexpr int kRawStages = NMAX > 64 ? 5 : 8;             // 16 KiB units in flight
+  static constexpr int kSub = 2;                                   // 64-K sub-tiles per stage
+  static constexpr int kAStages = NMAX > 64 ? 2 : 6;               // tensor memory
+  static constexpr int kBStages = NMAX > 64 ? 3 : 6;               // shared memory
+  static constexpr uint32_t kSubTile = NMAX * 128;                 // [NMAX rows][64 K] f16
+  static constexpr uint32_t kBStage = kSub * kSubTile;
+  static constexpr uint32_t kStageCols = kSub * kSubCols;
   static constexpr uint32_t kOffB = 0;
-  static constexpr uint32_t kOffRaw = kOffB + kBStages * kBTile;
+  static constexpr uint32_t kOffRaw = kOffB + kBStages * kBStage;
   static constexpr uint32_t kOffCtl = kOffRaw + kRawStages * kUnitBytes;
   static constexpr uint32_t kAccCols = NMAX;                       // per accumulator buffer
   static constexpr uint32_t kACol0 = 2 * kAccCols;                 // first A-stage column
   static constexpr size_t kTcSmem = kOffCtl + 1024 + 1024;  // control block + alignment slack
-  static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "tensor memory");
-  static_assert(kBTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+  static_assert(kBStages >= kAStages, "an A slot is reused after its stage's commit");
+  static_assert(kACol0 + kAStages * kStageCols <= kTmemCols, "tensor memory");
+  static_assert(kSubTile % 1024 == 0 && kOffRaw % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
   static_assert(kTcSmem <= 232448, "shared memory");
   static_assert(NMAX % 64 == 0 && kLoadPasses * (kLoadThreads / 2) == NMAX, "item width");
+  static_assert(2 % kSub == 0, "a weight unit is two 64-K halves");
 };
 
-template <int R, int kBStages>
+template <int R, int A, int B>
 struct CtlT {
-  uint64_t full[kStages];    // A stage written: the 4 dequant warps
-  uint64_t empty[kStages];   // A stage consumed: MMA commit
-  uint64_t bfull[kBStages];  // B stage landed: gather threads or the TMA issuer (+ bytes)
-  uint64_t bempty[kBStages]; // B stage consumed: MMA commit
+  uint64_t full[A];    // A columns written: the 4 dequant warps
+  uint64_t empty[B];   // stage t consumed (slot t % B): one MMA commit
+  uint64_t bfull[B];   // B tile landed: gather threads or the TMA issuer (+ bytes)
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t raw_full[R];      // expect_tx + the unit's bytes
   uint64_t raw_empty[R];     // 4 dequant warps
   uint64_t done;
   uint2 raw_mult[R];         // f16x2 multipliers: top 8 rows of every 16, bottom 8
+  uint2 wmult[32];           // the weight warp's multipliers for its next 32 units
   int info[kInfoSlots];      // (item << 9) | N of the item's MMAs, atomicMax-combined
   uint32_t tmem;
   int abort;
 };
-static_assert(sizeof(CtlT<8, 12>) <= 1024, "control block");
+static_assert(sizeof(CtlT<8, 6, 6>) <= 1024, "control block");
+
+// Position in a ring of N slots: slot index and the parity of its phase.
+template <int N>
+struct RingPos {
+  uint32_t idx = 0, phase = 0;
+  __device__ __forceinline__ void advance() {
+    if (++idx == (uint32_t)N) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 
 __device__ __forceinline__ uint32_t instr_desc_f16(int n) {
@@ -178,10 +222,56 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* ct
   }
 }
 
-// The same wait, taken by every lane of the warp, with one shared outcome.
+// Bounded wait for two barriers at once: both polls go out before the branch
+// on their results, so a thread whose two operands are ready pays one poll
+// latency (~190 clocks on B200), not two.
 template <class Ctl>
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status) {
-  return __all_sync(0xffffffffu, wait_bar(bar, parity, ctl, status));
+__device__ __forceinline__ bool wait_bar2(uint64_t* bar_a, uint32_t par_a, uint64_t* bar_b,
+                                          uint32_t par_b, Ctl* ctl, int* status) {
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 0;; ++i) {
+    const bool a = mbar_try_wait(bar_a, par_a);
+    const bool b = mbar_try_wait(bar_b, par_b);
+    if (a && b) return true;
+    if ((i & 63u) == 63u) {
+      if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (status) atomicOr(status, kDevWaitTimeout);
+        *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// The same wait for a role off the critical path: a pause of about pause_ns
+// between polls leaves the SM's barrier unit to the MMA thread, whose waits,
+// fences and commits otherwise queue behind a dozen spinning warps.
+#ifndef B200_TC_PAUSE_NS
+#define B200_TC_PAUSE_NS 64
+#endif
+template <class Ctl>
+__device__ __forceinline__ bool wait_bar_lazy(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status,
+                                              uint32_t pause_ns = B200_TC_PAUSE_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(pause_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicOr(status, kDevWaitTimeout);
+      *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+      return false;
+    }
+  }
+}
+
+// A lazy wait taken by every lane of the warp, with one shared outcome.
+template <class Ctl>
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, int* status,
+                                          uint32_t pause_ns = B200_TC_PAUSE_NS) {
+  return __all_sync(0xffffffffu, wait_bar_lazy(bar, parity, ctl, status, pause_ns));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -312,12 +402,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x) {
   using C = TcCfg<NMAX>;
-  using Ctl = CtlT<C::kRawStages, C::kBStages>;
+  using Ctl = CtlT<C::kRawStages, C::kAStages, C::kBStages>;
   constexpr int kNMax = C::kNMax;
+  constexpr int kAStages = C::kAStages;
   constexpr int kBStages = C::kBStages;
+  constexpr int kSub = C::kSub;
   constexpr int kLoadPasses = C::kLoadPasses;
   constexpr int kRawStages = C::kRawStages;
-  constexpr uint32_t kBTile = C::kBTile;
+  constexpr uint32_t kSubTile = C::kSubTile;
+  constexpr uint32_t kBStage = C::kBStage;
+  constexpr uint32_t kStageCols = C::kStageCols;
   constexpr uint32_t kOffB = C::kOffB;
   constexpr uint32_t kOffRaw = C::kOffRaw;
   constexpr uint32_t kOffCtl = C::kOffCtl;
@@ -339,13 +433,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // bfull: every gather thread (cp.async arrivals) or the one thread that
     // issues the stage's TMA tiles.
     const uint32_t b_arrivals = p.xs != nullptr ? 1u : (uint32_t)kLoadThreads;
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full[s], 4);
-      mbar_init(&ctl->empty[s], 1);
-    }
+    for (int s = 0; s < kAStages; ++s) mbar_init(&ctl->full[s], 4);
     for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&ctl->empty[s], 1);
       mbar_init(&ctl->bfull[s], b_arrivals);
-      mbar_init(&ctl->bempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&ctl->acc_full[s], 1);
@@ -388,7 +479,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == kWarpMeta) {
     // ------------------------------------------------------------- weights
-    long long u = 0;  // units issued by this CTA
+    long long u = 0;         // units issued by this CTA (lane 0)
+    RingPos<kRawStages> rp;  // the next raw slot (lane 0)
     bool ok = true;
     int2 pe_next = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
     for (long long j = 0; j < my_items && ok; ++j) {
@@ -421,35 +513,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // The unit's rows of 128 bytes in the weight tensor map.
       constexpr int kUnitRows = (kFp4 ? kFp4UnitBytes : kFp8UnitBytes) / 128;
       const int row0 = (int)(((long long)it.e * nrb + it.rb) * kch * kUnitRows);
-      for (int i = 0; i < it.nk; ++i, ++u) {
-        const int kc = it.kc0 + i;
-        if (!kFp4 && i > 0 && (i & 31) == 0) {
+      // Windows of 32 units: every lane computes its unit's multipliers, then
+      // lane 0 alone waits for raw slots and issues the copies.
+      for (int w0 = 0; w0 < it.nk && ok; w0 += 32) {
+        if (!kFp4 && w0 > 0) {
           ct = nt;
           cb = nb;
-          nt = ldg_or0(stop, kc + 32 + lane, kch);
-          nb = ldg_or0(sbot, kc + 32 + lane, kch);
+          nt = ldg_or0(stop, it.kc0 + w0 + 32 + lane, kch);
+          nb = ldg_or0(sbot, it.kc0 + w0 + 32 + lane, kch);
         }
-        const float vt = __shfl_sync(0xffffffffu, ct, i & 31);
-        const float vb = __shfl_sync(0xffffffffu, cb, i & 31);
-        const int s = (int)(u % kRawStages);
-        const uint32_t ph = (uint32_t)((u / kRawStages) & 1);
+        if constexpr (kFp4)
+          ctl->wmult[lane] = make_uint2(__float_as_uint(gsc), 0u);
+        else
+          ctl->wmult[lane] = make_uint2(mult_f16x2(ct, et), mult_f16x2(cb, eb));
+        __syncwarp();
+        const int nw = it.nk - w0 < 32 ? it.nk - w0 : 32;
         int good = 1;
         if (lane == 0) {
-          good = wait_bar(&ctl->raw_empty[s], ph ^ 1u, ctl, p.status) ? 1 : 0;
-          if (good) {
-            if constexpr (kFp4)
-              ctl->raw_mult[s] = make_uint2(__float_as_uint(gsc), 0u);
-            else
-              ctl->raw_mult[s] = make_uint2(mult_f16x2(vt, et), mult_f16x2(vb, eb));
-            mbar_arrive_expect_tx(&ctl->raw_full[s], (uint32_t)(kUnitRows * 128));
-            tma_load_2d(smem + kOffRaw + s * kUnitBytes, &tmap_w, 0, row0 + kc * kUnitRows,
-                        &ctl->raw_full[s]);
+          for (int i = 0; i < nw; ++i) {
+            if (!wait_bar_lazy(&ctl->raw_empty[rp.idx], rp.phase ^ 1u, ctl, p.status)) {
+              good = 0;
+              break;
+            }
+            ctl->raw_mult[rp.idx] = ctl->wmult[i];
+            mbar_arrive_expect_tx(&ctl->raw_full[rp.idx], (uint32_t)(kUnitRows * 128));
+            tma_load_2d(smem + kOffRaw + rp.idx * kUnitBytes, &tmap_w, 0,
+                        row0 + (it.kc0 + w0 + i) * kUnitRows, &ctl->raw_full[rp.idx]);
+            rp.advance();
+            ++u;
           }
         }
-        if (!__shfl_sync(0xffffffffu, good, 0)) {
-          ok = false;
-          break;
-        }
+        // Also holds the other lanes until lane 0 has read the window.
+        if (!__shfl_sync(0xffffffffu, good, 0)) ok = false;
       }
     }
     // Copies still in flight land before the CTA exits (only after an abort).
@@ -459,96 +554,122 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == kWarpMma) {
     // ----------------------------------------------------------------- MMA
-    // The whole warp walks the pipeline (uniform control flow keeps the
-    // operands in uniform registers); one elected lane issues the MMAs and
-    // commits. A stage's B descriptor differs from stage 0's only in the
-    // start-address field, advanced by 2 (32 bytes) per K=16 MMA.
-    const uint32_t dhi = (uint32_t)(smem_desc_sw128(0) >> 32);
-    const uint32_t b_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffB));
-    long long t = 0;  // 64-K stages consumed
-    bool ok = true;
-    for (long long j = 0; j < my_items && ok; ++j) {
-      const int buf = (int)(j & 1);
-      ok = warp_wait(&ctl->acc_empty[buf], (uint32_t)(((j >> 1) & 1) ^ 1), ctl, p.status);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t dcol = tmem + (uint32_t)buf * kAccCols;
-      uint32_t idesc = 0;
-      int kc0, nk;
-      item_k_range(p, g0 + j * gs, kch, kc0, nk);
-      for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
-        const int s = (int)(t % kStages);
-        const int sb = (int)(t % kBStages);
-        ok = warp_wait(&ctl->bfull[sb], (uint32_t)((t / kBStages) & 1), ctl, p.status) &&
-             warp_wait(&ctl->full[s], (uint32_t)((t / kStages) & 1), ctl, p.status);
+    // Lane 0 alone runs the loop: per stage its two barriers (`bfull`: B
+    // landed, `full`: A written), kSub x 4 MMAs and one commit that releases
+    // the stage. A barrier poll whose result feeds a branch costs ~190 clocks
+    // (measured on B200), so the next stage's barriers are tested (test_wait,
+    // which never suspends) before this stage's MMAs are issued and the
+    // results are read at the next stage; when they were not yet complete the
+    // thread polls both together.
+    // A stage's B descriptor differs from stage 0's only in the start-address
+    // field: + the stage's and the sub-tile's offsets, + 2 (32 bytes) per K=16
+    // MMA.
+    if (lane == 0) {
+      const uint32_t dhi = (uint32_t)(smem_desc_sw128(0) >> 32);
+      const uint32_t b_lo0 = (uint32_t)smem_desc_sw128(smem_u32(smem + kOffB));
+      RingPos<kAStages> sa;  // A slot / `full`
+      RingPos<kBStages> sb;  // B slot / `bfull` / `empty`
+      bool ok = true;
+      bool ready = false;  // the current stage's barriers, tested ahead
+      for (long long j = 0; j < my_items && ok; ++j) {
+        const int buf = (int)(j & 1);
+        ok = wait_bar(&ctl->acc_empty[buf], (uint32_t)(((j >> 1) & 1) ^ 1), ctl, p.status);
         if (!ok) break;
         tc_fence_after();
-        if (ts == 0) {
-          const int v = *reinterpret_cast<volatile int*>(&ctl->info[j % kInfoSlots]);
-          int n = (v >> 9) == (int)(j & 0x3fffff) ? (v & 511) : kNMax;
-          n = n < 16 ? 16 : (n > kNMax ? kNMax : n);
-          idesc = instr_desc_f16(n);
-        }
-        const uint32_t acol = tmem + kACol0 + (uint32_t)s * kAStageCols;
-        const uint32_t blo = b_lo0 + (uint32_t)sb * (kBTile >> 4);
-        if (elect_one()) {
-          if (!p.loads_only) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_ts(dcol, acol + 8u * kk, ((uint64_t)dhi << 32) | (blo + 2u * kk), idesc,
-                     (ts > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t dcol = tmem + (uint32_t)buf * kAccCols;
+        uint32_t idesc = 0;
+        int kc0, nk;
+        item_k_range(p, g0 + j * gs, kch, kc0, nk);
+        const int nst = nk * (2 / kSub);
+        for (int ts = 0; ts < nst; ++ts) {
+          if (!ready) {
+            ok = wait_bar2(&ctl->bfull[sb.idx], sb.phase, &ctl->full[sa.idx], sa.phase, ctl,
+                           p.status);
+            if (!ok) break;
           }
-          mma_commit(&ctl->empty[s]);
-          mma_commit(&ctl->bempty[sb]);
+          tc_fence_after();
+          if (ts == 0) {
+            const int v = *reinterpret_cast<volatile int*>(&ctl->info[j % kInfoSlots]);
+            int n = (v >> 9) == (int)(j & 0x3fffff) ? (v & 511) : kNMax;
+            n = n < 16 ? 16 : (n > kNMax ? kNMax : n);
+            idesc = instr_desc_f16(n);
+          }
+          RingPos<kAStages> na_pos = sa;
+          RingPos<kBStages> nb_pos = sb;
+          na_pos.advance();
+          nb_pos.advance();
+          const bool nb = mbar_test_wait(&ctl->bfull[nb_pos.idx], nb_pos.phase);
+          const bool na = mbar_test_wait(&ctl->full[na_pos.idx], na_pos.phase);
+          if (!p.loads_only) {
+            const uint32_t acol = tmem + kACol0 + sa.idx * kStageCols;
+            const uint32_t blo = b_lo0 + sb.idx * (kBStage >> 4);
+#pragma unroll
+            for (int q = 0; q < kSub; ++q)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_ts(dcol, acol + q * kSubCols + 8u * kk,
+                       ((uint64_t)dhi << 32) | (blo + q * (kSubTile >> 4) + 2u * kk), idesc,
+                       (ts > 0 || q > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&ctl->empty[sb.idx]);
+          sa = na_pos;
+          sb = nb_pos;
+          ready = nb && na;
         }
-        __syncwarp();
+        if (ok) mma_commit(&ctl->acc_full[buf]);
       }
-      if (ok && elect_one()) mma_commit(&ctl->acc_full[buf]);
-      __syncwarp();
-    }
-    // Every issued MMA has completed before tensor memory is released.
-    if (elect_one()) {
+      // Every issued MMA has completed before tensor memory is released.
       mma_commit(&ctl->done);
       mbar_wait(&ctl->done, 0u, nullptr);
     }
     __syncwarp();
   } else if (warp < kWarpDeq && p.xs != nullptr) {
     // ------------------------------------- B (activations) by 2-D TMA tiles
-    // The operand is already in slot order: a stage is ceil(rows / 64) boxes
-    // of 64 rows x 64 K, landing in the 128-byte-swizzled K-major layout the
-    // MMA descriptor reads. Warp 3 has nothing to do.
+    // The operand is already in slot order: a 64-K sub-tile is ceil(rows / 64)
+    // boxes of 64 rows x 64 K, landing in the 128-byte-swizzled K-major layout
+    // the MMA descriptor reads. Lane 0 of warp 2 issues; warp 3 has nothing to
+    // do.
     if (warp == kWarpLoad) {
-      long long t = 0;  // 64-K stages issued
+      long long t = 0;  // stages issued (lane 0)
+      RingPos<kBStages> sp;
       bool ok = true;
       for (long long j = 0; j < my_items && ok; ++j) {
         const long long g = g0 + j * gs;
         const Item it = make_item<kNMax>(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
         // The MMA's N: slots up to the item's last valid route.
         int nmax = 0;
-#pragma unroll
+  #pragma unroll
         for (int q = 0; q < kNMax / 32; ++q) {
           const int n = q * 32 + lane;
           if (id_row(p, slot_id(p, it, n)) >= 0) nmax = n + 1;
         }
         nmax = (int)__reduce_max_sync(0xffffffffu, (unsigned)nmax);
-        if (lane == 0)
+        int good = 1;
+        if (lane == 0) {
           atomicMax(&ctl->info[j % kInfoSlots], (int)(((j & 0x3fffff) << 9) | ((nmax + 15) & ~15)));
-        const int nbox = nmax > 64 ? (nmax + 63) / 64 : 1;
-        int kc0, nk;
-        item_k_range(p, g, kch, kc0, nk);
-        for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
-          const int s = (int)(t % kBStages);
-          ok = warp_wait(&ctl->bempty[s], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl, p.status);
-          if (!ok) break;
-          if (lane == 0) {
-            uint8_t* B = smem + kOffB + s * kBTile;
-            const int kofs = (kc0 + (ts >> 1)) * 128 + (ts & 1) * 64;
-            mbar_arrive_expect_tx(&ctl->bfull[s], (uint32_t)nbox * 8192u);
-            for (int b = 0; b < nbox; ++b)
-              tma_load_2d(B + b * 8192, &tmap_x, kofs, (int)(it.slot0 + 64 * b), &ctl->bfull[s]);
+          const int nbox = nmax > 64 ? (nmax + 63) / 64 : 1;
+          int kc0, nk;
+          item_k_range(p, g, kch, kc0, nk);
+          const int nst = nk * (2 / kSub);
+          for (int ts = 0; ts < nst; ++ts) {
+            if (!wait_bar_lazy(&ctl->empty[sp.idx], sp.phase ^ 1u, ctl, p.status)) {
+              good = 0;
+              break;
+            }
+            uint8_t* B = smem + kOffB + sp.idx * kBStage;
+            mbar_arrive_expect_tx(&ctl->bfull[sp.idx], (uint32_t)(nbox * kSub) * 8192u);
+  #pragma unroll
+            for (int q = 0; q < kSub; ++q) {
+              const int kofs = kc0 * 128 + (ts * kSub + q) * 64;
+              for (int b = 0; b < nbox; ++b)
+                tma_load_2d(B + q * kSubTile + b * 8192, &tmap_x, kofs, (int)(it.slot0 + 64 * b),
+                            &ctl->bfull[sp.idx]);
+            }
+            sp.advance();
+            ++t;
           }
-          __syncwarp();
         }
+        if (!__shfl_sync(0xffffffffu, good, 0)) ok = false;
       }
       // After an abort, tiles still in flight land before the CTA exits.
       if (lane == 0 && !ok) {
@@ -561,7 +682,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int ltid = tid - kWarpLoad * 32;  // 0..kLoadThreads-1
     const int rsub = ltid >> 1;             // row within a pass of kLoadThreads/2 rows
     const int cpar = ltid & 1;              // chunk parity
-    long long t = 0;
+    RingPos<kBStages> sp;
     bool ok = true;
     // Item j's route ids (ids_a), item j+1's plan entry (pe_b): one item ahead.
     int2 pe_a = my_items > 0 ? plan_entry(p, plan, g0, nrb) : make_int2(0, 0);
@@ -596,24 +717,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       int kc0, nk;
       item_k_range(p, g0 + j * gs, kch, kc0, nk);
-      for (int ts = 0; ts < 2 * nk; ++ts, ++t) {
-        const int s = (int)(t % kBStages);
-        ok = warp_wait(&ctl->bempty[s], (uint32_t)(((t / kBStages) & 1) ^ 1), ctl, p.status);
+      const int nst = nk * (2 / kSub);
+      for (int ts = 0; ts < nst; ++ts) {
+        ok = warp_wait(&ctl->empty[sp.idx], sp.phase ^ 1u, ctl, p.status);
         if (!ok) break;
-        uint8_t* B = smem + kOffB + s * kBTile;
-        const long long kofs = (long long)(kc0 + (ts >> 1)) * 128 + (ts & 1) * 64;
+        uint8_t* B = smem + kOffB + sp.idx * kBStage;
 #pragma unroll
-        for (int q = 0; q < kLoadPasses; ++q) {
-          if (rowp[q] != nullptr) {
-            const int n = q * (kLoadThreads / 2) + rsub;
+        for (int sq = 0; sq < kSub; ++sq) {
+          const long long kofs = (long long)kc0 * 128 + (ts * kSub + sq) * 64;
 #pragma unroll
-            for (int c2 = 0; c2 < 4; ++c2) {
-              const int c = 2 * c2 + cpar;
-              cp_async_16(B + sw128_off(n, c), rowp[q] + kofs + c * 8);
+          for (int q = 0; q < kLoadPasses; ++q) {
+            if (rowp[q] != nullptr) {
+              const int n = q * (kLoadThreads / 2) + rsub;
+#pragma unroll
+              for (int c2 = 0; c2 < 4; ++c2) {
+                const int c = 2 * c2 + cpar;
+                cp_async_16(B + sq * kSubTile + sw128_off(n, c), rowp[q] + kofs + c * 8);
+              }
             }
           }
         }
-        cp_async_arrive_noinc(&ctl->bfull[s]);
+        cp_async_arrive_noinc(&ctl->bfull[sp.idx]);
+        sp.advance();
       }
       pe_b = pe_c;
     }
@@ -632,9 +757,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int r8 = m & 7;
     const int rbase = (m >> 4) * 16 + (r8 >> 1);  // 128-byte row of q = 0
     const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
-    long long t = 0, u = 0;
+    RingPos<kRawStages> rr;  // raw unit
+    RingPos<kAStages> st;    // A slot / `full` of the current stage
+    RingPos<kBStages> ew;    // the commit that frees it: stage t - kAStages
+    int taken = 0;           // stages taken
     bool ok = true;
     int nk_left = 0;  // units left in the current item
+    // Half h of a unit is sub-tile h % kSub of the current stage: the stage's
+    // A slot is taken at sub-tile 0 (once the MMAs of the stage kAStages
+    // earlier have completed) and handed to the MMA thread after the last one.
+    auto take_stage = [&]() -> bool {
+      if (taken >= kAStages) {
+        // On the critical path when the A ring is short: polled without pauses.
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl->empty[ew.idx], ew.phase, ctl, p.status)))
+          return false;
+        ew.advance();
+      }
+      ++taken;
+      tc_fence_after();
+      return true;
+    };
+    auto give_stage = [&]() -> bool {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->full[st.idx]);
+      st.advance();
+      return true;
+    };
     for (long long j = 0; ok;) {
       if (nk_left == 0) {
         if (j >= my_items) break;
@@ -643,35 +792,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++j;
       }
       --nk_left;
-      const int rs = (int)(u % kRawStages);
-      ok = warp_wait(&ctl->raw_full[rs], (uint32_t)((u / kRawStages) & 1), ctl, p.status);
+      ok = warp_wait(&ctl->raw_full[rr.idx], rr.phase, ctl, p.status);
       if (!ok) break;
-      const volatile uint32_t* mm = reinterpret_cast<volatile uint32_t*>(&ctl->raw_mult[rs]);
+      const volatile uint32_t* mm = reinterpret_cast<volatile uint32_t*>(&ctl->raw_mult[rr.idx]);
       const uint32_t m2 = hf ? mm[1] : mm[0];  // FP8: this row's multiplier
       const float gsc = __uint_as_float(mm[0]);  // NVFP4: the expert's global scale
-      const uint8_t* raw = smem + kOffRaw + rs * kUnitBytes;
+      const uint8_t* raw = smem + kOffRaw + rr.idx * kUnitBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        const int sq = h % kSub;
         if (p.loads_only) {
-          // pipeline floor: hand the A stage on without dequantizing into it
-          const int s0 = (int)(t % kStages);
-          ok = warp_wait(&ctl->empty[s0], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
-          if (!ok) break;
-          tc_fence_after();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->full[s0]);
-          ++t;
+          // pipeline floor: hand the stage on without dequantizing into it
+          if (sq == 0 && !(ok = take_stage())) break;
+          if (sq == kSub - 1 && !(ok = give_stage())) break;
           continue;
         }
         uint32_t v[32];
-        int s = 0;
         if constexpr (kFp4) {
           // NVFP4: row m's codes for K 32c .. +31 are bytes hf*16 .. +15 of
           // the 32-byte lane record (w = m/16, lane 4*(m&7) + c), i.e. 128-byte
           // row 8w + (m&7), chunk 2c + hf; its two group scales are bytes
           // 2hf, 2hf+1 of the record's 4 scale bytes, in row 64 + w at byte
-          // 16*(m&7) + 4c. Stage h takes c = 2h, 2h + 1.
+          // 16*(m&7) + 4c. Half h takes c = 2h, 2h + 1.
           const int wr = m >> 4, g = m & 7;
           const int row = 8 * wr + g;
           uint4 code[2];
@@ -682,10 +824,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           const uint2 sc = *reinterpret_cast<const uint2*>(
               raw + (64 + wr) * 128 + ((g ^ wr) & 7) * 16 + 8 * h);
-          s = (int)(t % kStages);
-          ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
-          if (!ok) break;
-          tc_fence_after();
+          if (sq == 0 && !(ok = take_stage())) break;
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             // Scale bytes of record c: top g0, top g1, bottom g0, bottom g1.
@@ -712,10 +851,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int chunk = (((r8 & 1) * 4 + kg4) ^ row) & 7;
             r[i] = *reinterpret_cast<const uint2*>(raw + row * 128 + chunk * 16 + hf * 8);
           }
-          s = (int)(t % kStages);
-          ok = warp_wait(&ctl->empty[s], (uint32_t)(((t / kStages) & 1) ^ 1), ctl, p.status);
-          if (!ok) break;
-          tc_fence_after();
+          if (sq == 0 && !(ok = take_stage())) break;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             uint32_t* o = v + 16 * (i >> 2) + 4 * (i & 3);
@@ -725,16 +861,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             o[3] = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(r[i].y >> 16)), m2);
           }
         }
-        tmem_st32(tmem + tlane + kACol0 + (uint32_t)s * kAStageCols, v);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->full[s]);
-        ++t;
+        tmem_st32(tmem + tlane + kACol0 + st.idx * kStageCols + (uint32_t)sq * kSubCols, v);
+        if (sq == kSub - 1 && !(ok = give_stage())) break;
       }
       if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->raw_empty[rs]);
-      ++u;
+      if (lane == 0) mbar_arrive(&ctl->raw_empty[rr.idx]);
+      rr.advance();
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -787,7 +920,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (p.mul_w) wr[gg] = __ldg(p.topk_w + id);
         }
       }
-      if (!warp_wait(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl, p.status)) break;
+      if (!warp_wait(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl, p.status, 4 * B200_TC_PAUSE_NS))
+        break;
       tc_fence_after();
       const int ngroups = p.loads_only ? 0 : (it.rows + 31) >> 5;
       for (int gg = 0; gg < ngroups; ++gg) {
