@@ -112,6 +112,13 @@ struct TcCfg {
   static constexpr int kSub = 2;                                   // 64-K sub-tiles per stage
   static constexpr int kAStages = NMAX > 64 ? 2 : 6;               // tensor memory
   static constexpr int kBStages = NMAX > 64 ? 3 : 6;               // shared memory
+  // Dequant and epilogue warp groups (four warps each, one per tensor-memory
+  // lane quarter) among warps 4-15. The narrow configuration's 64-column
+  // epilogue is light, so one group drains both accumulator buffers and a
+  // second dequant group (warps 12-15) takes the odd units: measured on B200,
+  // one group's ~450 clocks per 128-K stage per warp paced the narrow tiles.
+  static constexpr int kDqGroups = NMAX > 64 ? 1 : 2;
+  static constexpr int kEpiGroups = 3 - kDqGroups;
   static constexpr uint32_t kSubTile = NMAX * 128;                 // [NMAX rows][64 K] f16
   static constexpr uint32_t kBStage = kSub * kSubTile;
   static constexpr uint32_t kStageCols = kSub * kSubCols;
@@ -127,6 +134,7 @@ struct TcCfg {
   static_assert(kTcSmem <= 232448, "shared memory");
   static_assert(NMAX % 64 == 0 && kLoadPasses * (kLoadThreads / 2) == NMAX, "item width");
   static_assert(2 % kSub == 0, "a weight unit is two 64-K halves");
+  static_assert(kDqGroups == 1 || kSub == 2, "dequant groups split units, one stage each");
 };
 
 template <int R, int A, int B>
@@ -743,7 +751,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       pe_b = pe_c;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp < kWarpEpi) {
+  } else if (warp < kWarpEpi || warp >= kWarpEpi + 4 * C::kEpiGroups) {
     // ------------------------------------------------------------- dequant
     // Lane = weight row m of this warp's tensor-memory quarter. In the
     // streamed unit, row m's 8 K values K = 32*kg4 + 8q + 0..7 are bytes
@@ -752,6 +760,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // The TMA copy stores the unit as 128 rows of 128 bytes with 16-byte chunk
     // c of row r at chunk c ^ (r & 7). A 64-K stage h takes kg4 = 2h + kg.
     const int quarter = warp & 3;
+    const int dg = warp < kWarpEpi ? 0 : 1;  // dequant group: units u with u % kDqGroups == dg
     const int m = quarter * 32 + lane;
     const int hf = (m >> 3) & 1;
     const int r8 = m & 7;
@@ -760,7 +769,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     RingPos<kRawStages> rr;  // raw unit
     RingPos<kAStages> st;    // A slot / `full` of the current stage
     RingPos<kBStages> ew;    // the commit that frees it: stage t - kAStages
-    int taken = 0;           // stages taken
+    int taken = 0;           // stages taken (by either group)
+    int ug = 0;              // units passed (by either group)
     bool ok = true;
     int nk_left = 0;  // units left in the current item
     // Half h of a unit is sub-tile h % kSub of the current stage: the stage's
@@ -792,6 +802,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++j;
       }
       --nk_left;
+      if constexpr (C::kDqGroups > 1) {
+        // The other group's unit (one stage): only the ring positions move.
+        if (ug++ % C::kDqGroups != dg) {
+          rr.advance();
+          st.advance();
+          if (taken >= kAStages) ew.advance();
+          ++taken;
+          continue;
+        }
+      }
       ok = warp_wait(&ctl->raw_full[rr.idx], rr.phase, ctl, p.status);
       if (!ok) break;
       const volatile uint32_t* mm = reinterpret_cast<volatile uint32_t*>(&ctl->raw_mult[rr.idx]);
@@ -871,17 +891,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warps 8-11 take the even items (TMEM buffer 0), warps 12-15 the odd
-    // ones (buffer 1): each group has two items' main-loop time for one.
+    // Item j's accumulator is TMEM buffer j & 1. With two groups warps 8-11
+    // take the even items and warps 12-15 the odd ones (each has two items'
+    // main-loop time for one); with one group warps 8-11 take them all.
     const int quarter = warp & 3;  // tensor-memory lanes 32*quarter..+31
     const int eg = (warp - kWarpEpi) >> 2;
     const int m = quarter * 32 + lane;  // weight row within the block
     const bool top = (m & 15) < 8;
     const bool fused = p.gated && p.fuse_act;
     const bool lane_stores = !fused || top;
-    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)eg * kAccCols;
+    const uint32_t tlanes = tmem + ((uint32_t)(quarter * 32) << 16);
     constexpr int kGroups = kNMax / 32;
-    for (long long j = eg; j < my_items; j += 2) {
+    for (long long j = eg; j < my_items; j += C::kEpiGroups) {
+      const int ab = (int)(j & 1);
+      const uint32_t tbase = tlanes + (uint32_t)ab * kAccCols;
       const long long g = g0 + j * gs;
       const Item it = make_item<kNMax>(p, plan_entry(p, plan, g, nrb), g, nrb, kch);
       float fself = 1.f;  // this lane's row: 2^E (FP8), 1 (NVFP4)
@@ -920,7 +943,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (p.mul_w) wr[gg] = __ldg(p.topk_w + id);
         }
       }
-      if (!warp_wait(&ctl->acc_full[eg], (uint32_t)((j >> 1) & 1), ctl, p.status, 4 * B200_TC_PAUSE_NS))
+      if (!warp_wait(&ctl->acc_full[ab], (uint32_t)((j >> 1) & 1), ctl, p.status, 4 * B200_TC_PAUSE_NS))
         break;
       tc_fence_after();
       const int ngroups = p.loads_only ? 0 : (it.rows + 31) >> 5;
@@ -990,7 +1013,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->acc_empty[eg]);
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[ab]);
     }
   }
 
