@@ -445,11 +445,15 @@ int b200_w8a8_moe_gemm(const void* a, int32_t a_dtype, int64_t a_rows, int64_t k
  * 64-bit addresses: entry r = rank r's region as mapped in this process (its
  * own entry = its own region). One layer forward on every rank, in this order
  * on one stream:
- *   b200_ep_dispatch        rows + routing to the owners (P2P stores)
+ *   b200_ep_dispatch        each token's row once per owner of one of its
+ *                           experts, with its top_k route slots (P2P stores)
  *   b200_ep_expert_forward  wait for every source, align, gate/up + down GEMMs
- *                           storing each weighted row into its source's region
- *   b200_ep_combine         wait for every owner, sum the top-k rows per
- *                           token (+ shared_out) x routed_scaling_factor
+ *                           over the received rows, then one summed row per
+ *                           received row stored into its source's region
+ *   b200_ep_combine         wait for every owner, sum each token's returned
+ *                           rows (one per owner) + shared_out, times
+ *                           routed_scaling_factor
+ * NVLink bytes scale with the distinct owners per token, not with top_k.
  * No host synchronization: the three calls can be captured in a CUDA graph.
  * Waits on other ranks are bounded (2 s) and set bit 8 in the region's status
  * word (read it with b200_workspace_status(region, ...)). Every rank must run
@@ -457,11 +461,13 @@ int b200_w8a8_moe_gemm(const void* a, int32_t a_dtype, int64_t a_rows, int64_t k
  */
 int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden);
 
-/* Byte offsets inside a region, for inspection: offsets[0..6] = receive slots'
- * local expert ids (int32 [world * max_tokens * top_k], -1 = empty once
- * received), router weights (fp32), source route indices (int32), destination
- * row addresses (u64), received rows (f16 [slots][hidden]), returned rows
- * (f16 [max_tokens * top_k][hidden]), total bytes. */
+/* Byte offsets inside a region, for inspection: offsets[0..6] = received
+ * route slots' local expert ids (int32 [world * max_tokens][top_k], -1 = not
+ * on this rank or empty once received), their router weights (fp32, same
+ * shape), each received row's source token (int32 [world * max_tokens]), each
+ * row's return address (u64, 0 = empty), received rows (f16
+ * [world * max_tokens][hidden]), returned rows (f16 [max_tokens * world]
+ * [hidden], token t from owner o at t * world + o), total bytes. top_k <= 32. */
 int b200_ep_region_layout(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden,
                           int64_t* offsets);
 
@@ -497,8 +503,9 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
                            int64_t max_tokens, int32_t top_k, void* workspace,
                            int64_t workspace_bytes, void* stream);
 
-/* Source side: out [tokens, hidden] = rsf * sum_k (weighted rows returned for
- * topk_ids[t, k]) + shared_out[t] (optional). */
+/* Source side: out [tokens, hidden] = rsf * sum over the owners of token t's
+ * routes of the row each returned (its experts' weighted outputs, summed) +
+ * shared_out[t] (optional). tokens and topk_ids as given to b200_ep_dispatch. */
 int b200_ep_combine(int64_t tokens, int64_t hidden, const int32_t* topk_ids, int32_t top_k,
                     int32_t num_experts, float routed_scaling_factor, const void* shared_out,
                     int32_t shared_dtype, void* out, int32_t out_dtype, int32_t world, void* region,

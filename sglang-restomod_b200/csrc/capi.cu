@@ -1102,8 +1102,9 @@ int check_ep_common(int32_t rank, int32_t world, int64_t max_tokens, int32_t top
   if (world < 1 || world > kEpMaxWorld)
     return fail(B200_ERR_INVALID, "world must be in [1, %d], got %d", kEpMaxWorld, world);
   if (rank < 0 || rank >= world) return fail(B200_ERR_INVALID, "rank %d outside [0, %d)", rank, world);
-  if (max_tokens <= 0 || top_k <= 0 || hidden <= 0 || hidden % 128)
-    return fail(B200_ERR_INVALID, "bad max_tokens=%lld top_k=%d hidden=%lld (hidden %% 128 == 0)",
+  if (max_tokens <= 0 || top_k <= 0 || top_k > 32 || hidden <= 0 || hidden % 128)
+    return fail(B200_ERR_INVALID,
+                "bad max_tokens=%lld top_k=%d hidden=%lld (top_k <= 32, hidden %% 128 == 0)",
                 (long long)max_tokens, top_k, (long long)hidden);
   if ((int64_t)world * max_tokens * top_k >= (1ll << 31))
     return fail(B200_ERR_INVALID, "world * max_tokens * top_k must stay below 2^31");
@@ -1114,8 +1115,9 @@ int check_ep_common(int32_t rank, int32_t world, int64_t max_tokens, int32_t top
   return B200_OK;
 }
 
-// Expert-parallel owner workspace: fixed part, routing, align scratch,
-// gate_up output for every receive slot.
+// Expert-parallel owner workspace: fixed part, routing, align scratch, the
+// gate_up output for every received route slot, and the down GEMM's weighted
+// route rows that the pre-sum adds up per received row.
 struct EpWs {
   int64_t numel, cap_a, blocks, total;
 };
@@ -1133,7 +1135,7 @@ EpWs ep_ws(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden, int
       block_size >= 64 ? align_up(w.cap_a * hidden * 2) + align_up(w.cap_a * inter * 2) : 0;
   w.total = stream_ws_bytes() + align_up(w.cap_a * 4) + align_up(w.blocks * 4) + align_up(4) +
             align_up(moe_align_scratch_ints(w.numel, local_experts) * 4) +
-            (stream_ops > tc_ops ? stream_ops : tc_ops);
+            (stream_ops > tc_ops ? stream_ops : tc_ops) + align_up(w.numel * hidden * 2);
   return w;
 }
 
@@ -1143,7 +1145,7 @@ extern "C" {
 
 int64_t b200_ep_region_bytes(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden) {
   if (world < 1 || world > kEpMaxWorld || max_tokens <= 0 || top_k <= 0 || hidden <= 0) return -1;
-  return ep_layout(world, max_tokens * top_k, hidden).total;
+  return ep_layout(world, max_tokens, top_k, hidden).total;
 }
 
 int b200_ep_region_layout(int32_t world, int64_t max_tokens, int32_t top_k, int64_t hidden,
@@ -1151,7 +1153,7 @@ int b200_ep_region_layout(int32_t world, int64_t max_tokens, int32_t top_k, int6
   if (world < 1 || world > kEpMaxWorld || max_tokens <= 0 || top_k <= 0 || hidden <= 0 ||
       offsets == nullptr)
     return fail(B200_ERR_INVALID, "bad region shape");
-  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  const EpLayout L = ep_layout(world, max_tokens, top_k, hidden);
   const int64_t v[7] = {L.off_ids, L.off_w, L.off_orig, L.off_rows, L.off_recv, L.off_comb, L.total};
   for (int i = 0; i < 7; ++i) offsets[i] = v[i];
   return B200_OK;
@@ -1211,10 +1213,9 @@ int b200_ep_dispatch(const void* x, int32_t x_dtype, int64_t tokens, int64_t hid
   if (tokens > 0 && (x == nullptr || topk_ids == nullptr || topk_weights == nullptr))
     return fail(B200_ERR_INVALID, "null pointer argument");
   if (tokens > 0 && !aligned16(x)) return fail(B200_ERR_INVALID, "x must be 16-byte aligned");
-  const int64_t routes = tokens * top_k;
-  if (ep_dispatch_chunk(routes > 0 ? routes : 1) > 12288)
-    return fail(B200_ERR_UNSUPPORTED, "too many routes for one dispatch");
-  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  if ((int64_t)ep_dispatch_chunk(tokens > 0 ? tokens : 1) * world * 4 > 48 * 1024)
+    return fail(B200_ERR_UNSUPPORTED, "too many tokens for one dispatch");
+  const EpLayout L = ep_layout(world, max_tokens, top_k, hidden);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return check_cuda(launch_ep_dispatch(x, x_dtype == B200_DTYPE_F16, tokens, hidden, topk_ids,
                                        topk_weights, top_k, num_experts, shared_expert != 0,
@@ -1262,14 +1263,17 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   if (!carve(workspace, workspace_bytes, ws))
     return fail(B200_ERR_INVALID, "workspace missing or misaligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
+  const EpLayout L = ep_layout(world, max_tokens, top_k, hidden);
   const unsigned long long* peers = reinterpret_cast<const unsigned long long*>(peer_regions);
   uint8_t* reg = static_cast<uint8_t*>(region);
 
-  rc = check_cuda(launch_ep_receive(region, peers, world, L, local_experts, st), "ep receive launch");
+  rc = check_cuda(launch_ep_receive(region, peers, rank, world, L, local_experts, st),
+                  "ep receive launch");
   if (rc) return rc;
 
+  // The received rows are the layer's tokens, each with top_k route slots.
   const int64_t numel = w.numel;
+  const int64_t rows = (int64_t)world * max_tokens;
   int64_t used = 0;
   int32_t* sorted = reinterpret_cast<int32_t*>(ws.scratch + used);
   used += align_up(w.cap_a * 4);
@@ -1300,11 +1304,18 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   if (rc) return rc;
   const __half* recv = reinterpret_cast<const __half*>(reg + L.off_recv);
   if (tc) {
-    rc = check_cuda(launch_permute_rows(recv, 1, hidden, numel, hidden, sorted, ntpp, w.cap_a, 1,
+    rc = check_cuda(launch_permute_rows(recv, 1, hidden, rows, hidden, sorted, ntpp, w.cap_a, top_k,
                                         numel, xs, st),
                     "permute launch");
     if (rc) return rc;
   }
+  // The down GEMM's weighted route rows (after the GEMM operands, as sized by
+  // ep_ws), summed per received row by the pre-sum.
+  const int64_t stream_ops = align_up(numel * inter * 2);
+  const int64_t tc_ops =
+      block_size >= 64 ? align_up(w.cap_a * hidden * 2) + align_up(w.cap_a * inter * 2) : 0;
+  __half* routed = reinterpret_cast<__half*>(ws.scratch + used +
+                                             (stream_ops > tc_ops ? stream_ops : tc_ops));
 
   StreamParams p{};
   p.wq = w13_packed;
@@ -1312,7 +1323,7 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   p.gscale = w13_global;
   p.x = recv;
   p.ldx = hidden;
-  p.x_rows = numel;
+  p.x_rows = rows;
   p.xs = xs;
   p.xs_rows = w.cap_a;
   p.out_by_slot = tc ? 1 : 0;
@@ -1321,7 +1332,7 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   p.ntpp = ntpp;
   p.block_m = block_size;
   p.max_groups = w.cap_a / block_size;
-  p.top_k = 1;
+  p.top_k = top_k;
   p.num_routes = (int)numel;
   p.topk_w = reinterpret_cast<const float*>(reg + L.off_w);
   p.E = local_experts;
@@ -1347,6 +1358,8 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   q.gscale = w2_global;
   q.x = inter_out;
   q.ldx = inter;
+  q.x_rows = numel;  // the intermediate has one row per route
+  q.top_k = 1;
   q.xs = tc ? inter_out : nullptr;  // written in slot order by the gate/up epilogue
   q.xs_rows = w.cap_a;
   q.out_by_slot = 0;
@@ -1355,8 +1368,8 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
   q.gated = 0;
   q.fuse_act = 0;
   q.mul_w = 1;
-  q.out = nullptr;
-  q.out_rows = reinterpret_cast<const unsigned long long*>(reg + L.off_rows);
+  q.out = routed;
+  q.out_rows = nullptr;
   q.ldo = hidden;
   q.out_f16 = 1;
   if (tc)
@@ -1364,6 +1377,8 @@ int b200_ep_expert_forward(int32_t quant, int64_t hidden, int64_t inter, int32_t
                 narrow_moe(block_size, max_tokens * top_k, local_experts));
   else
     rc = run_stream(quant, nt, q, w.blocks * (hidden / 128) * (inter / 128), ws, st);
+  if (rc) return rc;
+  rc = check_cuda(launch_ep_presum(region, routed, world, L, st), "ep pre-sum launch");
   if (rc) return rc;
   return check_cuda(launch_ep_signal(region, peers, rank, world, L, st), "ep signal launch");
 }
@@ -1384,9 +1399,8 @@ int b200_ep_combine(int64_t tokens, int64_t hidden, const int32_t* topk_ids, int
     return fail(B200_ERR_INVALID, "null pointer argument");
   if (!aligned16(out) || (shared_out && !aligned16(shared_out)))
     return fail(B200_ERR_INVALID, "buffers must be 16-byte aligned");
-  const EpLayout L = ep_layout(world, max_tokens * top_k, hidden);
-  return check_cuda(launch_ep_combine(region, L, world, tokens, top_k, topk_ids, num_experts,
-                                      routed_scaling_factor, shared_out,
+  const EpLayout L = ep_layout(world, max_tokens, top_k, hidden);
+  return check_cuda(launch_ep_combine(region, L, world, tokens, routed_scaling_factor, shared_out,
                                       shared_dtype == B200_DTYPE_F16, out,
                                       out_dtype == B200_DTYPE_F16,
                                       reinterpret_cast<cudaStream_t>(stream)),

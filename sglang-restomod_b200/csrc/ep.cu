@@ -6,26 +6,31 @@
 // local ones and marks foreign routes -1
 // (sglang_restomod/quant/sm70_fp8_moe/method.py:8-12, 253-283), and the expert
 // method's combine (method.py:305-309). Here every rank owns a contiguous
-// range of experts and one forward is four launches per rank, none of which
+// range of experts and one forward is five launches per rank, none of which
 // involves the host:
 //
-//   dispatch (source)  every route's activation row is converted to f16 and
-//                      stored straight into its owner's receive segment for
-//                      this source (P2P stores), with (local expert, router
-//                      weight, route index); the grid's last CTA publishes the
-//                      per-owner counts and raises the owner's dispatch flag;
+//   dispatch (source)  every token's activation row is converted to f16 and
+//                      stored once into each owner that holds one of its
+//                      experts (P2P stores), with the token's top_k route
+//                      slots (local expert or -1, router weight); the grid's
+//                      last CTA publishes the per-owner row counts and raises
+//                      the owner's dispatch flag;
 //   receive  (owner)   waits for every source's flag, marks slots past each
-//                      source's count empty and builds the table of
-//                      destination rows (the source's combine buffer);
-//   expert GEMMs       (capi.cu) align + gate/up + down, the down GEMM's
-//                      epilogue storing each route's weighted row directly
-//                      into the source's combine buffer through the table;
-//   signal   (owner)   raises each source's combine flag once the down GEMM
-//                      has completed;
-//   combine  (source)  waits for every owner's flag, sums the k rows of each
-//                      token (+ shared expert, x routed_scaling_factor) and
-//                      advances the step counter.
+//                      source's count empty and records where each row's
+//                      return goes (the source's combine buffer);
+//   expert GEMMs       (capi.cu) align + gate/up + down over the received
+//                      rows as tokens, the down GEMM writing weighted route
+//                      rows locally;
+//   pre-sum  (owner)   adds each row's routes and stores the one summed row
+//                      into the source's combine buffer (P2P stores), then
+//                      raises each source's combine flag (signal);
+//   combine  (source)  waits for every owner's flag, sums the (at most one per
+//                      owner) returned rows of each token (+ shared expert,
+//                      x routed_scaling_factor) and advances the step counter.
 //
+// A token whose top_k experts sit on d distinct owners crosses NVLink d
+// times each way instead of top_k times (top-8 over 8 ranks: ~5.3 on
+// average for uniform routing).
 // Flags carry the step number (the region's local counter + 1), so nothing is
 // reset between steps; every rank runs the same steps in the same order.
 // Every wait is bounded (kWaitLimitNs) and reports kDevPeerTimeout in the
@@ -99,7 +104,7 @@ struct DispatchParams {
   const unsigned long long* peers;  // [world] region bases in this process
   uint8_t* region;                  // this rank's region
   EpLayout L;
-  int chunk;  // routes per CTA (multiple of 8)
+  int chunk;  // tokens per CTA
 };
 
 // Owner rank and local expert of global expert e (-1: not sent). With a
@@ -118,74 +123,92 @@ __device__ __forceinline__ int route_owner(const DispatchParams& p, int e, int& 
   return -1;
 }
 
-// One CTA per chunk of routes. Positions inside an owner's segment follow
-// route order (stable), so a receiver's slots are in the source's route order.
+// Owners token t's routes go to, as a bitmask.
+__device__ __forceinline__ unsigned long long token_owners(const DispatchParams& p, long long t) {
+  unsigned long long m = 0;
+  for (int k = 0; k < p.top_k; ++k) {
+    int local;
+    const int o = route_owner(p, __ldg(p.ids + t * p.top_k + k), local);
+    if (o >= 0) m |= 1ull << o;
+  }
+  return m;
+}
+
+// One CTA per chunk of tokens. Each (token, owner) pair becomes one row in
+// the owner's segment for this source, at a position that follows token order
+// (stable), so a receiver's rows are in the source's token order.
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const DispatchParams p) {
-  extern __shared__ int pos[];  // [chunk]
+  extern __shared__ int pos[];  // [chunk][world]
   __shared__ int base[kEpMaxWorld];
   __shared__ int mine[kEpMaxWorld];
   __shared__ int last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const long long routes = p.tokens * p.top_k;
   const long long c0 = (long long)blockIdx.x * p.chunk;
-  const long long c1 = c0 + p.chunk < routes ? c0 + p.chunk : routes;
+  const long long c1 = c0 + p.chunk < p.tokens ? c0 + p.chunk : p.tokens;
   const int epoch = next_epoch(p.region);
   int* hdr = hdr_of(p.region);
+  unsigned long long* masks = reinterpret_cast<unsigned long long*>(p.region + p.L.off_mask);
   if (tid < kEpMaxWorld) {
     base[tid] = 0;
     mine[tid] = 0;
   }
   __syncthreads();
-  // Routes of earlier chunks per owner.
-  for (long long r = tid; r < c0; r += kEpThreads) {
-    int local;
-    const int o = route_owner(p, __ldg(p.ids + r), local);
-    if (o >= 0) atomicAdd(&base[o], 1);
+  // Rows of earlier chunks per owner.
+  for (long long t = tid; t < c0; t += kEpThreads) {
+    unsigned long long m = token_owners(p, t);
+    while (m) {
+      atomicAdd(&base[__ffsll((long long)m) - 1], 1);
+      m &= m - 1;
+    }
   }
   __syncthreads();
   if (warp == 0) {
     for (long long g = c0; g < c1; g += 32) {
-      const long long r = g + lane;
-      int o = -1, local;
-      if (r < c1) o = route_owner(p, __ldg(p.ids + r), local);
-      int mypos = -1;
+      const long long t = g + lane;
+      const unsigned long long m = t < c1 ? token_owners(p, t) : 0ull;
+      if (t < c1) masks[t] = m;
       for (int d = 0; d < p.world; ++d) {
-        const unsigned m = __ballot_sync(0xffffffffu, o == d);
-        if (o == d) mypos = base[d] + __popc(m & ((1u << lane) - 1u));
+        const bool has = (m >> d) & 1ull;
+        const unsigned b = __ballot_sync(0xffffffffu, has);
+        if (t < c1) pos[(t - c0) * p.world + d] = has ? base[d] + __popc(b & ((1u << lane) - 1u)) : -1;
         __syncwarp();
         if (lane == 0) {
-          base[d] += __popc(m);
-          mine[d] += __popc(m);
+          base[d] += __popc(b);
+          mine[d] += __popc(b);
         }
         __syncwarp();
       }
-      if (r < c1) pos[r - c0] = mypos;
     }
   }
   __syncthreads();
-  // Rows: one warp per route, 16 bytes per lane per access.
+  // Rows: one warp per (token, owner) pair, 16 bytes per lane per access;
+  // lanes k < top_k write the row's route slots.
   const long long h8 = p.hidden / 8;
-  for (long long r = c0 + warp; r < c1; r += kEpThreads / 32) {
-    const int ps = pos[r - c0];
+  const long long pairs = (c1 - c0) * p.world;
+  for (long long q = warp; q < pairs; q += kEpThreads / 32) {
+    const long long t = c0 + q / p.world;
+    const int d = (int)(q % p.world);
+    const int ps = pos[q];
     if (ps < 0) continue;
-    int local;
-    const int o = route_owner(p, __ldg(p.ids + r), local);
-    uint8_t* dst = reinterpret_cast<uint8_t*>(p.peers[o]);
-    const long long slot = (long long)p.rank * p.L.cap + ps;
-    if (lane == 0) {
-      reinterpret_cast<int*>(dst + p.L.off_ids)[slot] = local;
-      reinterpret_cast<float*>(dst + p.L.off_w)[slot] = __ldg(p.w + r);
-      reinterpret_cast<int*>(dst + p.L.off_orig)[slot] = (int)r;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.peers[d]);
+    const long long row = (long long)p.rank * p.L.cap + ps;
+    if (lane < p.top_k) {
+      const long long r = t * p.top_k + lane;
+      int local = -1;
+      const int o = route_owner(p, __ldg(p.ids + r), local);
+      reinterpret_cast<int*>(dst + p.L.off_ids)[row * p.top_k + lane] = o == d ? local : -1;
+      reinterpret_cast<float*>(dst + p.L.off_w)[row * p.top_k + lane] = __ldg(p.w + r);
     }
-    const uint4* src = reinterpret_cast<const uint4*>(p.x) + (r / p.top_k) * h8;
-    uint8_t* drow = dst + p.L.off_recv + slot * p.hidden * 2;
+    if (lane == 0) reinterpret_cast<int*>(dst + p.L.off_orig)[row] = (int)t;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x) + t * h8;
+    uint8_t* drow = dst + p.L.off_recv + row * p.hidden * 2;
     for (long long v = lane; v < h8; v += 32) {
       uint4 val = __ldg(src + v);
       if (!p.x_f16) val = bf16x8_to_f16x8(val);
       st_u128(drow + v * 16, val);
     }
   }
-  // Publish: this CTA's per-owner counts, then (last CTA) the totals + flags.
+  // Publish: this CTA's per-owner row counts, then (last CTA) the totals + flags.
   if (tid < p.world && mine[tid] != 0)
     atomicAdd(reinterpret_cast<int*>(p.region + p.L.off_cnt_local) + tid, mine[tid]);
   __threadfence_system();
@@ -204,11 +227,13 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const DispatchP
   if (tid == 0) hdr[kEpHdrDispatchDone] = 0;
 }
 
-// Owner: wait for every source, then per slot keep (local expert, weight) or
-// mark it empty, and point the slot's output row at the source's combine
-// buffer. Every CTA takes the waits itself.
+// Owner: wait for every source, then per received row keep its route slots
+// (local expert, weight) or mark them empty, and point the row's return at the
+// source's combine buffer (token-major, this owner's column). Every CTA takes
+// the waits itself.
 __global__ void __launch_bounds__(kEpThreads) ep_receive_kernel(
-    uint8_t* region, const unsigned long long* peers, int world, EpLayout L, int experts_local) {
+    uint8_t* region, const unsigned long long* peers, int rank, int world, EpLayout L,
+    int experts_local) {
   __shared__ int cnt[kEpMaxWorld];
   const int tid = threadIdx.x;
   int* hdr = hdr_of(region);
@@ -225,30 +250,73 @@ __global__ void __launch_bounds__(kEpThreads) ep_receive_kernel(
   __syncthreads();
   __threadfence();
   int* ids = reinterpret_cast<int*>(region + L.off_ids);
-  float* wts = reinterpret_cast<float*>(region + L.off_w);
   const int* orig = reinterpret_cast<const int*>(region + L.off_orig);
   unsigned long long* rows = reinterpret_cast<unsigned long long*>(region + L.off_rows);
   const long long total = (long long)world * L.cap;
-  for (long long slot = blockIdx.x * (long long)kEpThreads + tid; slot < total;
-       slot += (long long)gridDim.x * kEpThreads) {
-    const int s = (int)(slot / L.cap);
-    const long long j = slot - (long long)s * L.cap;
-    int id = -1;
+  for (long long row = blockIdx.x * (long long)kEpThreads + tid; row < total;
+       row += (long long)gridDim.x * kEpThreads) {
+    const int s = (int)(row / L.cap);
+    const long long j = row - (long long)s * L.cap;
+    bool live = false;
     if (j < cnt[s]) {
-      const int lid = __ldcg(ids + slot);
-      const int r = __ldcg(orig + slot);
-      if (lid >= 0 && lid < experts_local && r >= 0 && r < L.cap) {
-        id = lid;
-        rows[slot] = peers[s] + (unsigned long long)L.off_comb +
-                     (unsigned long long)r * (unsigned long long)L.hidden * 2ull;
-        wts[slot] = __ldcg(wts + slot);
+      const int t = __ldcg(orig + row);
+      if (t >= 0 && t < L.cap) {
+        live = true;
+        rows[row] = peers[s] + (unsigned long long)L.off_comb +
+                    ((unsigned long long)t * world + rank) * (unsigned long long)L.hidden * 2ull;
       }
     }
-    ids[slot] = id;
+    if (!live) rows[row] = 0ull;
+    for (int k = 0; k < L.top_k; ++k) {
+      const long long slot = row * L.top_k + k;
+      int id = live ? __ldcg(ids + slot) : -1;
+      if (id < 0 || id >= experts_local) id = -1;
+      ids[slot] = id;
+    }
   }
 }
 
-// Owner, after its down GEMM has completed (plain stream order): raise each
+// Owner, after its down GEMM (stream order): one thread per 16 bytes of a
+// received row sums the row's weighted route outputs (fp32) and stores the f16
+// sum at the row's destination - the source's combine buffer, over NVLink.
+// Element-parallel like the combine: a warp per row left most SMs idle.
+__global__ void __launch_bounds__(kEpThreads) ep_presum_kernel(const uint8_t* region,
+                                                               const uint8_t* routed, int world,
+                                                               EpLayout L) {
+  const int* ids = reinterpret_cast<const int*>(region + L.off_ids);
+  const unsigned long long* rows = reinterpret_cast<const unsigned long long*>(region + L.off_rows);
+  const long long h8 = L.hidden / 8;
+  const long long total = (long long)world * L.cap * h8;
+  for (long long id = blockIdx.x * (long long)kEpThreads + threadIdx.x; id < total;
+       id += (long long)gridDim.x * kEpThreads) {
+    const long long row = id / h8;
+    const long long v = id - row * h8;
+    const unsigned long long dst = __ldg(rows + row);
+    if (dst == 0ull) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < L.top_k; ++k) {
+      if (__ldg(ids + row * L.top_k + k) < 0) continue;
+      const uint4 raw =
+          __ldcg(reinterpret_cast<const uint4*>(routed + (row * L.top_k + k) * L.hidden * 2) + v);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+      o[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    st_u128(reinterpret_cast<uint8_t*>(dst) + v * 16, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+// Owner, after its pre-sum has completed (plain stream order): raise each
 // source's combine flag.
 __global__ void ep_signal_kernel(uint8_t* region, const unsigned long long* peers, int rank,
                                  int world, EpLayout L) {
@@ -266,9 +334,6 @@ struct CombineParams {
   EpLayout L;
   int world;
   long long tokens;
-  int top_k;
-  const int* topk_ids;  // routes with ids outside [0, E) were not dispatched
-  int num_experts;
   float scale;
   const void* shared_out;
   int shared_f16;
@@ -276,8 +341,9 @@ struct CombineParams {
   int out_f16;
 };
 
-// Source: wait for every owner, then out[t] = scale * sum_k rows[t*k + k] (+
-// shared[t]); the last CTA advances the step counter.
+// Source: wait for every owner, then out[t] = scale * sum over the owners
+// token t went to of their returned row (+ shared[t]); the last CTA advances
+// the step counter.
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const CombineParams p) {
   __shared__ int last;
   const int tid = threadIdx.x;
@@ -290,6 +356,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const CombinePar
   __syncthreads();
   __threadfence();
   const uint8_t* rows = p.region + p.L.off_comb;
+  const unsigned long long* masks =
+      reinterpret_cast<const unsigned long long*>(p.region + p.L.off_mask);
   const long long hidden = p.L.hidden;
   const long long h8 = hidden / 8;
   const long long total = p.tokens * h8;
@@ -298,11 +366,12 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const CombinePar
     const long long t = id / h8;
     const long long c = (id - t * h8) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < p.top_k; ++k) {
-      const int e = __ldg(p.topk_ids + t * p.top_k + k);
-      if (e < 0 || e >= p.num_experts) continue;
+    unsigned long long m = masks[t];
+    while (m) {
+      const int o = __ffsll((long long)m) - 1;
+      m &= m - 1;
       const uint4 raw =
-          __ldcg(reinterpret_cast<const uint4*>(rows + ((t * p.top_k + k) * hidden + c) * 2));
+          __ldcg(reinterpret_cast<const uint4*>(rows + ((t * p.world + o) * hidden + c) * 2));
       const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -362,13 +431,12 @@ int ep_grid(long long work) {
 
 }  // namespace
 
-// Routes per dispatch CTA: spread over up to 4 CTAs per SM (one warp per
-// route row, eight rows in flight per CTA), at least 8 routes per CTA.
-int ep_dispatch_chunk(long long routes) {
+// Tokens per dispatch CTA: spread over up to 4 CTAs per SM (one warp per
+// (token, owner) row, eight rows in flight per CTA).
+int ep_dispatch_chunk(long long tokens) {
   const long long ctas = 4ll * device_sm_count();
-  long long chunk = (routes + ctas - 1) / ctas;
-  chunk = (chunk + 7) / 8 * 8;
-  return chunk < 8 ? 8 : (int)chunk;
+  long long chunk = (tokens + ctas - 1) / ctas;
+  return chunk < 1 ? 1 : (int)chunk;
 }
 
 cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
@@ -376,8 +444,7 @@ cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long 
                                int shared_expert, int experts_per_rank, int rank, int world,
                                const unsigned long long* peers, void* region, const EpLayout& L,
                                cudaStream_t stream) {
-  // With no routes one CTA still publishes this step's (zero) counts and flags.
-  const long long routes = tokens * top_k;
+  // With no tokens one CTA still publishes this step's (zero) counts and flags.
   DispatchParams p;
   p.x = x;
   p.x_f16 = x_f16;
@@ -394,37 +461,40 @@ cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long 
   p.peers = peers;
   p.region = static_cast<uint8_t*>(region);
   p.L = L;
-  p.chunk = ep_dispatch_chunk(routes);
-  const int grid = routes > 0 ? (int)((routes + p.chunk - 1) / p.chunk) : 1;
-  ep_dispatch_kernel<<<grid, kEpThreads, (size_t)p.chunk * 4, stream>>>(p);
+  p.chunk = ep_dispatch_chunk(tokens);
+  const int grid = tokens > 0 ? (int)((tokens + p.chunk - 1) / p.chunk) : 1;
+  ep_dispatch_kernel<<<grid, kEpThreads, (size_t)p.chunk * world * 4, stream>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int world,
+cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int rank, int world,
                               const EpLayout& L, int experts_local, cudaStream_t stream) {
   ep_receive_kernel<<<ep_grid((long long)world * L.cap), kEpThreads, 0, stream>>>(
-      static_cast<uint8_t*>(region), peers, world, L, experts_local);
+      static_cast<uint8_t*>(region), peers, rank, world, L, experts_local);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_presum(const void* region, const void* routed, int world, const EpLayout& L,
+                             cudaStream_t stream) {
+  ep_presum_kernel<<<ep_grid((long long)world * L.cap * (L.hidden / 8)), kEpThreads, 0, stream>>>(
+      static_cast<const uint8_t*>(region), static_cast<const uint8_t*>(routed), world, L);
   return cudaGetLastError();
 }
 
 cudaError_t launch_ep_signal(void* region, const unsigned long long* peers, int rank, int world,
                              const EpLayout& L, cudaStream_t stream) {
-  ep_signal_kernel<<<1, 32, 0, stream>>>(static_cast<uint8_t*>(region), peers, rank, world, L);
+  ep_signal_kernel<<<1, 64, 0, stream>>>(static_cast<uint8_t*>(region), peers, rank, world, L);
   return cudaGetLastError();
 }
 
 cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long long tokens,
-                              int top_k, const int* topk_ids, int num_experts, float scale,
-                              const void* shared_out, int shared_f16, void* out, int out_f16,
-                              cudaStream_t stream) {
+                              float scale, const void* shared_out, int shared_f16, void* out,
+                              int out_f16, cudaStream_t stream) {
   CombineParams p;
   p.region = static_cast<uint8_t*>(region);
   p.L = L;
   p.world = world;
   p.tokens = tokens;
-  p.top_k = top_k;
-  p.topk_ids = topk_ids;
-  p.num_experts = num_experts;
   p.scale = scale;
   p.shared_out = shared_out;
   p.shared_f16 = shared_f16;

@@ -161,50 +161,63 @@ int device_sm_count();
 // rank, mapped into every peer (CUDA IPC). Offsets in bytes, each 256-aligned.
 constexpr int kEpMaxWorld = 64;
 enum EpHdr : int { kEpHdrStatus = 0, kEpHdrEpoch = 1, kEpHdrDispatchDone = 2, kEpHdrCombineDone = 3 };
+// A source sends each token's activation row once per owner that holds one
+// of its experts (a "row"), with the token's top_k route slots (local expert
+// id, -1 for the routes elsewhere, and router weight); the owner returns one
+// row per received row, the weighted sum of its experts' outputs.
 struct EpLayout {
-  long long cap;     // routes one source may send (max tokens x top_k)
+  long long cap;     // rows one source may send to one owner (max tokens)
+  int top_k;
   long long hidden;
   long long off_dflag, off_cflag, off_count, off_cnt_local;  // [kEpMaxWorld] ints each
-  long long off_ids, off_w, off_orig;  // [world * cap]: local expert id, router weight, route index
-  long long off_rows;                  // [world * cap] u64: destination row of each slot
-  long long off_recv;                  // [world * cap][hidden] f16: received activation rows
-  long long off_comb;                  // [cap][hidden] f16: returned (weighted) rows, route order
+  long long off_ids, off_w;  // [world * cap * top_k]: local expert id (-1 none), router weight
+  long long off_orig;        // [world * cap]: source token of each received row
+  long long off_rows;        // [world * cap] u64: destination of each row's summed return (0 = none)
+  long long off_recv;        // [world * cap][hidden] f16: received activation rows
+  long long off_comb;        // [cap * world][hidden] f16: returned rows, token t of owner o at t*world+o
+  long long off_mask;        // [cap] u64: owners each token of the last dispatch went to (source)
   long long total;
 };
-inline EpLayout ep_layout(int world, long long cap, long long hidden) {
+inline EpLayout ep_layout(int world, long long max_tokens, int top_k, long long hidden) {
   auto up = [](long long v) { return (v + 255) / 256 * 256; };
   EpLayout L;
-  L.cap = cap;
+  L.cap = max_tokens;
+  L.top_k = top_k;
   L.hidden = hidden;
   long long o = 256;  // header: status, step counter, two done counters
   L.off_dflag = o; o += up(4 * kEpMaxWorld);
   L.off_cflag = o; o += up(4 * kEpMaxWorld);
   L.off_count = o; o += up(4 * kEpMaxWorld);
   L.off_cnt_local = o; o += up(4 * kEpMaxWorld);
-  const long long slots = (long long)world * cap;
-  L.off_ids = o; o += up(4 * slots);
-  L.off_w = o; o += up(4 * slots);
-  L.off_orig = o; o += up(4 * slots);
-  L.off_rows = o; o += up(8 * slots);
-  L.off_recv = o; o += up(2 * slots * hidden);
-  L.off_comb = o; o += up(2 * cap * hidden);
+  const long long rows = (long long)world * max_tokens;
+  L.off_ids = o; o += up(4 * rows * top_k);
+  L.off_w = o; o += up(4 * rows * top_k);
+  L.off_orig = o; o += up(4 * rows);
+  L.off_rows = o; o += up(8 * rows);
+  L.off_recv = o; o += up(2 * rows * hidden);
+  L.off_comb = o; o += up(2 * rows * hidden);
+  L.off_mask = o; o += up(8 * max_tokens);
   L.total = o;
   return L;
 }
-int ep_dispatch_chunk(long long routes);
+int ep_dispatch_chunk(long long tokens);
 cudaError_t launch_ep_dispatch(const void* x, int x_f16, long long tokens, long long hidden,
                                const int* ids, const float* w, int top_k, int num_experts,
                                int shared_expert, int experts_per_rank, int rank, int world,
                                const unsigned long long* peers, void* region, const EpLayout& L,
                                cudaStream_t stream);
-cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int world,
+cudaError_t launch_ep_receive(void* region, const unsigned long long* peers, int rank, int world,
                               const EpLayout& L, int experts_local, cudaStream_t stream);
+// Owner, after its down GEMM: row r's return = sum over its valid route slots
+// of routed[r * top_k + k] (f16 [world * cap * top_k][hidden]), stored at the
+// row's destination (a peer address).
+cudaError_t launch_ep_presum(const void* region, const void* routed, int world, const EpLayout& L,
+                             cudaStream_t stream);
 cudaError_t launch_ep_signal(void* region, const unsigned long long* peers, int rank, int world,
                              const EpLayout& L, cudaStream_t stream);
 cudaError_t launch_ep_combine(void* region, const EpLayout& L, int world, long long tokens,
-                              int top_k, const int* topk_ids, int num_experts, float scale,
-                              const void* shared_out, int shared_f16, void* out, int out_f16,
-                              cudaStream_t stream);
+                              float scale, const void* shared_out, int shared_f16, void* out,
+                              int out_f16, cudaStream_t stream);
 
 // W8A8 block-FP8 GEMM (w8a8.cu): e4m3 weights [E][N][K] row-major with fp32
 // scales per 128x128 block, times e4m3 activations [rows][K] with fp32 scales

@@ -6,17 +6,23 @@ dispatcher, which maps global ids to local ones and marks foreign routes -1
 (``sglang_restomod/quant/sm70_fp8_moe/method.py:8-12, 253-283``), followed by
 an all-reduce. Here each rank owns ``E / world`` experts and one forward is:
 
-1. route -> destination rank; routes sorted stably by destination;
-2. per-destination route counts exchanged (``all_to_all_single`` of ``world``
-   ints over NCCL);
-3. token rows and (local expert, weight) metadata sent to their owners
-   (``all_to_all_single`` with the exchanged split sizes);
-4. the owner runs its local experts on the received routes as one-slot
-   tokens (``b200_moe_layer_forward`` with top_k = 1: the output rows come
-   back already multiplied by their router weight);
-5. rows returned with the reverse exchange and summed per token by the
-   library's combine kernel, which also adds the shared expert (computed
-   on the rank's own tokens) and applies ``routed_scaling_factor``.
+1. per token, the set of owner ranks its routes go to; one (token, owner)
+   pair per owner, pairs sorted stably by owner;
+2. per-owner pair counts exchanged (``all_to_all_single`` of ``world`` ints
+   over NCCL);
+3. each pair's token row, once, with the token's top_k route slots (local
+   expert id, -1 for the routes owned elsewhere, and router weight) sent to
+   the owner (``all_to_all_single`` with the exchanged split sizes);
+4. the owner runs its local experts on the received rows as tokens with
+   top_k slots (``b200_moe_layer_forward``, foreign slots skipped): each
+   output row is already the weighted sum over the owner's routes of that
+   token, times ``routed_scaling_factor``;
+5. one row per pair returned with the reverse exchange; the source adds its
+   token's returned rows (one per owner) and the shared expert (computed on
+   the rank's own tokens).
+
+A token crosses the network once per distinct owner each way, not once per
+route (top-8 over 8 ranks: ~5.3 times for uniform routing).
 
 The split sizes make one host read per forward (step 2); the collectives run
 on the current stream. That is the NCCL transport (``transport="nccl"``).
@@ -25,9 +31,10 @@ The peer transport (``transport="peer"``, the default on GPUs) needs no host
 read and no NCCL call per forward: every rank maps every other rank's
 exchange region (:class:`PeerExchange`, CUDA IPC over NVLink) and one
 forward is three library calls on the current stream -
-``b200_ep_dispatch`` (rows stored straight into the owners' regions),
-``b200_ep_expert_forward`` (the owner's experts; the down GEMM's epilogue
-stores each weighted row into its source's region) and ``b200_ep_combine``.
+``b200_ep_dispatch`` (one row per (token, owner) stored straight into the
+owners' regions), ``b200_ep_expert_forward`` (the owner's experts, then one
+summed row per received row stored into its source's region) and
+``b200_ep_combine``.
 Ranks synchronize through flags in the regions, so the forward can be
 captured in a CUDA graph and replayed on every rank.
 """
@@ -82,15 +89,17 @@ class PeerExchange:
 
     def received(self):
         """Views of what the last expert step received: (local ids int32
-        [slots, 1], -1 = empty; router weights fp32 [slots, 1]; rows f16
-        [slots, hidden]), slots = world * max_tokens * top_k."""
+        [rows, top_k], -1 = not on this rank or empty; router weights fp32
+        [rows, top_k]; activation rows f16 [rows, hidden]),
+        rows = world * max_tokens."""
         lay = ops.ep_region_layout(self.world, self.max_tokens, self.top_k, self.hidden)
-        slots = self.world * self.max_tokens * self.top_k
+        rows = self.world * self.max_tokens
+        slots = rows * self.top_k
         reg = self.region
-        ids = reg[lay["ids"] : lay["ids"] + 4 * slots].view(torch.int32).view(slots, 1)
-        w = reg[lay["weights"] : lay["weights"] + 4 * slots].view(torch.float32).view(slots, 1)
-        rows = reg[lay["recv"] : lay["recv"] + 2 * slots * self.hidden].view(torch.float16)
-        return ids, w, rows.view(slots, self.hidden)
+        ids = reg[lay["ids"] : lay["ids"] + 4 * slots].view(torch.int32).view(rows, self.top_k)
+        w = reg[lay["weights"] : lay["weights"] + 4 * slots].view(torch.float32).view(rows, self.top_k)
+        x = reg[lay["recv"] : lay["recv"] + 2 * rows * self.hidden].view(torch.float16)
+        return ids, w, x.view(rows, self.hidden)
 
     def status(self, reset: bool = True) -> int:
         return ops.region_status(self.region, reset)
@@ -104,10 +113,12 @@ class PeerExchange:
 class ExpertParallelMoE:
     """``local`` holds this rank's ``num_experts / world`` experts.
 
-    ``local_fn(rows, local_ids[R,1], weights[R,1]) -> weighted rows`` and
-    ``combine_fn(routed[T*k,H], topk_ids, shared) -> out`` default to the
-    library (the local layer and its combine kernel); tests substitute CPU
-    implementations to check the exchange itself over gloo.
+    ``local_fn(rows[R,H], local_ids[R,k], weights[R,k]) -> summed rows[R,H]``
+    (slots with id -1 belong to other ranks) and ``combine_fn(returned[P,H],
+    pair_token[P], topk_ids, shared) -> out`` default to the library (the local
+    layer, and a sum of each token's returned rows plus the shared expert);
+    tests substitute CPU implementations to check the exchange itself over
+    gloo.
     """
 
     def __init__(self, local: QuantMoELayer | None, num_experts: int, rank: int, world: int,
@@ -124,7 +135,7 @@ class ExpertParallelMoE:
         self.world = world
         self.group = group
         self.experts_per_rank = num_experts // world
-        self.last_recv = None  # (rows, local ids, weights) of the last forward
+        self.last_recv = None  # (rows, local ids [R, k], weights [R, k]) of the last forward
         self._local_fn = local_fn
         self._combine_fn = combine_fn
         self._shared_fn = shared_fn
@@ -153,21 +164,23 @@ class ExpertParallelMoE:
             self.peer_block_size = local.block_size or block_size_for(
                 max_tokens * routes_k, local.num_experts + (1 if self.fused else 0))
 
-    def _run_local(self, rows, ids1, w1):
+    def _run_local(self, rows, ids, w):
         if self._local_fn is not None:
-            return self._local_fn(rows, ids1, w1)
-        bs = self.local.block_size or block_size_for(rows.shape[0], self.local.num_experts)
-        return self.local.forward(rows, ids1, w1, block_size=bs, use_shared=False)
+            return self._local_fn(rows, ids, w)
+        bs = self.local.block_size or block_size_for(int((ids >= 0).sum()), self.local.num_experts)
+        return self.local.forward(rows, ids, w, block_size=bs, use_shared=False)
 
-    def _combine(self, routed, topk_ids, shared, out):
+    def _combine(self, returned, pair_token, topk_ids, shared, out):
         if self._combine_fn is not None:
-            return self._combine_fn(routed, topk_ids, shared)
-        # every route was computed by its owner: no id is dropped here
-        y = B.moe_combine(routed, topk_ids.clamp(min=0), self.num_experts, 1.0, shared,
-                          routed.dtype)
+            return self._combine_fn(returned, pair_token, topk_ids, shared)
+        tokens = topk_ids.shape[0]
+        acc = torch.zeros(tokens, returned.shape[1], dtype=torch.float32, device=returned.device)
+        acc.index_add_(0, pair_token, returned.float())
+        if shared is not None:
+            acc += shared.float()
         if out is None:
-            return y
-        out.copy_(y)
+            return acc.to(returned.dtype)
+        out.copy_(acc)
         return out
 
     def _shared(self, x):
@@ -178,11 +191,20 @@ class ExpertParallelMoE:
         return None
 
     def dispatch_plan(self, topk_ids: torch.Tensor):
-        """(order, send_counts): routes sorted stably by destination rank."""
-        dest = (topk_ids.reshape(-1).long() // self.experts_per_rank).clamp_(0, self.world - 1)
-        order = torch.argsort(dest, stable=True)
-        send_counts = torch.bincount(dest, minlength=self.world)
-        return order, dest, send_counts
+        """(pair_token, pair_owner, send_counts): one (token, owner) pair per
+        distinct owner of a token's valid routes, sorted stably by owner."""
+        tokens = topk_ids.shape[0]
+        ids = topk_ids.long()
+        valid = (ids >= 0) & (ids < self.num_experts)
+        dest = torch.where(valid, ids // self.experts_per_rank, torch.zeros_like(ids))
+        owned = torch.zeros(tokens, self.world, dtype=torch.bool, device=ids.device)
+        owned.scatter_(1, dest, valid)
+        # nonzero walks token-major; a stable sort by owner keeps token order
+        pair_token, pair_owner = owned.nonzero(as_tuple=True)
+        order = torch.argsort(pair_owner, stable=True)
+        pair_token, pair_owner = pair_token[order], pair_owner[order]
+        send_counts = torch.bincount(pair_owner, minlength=self.world)
+        return pair_token, pair_owner, send_counts
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
@@ -197,7 +219,7 @@ class ExpertParallelMoE:
             return self._forward_peer(x, topk_ids, topk_weights, shared, out)
 
         tokens, top_k = topk_ids.shape
-        order, dest, send_counts = self.dispatch_plan(topk_ids)
+        pair_token, pair_owner, send_counts = self.dispatch_plan(topk_ids)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         counts = torch.stack([send_counts, recv_counts]).to("cpu")
@@ -205,28 +227,31 @@ class ExpertParallelMoE:
         recv_split = counts[1].tolist()
         n_recv = int(sum(recv_split))
 
-        flat_ids = topk_ids.reshape(-1)[order]
-        local_ids = (flat_ids - dest[order].to(flat_ids.dtype) * self.experts_per_rank).to(torch.int32)
-        meta = torch.stack([local_ids, topk_weights.reshape(-1)[order].view(torch.int32)], dim=1)
-        rows = x.index_select(0, order // top_k)
+        # Each pair carries its token's top_k slots: the local expert where the
+        # route belongs to the pair's owner, -1 elsewhere.
+        ids = topk_ids.long()[pair_token]
+        valid = (ids >= 0) & (ids < self.num_experts)
+        mine = valid & (ids // self.experts_per_rank == pair_owner[:, None])
+        local_ids = torch.where(mine, ids - pair_owner[:, None] * self.experts_per_rank,
+                                torch.full_like(ids, -1)).to(torch.int32)
+        meta = torch.cat([local_ids, topk_weights[pair_token].float().view(torch.int32)], dim=1)
+        rows = x.index_select(0, pair_token)
 
         recv_rows = torch.empty(n_recv, x.shape[1], dtype=x.dtype, device=x.device)
-        recv_meta = torch.empty(n_recv, 2, dtype=torch.int32, device=x.device)
+        recv_meta = torch.empty(n_recv, 2 * top_k, dtype=torch.int32, device=x.device)
         dist.all_to_all_single(recv_rows, rows, recv_split, send_split, group=self.group)
         dist.all_to_all_single(recv_meta, meta, recv_split, send_split, group=self.group)
 
         if n_recv:
-            ids1 = recv_meta[:, :1].contiguous()
-            w1 = recv_meta[:, 1:].contiguous().view(torch.float32)
-            done = self._run_local(recv_rows, ids1, w1).contiguous()
-            self.last_recv = (recv_rows, ids1, w1)
+            ids_r = recv_meta[:, :top_k].contiguous()
+            w_r = recv_meta[:, top_k:].contiguous().view(torch.float32)
+            done = self._run_local(recv_rows, ids_r, w_r).contiguous()
+            self.last_recv = (recv_rows, ids_r, w_r)
         else:
             done = recv_rows
-        back = torch.empty(tokens * top_k, x.shape[1], dtype=done.dtype, device=x.device)
+        back = torch.empty(pair_token.numel(), x.shape[1], dtype=done.dtype, device=x.device)
         dist.all_to_all_single(back, done, send_split, recv_split, group=self.group)
-        routed = torch.empty_like(back)
-        routed.index_copy_(0, order, back)
-        return self._combine(routed, topk_ids, shared, out)
+        return self._combine(back, pair_token, topk_ids, shared, out)
 
     def _forward_peer(self, x, topk_ids, topk_weights, shared, out):
         self.peer_dispatch(x, topk_ids, topk_weights)

@@ -179,12 +179,14 @@ def test_ep_region_layout_sizes():
     for world, tokens, k, h in [(1, 1, 1, 128), (2, 24, 4, 256), (8, 128, 9, 7168), (8, 4096, 8, 7168)]:
         lay = ops.ep_region_layout(world, tokens, k, h)
         assert lay["total"] == ops.ep_region_bytes(world, tokens, k, h)
-        slots = world * tokens * k
+        rows = world * tokens  # one row per (source token, owner), top_k slots each
         offs = [lay[n] for n in ("ids", "weights", "orig", "rows", "recv", "comb")]
         assert all(o % 256 == 0 for o in offs) and offs == sorted(offs)
-        assert lay["recv"] - lay["rows"] >= 8 * slots
-        assert lay["comb"] - lay["recv"] >= 2 * slots * h
-        assert lay["total"] - lay["comb"] >= 2 * tokens * k * h
+        assert lay["weights"] - lay["ids"] >= 4 * rows * k
+        assert lay["orig"] - lay["weights"] >= 4 * rows * k
+        assert lay["recv"] - lay["rows"] >= 8 * rows
+        assert lay["comb"] - lay["recv"] >= 2 * rows * h
+        assert lay["total"] - lay["comb"] >= 2 * rows * h + 8 * tokens
 
 
 def test_w8a8_validation():

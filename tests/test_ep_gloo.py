@@ -58,14 +58,19 @@ def _worker(rank, world, port, mode, results):
         per = E // world
         mine = slice(rank * per, (rank + 1) * per)
 
-        def local_fn(rows, ids1, w1):
-            ids_g = ids1  # local ids
-            out = oracle.moe_layer_ref(rows, ids_g, w1, w13[mine], w2[mine], inter_dtype=None)
+        def local_fn(rows, ids_r, w_r):
+            # one row per (token, this owner); slots of other owners are -1
+            assert ids_r.shape == w_r.shape == (rows.shape[0], K)
+            out = oracle.moe_layer_ref(rows, ids_r, w_r, w13[mine], w2[mine], inter_dtype=None)
             return out.to(rows.dtype)
 
-        def combine_fn(routed, topk_ids, shared):
-            t, k = topk_ids.shape
-            return routed.float().view(t, k, -1).sum(1)
+        def combine_fn(returned, pair_token, topk_ids, shared):
+            # exactly one returned row per (token, distinct owner of its routes)
+            owners = [len({int(e) // per for e in row}) for row in topk_ids.tolist()]
+            assert returned.shape[0] == pair_token.numel() == sum(owners)
+            assert torch.bincount(pair_token, minlength=len(owners)).tolist() == owners
+            acc = torch.zeros(topk_ids.shape[0], returned.shape[1])
+            return acc.index_add_(0, pair_token, returned.float())
 
         ep = ExpertParallelMoE(None, E, rank, world, local_fn=local_fn, combine_fn=combine_fn)
         x, ids, w = _inputs(rank)

@@ -186,3 +186,28 @@ def test_peer_ep_missing_rank_times_out_with_status(cuda_device):
     elapsed = time.time() - t0
     assert m0.exchange.status() & 8
     assert elapsed < 30, elapsed
+
+
+def test_peer_ep_one_row_per_token_and_owner(cuda_device):
+    """Deduplicated dispatch: each owner receives exactly one row per
+    (source token, owner) pair, whatever the number of that token's routes it
+    owns, and the output still matches the single-GPU layer."""
+    dev = cuda_device
+    world, tokens = 4, 32
+    full, models = _setup(world, tokens, _lib.QUANT_FP8_BLOCK, dev)
+    inputs = [_inputs(tokens, SHAPE, dev, 900 + r) for r in range(world)]
+    outs = _step(models, inputs)
+    torch.cuda.synchronize()
+    per = SHAPE.experts // world
+    for o, m in enumerate(models):
+        want_rows = sum(int(((ids.long() // per) == o).any(1).sum()) for _, ids, _ in inputs)
+        ids_r, _, _ = m.exchange.received()
+        assert ids_r.shape == (world * tokens, SHAPE.top_k)
+        live = int((ids_r >= 0).any(1).sum())
+        assert live == want_rows, (o, live, want_rows)
+        routes_here = sum(int(((ids.long() // per) == o).sum()) for _, ids, _ in inputs)
+        assert int((ids_r >= 0).sum()) == routes_here
+    for r, ((x, ids, w), out) in enumerate(zip(inputs, outs)):
+        assert_close(out, full.forward(x, ids, w), what=f"rank {r}")
+    for m in models:
+        assert m.exchange.status() == 0
