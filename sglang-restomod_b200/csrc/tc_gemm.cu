@@ -104,8 +104,12 @@ constexpr int kNMaxNarrow = 64;  // items of few routes (expert-parallel owners,
 // its B tiles come from L2 ~2,000 clocks after they are asked for, so three
 // 48 KiB B stages are in flight, and five raw weight units. The narrow
 // configuration's 64-column accumulators leave room for six A stages.
-template <int NMAX>
+// Configurations: kTcWideShort (items of 192 slots, fewer than 32 weight
+// units), kTcWideLong (192 slots, 32 units or more), kTcNarrow (64 slots).
+constexpr int kTcWideShort = 0, kTcWideLong = 1, kTcNarrow = 2;
+template <int CFG>
 struct TcCfg {
+  static constexpr int NMAX = CFG == kTcNarrow ? 64 : 192;
   static constexpr int kNMax = NMAX;
   static constexpr int kLoadPasses = NMAX / (kLoadThreads / 2);  // rows per gather thread
   static constexpr int kRawStages = NMAX > 64 ? 5 : 8;             // 16 KiB units in flight
@@ -113,12 +117,17 @@ struct TcCfg {
   static constexpr int kAStages = NMAX > 64 ? 2 : 6;               // tensor memory
   static constexpr int kBStages = NMAX > 64 ? 3 : 6;               // shared memory
   // Dequant and epilogue warp groups (four warps each, one per tensor-memory
-  // lane quarter) among warps 4-15. The narrow configuration's 64-column
-  // epilogue is light, so one group drains both accumulator buffers and a
-  // second dequant group (warps 12-15) takes the odd units: measured on B200,
-  // one group's ~450 clocks per 128-K stage per warp paced the narrow tiles.
-  static constexpr int kDqGroups = NMAX > 64 ? 1 : 2;
+  // lane quarter) among warps 4-15. Measured on B200: with long items the
+  // one epilogue group keeps up, and two dequant groups pay - on the wide
+  // tiles each converts one 64-K half of every unit (halving the refill
+  // latency of the two A slots: config4 T=4096 gate/up 3.30 -> 2.98 ms), on
+  // the narrow ones group g takes the units u with u % 2 == g (one group's
+  // ~450 clocks per 128-K stage per warp paced them); with short wide items
+  // (K = 512-2048) the second epilogue group is needed (config2 T=8192
+  // gate/up 556 us with it, 630 us without).
+  static constexpr int kDqGroups = CFG == kTcWideShort ? 1 : 2;
   static constexpr int kEpiGroups = 3 - kDqGroups;
+  static constexpr bool kDqHalves = CFG == kTcWideLong;
   static constexpr uint32_t kSubTile = NMAX * 128;                 // [NMAX rows][64 K] f16
   static constexpr uint32_t kBStage = kSub * kSubTile;
   static constexpr uint32_t kStageCols = kSub * kSubCols;
@@ -134,7 +143,7 @@ struct TcCfg {
   static_assert(kTcSmem <= 232448, "shared memory");
   static_assert(NMAX % 64 == 0 && kLoadPasses * (kLoadThreads / 2) == NMAX, "item width");
   static_assert(2 % kSub == 0, "a weight unit is two 64-K halves");
-  static_assert(kDqGroups == 1 || kSub == 2, "dequant groups split units, one stage each");
+  static_assert(kDqGroups == 1 || kSub == 2, "two dequant groups need 128-K stages");
 };
 
 template <int R, int A, int B>
@@ -404,12 +413,12 @@ __device__ __forceinline__ T pick(const T (&v)[M], int g) {
 
 // kFp4: NVFP4 units (9 KiB: codes, then per-16-K E4M3 scales; weights
 // e2m1 * fp16_rne(e4m3 * global)), else block-FP8 units (16 KiB).
-template <bool kFp4, int NMAX>
+template <bool kFp4, int CFG>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const StreamParams p, const int2* __restrict__ plan,
                    const int* __restrict__ plan_count, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x) {
-  using C = TcCfg<NMAX>;
+  using C = TcCfg<CFG>;
   using Ctl = CtlT<C::kRawStages, C::kAStages, C::kBStages>;
   constexpr int kNMax = C::kNMax;
   constexpr int kAStages = C::kAStages;
@@ -441,7 +450,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // bfull: every gather thread (cp.async arrivals) or the one thread that
     // issues the stage's TMA tiles.
     const uint32_t b_arrivals = p.xs != nullptr ? 1u : (uint32_t)kLoadThreads;
-    for (int s = 0; s < kAStages; ++s) mbar_init(&ctl->full[s], 4);
+    for (int s = 0; s < kAStages; ++s) mbar_init(&ctl->full[s], C::kDqHalves ? 8 : 4);
     for (int s = 0; s < kBStages; ++s) {
       mbar_init(&ctl->empty[s], 1);
       mbar_init(&ctl->bfull[s], b_arrivals);
@@ -452,7 +461,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&ctl->raw_full[s], 1);
-      mbar_init(&ctl->raw_empty[s], 4);
+      mbar_init(&ctl->raw_empty[s], C::kDqHalves ? 8 : 4);
     }
     mbar_init(&ctl->done, 1);
     for (int i = 0; i < kInfoSlots; ++i) ctl->info[i] = 0;
@@ -760,7 +769,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // The TMA copy stores the unit as 128 rows of 128 bytes with 16-byte chunk
     // c of row r at chunk c ^ (r & 7). A 64-K stage h takes kg4 = 2h + kg.
     const int quarter = warp & 3;
-    const int dg = warp < kWarpEpi ? 0 : 1;  // dequant group: units u with u % kDqGroups == dg
+    const int dg = warp < kWarpEpi ? 0 : 1;  // dequant group (its units or its halves)
     const int m = quarter * 32 + lane;
     const int hf = (m >> 3) & 1;
     const int r8 = m & 7;
@@ -802,7 +811,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++j;
       }
       --nk_left;
-      if constexpr (C::kDqGroups > 1) {
+      if constexpr (C::kDqGroups > 1 && !C::kDqHalves) {
         // The other group's unit (one stage): only the ring positions move.
         if (ug++ % C::kDqGroups != dg) {
           rr.advance();
@@ -820,11 +829,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint8_t* raw = smem + kOffRaw + rr.idx * kUnitBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        if (C::kDqHalves && h != dg) continue;  // the other group's half
         const int sq = h % kSub;
+        const bool first = C::kDqHalves || sq == 0;        // takes the stage
+        const bool last = C::kDqHalves || sq == kSub - 1;  // hands it on
         if (p.loads_only) {
           // pipeline floor: hand the stage on without dequantizing into it
-          if (sq == 0 && !(ok = take_stage())) break;
-          if (sq == kSub - 1 && !(ok = give_stage())) break;
+          if (first && !(ok = take_stage())) break;
+          if (last && !(ok = give_stage())) break;
           continue;
         }
         uint32_t v[32];
@@ -844,7 +856,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           const uint2 sc = *reinterpret_cast<const uint2*>(
               raw + (64 + wr) * 128 + ((g ^ wr) & 7) * 16 + 8 * h);
-          if (sq == 0 && !(ok = take_stage())) break;
+          if (first && !(ok = take_stage())) break;
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             // Scale bytes of record c: top g0, top g1, bottom g0, bottom g1.
@@ -871,7 +883,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int chunk = (((r8 & 1) * 4 + kg4) ^ row) & 7;
             r[i] = *reinterpret_cast<const uint2*>(raw + row * 128 + chunk * 16 + hf * 8);
           }
-          if (sq == 0 && !(ok = take_stage())) break;
+          if (first && !(ok = take_stage())) break;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             uint32_t* o = v + 16 * (i >> 2) + 4 * (i & 3);
@@ -882,7 +894,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         tmem_st32(tmem + tlane + kACol0 + st.idx * kStageCols + (uint32_t)sq * kSubCols, v);
-        if (sq == kSub - 1 && !(ok = give_stage())) break;
+        if (last && !(ok = give_stage())) break;
       }
       if (!ok) break;
       __syncwarp();
@@ -1198,7 +1210,7 @@ cudaError_t launch_tc_split_finish(const StreamParams& p, cudaStream_t stream) {
 // caller. `plan_buf` holds launch_tc_plan's output (moe mode).
 namespace {
 
-template <bool kFp4, int NMAX>
+template <bool kFp4, int CFG>
 cudaError_t launch_tc_config(const StreamParams& p, const int2* plan, const int* count, int grid,
                              const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                              cudaStream_t stream) {
@@ -1206,14 +1218,14 @@ cudaError_t launch_tc_config(const StreamParams& p, const int2* plan, const int*
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  constexpr size_t smem = TcCfg<NMAX>::kTcSmem;
+  constexpr size_t smem = TcCfg<CFG>::kTcSmem;
   if (!configured[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<kFp4, NMAX>,
+    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<kFp4, CFG>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     configured[dev] = true;
   }
-  return launch_pdl(tc_gemm_kernel<kFp4, NMAX>, dim3(grid), dim3(kTcThreads), smem, stream, p,
+  return launch_pdl(tc_gemm_kernel<kFp4, CFG>, dim3(grid), dim3(kTcThreads), smem, stream, p,
                     plan, count, tmap_w, tmap_x);
 }
 
@@ -1248,11 +1260,23 @@ cudaError_t launch_tc_gemm(int quant, const StreamParams& p, const void* plan_bu
   }
   const int* count = reinterpret_cast<const int*>(plan_buf);
   const int2* plan = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(plan_buf) + 256);
-  if (fp4)
-    return narrow ? launch_tc_config<true, kNMaxNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream)
-                  : launch_tc_config<true, kNMaxWide>(p, plan, count, grid, tmap_w, tmap_x, stream);
-  return narrow ? launch_tc_config<false, kNMaxNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream)
-                : launch_tc_config<false, kNMaxWide>(p, plan, count, grid, tmap_w, tmap_x, stream);
+  // Weight units per item (per K part when K is split).
+  const int kch = p.K / 128;
+  const int item_units =
+      p.sorted_ids == nullptr && p.ksplit > 1 ? (kch + p.ksplit - 1) / p.ksplit : kch;
+  const int cfg = narrow ? kTcNarrow : (item_units >= 32 ? kTcWideLong : kTcWideShort);
+  if (fp4) {
+    if (cfg == kTcNarrow)
+      return launch_tc_config<true, kTcNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream);
+    if (cfg == kTcWideLong)
+      return launch_tc_config<true, kTcWideLong>(p, plan, count, grid, tmap_w, tmap_x, stream);
+    return launch_tc_config<true, kTcWideShort>(p, plan, count, grid, tmap_w, tmap_x, stream);
+  }
+  if (cfg == kTcNarrow)
+    return launch_tc_config<false, kTcNarrow>(p, plan, count, grid, tmap_w, tmap_x, stream);
+  if (cfg == kTcWideLong)
+    return launch_tc_config<false, kTcWideLong>(p, plan, count, grid, tmap_w, tmap_x, stream);
+  return launch_tc_config<false, kTcWideShort>(p, plan, count, grid, tmap_w, tmap_x, stream);
 }
 
 }  // namespace b200
