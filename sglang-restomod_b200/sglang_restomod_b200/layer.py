@@ -31,26 +31,27 @@ def block_size_for(routes: int, experts: int) -> int:
     which the decode regime can afford (it is HBM-bound).
 
     Measured on B200 (block FP8, H=7168, I=2048, 1024 routes spread evenly
-    over 256 / 128 / 64 / 32 experts, graph replay, ms per layer):
+    over 256 / 128 / 64 / 32 experts, graph replay, ms per layer; blocks of 64
+    run on the tensor-core GEMM, re-measured after its single-thread MMA loop):
 
     ============  =====  =====  =====  =====
     routes/expert   4      8     16     32
-    blocks of 8   1.765  1.291  1.090  0.874
-    blocks of 16  1.843  0.994  0.729  0.639
-    blocks of 32  2.929  1.592  0.888  0.778
-    blocks of 64  2.941  1.563  0.806  0.443
+    blocks of 8   1.765  1.305  1.095  0.876
+    blocks of 16  1.843  1.067  0.770  0.717
+    blocks of 32  2.929  1.807  1.088  0.957
+    blocks of 64  2.941  1.338  0.714  0.409
     ============  =====  =====  =====  =====
 
     and on the E=512 bank (H=2048, I=512, top-10; FP8 / NVFP4): 8 slots
     0.300 / 0.262 against 16 slots 0.309 / 0.302 ms at 5 routes per expert,
     0.377 / 0.328 against 0.331 / 0.329 ms at 7.5, so 8-slot groups up to 6
-    routes per expert on average, 16-slot groups up to 16, and above that
+    routes per expert on average, 16-slot groups below 12, and from 12 on
     blocks of 64 on the tensor-core GEMM.
     """
     avg = routes / max(experts, 1)
     if avg <= 6:
         return 8
-    if avg <= 16:
+    if avg < 12:
         return 16
     return 64
 

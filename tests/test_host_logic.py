@@ -187,8 +187,10 @@ def test_block_size_rule_follows_the_measured_crossovers():
     assert block_size_for(2816, 513) == 8      # config2 T=256 with the shared route
     assert block_size_for(600, 100) == 8       # 6.0
     assert block_size_for(601, 100) == 16
-    assert block_size_for(1024, 64) == 16      # 16 per expert
-    assert block_size_for(1025, 64) == 64
+    assert block_size_for(1024, 128) == 16     # 8 per expert
+    assert block_size_for(1535, 128) == 16     # just under 12
+    assert block_size_for(1536, 128) == 64     # 12 per expert
+    assert block_size_for(1024, 64) == 64      # 16 per expert: the tensor-core GEMM
     assert block_size_for(1024, 32) == 64      # expert-parallel owner at 8 ranks
     assert block_size_for(0, 512) == 8
 
