@@ -20,7 +20,7 @@
 // mbarrier rings (every wait bounded, no named barriers):
 //   warp 0       weights: per 16 KiB FP8 unit (one 128x128 block of
 //                prepack.cu's streamed layout) its two f16 scale multipliers
-//                and a 2-D TMA copy (128-byte swizzle) into an 8-deep raw ring;
+//                and a 2-D TMA copy (128-byte swizzle) into the raw ring;
 //                the warp computes 32 units' multipliers at a time and lane 0
 //                issues their copies;
 //   warp 1       MMA: lane 0 alone runs the main loop - per stage its B tile
@@ -38,10 +38,14 @@
 //                from the swizzled raw unit (conflict-free 8-byte reads),
 //                f16(e4m3) * m with one hmul2 per two values, and writes them
 //                into the stage's tensor-memory columns (tcgen05.st), then
-//                arrive on the stage's `full` barrier (4 arrivals);
-//   warps 8-15   epilogue: tcgen05.ld of a double-buffered accumulator, 2^E,
-//                SiLU*up, router weight and store, overlapping the next item's
-//                main loop; warps 8-11 drain buffer 0 (even items), warps 12-15
+//                arrive on the stage's `full` barrier; warps 12-15 are a
+//                second dequant group in two of the three configurations
+//                (TcCfg: alternate units on the narrow tiles, the other 64-K
+//                half of every unit on long wide items);
+//   warps 8-15   epilogue (8-11 where 12-15 dequantize): tcgen05.ld of a
+//                double-buffered accumulator, 2^E, SiLU*up, router weight and
+//                store, overlapping the next item's main loop; with two
+//                groups warps 8-11 drain buffer 0 (even items), warps 12-15
 //                buffer 1.
 // The MMA thread's loop is the pipeline's critical path. Measured on B200 with
 // a per-stage timeline of every role: the producers ran ~2,000 clocks ahead
