@@ -261,10 +261,10 @@ class ExpertParallelMoE:
     def peer_launches_per_forward(self, x_dtype=torch.bfloat16) -> int:
         """Kernels of one peer-transport forward: dispatch, receive, align (3
         kernels from 4096 receive slots on), [tcgen05 plan], gate/up, down,
-        signal, combine, + the shared expert's."""
+        pre-sum, signal, combine, + the shared expert's."""
         layer = self.local
         slots = self.world * self.exchange.max_tokens * self.exchange.top_k
-        n = 1 + 1 + (3 if slots >= 4096 else 1) + (1 if self.peer_block_size >= 64 else 0) + 4
+        n = 1 + 1 + (3 if slots >= 4096 else 1) + (1 if self.peer_block_size >= 64 else 0) + 5
         if self.fused:
             n += 1 + (1 if self.peer_block_size >= 64 else 0)  # route append, permute
         elif layer.shared is not None:
